@@ -1,0 +1,456 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 Qwen3-TTS decode path.
+
+One "step" is one talker decode step for a continuous batch of 32 slots:
+the 28-layer Qwen3 talker (hidden 2048, 16q/8kv x 128, FFN 6144, vocab 3072,
+random-init N(0, 0.02) weights from a seed) on the slot-table KV arena with
+ragged contexts U[64, 2048], greedy next-token selection, and the next
+step's input embedding, replayed as one CUDA graph. Every 16 steps a few
+slots are evicted and re-admitted with new seeded contexts. Each step emits
+one codec frame per slot, so throughput is reported as frames/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+N > 1 runs one independent engine replica per GPU (request-level data
+parallelism: no collective on the data path); rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "qwen3-tts-rsi-engine_b200"))
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "codec frames/s (talker decode step, C=32)"
+UNIT = "frames/s"
+SLOTS = 32
+CAPACITY = 4096
+ADMIT_EVERY = 16
+ADMIT_SLOTS = 4
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=40)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--layers", type=int, default=28, help="talker depth (28 = the benchmarked model)")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------- distributed plumbing
+class Dist:
+    def __init__(self, backend: str):
+        self.rank = int(os.environ.get("RANK", 0))
+        self.world = int(os.environ.get("WORLD_SIZE", 1))
+        self.local = int(os.environ.get("LOCAL_RANK", 0))
+        self.enabled = self.world > 1
+        if self.enabled:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+
+    def barrier(self):
+        if self.enabled:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max(self, value: float) -> float:
+        if not self.enabled:
+            return value
+        import torch.distributed as dist
+        t = torch.tensor([value], dtype=torch.float64,
+                         device="cuda" if dist.get_backend() == "nccl" else "cpu")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.enabled:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------- workload
+class Workload:
+    """Seeded ragged contexts and the eviction/admission schedule."""
+
+    def __init__(self, seed: int, slots: int = SLOTS):
+        self.g = torch.Generator().manual_seed(seed)
+        self.slots = slots
+        self.positions = torch.randint(64, 2049, (slots,), generator=self.g)
+
+    def admit(self):
+        """Evict ADMIT_SLOTS seeded slots and admit new requests with fresh contexts."""
+        slots = torch.randperm(self.slots, generator=self.g)[:ADMIT_SLOTS]
+        fresh = torch.randint(64, 2049, (ADMIT_SLOTS,), generator=self.g)
+        return slots, fresh
+
+
+# ---------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-f", self.path], stdout=subprocess.DEVNULL,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self, uuid: str | None):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        try:
+            for line in Path(self.path).read_text().splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9 and (uuid is None or parts[0] == uuid):
+                    rows.append(parts)
+        finally:
+            os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, val in zip(names, r[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def device_uuid(index: int):
+    try:
+        u = str(torch.cuda.get_device_properties(index).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return None
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic(kernel: str):
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary, if present."""
+    path = ROOT / "profiles" / "traffic.json"
+    if not path.exists():
+        return None
+    data = json.loads(path.read_text())
+    entry = data.get(kernel)
+    return None if entry is None else entry.get("dram_bytes_per_launch")
+
+
+# ---------------------------------------------------------------------- CPU baseline (oracle)
+def cpu_decode_sample(cfg, positions, steps: int, sample_layers: int, seed: int):
+    """Time the oracle's fp32 talker layers on the host cores for `steps` steps.
+
+    Bounded sample: `sample_layers` of the 28 layers at full widths and the
+    real ragged contexts; the per-step time is scaled by 28 / sample_layers.
+    """
+    from dataclasses import replace
+
+    from oracle import decoder as OD
+    from qwen3_tts_b200.weights import decoder_weights
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    small = replace(cfg, layers=sample_layers)
+    weights = decoder_weights(small, seed, device="cpu", dtype=torch.bfloat16)
+    for layer in weights["layers"]:
+        for key in list(layer):
+            layer[key] = layer[key].float()
+    cap = int(positions.max()) + steps + 2
+    cache = OD.new_cache(small, len(positions), cap)
+    tables = OD.Tables(cap + 1, cfg.head_dim, cfg.theta)
+    h = torch.randn(len(positions), 1, cfg.hidden) * 0.1
+    pos = positions.clone().view(-1, 1)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        x = h
+        for w, (ck, cv) in zip(weights["layers"], cache):
+            x = OD.layer_forward(small, w, x, pos, ck, cv, pos, tables, "fp32")
+        times.append(time.perf_counter() - t0)
+        pos = pos + 1
+    per_step = float(np.median(times)) * (cfg.layers / sample_layers)
+    return per_step, torch.get_num_threads()
+
+
+# ---------------------------------------------------------------------- B200 arm
+def run_b200(args, dist: Dist):
+    from qwen3_tts_b200 import _lib, ops
+    from qwen3_tts_b200.config import TALKER
+    from dataclasses import replace
+    from qwen3_tts_b200.talker import TalkerDecoder
+    from qwen3_tts_b200.weights import decoder_weights
+
+    cfg = TALKER if args.layers == TALKER.layers else replace(TALKER, layers=args.layers)
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    work = Workload(args.seed + dist.rank)
+    weights = decoder_weights(cfg, seed=args.seed, device=dev)
+    engine = TalkerDecoder(cfg, weights, slots=SLOTS, capacity=CAPACITY, device=dev, use_graphs=False)
+    del weights
+    step = engine.step_for(SLOTS, CAPACITY)
+    table = engine.weights["embedding"]
+    tokens = torch.zeros(SLOTS, 1, dtype=torch.long, device=dev)
+    zero_u = torch.zeros(SLOTS, dtype=torch.float32, device=dev)
+    step.positions.copy_(work.positions.to(dev))
+    step.rotary.copy_(work.positions.to(dev))
+    step.inputs.copy_((torch.randn(SLOTS, cfg.hidden, device=dev) * 0.05).to(torch.bfloat16))
+
+    def tick():
+        step.compute()
+        ops.sample(step.logits, uniforms=zero_u, top_k=1, temperature=1.0, tokens=tokens)  # greedy
+        ops.embedding(tokens.view(-1), table, out=step.inputs)
+        ops.advance(step.positions)
+        ops.advance(step.rotary)
+
+    # count our kernels per step (eager pass), then capture the step as one graph
+    before = _lib.launch_count()
+    tick()
+    torch.cuda.synchronize()
+    launches_per_step = _lib.launch_count() - before
+    saved = step.positions.clone(), step.rotary.clone()
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            tick()
+    torch.cuda.current_stream().wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        tick()
+    torch.cuda.synchronize()
+    step.positions.copy_(saved[0])
+    step.rotary.copy_(saved[1])
+
+    def admit(i):
+        if i and i % ADMIT_EVERY == 0:
+            slots, fresh = work.admit()
+            step.positions[slots.to(dev)] = fresh.to(dev)
+            step.rotary[slots.to(dev)] = fresh.to(dev)
+
+    for i in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    positions_at_start = step.positions.cpu()
+
+    clocks = ClockSampler()
+    clocks.start()
+    dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(args.steps):
+        admit(i)
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    elapsed_ms = dist.max(start.elapsed_time(end))
+    clock_info = clocks.stop(device_uuid(dev.index))
+    status = ops.read_status(dev)
+
+    # ---- end to end through the public step API: pinned host inputs in, token ids out, every step
+    host_in = torch.empty(SLOTS, cfg.hidden, dtype=torch.bfloat16).pin_memory()
+    host_in.copy_((torch.randn(SLOTS, cfg.hidden) * 0.05).to(torch.bfloat16))
+    host_pos = work.positions.clone().pin_memory()
+    host_tok = torch.empty(SLOTS, 1, dtype=torch.long).pin_memory()
+    step_g = engine.step_for(SLOTS, CAPACITY)
+    step_g.positions.copy_(host_pos.to(dev))
+    e2e_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        step_g.compute()
+        ops.sample(step_g.logits, uniforms=zero_u, top_k=1, temperature=1.0, tokens=tokens)
+    torch.cuda.current_stream().wait_stream(stream)
+    with torch.cuda.graph(e2e_graph, stream=stream):
+        step_g.compute()
+        ops.sample(step_g.logits, uniforms=zero_u, top_k=1, temperature=1.0, tokens=tokens)
+    torch.cuda.synchronize()
+    e2e_steps = max(4, args.steps // 2)
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(e2e_steps):
+        step_g.inputs.copy_(host_in, non_blocking=True)
+        step_g.positions.copy_(host_pos, non_blocking=True)
+        step_g.rotary.copy_(host_pos, non_blocking=True)
+        e2e_graph.replay()
+        host_tok.copy_(tokens, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        host_pos += 1
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = dist.max(e0.elapsed_time(e1))
+    h2d = host_in.numel() * 2 + host_pos.numel() * 8 * 2
+    d2h = host_tok.numel() * 8
+
+    # ---- roofline of the dominant kernels, timed alone with L2 flushed between launches
+    kernels = kernel_rooflines(cfg, engine, step, positions_at_start, dev)
+    result = {
+        "elapsed_ms": elapsed_ms, "launches_per_step": launches_per_step, "status": status,
+        "clocks": clock_info, "e2e_ms": e2e_ms, "e2e_steps": e2e_steps, "h2d": h2d, "d2h": d2h,
+        "kernels": kernels, "positions": positions_at_start, "cfg": cfg,
+    }
+    graph.reset()
+    e2e_graph.reset()
+    engine.close()
+    return result
+
+
+def kernel_rooflines(cfg, engine, step, positions, dev):
+    from qwen3_tts_b200 import _lib, ops
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    B = SLOTS
+    layer = engine.weights["layers"][0]
+    pos = positions.to(dev)
+
+    def timed(fn, reps=10):
+        total = 0.0
+        for _ in range(reps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            total += a.elapsed_time(b)
+        return total / reps / 1e3  # seconds per launch
+
+    kv_bytes = int(((positions + 1).sum()).item()) * cfg.kv_heads * cfg.head_dim * 2 * 2
+    q_bytes = B * cfg.q_width * 2 * 2
+    out = {}
+    t = timed(lambda: ops.decode_attention(step.q, engine.arena.keys[0], engine.arena.values[0], pos,
+                                           context=step.context, out=step.attn, workspace=step.ws_attn))
+    out["decode_attention"] = {"seconds": t, "bytes": kv_bytes + q_bytes, "per_step": cfg.layers}
+    for name, w, x, o, epi, res in (
+            ("linear_gate_up", layer.gate_up, step.xn, step.act, _lib.EPI_SWIGLU_PAIRED, None),
+            ("linear_qkv", layer.qkv, step.xn, step.qkv, _lib.EPI_STORE, None),
+            ("linear_down", layer.down, step.act, step.h, _lib.EPI_RESIDUAL, step.h),
+            ("linear_o", layer.o, step.attn.view(B, -1), step.h, _lib.EPI_RESIDUAL, step.h)):
+        t = timed(lambda: ops.linear(x, w, out=o, epilogue=epi, residual=res, workspace=step.ws_linear))
+        nbytes = w.numel() * 2 + x.numel() * 2 + o.numel() * 2 * (2 if res is not None else 1)
+        out[name] = {"seconds": t, "bytes": nbytes, "per_step": cfg.layers}
+    del flush
+    return out
+
+
+# ---------------------------------------------------------------------- reference (CPU) arm
+def run_reference(args, dist: Dist):
+    from qwen3_tts_b200.config import TALKER
+    work = Workload(args.seed)
+    layers = 2
+    per_step, threads = cpu_decode_sample(TALKER, work.positions, args.warmup + args.steps, layers, args.seed)
+    value = SLOTS / per_step
+    return {
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "BASELINE config 2: talker decode step, 32 slots, ctx U[64,2048]",
+                   "model": "qwen3-tts talker 28L h2048 (random init)", "global_batch": SLOTS,
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"oracle fp32 talker, {layers} of 28 layers at full width, 32 slots, "
+                                   f"ragged ctx; median step time scaled by 28/{layers}"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", 0))
+        if rank != 0:
+            return
+        print(json.dumps(run_reference(args, Dist.__new__(Dist))))
+        return
+    dist = Dist("nccl")
+    try:
+        res = run_b200(args, dist)
+    finally:
+        pass
+    cfg = res["cfg"]
+    frames = SLOTS * args.steps * dist.world
+    seconds = res["elapsed_ms"] / 1e3
+    value = frames / seconds
+    kernels = res["kernels"]
+    # dominant kernel = largest share of the step (seconds x launches per step)
+    dom_name = max(kernels, key=lambda k: kernels[k]["seconds"] * kernels[k]["per_step"])
+    dom = kernels[dom_name]
+    peak, peak_kind = measured_peaks()
+    achieved = dom["bytes"] / dom["seconds"] / 1e9
+    positions = res["positions"]
+    kv_step = int(((positions + 1).sum()).item()) * cfg.kv_heads * cfg.head_dim * 2 * 2 * cfg.layers
+    step_bytes = cfg.weight_bytes() + kv_step
+    e2e_value = SLOTS * res["e2e_steps"] * dist.world / (res["e2e_ms"] / 1e3)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": res["elapsed_ms"] / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights)",
+        "config": {"workload": "BASELINE config 2: talker decode step, 32 slots, ctx U[64,2048], "
+                               "greedy, evict/admit 4 slots every 16 steps",
+                   "layers": cfg.layers, "global_batch": SLOTS * dist.world, "slots_per_gpu": SLOTS,
+                   "parallelism": f"replicas x{dist.world} (request-level data parallel)",
+                   "l2": "inputs > L2 (6.7 GB streamed per step)",
+                   "hbm_fraction_step": step_bytes / (res["elapsed_ms"] / args.steps / 1e3) / (peak * 1e9),
+                   "bytes_per_step": step_bytes},
+        "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": peak_kind,
+                     "traffic": profile_traffic(dom_name)},
+        "kernels": {k: {"us": v["seconds"] * 1e6, "GBps": v["bytes"] / v["seconds"] / 1e9,
+                        "frac": v["bytes"] / v["seconds"] / 1e9 / peak} for k, v in kernels.items()},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"]},
+        "gpu_launches": res["launches_per_step"] * args.steps,
+        "status_word": res["status"],
+        "clocks": res["clocks"],
+    }
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        per_step, threads = cpu_decode_sample(cfg, positions, 3, 2, args.seed)
+        line["cpu_baseline"] = {"value": SLOTS / per_step, "unit": UNIT, "cores": threads, "kind": "port",
+                                "sample": "oracle fp32 talker, 2 of 28 layers at full width, 32 slots, same "
+                                          "contexts, median of 3 steps scaled by 14"}
+    if dist.rank == 0:
+        print(json.dumps(line))
+    dist.close()
+
+
+if __name__ == "__main__":
+    main()

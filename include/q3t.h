@@ -1,0 +1,250 @@
+/*
+ * q3t.h - C ABI of the B200 (sm_100a) kernels for the Qwen3-TTS
+ * talker -> code-predictor -> codec decode path.
+ *
+ * Conventions
+ *   - Every entry point is `extern "C"`, takes plain device pointers, element
+ *     counts and element strides, and enqueues work on `stream` (a
+ *     cudaStream_t passed as void*). Nothing synchronises with the host, so
+ *     every entry point may be recorded into a CUDA graph.
+ *   - Return value: Q3T_OK (0) or a negative error code. Arguments are
+ *     validated before any launch; on error nothing is written and
+ *     q3t_last_error() describes the failure (thread-local string).
+ *   - The library never allocates or frees caller memory. Kernels that need
+ *     scratch take a caller-owned `workspace` (size from the matching
+ *     *_workspace_bytes query, zero-filled once before first use; the kernels
+ *     leave it ready for the next call).
+ *   - `status` (nullable) is a caller-owned device word. Kernels OR error bits
+ *     into it instead of trapping: bit 0 TMA wait timeout, bit 1 MMA wait
+ *     timeout, bit 2 flag wait timeout, bit 3 out-of-range index skipped.
+ *
+ * Each declaration names the reference interface it replaces
+ * (InferMatrixLab/qwen3-tts-rsi-engine, paths inside that project).
+ */
+#ifndef Q3T_H
+#define Q3T_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  Q3T_OK = 0,
+  Q3T_EINVAL = -1,      /* invalid shape, stride, alignment or dtype */
+  Q3T_EUNSUPPORTED = -2,/* valid but outside the shapes this build supports */
+  Q3T_ECUDA = -3,       /* CUDA launch or driver error */
+  Q3T_ESPACE = -4       /* workspace too small */
+};
+
+enum { Q3T_BF16 = 0, Q3T_F32 = 1 };
+
+/* Epilogues of q3t_linear. */
+enum {
+  Q3T_EPI_STORE = 0,        /* out = acc (+ bias), rounded to out dtype */
+  Q3T_EPI_RESIDUAL = 1,     /* out = bf16(residual + bf16(acc)) */
+  Q3T_EPI_SWIGLU_PAIRED = 2 /* rows of each 128-row weight tile are [64 gate; 64 up];
+                               out[:, f] = bf16(bf16(silu(gate_f)) * up_f) */
+};
+
+/* RMSNorm rounding modes. */
+enum {
+  Q3T_NORM_REFERENCE = 0, /* bf16(w * bf16(x * rsqrt(mean(x^2) + eps))) - HF Qwen3 RMSNorm */
+  Q3T_NORM_NATIVE = 1     /* bf16(w * x * rsqrt(mean(x^2) + eps)) - one rounding */
+};
+
+int q3t_abi_version(void);
+const char* q3t_last_error(void);
+/* Number of kernels this library has launched from this process (all devices). */
+uint64_t q3t_launch_count(void);
+
+/* ------------------------------------------------------------------ KV arena */
+
+/* Replaces qwen3_tts_engine/kv_triton_ascend.py:39 write() and the scatter in
+ * qwen3_tts_engine/continuous.py:152-166 SlotCache.update().
+ * keys/values: [batch, heads, 1, width] with element strides
+ * {batch, head, dim} (strided views of a packed QKV projection are allowed).
+ * target_keys/target_values: contiguous [batch, heads, capacity, width].
+ * positions: int64 [batch]. target[b, h, positions[b], :] = source[b, h, 0, :].
+ * Out-of-range positions are skipped and raise status bit 3. */
+int q3t_kv_write(const void* keys, const int64_t* key_strides, const void* values,
+                 const int64_t* value_strides, void* target_keys, void* target_values,
+                 const int64_t* positions, int64_t batch, int64_t heads, int64_t width,
+                 int64_t capacity, int dtype, unsigned* status, void* stream);
+
+/* Replaces qwen3_tts_engine/packed_kv.py:6 copy_packed_prefix(target, source, slot, row, length).
+ * target: 5-D [planes, slots, heads, capacity, width], source: 5-D
+ * [planes, rows, heads, length, width], each with element strides.
+ * target[:, slot, :, :length] = source[:, row, :, :length]. elem_size 2, 4 or 8. */
+int q3t_copy_packed_prefix(void* target, const int64_t* target_shape, const int64_t* target_strides,
+                           const void* source, const int64_t* source_shape,
+                           const int64_t* source_strides, int elem_size, int64_t slot, int64_t row,
+                           int64_t length, void* stream);
+
+/* Replaces qwen3_tts_engine/continuous.py:124 SlotArena.move(),
+ * qwen3_tts_engine/codec_slots.py:328 CodecSlots.move() and
+ * qwen3_tts_engine/codec_code_buffer.py:29 CodecCodeBuffer.move().
+ * For every plane p: copy slot_elems contiguous elements from slot `source`
+ * to slot `destination` (strides in elements). No-op when source == destination. */
+int q3t_slot_move(void* base, int64_t planes, int64_t plane_stride, int64_t slot_stride,
+                  int64_t slot_elems, int elem_size, int64_t source, int64_t destination,
+                  void* stream);
+
+/* Replaces the capacity-doubling copy of qwen3_tts_engine/continuous.py:353-363
+ * ensure_capacity(): rows x row_bytes from src (pitch src_pitch bytes) to dst (pitch dst_pitch). */
+int q3t_copy_rows(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
+                  int64_t row_bytes, int64_t rows, void* stream);
+
+/* Replaces qwen3_tts_engine/codec_slots.py:313 CodecSlots.reset_range() /
+ * reset(): zero `count` slots starting at `start` in each plane. */
+int q3t_slot_zero(void* base, int64_t planes, int64_t plane_stride, int64_t slot_stride,
+                  int64_t slot_elems, int elem_size, int64_t start, int64_t count, void* stream);
+
+/* Per-tick counter update of continuous.py:628-629 (state.frames += 1,
+ * state.position += 1) on device-resident counters: values[i] += delta. */
+int q3t_advance(int64_t* values, int64_t count, int64_t delta, void* stream);
+
+/* ------------------------------------------------------------------ norms, rotary, activations */
+
+/* Replaces qwen3_tts_engine/operators.py:16 AscendRMSNorm.forward (both modes).
+ * x: [rows, width] (row stride x_stride), weight: [width], out: [rows, width] contiguous. */
+int q3t_rms_norm(const void* x, int64_t x_stride, const void* weight, void* out, int64_t rows,
+                 int64_t width, float eps, int mode, void* stream);
+
+/* Replaces torch_npu.npu_add_rms_norm at qwen3_tts_engine/fused_decoder.py:34.
+ * residual_out = bf16(a + h); normalized = rmsnorm(sum) * w. mode Q3T_NORM_NATIVE
+ * normalises the unrounded fp32 sum (npu semantics); Q3T_NORM_REFERENCE
+ * normalises the rounded residual with HF rounding. residual_out may alias h. */
+int q3t_add_rms_norm(const void* a, const void* h, const void* weight, void* normalized,
+                     void* residual_out, int64_t rows, int64_t width, float eps, int mode,
+                     void* stream);
+
+/* Replaces qwen3_tts_engine/rotary_triton_ascend.py:29 rotary(hidden, cos, sin):
+ * BSND bf16 [batch, length, heads, width], cos/sin [batch, length, width],
+ * bf16 rounding after every product and sum. */
+int q3t_rotary(const void* x, const void* cos, const void* sin, void* out, int64_t batch,
+               int64_t length, int64_t heads, int64_t width, void* stream);
+
+/* Replaces torch_npu.npu_swiglu / act_fn(gate) * up at qwen3_tts_engine/packed_mlp.py:20-26:
+ * packed [rows, 2*width] (gate | up) -> out [rows, width]. */
+int q3t_swiglu(const void* packed, void* out, int64_t rows, int64_t width, void* stream);
+
+/* Replaces qwen3_tts_engine/snake_triton_ascend.py:28 snake(hidden, alpha, inverse_beta):
+ * NCT [batch, channels, length], alpha/inverse_beta [channels] (fp32 or input dtype).
+ * dtype Q3T_BF16 rounds after every operation as the reference kernel does. */
+int q3t_snake(const void* x, const void* alpha, const void* inverse_beta, void* out,
+              int64_t batch, int64_t channels, int64_t length, int dtype, int coef_dtype,
+              void* stream);
+
+/* ------------------------------------------------------------------ dense projections */
+
+/* Replaces torch.nn.functional.linear at qwen3_tts_engine/packed_attention.py:42,85,
+ * qwen3_tts_engine/packed_mlp.py:20,27 and the codec head at continuous.py:613.
+ * out[r, n] = epilogue(sum_k x[r, k] * weight[n, k] (+ bias[n])). tcgen05 GEMM,
+ * weights as the 128-row UMMA operand, rows as N, split-K across SMs.
+ * x, weight, bias, residual: bf16; out: bf16 or fp32 (Q3T_EPI_STORE only).
+ * Alignment: base pointers 16 B, row strides multiples of 8 elements. */
+size_t q3t_linear_workspace_bytes(int64_t rows, int64_t in_features, int64_t out_features);
+int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t in_features,
+               const void* weight, int64_t out_features, const void* bias, void* out,
+               int64_t out_stride, int out_dtype, int epilogue, const void* residual,
+               int64_t residual_stride, void* workspace, size_t workspace_bytes, unsigned* status,
+               void* stream);
+
+/* ------------------------------------------------------------------ attention */
+
+/* Replaces the q_norm/k_norm, rotary and cache update of
+ * qwen3_tts_engine/packed_attention.py:42-74 (text-only rotary, decode and prefill rows).
+ * qkv: [rows, (q_heads + 2*kv_heads)*head_dim] bf16 (row stride qkv_stride);
+ * row r belongs to slot r / length and sequence offset r % length.
+ * cos/sin tables: [table_len, head_dim] bf16; rotary_positions[r] indexes them.
+ * cache_positions[r]: KV write position of row r in target [slots, kv_heads, capacity, head_dim].
+ * query_out: [rows, q_heads, head_dim]. */
+int q3t_qk_norm_rope_kv(const void* qkv, int64_t qkv_stride, const void* q_norm_weight,
+                        const void* k_norm_weight, float eps, const void* cos_table,
+                        const void* sin_table, int64_t table_len, const int64_t* rotary_positions,
+                        const int64_t* cache_positions, void* query_out, void* target_keys,
+                        void* target_values, int64_t rows, int64_t length, int64_t q_heads,
+                        int64_t kv_heads, int64_t head_dim, int64_t capacity, unsigned* status,
+                        void* stream);
+
+/* Replaces torch_npu.npu_fused_infer_attention_score at qwen3_tts_engine/npu_attention.py:21
+ * (and SDPA over SlotCache, continuous.py:188-198) for one query token per slot:
+ * query [batch, q_heads, head_dim] bf16, keys/values [slots, kv_heads, capacity, head_dim]
+ * bf16 contiguous (slot b serves row b), positions int64 [batch]: keys 0..positions[b]
+ * are visible. context bounds the grid (positions[b] < context <= capacity).
+ * out [batch, q_heads, head_dim] bf16. Split-KV with an in-kernel combine. */
+size_t q3t_decode_attention_workspace_bytes(int64_t batch, int64_t q_heads, int64_t head_dim,
+                                            int64_t context);
+int q3t_decode_attention(const void* query, const void* keys, const void* values,
+                         const int64_t* positions, void* out, int64_t batch, int64_t q_heads,
+                         int64_t kv_heads, int64_t head_dim, int64_t capacity, int64_t context,
+                         float scale, void* workspace, size_t workspace_bytes, unsigned* status,
+                         void* stream);
+
+/* ------------------------------------------------------------------ sampling */
+
+/* Replaces qwen3_tts_engine/cdf_triton_ascend.py:20 select(cdf, uniforms):
+ * token[r] = #{ j : cdf[r, j] / cdf[r, width-1] <= u[r] } with IEEE division. */
+int q3t_cdf_select(const float* cdf, const float* uniforms, int64_t* tokens, int64_t rows,
+                   int64_t width, void* stream);
+
+/* Replaces qwen3_tts_engine/sampling.py:5 categorical(), the semantic
+ * preprocessing of qwen3_tts_engine/continuous.py:365-370 and the seen update of
+ * qwen3_tts_engine/sampling_graph.py:14-16, in one kernel per row:
+ *   scores = float(logits)                         (bf16 or fp32 logits)
+ *   if seen:    scores = seen ? (s < 0 ? s*penalty : s/penalty) : s
+ *   if allowed: scores[~allowed] = -inf
+ *   if steps:   scores[eos] = -inf where steps[r] < min_steps
+ *   scores /= temperature; keep scores >= k-th largest (ties kept);
+ *   softmax; optional top-p (smallest set with mass >= top_p; 1.0 disables);
+ *   cdf = cumsum; token = #{ cdf / cdf[-1] <= u }.
+ * u: uniforms[r * uniform_stride] when uniforms != NULL, else Philox4x32-10
+ *    (key = seed, counter = {philox_offsets[r] lo, hi, r, 0}) mapped to [0, 1).
+ * seen_out (nullable, may alias seen): seen row copied, then seen_out[r, token] = 1. */
+int q3t_sample(const void* logits, int logits_dtype, int64_t logits_stride, const uint8_t* seen,
+               int64_t seen_stride, const uint8_t* allowed, const int64_t* steps, int64_t eos,
+               int64_t min_steps, float penalty, float temperature, int64_t top_k, float top_p,
+               const float* uniforms, int64_t uniform_stride, uint64_t seed,
+               const int64_t* philox_offsets, int64_t* tokens, int64_t token_stride,
+               uint8_t* seen_out, int64_t seen_out_stride, int64_t rows, int64_t width,
+               void* stream);
+
+/* Philox4x32-10 uniforms in [0, 1): out[i] = u(key=seed, counter={offset + i/4 lo, hi, 0, 0})[i%4]. */
+int q3t_philox_uniforms(uint64_t seed, uint64_t offset, float* out, int64_t count, void* stream);
+
+/* ------------------------------------------------------------------ embeddings */
+
+/* Replaces the frame embedding of qwen3_tts_engine/continuous.py:584-601
+ * (talker codec embedding of codes[:, 0] plus the 15 predictor embeddings of
+ * codes[:, 1..15], summed in fp32 and rounded once, then + text):
+ * codes int64 [batch, 1 + groups] (row stride codes_stride);
+ * first_table [first_vocab, hidden]; group_tables [groups, group_vocab, hidden];
+ * text [batch, hidden] (row stride text_stride, nullable); out [batch, hidden] bf16. */
+int q3t_frame_embed(const int64_t* codes, int64_t codes_stride, const void* first_table,
+                    int64_t first_vocab, const void* group_tables, int64_t groups,
+                    int64_t group_vocab, const void* text, int64_t text_stride, void* out,
+                    int64_t batch, int64_t hidden, unsigned* status, void* stream);
+
+/* Row gather out[r] = table[ids[r]] (embedding lookup, bf16 rows of `hidden`). */
+int q3t_embedding(const int64_t* ids, int64_t ids_stride, const void* table, int64_t vocab,
+                  void* out, int64_t out_stride, int64_t rows, int64_t hidden, unsigned* status,
+                  void* stream);
+
+/* ------------------------------------------------------------------ codec state */
+
+/* Replaces qwen3_tts_engine/codec_row_scatter.py:48 scatter_rows(target, indices, source):
+ * target contiguous [slots, ...]; source [n, ...] with element strides (ndim 1..4);
+ * target[indices[i]] = source[i]. Out-of-range indices are skipped (status bit 3). */
+int q3t_scatter_rows(void* target, int64_t target_rows, const int64_t* indices,
+                     const void* source, int ndim, const int64_t* source_shape,
+                     const int64_t* source_strides, int elem_size, unsigned* status,
+                     void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* Q3T_H */

@@ -1,0 +1,148 @@
+"""Qwen3-style decoder (talker and code predictor) restated on the CPU.
+
+The layer is the one the reference drives through HF modules and replaces
+piecewise: RMSNorm (operators.py:16-23), packed QKV projection, per-head
+q_norm/k_norm, rotate-half RoPE, cache update and GQA attention
+(packed_attention.py:42-85), residual add, post-attention RMSNorm, SwiGLU MLP
+(packed_mlp.py:19-27), final norm and LM head (continuous.py:188-198, 613).
+Layer internals belong to qwen-tts==0.1.1 (absent here), so they are restated
+from those call sites: this part of the oracle is unpinned.
+
+Two precisions:
+  mode="fp32"  every op in fp32 from the bf16 weights (the parity truth);
+  mode="bf16"  fp32 math with bf16 rounding at each point the reference's
+               bf16 tensors round (linear outputs, norms, RoPE ops, residuals).
+"""
+from __future__ import annotations
+
+import torch
+
+from .elementwise import bf, rope_tables
+from .sampling import categorical
+
+
+def _r(x, mode):
+    return bf(x) if mode == "bf16" else x
+
+
+def _rms(x, w, eps, mode):
+    r = 1.0 / torch.sqrt(x.pow(2).mean(-1, keepdim=True) + eps)
+    if mode == "bf16":
+        return bf(w.float() * bf(x * r))
+    return w.float() * (x * r)
+
+
+def _rope(x, cos, sin, mode):
+    half = x.shape[-1] // 2
+    rot = torch.cat([-x[..., half:], x[..., :half]], dim=-1)
+    if mode == "bf16":
+        return bf(bf(x * cos) + bf(rot * sin))
+    return x * cos + rot * sin
+
+
+class Tables:
+    """RoPE cos/sin tables (bf16-rounded as the model's bf16 rotary embedding returns them)."""
+
+    def __init__(self, positions: int, dim: int, theta: float):
+        cos, sin = rope_tables(positions, dim, theta)
+        self.cos = bf(cos)
+        self.sin = bf(sin)
+
+
+def layer_forward(cfg, w, h, rot_pos, cache_k, cache_v, cache_pos, tables, mode):
+    """One decoder layer. h [B, L, H] fp32; rot_pos/cache_pos [B, L] int64;
+    cache_k/cache_v [B, Hkv, cap, D] fp32 (written in place). Query (b, t)
+    attends to cache positions 0..cache_pos[b, t]."""
+    B, L, H = h.shape
+    D, Hq, Hkv = cfg.head_dim, cfg.q_heads, cfg.kv_heads
+    x = _rms(h, w["input_norm"], cfg.eps, mode)
+    q = _r(x @ w["q"].float().T, mode).view(B, L, Hq, D)
+    k = _r(x @ w["k"].float().T, mode).view(B, L, Hkv, D)
+    v = _r(x @ w["v"].float().T, mode).view(B, L, Hkv, D)
+    q = _rms(q, w["q_norm"], cfg.eps, mode)
+    k = _rms(k, w["k_norm"], cfg.eps, mode)
+    cos = tables.cos[rot_pos][:, :, None, :]
+    sin = tables.sin[rot_pos][:, :, None, :]
+    q = _rope(q, cos, sin, mode)
+    k = _rope(k, cos, sin, mode)
+    for b in range(B):
+        for t in range(L):
+            p = int(cache_pos[b, t])
+            cache_k[b, :, p] = k[b, t]
+            cache_v[b, :, p] = v[b, t]
+    group = Hq // Hkv
+    attn = torch.empty(B, L, Hq, D)
+    for b in range(B):
+        for t in range(L):
+            n = int(cache_pos[b, t]) + 1
+            kk = cache_k[b, :, :n].repeat_interleave(group, 0)
+            vv = cache_v[b, :, :n].repeat_interleave(group, 0)
+            s = torch.einsum("hd,hnd->hn", q[b, t], kk) * (D ** -0.5)
+            attn[b, t] = torch.einsum("hn,hnd->hd", torch.softmax(s, -1), vv)
+    attn = _r(attn, mode).reshape(B, L, Hq * D)
+    h = _r(h + _r(attn @ w["o"].float().T, mode), mode)
+    x = _rms(h, w["post_norm"], cfg.eps, mode)
+    gate = _r(x @ w["gate"].float().T, mode)
+    up = _r(x @ w["up"].float().T, mode)
+    act = _r(_r(torch.nn.functional.silu(gate), mode) * up, mode)
+    h = _r(h + _r(act @ w["down"].float().T, mode), mode)
+    return h
+
+
+def decoder_forward(cfg, weights, h, rot_pos, cache, cache_pos, tables, mode="fp32"):
+    """All layers then the final norm. cache: list of (K, V) per layer."""
+    h = h.float()
+    for w, (ck, cv) in zip(weights["layers"], cache):
+        h = layer_forward(cfg, w, h, rot_pos, ck, cv, cache_pos, tables, mode)
+    return _rms(h, weights["norm"], cfg.eps, mode)
+
+
+def new_cache(cfg, batch, capacity):
+    return [(torch.zeros(batch, cfg.kv_heads, capacity, cfg.head_dim),
+             torch.zeros(batch, cfg.kv_heads, capacity, cfg.head_dim)) for _ in range(cfg.layers)]
+
+
+def talker_decode_step(cfg, weights, embeds, positions, rope_deltas, cache, tables, mode="fp32"):
+    """SlotGraph.compute + codec_head (continuous.py:188-198, 612-613).
+
+    embeds [B, H]; positions [B] (KV write position); rotary = position + rope_delta.
+    Returns (hidden [B, H], logits [B, vocab])."""
+    pos = positions.view(-1, 1).long()
+    rot = (positions + rope_deltas).view(-1, 1).long()
+    hidden = decoder_forward(cfg, weights, embeds.view(embeds.shape[0], 1, -1), rot, cache, pos, tables, mode)
+    logits = _r(hidden @ weights["head"].float().T, mode)
+    return hidden[:, 0], logits[:, 0]
+
+
+def predictor_frame(cfg, weights, hidden, first, draws, tables, mode="fp32", *, temperature=0.9, top_k=50,
+                    top_p=1.0, uniforms_fn=None):
+    """The 15-codebook loop of UniformPredictor.run (continuous.py:49-68).
+
+    hidden/first [B, talker_hidden]; draws [B, 16] (column step+1 feeds step).
+    Step 0 runs (hidden, first) at positions [0, 1]; step i runs the embedding
+    of the previous code (codebook i-1 table) at position i+1; head i samples
+    code i+1. Returns (subcodes [B, 15], summed embeddings [B, talker_hidden]).
+    """
+    B = hidden.shape[0]
+    cache = new_cache(cfg, B, cfg.groups + 1)
+    inputs = torch.stack([hidden, first], dim=1).float()
+    codes = []
+    token = None
+    for step in range(cfg.groups):
+        if step == 0:
+            x = inputs
+            pos = torch.tensor([[0, 1]]).expand(B, 2)
+        else:
+            x = weights["embeddings"][step - 1][token[:, 0]].float()[:, None, :]
+            pos = torch.full((B, 1), step + 1)
+        x = _r(x @ weights["proj"].float().T + weights["proj_bias"].float(), mode)
+        out = decoder_forward(cfg, weights, x, pos, cache, pos, tables, mode)
+        logits = _r(out[:, -1] @ weights["heads"][step].float().T, mode)
+        u = draws[:, step + 1] if uniforms_fn is None else uniforms_fn(step)
+        token = categorical(logits, u, temperature=temperature, top_k=top_k, top_p=top_p)
+        codes.append(token)
+    subcodes = torch.cat(codes, dim=-1)
+    acc = first.float()
+    for i in range(cfg.groups):
+        acc = acc + weights["embeddings"][i][subcodes[:, i]].float()
+    return subcodes, acc

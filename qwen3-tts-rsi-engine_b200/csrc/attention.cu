@@ -1,0 +1,365 @@
+// Ragged GQA decode attention over the slot-table KV arena.
+//
+// One query token per slot attends to keys 0..positions[b] of its own slot
+// (continuous.py:188-198 mask `indices <= positions`). The KV of one
+// (slot, kv_head) pair is contiguous ([slots, kv_heads, capacity, head_dim]),
+// so each CTA streams a chunk of keys with untiled bulk copies
+// (cp.async.bulk, mbarrier completion) into a two-slot shared-memory ring.
+// Grid = (chunks, kv_heads, batch); all G = q_heads/kv_heads query heads of a
+// kv head share every K/V tile. Inside a CTA each warp owns 32/G keys of a
+// tile: lanes hold 4 (D=128) or 2 (D=64) dims, partial q.k products are
+// combined with a 31-shuffle transpose reduction so lane l ends with the score
+// of (key l/G, head l%G); softmax is online (base-2 exponent, q pre-scaled by
+// scale*log2(e)). Chunks of a slot combine through fp32 partials and an
+// atomic ticket: the last chunk CTA merges them in chunk order.
+#include "common.cuh"
+#include "host.cuh"
+
+using namespace q3t;
+
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int D, int G>
+struct AttnCfg {
+  static constexpr int kDL = D / 32;           // dims per lane
+  static constexpr int kKW = 32 / G;           // keys per warp per tile
+  static constexpr int kTK = 4 * kKW;          // keys per tile
+  static constexpr int kTileBytes = kTK * D * 2;
+  static constexpr int kSmem = 2 * 2 * kTileBytes + 1024;
+  static constexpr int kPart = G * (D + 2);    // floats per chunk partial
+};
+
+// After the call lane l holds the warp-wide sum of v[l].
+Q3T_DEV float transpose_reduce32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int w = 16; w >= 1; w >>= 1) {
+    const bool up = (lane & w) != 0;
+#pragma unroll
+    for (int i = 0; i < w; ++i) {
+      const float send = up ? v[i] : v[i + w];
+      const float keep = up ? v[i + w] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+    }
+  }
+  return v[0];
+}
+
+template <int D, int G>
+__global__ void __launch_bounds__(128)
+    decode_attention_kernel(const __nv_bfloat16* __restrict__ query, const __nv_bfloat16* __restrict__ keys,
+                            const __nv_bfloat16* __restrict__ values, const int64_t* __restrict__ positions,
+                            __nv_bfloat16* __restrict__ out, int kv_heads, int64_t capacity, int64_t context,
+                            int chunk, float qscale, float* __restrict__ partials, unsigned* __restrict__ counters,
+                            int max_chunks, unsigned* status) {
+  using C = AttnCfg<D, G>;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  __nv_bfloat16* kt[2] = {reinterpret_cast<__nv_bfloat16*>(smem),
+                          reinterpret_cast<__nv_bfloat16*>(smem + C::kTileBytes)};
+  __nv_bfloat16* vt[2] = {reinterpret_cast<__nv_bfloat16*>(smem + 2 * C::kTileBytes),
+                          reinterpret_cast<__nv_bfloat16*>(smem + 3 * C::kTileBytes)};
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ float pbuf[4][32];
+  __shared__ float wm[4][G], wl[4][G];
+  __shared__ float wo[4][G][D];
+  __shared__ int last_flag;
+  __shared__ int tile_ok;
+
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  grid_dependency_launch();
+  grid_dependency_wait();
+
+  int64_t pos = positions[b];
+  if (pos < 0 || pos >= context) {
+    if (c == 0 && h == 0 && threadIdx.x == 0) raise_status(status, kStatusBadIndex);
+    pos = pos < 0 ? 0 : context - 1;
+  }
+  const int64_t nkeys = pos + 1;
+  const int active = int((nkeys + chunk - 1) / chunk);
+  if (c >= active) return;
+  const int64_t k_begin = int64_t(c) * chunk;
+  const int64_t k_end = (k_begin + chunk) < nkeys ? (k_begin + chunk) : nkeys;
+  const int ntiles = int((k_end - k_begin + C::kTK - 1) / C::kTK);
+  const size_t head_base = (size_t(b) * kv_heads + h) * size_t(capacity) * D;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int t) {
+    const int64_t t0 = k_begin + int64_t(t) * C::kTK;
+    const int64_t n = (k_end - t0) < C::kTK ? (k_end - t0) : C::kTK;
+    const uint32_t bytes = uint32_t(n) * D * 2;
+    uint64_t* bar = &bars[t & 1];
+    mbar_expect_tx(bar, 2 * bytes);
+    bulk_load(kt[t & 1], keys + head_base + size_t(t0) * D, bytes, bar);
+    bulk_load(vt[t & 1], values + head_base + size_t(t0) * D, bytes, bar);
+  };
+  if (threadIdx.x == 0) {
+    issue(0);
+    if (ntiles > 1) issue(1);
+  }
+
+  // q for the G heads of this kv head, this lane's dims, pre-scaled.
+  float q[G][C::kDL];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const __nv_bfloat16* qp = query + (size_t(b) * kv_heads * G + size_t(h) * G + g) * D + lane * C::kDL;
+#pragma unroll
+    for (int d = 0; d < C::kDL; ++d) q[g][d] = __bfloat162float(qp[d]) * qscale;
+  }
+  float m_run[G], l_run[G], o[G][C::kDL];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m_run[g] = -INFINITY;
+    l_run[g] = 0.f;
+#pragma unroll
+    for (int d = 0; d < C::kDL; ++d) o[g][d] = 0.f;
+  }
+
+  int failed_tile = -1;
+  for (int t = 0; t < ntiles; ++t) {
+    // One thread waits with a time bound; the verdict is made uniform before
+    // anyone proceeds, then every thread observes the completed phase.
+    if (threadIdx.x == 0) tile_ok = mbar_wait(&bars[t & 1], (t >> 1) & 1, status, kStatusTmaTimeout) ? 1 : 0;
+    __syncthreads();
+    if (!tile_ok) {
+      failed_tile = t;
+      break;
+    }
+    mbar_wait(&bars[t & 1], (t >> 1) & 1, status, kStatusTmaTimeout);
+    const int64_t t0 = k_begin + int64_t(t) * C::kTK;
+    const __nv_bfloat16* ks = kt[t & 1] + warp * C::kKW * D + lane * C::kDL;
+    const __nv_bfloat16* vs = vt[t & 1] + warp * C::kKW * D + lane * C::kDL;
+    const int64_t wkey0 = t0 + warp * C::kKW;
+
+    float part[32];
+#pragma unroll
+    for (int kl = 0; kl < C::kKW; ++kl) {
+      float kf[C::kDL];
+      if constexpr (C::kDL == 4) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(ks + kl * D);
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+        const float2 bb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+        kf[0] = a.x; kf[1] = a.y; kf[2] = bb.x; kf[3] = bb.y;
+      } else {
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ks + kl * D));
+        kf[0] = a.x; kf[1] = a.y;
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float acc = 0.f;
+#pragma unroll
+        for (int d = 0; d < C::kDL; ++d) acc = fmaf(q[g][d], kf[d], acc);
+        part[kl * G + g] = acc;
+      }
+    }
+    float s = transpose_reduce32(part, lane);
+    if (wkey0 + lane / G >= k_end) s = -INFINITY;
+    // per-head tile max and running max
+    float tmax = s;
+#pragma unroll
+    for (int off = 16; off >= G; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+    float alpha[G], mnew[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float mt = __shfl_sync(0xffffffffu, tmax, g);
+      mnew[g] = fmaxf(m_run[g], mt);
+      alpha[g] = mnew[g] == -INFINITY ? 1.f : exp2f(m_run[g] - mnew[g]);
+    }
+    const float mine = (G == 1 || (lane & 1) == 0) ? mnew[0] : mnew[G - 1];
+    const float p = (s == -INFINITY) ? 0.f : exp2f(s - mine);
+    float psum = p;
+#pragma unroll
+    for (int off = 16; off >= G; off >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float ls = __shfl_sync(0xffffffffu, psum, g);
+      l_run[g] = l_run[g] * alpha[g] + ls;
+      m_run[g] = mnew[g];
+#pragma unroll
+      for (int d = 0; d < C::kDL; ++d) o[g][d] *= alpha[g];
+    }
+    pbuf[warp][lane] = p;
+    __syncwarp();
+    // Keys past the chunk end hold stale shared memory: never touch them.
+    const int nvalid = int((k_end - wkey0) < 0 ? 0 : ((k_end - wkey0) > C::kKW ? C::kKW : (k_end - wkey0)));
+#pragma unroll 4
+    for (int kl = 0; kl < nvalid; ++kl) {
+      float vf[C::kDL];
+      if constexpr (C::kDL == 4) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(vs + kl * D);
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+        const float2 bb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+        vf[0] = a.x; vf[1] = a.y; vf[2] = bb.x; vf[3] = bb.y;
+      } else {
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(vs + kl * D));
+        vf[0] = a.x; vf[1] = a.y;
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float pg = pbuf[warp][kl * G + g];
+#pragma unroll
+        for (int d = 0; d < C::kDL; ++d) o[g][d] = fmaf(pg, vf[d], o[g][d]);
+      }
+    }
+    __syncwarp();
+    __syncthreads();  // every warp is done with ring slot t&1
+    if (threadIdx.x == 0 && t + 2 < ntiles) issue(t + 2);
+  }
+  if (failed_tile >= 0) {
+    // Failure path: wait (bounded) for this CTA's copies still in flight
+    // (the failed tile and the one prefetched behind it).
+    if (threadIdx.x == 0)
+      for (int t = failed_tile; t < ntiles && t < failed_tile + 2; ++t)
+        mbar_wait(&bars[t & 1], (t >> 1) & 1, status, kStatusTmaTimeout);
+    return;
+  }
+
+  // ---- merge the four warps
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    if (lane == 0) {
+      wm[warp][g] = m_run[g];
+      wl[warp][g] = l_run[g];
+    }
+#pragma unroll
+    for (int d = 0; d < C::kDL; ++d) wo[warp][g][lane * C::kDL + d] = o[g][d];
+  }
+  __syncthreads();
+  float* part = partials + ((size_t(b) * kv_heads + h) * max_chunks + c) * C::kPart;
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int g = e / D, d = e % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w][g]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float f = wm[w][g] == -INFINITY ? 0.f : exp2f(wm[w][g] - M);
+      L += wl[w][g] * f;
+      O += wo[w][g][d] * f;
+    }
+    if (active == 1) {
+      out[(size_t(b) * kv_heads * G + size_t(h) * G + g) * D + d] = __float2bfloat16_rn(O / L);
+    } else {
+      part[g * (D + 2) + 2 + d] = O;
+      if (d == 0) {
+        part[g * (D + 2)] = M;
+        part[g * (D + 2) + 1] = L;
+      }
+    }
+  }
+  if (active == 1) return;
+
+  // ---- chunk combine: last CTA of this (slot, kv head) merges in chunk order
+  __threadfence();
+  __syncthreads();
+  unsigned* counter = counters + size_t(b) * kv_heads + h;
+  if (threadIdx.x == 0) last_flag = (atomicAdd(counter, 1u) == unsigned(active - 1));
+  __syncthreads();
+  if (!last_flag) return;
+  __threadfence();
+  const float* base = partials + (size_t(b) * kv_heads + h) * max_chunks * C::kPart;
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int g = e / D, d = e % D;
+    float M = -INFINITY;
+    for (int cc = 0; cc < active; ++cc) M = fmaxf(M, __ldcg(base + cc * C::kPart + g * (D + 2)));
+    float L = 0.f, O = 0.f;
+    for (int cc = 0; cc < active; ++cc) {
+      const float* pc = base + cc * C::kPart + g * (D + 2);
+      const float mc = __ldcg(pc);
+      const float f = mc == -INFINITY ? 0.f : exp2f(mc - M);
+      L += __ldcg(pc + 1) * f;
+      O += __ldcg(pc + 2 + d) * f;
+    }
+    out[(size_t(b) * kv_heads * G + size_t(h) * G + g) * D + d] = __float2bfloat16_rn(O / L);
+  }
+  if (threadIdx.x == 0) *counter = 0u;
+}
+
+int pick_chunk(int64_t batch, int64_t kv_heads, int64_t context) {
+  // Enough CTAs to cover every SM a few times at the bucket's full context.
+  const int64_t target = 4LL * sm_count();
+  int chunk = 512;
+  while (chunk > 64 && batch * kv_heads * ((context + chunk - 1) / chunk) < target) chunk >>= 1;
+  return chunk;
+}
+
+template <int D, int G>
+int launch_attn(const void* q, const void* k, const void* v, const int64_t* pos, void* out, int64_t batch,
+                int64_t kv_heads, int64_t capacity, int64_t context, float scale, void* ws, unsigned* status,
+                void* stream) {
+  using C = AttnCfg<D, G>;
+  const int chunk = pick_chunk(batch, kv_heads, context);
+  const int max_chunks = int((context + chunk - 1) / chunk);
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(decode_attention_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
+        cudaSuccess)
+      return check_cuda("attention: set smem");
+    configured[dev] = true;
+  }
+  unsigned* counters = static_cast<unsigned*>(ws);
+  const size_t cbytes = ((size_t(batch) * kv_heads * sizeof(unsigned) + 255) / 256) * 256;
+  float* partials = reinterpret_cast<float*>(static_cast<char*>(ws) + cbytes);
+  return launch(decode_attention_kernel<D, G>, dim3(max_chunks, unsigned(kv_heads), unsigned(batch)), dim3(128),
+                size_t(C::kSmem), stream, true, "decode_attention", static_cast<const __nv_bfloat16*>(q),
+                static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), pos,
+                static_cast<__nv_bfloat16*>(out), int(kv_heads), capacity, context, chunk, scale * kLog2e, partials,
+                counters, max_chunks, status);
+}
+
+size_t attn_workspace(int64_t batch, int64_t q_heads, int64_t kv_heads_unused, int64_t head_dim, int64_t context) {
+  (void)kv_heads_unused;
+  // worst case over G: partial floats per (b, kv head, chunk) = G*(D+2); bound with q_heads*(D+2) per (b, chunk)
+  const int chunk = 64;
+  const int64_t max_chunks = (context + chunk - 1) / chunk;
+  const size_t cbytes = ((size_t(batch) * q_heads * sizeof(unsigned) + 255) / 256) * 256;
+  return cbytes + size_t(batch) * max_chunks * q_heads * (head_dim + 2) * sizeof(float);
+}
+
+}  // namespace
+
+extern "C" size_t q3t_decode_attention_workspace_bytes(int64_t batch, int64_t q_heads, int64_t head_dim,
+                                                       int64_t context) {
+  if (batch < 1 || q_heads < 1 || head_dim < 1 || context < 1) return 0;
+  return attn_workspace(batch, q_heads, 0, head_dim, context);
+}
+
+extern "C" int q3t_decode_attention(const void* query, const void* keys, const void* values, const int64_t* positions,
+                                    void* out, int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                    int64_t capacity, int64_t context, float scale, void* workspace,
+                                    size_t workspace_bytes, unsigned* status, void* stream) {
+  if (!query || !keys || !values || !positions || !out) return fail(Q3T_EINVAL, "attention: null pointer");
+  if (batch < 1 || batch > 65535 || kv_heads < 1 || kv_heads > 65535 || q_heads % kv_heads)
+    return fail(Q3T_EINVAL, "attention: invalid head geometry");
+  if (context < 1 || context > capacity) return fail(Q3T_EINVAL, "Attention context must fit the KV arena");
+  if (!aligned16(keys) || !aligned16(values) || !aligned16(query))
+    return fail(Q3T_EINVAL, "attention: 16-byte alignment");
+  const int64_t g = q_heads / kv_heads;
+  const size_t need = attn_workspace(batch, q_heads, kv_heads, head_dim, context);
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
+    return fail(Q3T_ESPACE, "attention: workspace needs %zu bytes", need);
+  if (head_dim == 128 && g == 2)
+    return launch_attn<128, 2>(query, keys, values, positions, out, batch, kv_heads, capacity, context, scale,
+                               workspace, status, stream);
+  if (head_dim == 128 && g == 1)
+    return launch_attn<128, 1>(query, keys, values, positions, out, batch, kv_heads, capacity, context, scale,
+                               workspace, status, stream);
+  if (head_dim == 64 && g == 1)
+    return launch_attn<64, 1>(query, keys, values, positions, out, batch, kv_heads, capacity, context, scale,
+                              workspace, status, stream);
+  if (head_dim == 64 && g == 2)
+    return launch_attn<64, 2>(query, keys, values, positions, out, batch, kv_heads, capacity, context, scale,
+                              workspace, status, stream);
+  return fail(Q3T_EUNSUPPORTED, "attention: head_dim %lld with %lld query heads per kv head", (long long)head_dim,
+              (long long)g);
+}

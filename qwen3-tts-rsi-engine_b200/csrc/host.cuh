@@ -1,0 +1,49 @@
+// Host-side helpers shared by the entry points: error strings, launch
+// accounting and a launcher that sets the programmatic-dependent-launch
+// attribute so a kernel may start while its predecessor drains.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+
+#include "q3t.h"
+
+namespace q3t {
+
+// Records a printf-style message for q3t_last_error() and returns `code`.
+int fail(int code, const char* fmt, ...);
+// Converts the last CUDA error (if any) into Q3T_ECUDA.
+int check_cuda(const char* what);
+// Counts kernel launches issued by this library.
+void note_launch();
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Launch `kernel` with optional programmatic stream serialization (PDL).
+template <typename... KArgs, typename... Args>
+int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, void* stream, bool pdl,
+           const char* name, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[1];
+  if (pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  if (err != cudaSuccess) return fail(Q3T_ECUDA, "%s launch failed: %s", name, cudaGetErrorString(err));
+  note_launch();
+  return Q3T_OK;
+}
+
+}  // namespace q3t

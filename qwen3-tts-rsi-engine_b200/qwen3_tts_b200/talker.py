@@ -1,0 +1,215 @@
+"""Talker decode step on the slot-table KV arena, captured as CUDA graphs.
+
+Mirrors ``SlotArena`` / ``SlotGraph`` of the reference (continuous.py:97-229):
+one KV arena holds every slot's keys and values, a decode step runs the whole
+28-layer stack for a bucket of slots, and one CUDA graph is captured per
+(batch bucket, context bucket) with static input buffers, so any slot
+assignment replays the same graph (positions live in device buffers).
+
+Per layer the step launches eight kernels, all from ``libq3t_b200.so``:
+RMSNorm -> QKV GEMM -> q/k norm + RoPE + KV write -> ragged GQA attention ->
+O GEMM (+ residual) -> RMSNorm -> gate/up GEMM (+ SwiGLU) -> down GEMM
+(+ residual); then the final norm and the LM head (fp32 logits).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib, ops
+from .config import DecoderConfig
+from .weights import pack_decoder
+
+BF16 = torch.bfloat16
+
+
+def rope_tables(positions: int, dim: int, theta: float, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """Default RoPE cos/sin [positions, dim] in bf16 (fp32 angles, duplicated halves)."""
+    inv_freq = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.int64).float() / dim))
+    freqs = torch.arange(positions, dtype=torch.float32)[:, None] * inv_freq[None, :]
+    emb = torch.cat([freqs, freqs], dim=-1)
+    return emb.cos().to(BF16).to(device), emb.sin().to(BF16).to(device)
+
+
+class SlotArena:
+    """Per-layer K/V for every slot in one packed allocation [2L, slots, kv_heads, capacity, head_dim].
+
+    ``keys[i]`` / ``values[i]`` are views of layer i (continuous.py:97-116 with packed_kv).
+    """
+
+    def __init__(self, cfg: DecoderConfig, slots: int, capacity: int, device):
+        self.cfg = cfg
+        self.slots = slots
+        self.capacity = capacity
+        self.device = torch.device(device)
+        self.packed = torch.zeros((cfg.layers * 2, slots, cfg.kv_heads, capacity, cfg.head_dim), dtype=BF16,
+                                  device=self.device)
+        self.keys = list(self.packed[:cfg.layers].unbind(0))
+        self.values = list(self.packed[cfg.layers:].unbind(0))
+
+    def load_packed(self, slot: int, source: torch.Tensor, row: int = 0, length=None) -> None:
+        """Copy one prefilled request prefix [2L, rows, kv, len, D] into `slot` (packed_kv.py:6)."""
+        ops.copy_packed_prefix(self.packed, source, slot, row=row, length=length)
+
+    def load(self, slot: int, keys: list, values: list, row: int = 0, length=None) -> None:
+        """Per-layer prefix copy from [rows, kv, len, D] caches (continuous.py:118-122)."""
+        source = torch.stack(list(keys) + list(values))
+        self.load_packed(slot, source, row=row, length=length)
+
+    def move(self, source: int, destination: int) -> None:
+        """Slot compaction: copy `source` over `destination` in every layer (continuous.py:124-128)."""
+        if source != destination:
+            ops.slot_move(self.packed, source, destination, dim=1)
+
+    def grown(self, capacity: int) -> "SlotArena":
+        """A new arena of larger capacity holding this arena's contents (continuous.py:353-363)."""
+        arena = SlotArena(self.cfg, self.slots, capacity, self.device)
+        ops.copy_prefix_along(arena.packed, self.packed, dim=3)
+        return arena
+
+
+class TalkerStep:
+    """Static-buffer decode step for `batch` slots attending over `context` keys."""
+
+    def __init__(self, cfg: DecoderConfig, weights: dict, arena: SlotArena, batch: int, context: int, cos, sin,
+                 norm_mode: int = _lib.NORM_REFERENCE):
+        if not 1 <= context <= arena.capacity:
+            raise ValueError("Attention context must fit the KV arena")
+        if batch > arena.slots:
+            raise ValueError("Decode batch exceeds the slot arena")
+        self.cfg, self.w, self.arena = cfg, weights, arena
+        self.batch, self.context = batch, context
+        self.cos, self.sin = cos, sin
+        self.norm_mode = norm_mode
+        dev = arena.device
+        B, H = batch, cfg.hidden
+        self.inputs = torch.zeros(B, H, dtype=BF16, device=dev)
+        self.positions = torch.zeros(B, dtype=torch.long, device=dev)
+        self.rotary = torch.zeros(B, dtype=torch.long, device=dev)
+        self.h = torch.zeros(B, H, dtype=BF16, device=dev)
+        self.xn = torch.zeros(B, H, dtype=BF16, device=dev)
+        self.qkv = torch.zeros(B, cfg.qkv_width, dtype=BF16, device=dev)
+        self.q = torch.zeros(B, cfg.q_heads, cfg.head_dim, dtype=BF16, device=dev)
+        self.attn = torch.zeros(B, cfg.q_heads, cfg.head_dim, dtype=BF16, device=dev)
+        self.act = torch.zeros(B, cfg.ffn, dtype=BF16, device=dev)
+        self.hidden = torch.zeros(B, H, dtype=BF16, device=dev)
+        self.logits = torch.zeros(B, cfg.vocab, dtype=torch.float32, device=dev)
+        gemms = [(H, cfg.qkv_width), (cfg.q_width, H), (H, 2 * cfg.ffn), (cfg.ffn, H), (H, cfg.vocab)]
+        need = max(ops.linear_workspace_bytes(B, k, n) for k, n in gemms)
+        self.ws_linear = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
+        need = ops.decode_attention_workspace_bytes(B, cfg.q_heads, cfg.head_dim, context)
+        self.ws_attn = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
+        self.status = ops.status_word(dev)
+        self.graph = None
+        self.output = (self.hidden, self.logits)
+
+    # ---------------------------------------------------------------- one eager pass
+    def compute(self) -> None:
+        cfg, w, B = self.cfg, self.w, self.batch
+        lw = ops.linear
+        res_in = self.inputs
+        for i, layer in enumerate(w["layers"]):
+            ops.rms_norm(res_in, layer.input_norm, cfg.eps, self.norm_mode, out=self.xn)
+            lw(self.xn, layer.qkv, out=self.qkv, workspace=self.ws_linear)
+            ops.qk_norm_rope_kv(self.qkv, layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin, self.rotary,
+                                self.positions, self.arena.keys[i], self.arena.values[i], q_heads=cfg.q_heads,
+                                kv_heads=cfg.kv_heads, head_dim=cfg.head_dim, query_out=self.q)
+            ops.decode_attention(self.q, self.arena.keys[i], self.arena.values[i], self.positions,
+                                 context=self.context, out=self.attn, workspace=self.ws_attn)
+            lw(self.attn.view(B, cfg.q_width), layer.o, out=self.h, epilogue=_lib.EPI_RESIDUAL, residual=res_in,
+               workspace=self.ws_linear)
+            ops.rms_norm(self.h, layer.post_norm, cfg.eps, self.norm_mode, out=self.xn)
+            lw(self.xn, layer.gate_up, out=self.act, epilogue=_lib.EPI_SWIGLU_PAIRED, workspace=self.ws_linear)
+            lw(self.act, layer.down, out=self.h, epilogue=_lib.EPI_RESIDUAL, residual=self.h,
+               workspace=self.ws_linear)
+            res_in = self.h
+        ops.rms_norm(res_in, w["norm"], cfg.eps, self.norm_mode, out=self.hidden)
+        lw(self.hidden, w["head"], out=self.logits, workspace=self.ws_linear)
+
+    def launches_per_step(self) -> int:
+        return 8 * self.cfg.layers + 2
+
+    # ---------------------------------------------------------------- graph capture / replay
+    @torch.inference_mode()
+    def capture(self, warmup: int = 3) -> None:
+        """Warm up on a side stream, then capture (continuous.py:200-216).
+
+        Warm-up really runs, so the KV entries it writes (position 0 of the
+        first `batch` slots) are saved before and restored after.
+        """
+        saved = [(k[:self.batch, :, 0].clone(), v[:self.batch, :, 0].clone())
+                 for k, v in zip(self.arena.keys, self.arena.values)]
+        self.positions.zero_()
+        self.rotary.zero_()
+        stream = torch.cuda.Stream(device=self.inputs.device)
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                self.compute()
+        torch.cuda.current_stream().wait_stream(stream)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=stream):
+            self.compute()
+        torch.cuda.synchronize()
+        for layer, (k, v) in enumerate(saved):
+            self.arena.keys[layer][:self.batch, :, 0].copy_(k)
+            self.arena.values[layer][:self.batch, :, 0].copy_(v)
+
+    @torch.inference_mode()
+    def run(self, inputs, positions, rotary, clone: bool = True):
+        """Copy inputs into the static buffers, replay, return (hidden, logits)."""
+        self.inputs.copy_(inputs)
+        self.positions.copy_(positions)
+        self.rotary.copy_(rotary)
+        if self.graph is None:
+            self.compute()
+        else:
+            self.graph.replay()
+        if clone:
+            return self.hidden.clone(), self.logits.clone()
+        return self.hidden, self.logits
+
+    def close(self) -> None:
+        if self.graph is not None:
+            torch.cuda.synchronize()
+            self.graph.reset()
+            self.graph = None
+
+
+class TalkerDecoder:
+    """Talker weights, arena and per-bucket step graphs."""
+
+    def __init__(self, cfg: DecoderConfig, weights: dict, slots: int, capacity: int, device, packed: bool = False,
+                 use_graphs: bool = True, max_positions: int = 1 << 15):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.weights = weights if packed else pack_decoder(weights, self.device)
+        self.arena = SlotArena(cfg, slots, capacity, self.device)
+        self.cos, self.sin = rope_tables(max_positions, cfg.head_dim, cfg.theta, self.device)
+        self.use_graphs = use_graphs
+        self.graphs: dict[tuple[int, int], TalkerStep] = {}
+
+    def ensure_capacity(self, required: int) -> None:
+        """Grow the arena by doubling when `required` does not fit (continuous.py:353-363)."""
+        if required < self.arena.capacity:
+            return
+        for graph in self.graphs.values():
+            graph.close()
+        self.graphs.clear()
+        new = max(self.arena.capacity * 2, 1 << int(required).bit_length())
+        self.arena = self.arena.grown(new)
+
+    def step_for(self, batch: int, context: int) -> TalkerStep:
+        key = (batch, context)
+        step = self.graphs.get(key)
+        if step is None:
+            step = TalkerStep(self.cfg, self.weights, self.arena, batch, context, self.cos, self.sin)
+            if self.use_graphs:
+                step.capture()
+            self.graphs[key] = step
+        return step
+
+    def close(self) -> None:
+        for graph in self.graphs.values():
+            graph.close()
+        self.graphs.clear()

@@ -1,0 +1,151 @@
+"""Generate the golden fixtures in this folder by running the REFERENCE engine.
+
+Run in a container where the reference checkout is available:
+
+    python tests/golden/make_golden.py /path/to/qwen3-tts-rsi-engine
+
+It imports the reference's own CPU-runnable modules (``qwen3_tts_engine``:
+batching, sampling, continuous.SlotCache / ContinuousModel.semantic,
+packed_kv, codec_code_buffer, request_views) and records their outputs on
+seeded inputs. The fixtures pin the CPU oracle in ``oracle/``; nothing at test
+or bench time reads the reference checkout.
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import sys
+from pathlib import Path
+from types import SimpleNamespace
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parents[1]))
+from tests.golden.inputs import bf16_scores, normal, uniform  # noqa: E402
+
+
+def sha(t: torch.Tensor) -> str:
+    return hashlib.sha256(t.contiguous().numpy().tobytes()).hexdigest()
+
+
+def main(reference: str) -> None:
+    sys.path.insert(0, reference)
+    from qwen3_tts_engine.batching import decode_batch_size
+    from qwen3_tts_engine.codec_code_buffer import CodecCodeBuffer
+    from qwen3_tts_engine.continuous import ContinuousModel, SlotCache
+    from qwen3_tts_engine.packed_kv import copy_packed_prefix
+    from qwen3_tts_engine.request_views import single_request_inputs
+    from qwen3_tts_engine.sampling import categorical, random_table
+
+    torch.set_num_threads(4)
+    out: dict = {}
+    arrays: dict = {}
+
+    # ---- batching: every (slots, step, active)
+    table = []
+    for slots in [1, 2, 4, 8, 16, 32, 64]:
+        for step in [0] + [x for x in [1, 2, 4, 8, 16, 32, 64] if x <= slots]:
+            for active in range(1, slots + 1):
+                table.append([slots, step, active, decode_batch_size(active, slots, step)])
+    out["decode_batch_size"] = table
+
+    # ---- random tables
+    arrays["random_table_42"] = random_table(42, 100).numpy()
+    arrays["random_table_7"] = random_table(7, 19).numpy()
+
+    # ---- categorical on Philox-derived scores (talker width 3072, predictor width 2048)
+    for seed, width in ((11, 3072), (12, 2048)):
+        scores = bf16_scores(seed, 256, width, 3.0)
+        uniforms = torch.from_numpy(uniform(seed + 100, (256,)))
+        arrays[f"cat_tokens_{width}"] = categorical(scores, uniforms).numpy().astype(np.int16)
+    boundary = torch.tensor([[-float("inf"), 0.0, -float("inf"), 0.0]]).repeat(3, 1)
+    draws = torch.tensor([0.0, 0.5, 1.0 - torch.finfo(torch.float32).eps])
+    out["cat_boundary"] = categorical(boundary, draws, top_k=2).flatten().tolist()
+
+    # ---- semantic sampling (ContinuousModel.semantic unbound, as the reference probes do)
+    eos, vocab = 2150, 3072
+    allowed = torch.ones(vocab, dtype=torch.bool)
+    allowed[-1024:] = False
+    allowed[eos] = True
+    state = SimpleNamespace(allowed=allowed, eos=eos, triton_cdf=False)
+    logits = bf16_scores(21, 128, vocab, 2.0).to(torch.bfloat16)
+    seen = torch.from_numpy(uniform(22, (128, vocab)) < 0.05)
+    steps = torch.from_numpy((uniform(23, (128,)) * 5).astype(np.int64))
+    uniforms = torch.from_numpy(uniform(24, (128,)))
+    tokens = ContinuousModel.semantic(state, logits, uniforms, seen, steps)
+    arrays["sem_tokens"] = tokens.numpy().astype(np.int16)
+
+    # ---- SlotCache.update + SDPA on the packed slot table (fp32)
+    g0 = torch.Generator().manual_seed(0)
+    lens = torch.randint(1, 513, (8,), generator=g0)
+    arena_k = torch.zeros(8, 8, 513, 128)
+    arena_v = torch.zeros(8, 8, 513, 128)
+    for b in range(8):
+        n = int(lens[b])
+        arena_k[b, :, :n] = torch.randn(8, n, 128, generator=g0)
+        arena_v[b, :, :n] = torch.randn(8, n, 128, generator=g0)
+    new_k = torch.randn(8, 8, 1, 128, generator=g0)
+    new_v = torch.randn(8, 8, 1, 128, generator=g0)
+    query = torch.randn(8, 16, 1, 128, generator=g0)
+    arena = SimpleNamespace(capacity=513, native_kv_update=False, triton_kv_update=False,
+                            keys=[arena_k], values=[arena_v])
+    cache = SlotCache(arena, lens.clone(), 513, False)
+    k_all, v_all = cache.update(new_k, new_v, 0, {})
+    mask = torch.arange(513)[None, :] <= lens[:, None]
+    attn = torch.nn.functional.scaled_dot_product_attention(query, k_all, v_all, mask[:, None, None, :],
+                                                            enable_gqa=True)
+    out["config1_lens"] = lens.tolist()
+    out["config1_arena_k_sha256"] = sha(arena_k)
+    out["config1_arena_v_sha256"] = sha(arena_v)
+    arrays["config1_attention"] = attn.numpy()
+
+    # ---- small SlotCache scatter (exact layout)
+    keys = torch.from_numpy(normal(31, (4, 2, 64, 16)))
+    values = torch.from_numpy(normal(32, (4, 2, 64, 16)))
+    positions = torch.tensor([0, 63, 17, 1])
+    nk = torch.from_numpy(normal(33, (4, 2, 1, 16)))
+    nv = torch.from_numpy(normal(34, (4, 2, 1, 16)))
+    small = SimpleNamespace(capacity=64, native_kv_update=False, triton_kv_update=False, keys=[keys], values=[values])
+    SlotCache(small, positions, 64, False).update(nk, nv, 0, {})
+    out["scatter_keys_sha256"] = sha(keys)
+    out["scatter_values_sha256"] = sha(values)
+
+    # ---- copy_packed_prefix
+    target = torch.full((4, 5, 2, 7, 3), -7.0)
+    source = torch.arange(4 * 3 * 2 * 5 * 6, dtype=torch.float32).view(4, 3, 2, 5, 6)[..., ::2]
+    for row, slot, length in ((2, 3, 1), (0, 1, 5), (1, 4, 3)):
+        copy_packed_prefix(target, source, slot, row=row, length=length)
+    arrays["packed_prefix_target"] = target.numpy()
+
+    # ---- codec code buffer ring
+    buffer = CodecCodeBuffer(4, 16, "cpu")
+    reads = []
+    for tick in range(19):
+        buffer.write(torch.arange(48).view(3, 16) + tick * 100, torch.tensor([tick, tick + 3, tick + 7]))
+        if tick >= 7:
+            reads.append(buffer.read([2, 0], [tick, tick - 7], 8).numpy())
+    buffer.move(2, 0)
+    reads.append(buffer.read([0], [18], 8).numpy()[:, :, :])
+    arrays["code_buffer_reads"] = np.stack([r if r.shape[0] == 2 else np.concatenate([r, r]) for r in reads])
+
+    # ---- request views
+    gen = torch.Generator().manual_seed(42)
+    st = SimpleNamespace(token=torch.tensor([[42]]), hidden=torch.randn(1, 1, 12, generator=gen),
+                         uniforms=torch.rand(129, 16, generator=gen), trailing=torch.randn(1, 3, 12, generator=gen),
+                         pad=torch.randn(1, 1, 12, generator=gen), seen=torch.zeros(1, 31, dtype=torch.bool),
+                         frames=2, position=165, rope_delta=-13)
+    views = single_request_inputs(st)
+    arrays["views_draws"] = views.draws.numpy()
+    arrays["views_text"] = views.text.numpy()
+    arrays["views_uniforms"] = views.uniforms.numpy()
+    out["views_integers"] = [int(views.positions[0]), int(views.rotary[0, 0, 0]), int(views.steps[0])]
+
+    np.savez_compressed(HERE / "decode_path.npz", **arrays)
+    (HERE / "decode_path.json").write_text(json.dumps(out, indent=1) + "\n")
+    print("wrote", HERE / "decode_path.npz", HERE / "decode_path.json")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

@@ -1,0 +1,390 @@
+"""Parity of each CUDA kernel (through the C ABI) with the CPU oracle.
+
+Integer / copy / index work is compared bit-exactly. Floating-point kernels
+state their tolerance next to the assertion.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import elementwise as E
+from oracle import kv as KV
+from oracle import sampling as S
+from tests.golden.inputs import bf16_scores, normal, uniform
+
+pytestmark = pytest.mark.gpu
+BF16 = torch.bfloat16
+
+
+@pytest.fixture(scope="module")
+def ops(cuda):
+    from qwen3_tts_b200 import ops as _ops
+    return _ops
+
+
+def rnd(seed, shape, scale=1.0, dtype=torch.float32):
+    return torch.from_numpy(normal(seed, shape, scale)).to(dtype)
+
+
+def assert_status_clean(ops, dev):
+    assert ops.read_status(dev) == 0
+
+
+# ------------------------------------------------------------------ KV arena
+@pytest.mark.parametrize("dtype", [BF16, torch.float32])
+@pytest.mark.parametrize("strided", [False, True])
+def test_kv_write_exact(ops, cuda, dtype, strided):
+    B, H, S_, D = 6, 8, 97, 128
+    arena_k = rnd(1, (B, H, S_, D), dtype=dtype)
+    arena_v = rnd(2, (B, H, S_, D), dtype=dtype)
+    if strided:  # K/V as views of one packed QKV projection [B, 1, (16+8+8)*D]
+        packed = rnd(3, (B, 1, 32 * D), dtype=dtype)
+        k = packed[..., 16 * D:24 * D].view(B, 1, H, D).transpose(1, 2)
+        v = packed[..., 24 * D:].view(B, 1, H, D).transpose(1, 2)
+    else:
+        k, v = rnd(4, (B, H, 1, D), dtype=dtype), rnd(5, (B, H, 1, D), dtype=dtype)
+    pos = torch.tensor([0, 96, 13, 1, 50, 95])
+    ek, ev = arena_k.clone(), arena_v.clone()
+    KV.kv_write(k, v, ek, ev, pos)
+    gk, gv = arena_k.to(cuda), arena_v.to(cuda)
+    ops.kv_write(k.to(cuda), v.to(cuda), gk, gv, pos.to(cuda))
+    assert torch.equal(gk.cpu(), ek) and torch.equal(gv.cpu(), ev)
+    assert_status_clean(ops, cuda)
+
+
+def test_kv_write_out_of_range_position_is_skipped_and_flagged(ops, cuda):
+    arena = torch.zeros(2, 2, 8, 16, dtype=BF16, device=cuda)
+    k = torch.ones(2, 2, 1, 16, dtype=BF16, device=cuda)
+    ops.kv_write(k, k, arena, arena.clone(), torch.tensor([3, 8], device=cuda))
+    assert arena[0, :, 3].eq(1).all() and arena[1].eq(0).all()
+    assert ops.read_status(cuda) & 8
+
+
+def test_kv_write_rejects_bad_layout_before_launch(ops, cuda):
+    arena = torch.zeros(2, 2, 8, 16, dtype=BF16, device=cuda)
+    k = torch.ones(2, 2, 1, 16, dtype=BF16, device=cuda)
+    with pytest.raises(ValueError):
+        ops.kv_write(k, k, arena, arena, torch.tensor([1, 2], dtype=torch.int32, device=cuda))
+    with pytest.raises(ValueError):
+        ops.kv_write(k, k[:, :1], arena, arena, torch.tensor([1, 2], device=cuda))
+
+
+@pytest.mark.parametrize("dtype", [BF16, torch.float32, torch.int64])
+def test_copy_packed_prefix_exact(ops, cuda, dtype):
+    target = torch.full((4, 5, 2, 7, 3), -7).to(dtype)
+    source = torch.arange(4 * 3 * 2 * 5 * 6).view(4, 3, 2, 5, 6).to(dtype)[..., ::2]
+    gt, gs = target.to(cuda), source.to(cuda)
+    for row, slot, length in ((2, 3, 1), (0, 1, 5), (1, 4, 3)):
+        KV.copy_packed_prefix(target, source, slot, row=row, length=length)
+        ops.copy_packed_prefix(gt, gs, slot, row=row, length=length)
+    assert torch.equal(gt.cpu(), target)
+    saved = gt.clone()
+    for slot, row, length in ((-1, 0, 1), (5, 0, 1), (0, 3, 1), (0, 0, 0), (0, 0, 6), (True, 0, 1)):
+        with pytest.raises(ValueError):
+            ops.copy_packed_prefix(gt, gs, slot, row=row, length=length)
+    assert torch.equal(gt, saved)
+
+
+def test_slot_move_zero_and_growth_exact(ops, cuda):
+    packed = rnd(7, (6, 4, 2, 33, 16), dtype=BF16)
+    g = packed.to(cuda)
+    ops.slot_move(g, 3, 1, dim=1)
+    packed[:, 1] = packed[:, 3]
+    assert torch.equal(g.cpu(), packed)
+    ops.slot_zero(g, 2, 2, dim=1)
+    packed[:, 2:4] = 0
+    assert torch.equal(g.cpu(), packed)
+    big = torch.zeros(6, 4, 2, 66, 16, dtype=BF16, device=cuda)
+    ops.copy_prefix_along(big, g, dim=3)
+    assert torch.equal(big[:, :, :, :33].cpu(), packed) and big[:, :, :, 33:].eq(0).all()
+    frames = torch.arange(8, device=cuda)
+    ops.slot_move(frames, 7, 0)
+    assert frames.tolist() == [7, 1, 2, 3, 4, 5, 6, 7]
+
+
+# ------------------------------------------------------------------ elementwise
+@pytest.mark.parametrize("mode", ["reference", "native"])
+@pytest.mark.parametrize("width", [128, 1024, 2048])
+def test_rms_norm(ops, cuda, mode, width):
+    from qwen3_tts_b200 import _lib
+    x = rnd(8, (37, width), 2.0, BF16)
+    w = (1 + rnd(9, (width,), 0.1)).to(BF16)
+    ref = E.rms_norm(x, w, 1e-6, mode)
+    out = ops.rms_norm(x.to(cuda), w.to(cuda), 1e-6, _lib.NORM_REFERENCE if mode == "reference" else _lib.NORM_NATIVE)
+    # bf16 output; the fp32 sum-of-squares order differs -> at most one bf16 ulp
+    torch.testing.assert_close(out.float().cpu(), ref.float(), atol=0, rtol=2 ** -7)
+    assert (out.cpu().float() == ref.float()).float().mean() > 0.97
+
+
+def test_add_rms_norm(ops, cuda):
+    a, h = rnd(10, (9, 2048), 1.0, BF16), rnd(11, (9, 2048), 1.0, BF16)
+    w = (1 + rnd(12, (2048,), 0.1)).to(BF16)
+    for mode in ("native", "reference"):
+        from qwen3_tts_b200 import _lib
+        ref_n, ref_r = E.add_rms_norm(a, h, w, 1e-6, mode)
+        n, r = ops.add_rms_norm(a.to(cuda), h.to(cuda), w.to(cuda), 1e-6,
+                                _lib.NORM_NATIVE if mode == "native" else _lib.NORM_REFERENCE)
+        assert torch.equal(r.cpu().float(), ref_r)
+        torch.testing.assert_close(n.cpu().float(), ref_n.float(), atol=0, rtol=2 ** -7)
+
+
+@pytest.mark.parametrize("heads,width", [(16, 128), (8, 128), (8, 64)])
+def test_rotary_bit_exact(ops, cuda, heads, width):
+    x = rnd(13, (3, 5, heads, width), 1.0, BF16)
+    phase = rnd(14, (3, 5, width // 2), 3.0).repeat(1, 1, 2)
+    cos, sin = phase.cos().to(BF16), phase.sin().to(BF16)
+    ref = E.rotary_bf16(x, cos, sin)
+    out = ops.rotary(x.to(cuda), cos.to(cuda), sin.to(cuda))
+    assert torch.equal(out.cpu(), ref)  # products and sums of bf16 are exact in fp32
+    with pytest.raises(ValueError):
+        ops.rotary(x.to(cuda)[..., :3, :], cos.to(cuda), sin.to(cuda))
+
+
+def test_swiglu(ops, cuda):
+    packed = rnd(15, (33, 2 * 6144), 2.0, BF16)
+    ref = E.swiglu(packed)
+    out = ops.swiglu(packed.to(cuda))
+    torch.testing.assert_close(out.cpu().float(), ref.float(), atol=1e-6, rtol=2 ** -7)
+
+
+@pytest.mark.parametrize("dtype", [BF16, torch.float32])
+@pytest.mark.parametrize("shape", [(4, 1536, 32), (4, 96, 15360), (1, 16, 2)])
+def test_snake(ops, cuda, dtype, shape):
+    x = rnd(16, shape, 2.0, dtype)
+    alpha = torch.from_numpy(0.5 + uniform(17, (shape[1],)))
+    inv = 1.0 / (torch.exp(rnd(18, (shape[1],), 0.3)) + 1e-9)
+    ref = E.snake(x, alpha, inv)
+    out = ops.snake(x.to(cuda), alpha.to(cuda), inv.to(cuda))
+    if dtype == BF16:
+        # sinf vs the CPU sin may differ by an ulp before the bf16 rounding
+        torch.testing.assert_close(out.cpu().float(), ref.float(), atol=2 ** -8, rtol=2 ** -7)
+        assert (out.cpu().float() == ref.float()).float().mean() > 0.99
+    else:
+        torch.testing.assert_close(out.cpu(), ref, atol=1e-5, rtol=1e-5)
+
+
+def test_scatter_rows_exact(ops, cuda):
+    target = rnd(19, (8, 3, 5, 4), dtype=BF16)
+    source_full = rnd(20, (3, 3, 10, 4), dtype=BF16)
+    source = source_full[:, :, ::2]  # strided
+    idx = torch.tensor([6, 0, 3])
+    ref = target.clone()
+    E.scatter_rows(ref, idx, source)
+    g = target.to(cuda)
+    ops.scatter_rows(g, idx.to(cuda), source_full.to(cuda)[:, :, ::2])
+    assert torch.equal(g.cpu(), ref)
+    frames = torch.zeros(8, dtype=torch.long, device=cuda)
+    ops.scatter_rows(frames, torch.tensor([2, 5], device=cuda), torch.tensor([7, 9], device=cuda))
+    assert frames.tolist() == [0, 0, 7, 0, 0, 9, 0, 0]
+    with pytest.raises(ValueError):
+        ops.scatter_rows(g, idx.to(cuda), g[:3])  # aliasing source
+
+
+def test_frame_embed_and_embedding_exact(ops, cuda):
+    first = rnd(21, (3072, 256), 0.02, BF16)
+    groups = rnd(22, (15, 2048, 256), 0.02, BF16)
+    codes = torch.cat([torch.from_numpy((uniform(23, (9, 1)) * 3072).astype(np.int64)),
+                       torch.from_numpy((uniform(24, (9, 15)) * 2048).astype(np.int64))], dim=1)
+    text = rnd(25, (9, 256), 0.05, BF16)
+    ref = E.frame_embed(codes, first, groups, text)
+    out = ops.frame_embed(codes.to(cuda), first.to(cuda), groups.to(cuda), text.to(cuda))
+    assert torch.equal(out.cpu(), ref)
+    emb = ops.embedding(codes[:, 0].contiguous().to(cuda), first.to(cuda))
+    assert torch.equal(emb.cpu(), first[codes[:, 0]])
+
+
+# ------------------------------------------------------------------ GEMM
+def torch_linear(x, w, bias=None):
+    y = x.float() @ w.float().T
+    return y if bias is None else y + bias.float()
+
+
+@pytest.mark.parametrize("rows", [1, 7, 16, 32, 33, 64, 100, 256, 300])
+@pytest.mark.parametrize("k,n", [(2048, 4096), (2048, 2048), (6144, 2048), (1024, 2048), (96, 200)])
+def test_linear_store_bf16(ops, cuda, rows, k, n):
+    x = rnd(30 + rows, (rows, k), 1.0, BF16)
+    w = rnd(31 + n, (n, k), 0.02, BF16)
+    ref = torch_linear(x, w)
+    out = ops.linear(x.to(cuda), w.to(cuda))
+    # bf16 output of an fp32-accumulated dot product: one bf16 rounding plus order effects
+    torch.testing.assert_close(out.cpu().float(), ref, atol=2e-3 * math.sqrt(k / 64), rtol=1e-2)
+    assert_status_clean(ops, cuda)
+
+
+def test_linear_fp32_bias_residual_and_strided_input(ops, cuda):
+    from qwen3_tts_b200 import _lib
+    rows, k, n = 24, 2048, 3072
+    base = rnd(40, (rows, k + 64), 1.0, BF16)
+    x = base[:, 32:32 + k]  # row stride k+64, 64-byte offset
+    w = rnd(41, (n, k), 0.02, BF16)
+    b = rnd(42, (n,), 0.1, BF16)
+    out = ops.linear(base.to(cuda)[:, 32:32 + k], w.to(cuda), b.to(cuda), out_dtype=torch.float32)
+    ref = torch_linear(x, w, b)
+    torch.testing.assert_close(out.cpu(), ref, atol=3e-3, rtol=1e-2)
+    res = rnd(43, (rows, n), 1.0, BF16)
+    out = ops.linear(x.contiguous().to(cuda), w.to(cuda), epilogue=_lib.EPI_RESIDUAL, residual=res.to(cuda))
+    ref = (res.float() + torch_linear(x, w).to(BF16).float()).to(BF16)
+    torch.testing.assert_close(out.cpu().float(), ref.float(), atol=1e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("rows", [1, 32, 64, 130])
+def test_linear_paired_swiglu(ops, cuda, rows):
+    from qwen3_tts_b200 import _lib
+    from qwen3_tts_b200.weights import interleave_gate_up
+    k, f = 2048, 6144
+    x = rnd(50, (rows, k), 1.0, BF16)
+    gate, up = rnd(51, (f, k), 0.02, BF16), rnd(52, (f, k), 0.02, BF16)
+    packed = interleave_gate_up(gate, up)
+    out = ops.linear(x.to(cuda), packed.to(cuda), epilogue=_lib.EPI_SWIGLU_PAIRED)
+    g = torch_linear(x, gate).to(BF16)
+    u = torch_linear(x, up).to(BF16)
+    ref = E.swiglu(torch.cat([g, u], dim=-1))
+    torch.testing.assert_close(out.cpu().float(), ref.float(), atol=1e-2, rtol=2e-2)
+
+
+def test_linear_graph_replay_is_deterministic(ops, cuda):
+    x = rnd(60, (32, 2048), 1.0, BF16).to(cuda)
+    w = rnd(61, (6144, 2048), 0.02, BF16).to(cuda)
+    out = torch.empty(32, 6144, dtype=BF16, device=cuda)
+    ops.linear(x, w, out=out)
+    first = out.clone()
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ops.linear(x, w, out=out)
+    torch.cuda.current_stream().wait_stream(s)
+    with torch.cuda.graph(graph, stream=s):
+        ops.linear(x, w, out=out)
+    for _ in range(3):
+        out.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, first)
+    graph.reset()
+
+
+def test_linear_rejects_bad_arguments(ops, cuda):
+    from qwen3_tts_b200 import _lib
+    x = torch.zeros(4, 100, dtype=BF16, device=cuda)
+    w = torch.zeros(128, 100, dtype=BF16, device=cuda)
+    with pytest.raises(ValueError):
+        ops.linear(x, w)  # in_features not a multiple of 8
+    with pytest.raises(ValueError):
+        ops.linear(torch.zeros(4, 64, dtype=BF16, device=cuda), torch.zeros(100, 64, dtype=BF16, device=cuda),
+                   epilogue=_lib.EPI_SWIGLU_PAIRED)
+
+
+# ------------------------------------------------------------------ attention
+def attention_case(cuda, B, Hq, Hkv, D, cap, positions, seed):
+    keys = rnd(seed, (B, Hkv, cap, D), 1.0, BF16)
+    values = rnd(seed + 1, (B, Hkv, cap, D), 1.0, BF16)
+    q = rnd(seed + 2, (B, Hq, D), 1.0, BF16)
+    pos = torch.tensor(positions)
+    ref = KV.decode_attention(q, keys, values, pos)
+    return ref, (q.to(cuda), keys.to(cuda), values.to(cuda), pos.to(cuda))
+
+
+def test_decode_attention_config1(ops, cuda):
+    g = torch.Generator().manual_seed(0)
+    lens = torch.randint(1, 513, (8,), generator=g)
+    ref, args = attention_case(cuda, 8, 16, 8, 128, 513, lens.tolist(), 70)
+    out = ops.decode_attention(*args)
+    # bf16 output vs fp32 oracle on the same bf16 inputs (north-star bar 2e-2)
+    torch.testing.assert_close(out.cpu().float(), ref, atol=2e-2, rtol=0)
+    assert (out.cpu().float() - ref).abs().max() < 1e-2
+    assert_status_clean(ops, cuda)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,D,cap", [(32, 16, 8, 128, 2304), (64, 16, 8, 128, 1024), (3, 8, 8, 64, 143),
+                                            (5, 16, 8, 128, 16), (2, 16, 8, 64, 300)])
+def test_decode_attention_ragged(ops, cuda, B, Hq, Hkv, D, cap):
+    pos = (uniform(80 + B, (B,)) * cap).astype(np.int64).clip(0, cap - 1)
+    pos[0] = 0
+    pos[-1] = cap - 1
+    ref, args = attention_case(cuda, B, Hq, Hkv, D, cap, pos.tolist(), 90 + B)
+    out = ops.decode_attention(*args)
+    torch.testing.assert_close(out.cpu().float(), ref, atol=2e-2, rtol=0)
+    # smaller context bucket: positions must stay below it
+    ctx = int(pos.max()) + 1
+    out2 = ops.decode_attention(*args, context=ctx)
+    torch.testing.assert_close(out2.cpu().float(), ref, atol=2e-2, rtol=0)
+
+
+def test_decode_attention_ignores_poisoned_tail(ops, cuda):
+    ref, (q, k, v, pos) = attention_case(cuda, 4, 16, 8, 128, 200, [5, 63, 64, 130], 100)
+    for b, p in enumerate(pos.tolist()):
+        k[b, :, p + 1:] = float("nan")
+        v[b, :, p + 1:] = float("inf")
+    out = ops.decode_attention(q, k, v, pos)
+    assert torch.isfinite(out).all()
+    torch.testing.assert_close(out.cpu().float(), ref, atol=2e-2, rtol=0)
+
+
+# ------------------------------------------------------------------ sampling
+def boundary_free(tokens_a, tokens_b, limit=1):
+    return int((tokens_a != tokens_b).sum()) <= limit
+
+
+@pytest.mark.parametrize("seed,width", [(11, 3072), (12, 2048)])
+def test_categorical_matches_oracle(ops, cuda, seed, width):
+    scores = bf16_scores(seed, 256, width, 3.0)
+    u = torch.from_numpy(uniform(seed + 100, (256,)))
+    ref = S.categorical(scores, u)
+    got = ops.sample(scores.to(cuda), uniforms=u.to(cuda)).cpu()
+    # identical CDFs up to fp32 rounding of exp/sum order: a draw can flip only
+    # when u lies within ~1e-6 of a CDF step (expected count << 1 here)
+    assert boundary_free(got, ref)
+
+
+def test_sample_boundary_cases(ops, cuda):
+    scores = torch.tensor([[-float("inf"), 0.0, -float("inf"), 0.0]]).repeat(3, 1)
+    draws = torch.tensor([0.0, 0.5, 1.0 - torch.finfo(torch.float32).eps])
+    got = ops.sample(scores.to(cuda), uniforms=draws.to(cuda), top_k=2, temperature=0.9).flatten().tolist()
+    assert got == [1, 3, 3]
+
+
+def test_semantic_sampling_and_seen_update(ops, cuda):
+    vocab, eos = 3072, 2150
+    logits = bf16_scores(21, 128, vocab, 2.0).to(BF16)
+    seen = torch.from_numpy(uniform(22, (128, vocab)) < 0.05)
+    steps = torch.from_numpy((uniform(23, (128,)) * 5).astype(np.int64))
+    u = torch.from_numpy(uniform(24, (128,)))
+    allowed = S.allowed_mask(vocab, eos)
+    ref_tokens, ref_seen = S.sampling_graph_step(logits, u, seen, steps, allowed, eos)
+    seen_out = torch.empty(128, vocab, dtype=torch.bool, device=cuda)
+    got = ops.sample(logits.to(cuda), uniforms=u.to(cuda), seen=seen.to(cuda), allowed=allowed.to(cuda),
+                     steps=steps.to(cuda), eos=eos, seen_out=seen_out)
+    assert boundary_free(got.cpu(), ref_tokens)
+    same = (got.cpu() == ref_tokens).flatten()
+    assert torch.equal(seen_out.cpu()[same], ref_seen[same])
+    # EOS is never drawn before step 2 and masked ids never drawn
+    assert not ((got.cpu().flatten() == eos) & (steps < 2)).any()
+    assert allowed[got.cpu().flatten()].all()
+
+
+def test_top_p_and_philox(ops, cuda):
+    scores = bf16_scores(33, 64, 2048, 3.0)
+    offsets = torch.arange(64, dtype=torch.int64) * 16 + 5
+    seed = 0x1234_5678_9ABC
+    u = torch.from_numpy(S.philox_uniform(seed, offsets.numpy()))
+    ref = S.categorical(scores, u, top_p=0.95)
+    got = ops.sample(scores.to(cuda), seed=seed, philox_offsets=offsets.to(cuda), top_p=0.95).cpu()
+    assert boundary_free(got, ref)
+    stream = ops.philox_uniforms(seed, 7, 1001, cuda).cpu().numpy()
+    assert np.array_equal(stream, S.philox_stream(seed, 7, 1001))
+
+
+def test_cdf_select_exact(ops, cuda):
+    p = torch.from_numpy(uniform(34, (32, 2048))) ** 4
+    cdf = p.cumsum(-1)
+    u = torch.from_numpy(uniform(35, (32,)))
+    ref = S.cdf_select(cdf, u)
+    assert torch.equal(ops.cdf_select(cdf.to(cuda), u.to(cuda)).cpu(), ref)
+    # plateau boundaries +-1 ulp (probe_cdf_tail semantics)
+    cdf = torch.tensor([[0.0, 0.25, 0.25, 0.5, 1.0]] * 3)
+    u = torch.tensor([0.25, np.nextafter(np.float32(0.25), np.float32(0)), np.nextafter(np.float32(0.25), np.float32(1))],
+                     dtype=torch.float32)
+    assert torch.equal(ops.cdf_select(cdf.to(cuda), u.to(cuda)).cpu(), S.cdf_select(cdf, u))
