@@ -20,9 +20,7 @@ import argparse
 import json
 import math
 import os
-import subprocess
 import sys
-import tempfile
 import time
 from pathlib import Path
 
@@ -103,60 +101,59 @@ class Workload:
 
 # ---------------------------------------------------------------------- clocks
 class ClockSampler:
-    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Samples SM clock, power and clock-event reasons every 200 ms through NVML (read-only)."""
 
-    def __init__(self):
-        self.proc = None
-        self.path = None
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self.stop_flag = None
+        self.thread = None
+        self.max_mhz = None
 
     def start(self):
+        import threading
         try:
-            fd, self.path = tempfile.mkstemp(suffix=".csv")
-            os.close(fd)
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-f", self.path], stdout=subprocess.DEVNULL,
-                                         stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            index = int(visible.split(",")[self.index]) if visible else self.index
+            handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            return
+        self.stop_flag = threading.Event()
 
-    def stop(self, uuid: str | None):
-        if self.proc is None:
+        def loop():
+            while not self.stop_flag.is_set():
+                try:
+                    sm = pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM)
+                    reasons = pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                    power = pynvml.nvmlDeviceGetPowerUsage(handle) / 1000.0
+                    self.samples.append((sm, reasons, power))
+                except Exception:
+                    pass
+                self.stop_flag.wait(0.2)
+
+        self.thread = threading.Thread(target=loop, daemon=True)
+        self.thread.start()
+
+    def stop(self):
+        if self.thread is None:
             return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        rows = []
-        try:
-            for line in Path(self.path).read_text().splitlines():
-                parts = [x.strip() for x in line.split(",")]
-                if len(parts) >= 9 and (uuid is None or parts[0] == uuid):
-                    rows.append(parts)
-        finally:
-            os.unlink(self.path)
-        if not rows:
+        self.stop_flag.set()
+        self.thread.join(timeout=2)
+        if not self.samples:
             return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            for name, val in zip(names, r[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": float(np.median(sm)) if sm else None,
-                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
-                "reasons": sorted(reasons), "samples": len(rows)}
-
-
-def device_uuid(index: int):
-    try:
-        u = str(torch.cuda.get_device_properties(index).uuid)
-        return u if u.startswith("GPU-") else "GPU-" + u
-    except Exception:
-        return None
+        active = set()
+        for _, bits, _ in self.samples:
+            for name, bit in self.REASONS.items():
+                if bits & bit:
+                    active.add(name)
+        return {"sm_mhz": float(np.median([s[0] for s in self.samples])), "sm_max_mhz": float(self.max_mhz),
+                "reasons": sorted(active), "power_w_max": max(s[2] for s in self.samples),
+                "samples": len(self.samples)}
 
 
 def measured_peaks():
@@ -272,7 +269,7 @@ def run_b200(args, dist: Dist):
     torch.cuda.synchronize()
     positions_at_start = step.positions.cpu()
 
-    clocks = ClockSampler()
+    clocks = ClockSampler(dev.index)
     clocks.start()
     dist.barrier()
     torch.cuda.synchronize()
@@ -285,7 +282,7 @@ def run_b200(args, dist: Dist):
     torch.cuda.synchronize()
     dist.barrier()
     elapsed_ms = dist.max(start.elapsed_time(end))
-    clock_info = clocks.stop(device_uuid(dev.index))
+    clock_info = clocks.stop()
     status = ops.read_status(dev)
 
     # ---- end to end through the public step API: pinned host inputs in, token ids out, every step

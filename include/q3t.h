@@ -171,18 +171,21 @@ int q3t_qk_norm_rope_kv(const void* qkv, int64_t qkv_stride, const void* q_norm_
                         void* stream);
 
 /* Replaces torch_npu.npu_fused_infer_attention_score at qwen3_tts_engine/npu_attention.py:21
- * (and SDPA over SlotCache, continuous.py:188-198) for one query token per slot:
- * query [batch, q_heads, head_dim] bf16, keys/values [slots, kv_heads, capacity, head_dim]
- * bf16 contiguous (slot b serves row b), positions int64 [batch]: keys 0..positions[b]
- * are visible. context bounds the grid (positions[b] < context <= capacity).
- * out [batch, q_heads, head_dim] bf16. Split-KV with an in-kernel combine. */
-size_t q3t_decode_attention_workspace_bytes(int64_t batch, int64_t q_heads, int64_t head_dim,
+ * (and SDPA over SlotCache, continuous.py:188-198; the predictor's causal
+ * 2-token first step, continuous.py:37-40; the codec's sliding window,
+ * codec_slots.py:73-77). query rows [rows, q_heads, head_dim] bf16; row r
+ * reads slot r / rows_per_slot of keys/values [slots, kv_heads, capacity, head_dim]
+ * (bf16, contiguous) and sees keys max(0, p - window + 1) .. p with
+ * p = positions[r] (window 0 = unbounded). context bounds the grid
+ * (positions < context <= capacity). out [rows, q_heads, head_dim] bf16.
+ * Split-KV with an in-kernel combine. */
+size_t q3t_decode_attention_workspace_bytes(int64_t rows, int64_t q_heads, int64_t head_dim,
                                             int64_t context);
 int q3t_decode_attention(const void* query, const void* keys, const void* values,
-                         const int64_t* positions, void* out, int64_t batch, int64_t q_heads,
-                         int64_t kv_heads, int64_t head_dim, int64_t capacity, int64_t context,
-                         float scale, void* workspace, size_t workspace_bytes, unsigned* status,
-                         void* stream);
+                         const int64_t* positions, void* out, int64_t rows, int64_t rows_per_slot,
+                         int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t capacity,
+                         int64_t context, int64_t window, float scale, void* workspace,
+                         size_t workspace_bytes, unsigned* status, void* stream);
 
 /* ------------------------------------------------------------------ sampling */
 
@@ -201,14 +204,15 @@ int q3t_cdf_select(const float* cdf, const float* uniforms, int64_t* tokens, int
  *   scores /= temperature; keep scores >= k-th largest (ties kept);
  *   softmax; optional top-p (smallest set with mass >= top_p; 1.0 disables);
  *   cdf = cumsum; token = #{ cdf / cdf[-1] <= u }.
- * u: uniforms[r * uniform_stride] when uniforms != NULL, else Philox4x32-10
- *    (key = seed, counter = {philox_offsets[r] lo, hi, r, 0}) mapped to [0, 1).
+ * u: uniforms[r * uniform_stride] when uniforms != NULL, else Philox4x32-10 with
+ *    key = seed and counter = {c lo, c hi, 0, 0}, c = philox_offsets[r] + philox_add
+ *    (row r when philox_offsets is NULL), first word mapped to [0, 1) as (x >> 8) * 2^-24.
  * seen_out (nullable, may alias seen): seen row copied, then seen_out[r, token] = 1. */
 int q3t_sample(const void* logits, int logits_dtype, int64_t logits_stride, const uint8_t* seen,
                int64_t seen_stride, const uint8_t* allowed, const int64_t* steps, int64_t eos,
                int64_t min_steps, float penalty, float temperature, int64_t top_k, float top_p,
                const float* uniforms, int64_t uniform_stride, uint64_t seed,
-               const int64_t* philox_offsets, int64_t* tokens, int64_t token_stride,
+               const int64_t* philox_offsets, int64_t philox_add, int64_t* tokens, int64_t token_stride,
                uint8_t* seen_out, int64_t seen_out_stride, int64_t rows, int64_t width,
                void* stream);
 

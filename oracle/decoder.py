@@ -115,7 +115,7 @@ def talker_decode_step(cfg, weights, embeds, positions, rope_deltas, cache, tabl
 
 
 def predictor_frame(cfg, weights, hidden, first, draws, tables, mode="fp32", *, temperature=0.9, top_k=50,
-                    top_p=1.0, uniforms_fn=None):
+                    top_p=1.0, uniforms_fn=None, forced_codes=None):
     """The 15-codebook loop of UniformPredictor.run (continuous.py:49-68).
 
     hidden/first [B, talker_hidden]; draws [B, 16] (column step+1 feeds step).
@@ -127,6 +127,7 @@ def predictor_frame(cfg, weights, hidden, first, draws, tables, mode="fp32", *, 
     cache = new_cache(cfg, B, cfg.groups + 1)
     inputs = torch.stack([hidden, first], dim=1).float()
     codes = []
+    all_logits = []
     token = None
     for step in range(cfg.groups):
         if step == 0:
@@ -141,8 +142,11 @@ def predictor_frame(cfg, weights, hidden, first, draws, tables, mode="fp32", *, 
         u = draws[:, step + 1] if uniforms_fn is None else uniforms_fn(step)
         token = categorical(logits, u, temperature=temperature, top_k=top_k, top_p=top_p)
         codes.append(token)
+        all_logits.append(logits)
+        if forced_codes is not None:
+            token = forced_codes[:, step:step + 1]
     subcodes = torch.cat(codes, dim=-1)
     acc = first.float()
     for i in range(cfg.groups):
         acc = acc + weights["embeddings"][i][subcodes[:, i]].float()
-    return subcodes, acc
+    return subcodes, acc, torch.stack(all_logits)

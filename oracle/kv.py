@@ -38,12 +38,16 @@ def grow(buffer, new_capacity: int, dim: int = 2):
     return out
 
 
-def decode_attention(query, keys, values, positions, scale=None):
-    """One query token per slot over keys 0..positions[b] of that slot, GQA.
+def decode_attention(query, keys, values, positions, scale=None, rows_per_slot=1, window=0):
+    """Query rows over their slot's keys, GQA.
 
-    query [B, Hq, D], keys/values [slots, Hkv, cap, D] -> [B, Hq, D] (fp32).
-    Mask `indices <= positions` as SlotGraph.compute builds it (continuous.py:191-192),
-    attention as torch SDPA with enable_gqa (scaled dot product, softmax, V).
+    query [R, Hq, D], keys/values [slots, Hkv, cap, D] -> [R, Hq, D] (fp32).
+    Row r reads slot r // rows_per_slot and sees keys lo..p, p = positions[r],
+    lo = max(0, p - window + 1) with a sliding window (0 = none): the mask
+    `indices <= positions` of SlotGraph.compute (continuous.py:191-192), the
+    predictor's 2x2 causal first step (continuous.py:37-40) and the codec
+    window `key > position - window` (codec_slots.py:73-77). Attention as
+    torch SDPA with enable_gqa (scaled dot product, softmax, V).
     """
     batch, q_heads, dim = query.shape
     kv_heads = keys.shape[1]
@@ -51,9 +55,11 @@ def decode_attention(query, keys, values, positions, scale=None):
     scale = dim ** -0.5 if scale is None else scale
     out = torch.empty(batch, q_heads, dim, dtype=torch.float32)
     for b in range(batch):
-        n = int(positions[b]) + 1
-        k = keys[b, :, :n].float().repeat_interleave(group, dim=0)      # [Hq, n, D]
-        v = values[b, :, :n].float().repeat_interleave(group, dim=0)
+        p = int(positions[b])
+        lo = max(0, p - window + 1) if window > 0 else 0
+        slot = b // rows_per_slot
+        k = keys[slot, :, lo:p + 1].float().repeat_interleave(group, dim=0)      # [Hq, n, D]
+        v = values[slot, :, lo:p + 1].float().repeat_interleave(group, dim=0)
         s = torch.einsum("hd,hnd->hn", query[b].float(), k) * scale
         p = torch.softmax(s, dim=-1)
         out[b] = torch.einsum("hn,hnd->hd", p, v)

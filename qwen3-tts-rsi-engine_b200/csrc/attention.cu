@@ -51,7 +51,8 @@ __global__ void __launch_bounds__(128)
     decode_attention_kernel(const __nv_bfloat16* __restrict__ query, const __nv_bfloat16* __restrict__ keys,
                             const __nv_bfloat16* __restrict__ values, const int64_t* __restrict__ positions,
                             __nv_bfloat16* __restrict__ out, int kv_heads, int64_t capacity, int64_t context,
-                            int chunk, float qscale, float* __restrict__ partials, unsigned* __restrict__ counters,
+                            int window, int rows_per_slot, int chunk, float qscale, float* __restrict__ partials,
+                            unsigned* __restrict__ counters,
                             int max_chunks, unsigned* status) {
   using C = AttnCfg<D, G>;
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -77,13 +78,16 @@ __global__ void __launch_bounds__(128)
     if (c == 0 && h == 0 && threadIdx.x == 0) raise_status(status, kStatusBadIndex);
     pos = pos < 0 ? 0 : context - 1;
   }
+  // visible keys: [k_lo, pos]; a sliding window keeps only the last `window`
+  const int64_t k_lo = (window > 0 && pos + 1 > window) ? pos + 1 - window : 0;
   const int64_t nkeys = pos + 1;
-  const int active = int((nkeys + chunk - 1) / chunk);
+  const int active = int((nkeys - k_lo + chunk - 1) / chunk);
   if (c >= active) return;
-  const int64_t k_begin = int64_t(c) * chunk;
+  const int64_t k_begin = k_lo + int64_t(c) * chunk;
   const int64_t k_end = (k_begin + chunk) < nkeys ? (k_begin + chunk) : nkeys;
   const int ntiles = int((k_end - k_begin + C::kTK - 1) / C::kTK);
-  const size_t head_base = (size_t(b) * kv_heads + h) * size_t(capacity) * D;
+  const int slot = b / rows_per_slot;  // query row b reads the keys of its slot
+  const size_t head_base = (size_t(slot) * kv_heads + h) * size_t(capacity) * D;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars[0], 1);
@@ -283,6 +287,12 @@ __global__ void __launch_bounds__(128)
   if (threadIdx.x == 0) *counter = 0u;
 }
 
+// Workspace layout: a fixed ticket region (one counter per (row, kv head),
+// zero between calls) followed by the chunk partials; fixed so that calls of
+// different shapes sharing a workspace never read partials as tickets.
+constexpr size_t kMaxTickets = 65536;
+constexpr size_t kTicketBytes = kMaxTickets * sizeof(unsigned);
+
 int pick_chunk(int64_t batch, int64_t kv_heads, int64_t context) {
   // Enough CTAs to cover every SM a few times at the bucket's full context.
   const int64_t target = 4LL * sm_count();
@@ -292,12 +302,13 @@ int pick_chunk(int64_t batch, int64_t kv_heads, int64_t context) {
 }
 
 template <int D, int G>
-int launch_attn(const void* q, const void* k, const void* v, const int64_t* pos, void* out, int64_t batch,
-                int64_t kv_heads, int64_t capacity, int64_t context, float scale, void* ws, unsigned* status,
-                void* stream) {
+int launch_attn(const void* q, const void* k, const void* v, const int64_t* pos, void* out, int64_t rows,
+                int64_t rows_per_slot, int64_t kv_heads, int64_t capacity, int64_t context, int64_t window,
+                float scale, void* ws, unsigned* status, void* stream) {
   using C = AttnCfg<D, G>;
-  const int chunk = pick_chunk(batch, kv_heads, context);
-  const int max_chunks = int((context + chunk - 1) / chunk);
+  const int64_t span = window > 0 && window < context ? window : context;
+  const int chunk = pick_chunk(rows, kv_heads, span);
+  const int max_chunks = int((span + chunk - 1) / chunk);
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -308,13 +319,12 @@ int launch_attn(const void* q, const void* k, const void* v, const int64_t* pos,
     configured[dev] = true;
   }
   unsigned* counters = static_cast<unsigned*>(ws);
-  const size_t cbytes = ((size_t(batch) * kv_heads * sizeof(unsigned) + 255) / 256) * 256;
-  float* partials = reinterpret_cast<float*>(static_cast<char*>(ws) + cbytes);
-  return launch(decode_attention_kernel<D, G>, dim3(max_chunks, unsigned(kv_heads), unsigned(batch)), dim3(128),
+  float* partials = reinterpret_cast<float*>(static_cast<char*>(ws) + kTicketBytes);
+  return launch(decode_attention_kernel<D, G>, dim3(max_chunks, unsigned(kv_heads), unsigned(rows)), dim3(128),
                 size_t(C::kSmem), stream, true, "decode_attention", static_cast<const __nv_bfloat16*>(q),
                 static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), pos,
-                static_cast<__nv_bfloat16*>(out), int(kv_heads), capacity, context, chunk, scale * kLog2e, partials,
-                counters, max_chunks, status);
+                static_cast<__nv_bfloat16*>(out), int(kv_heads), capacity, context, int(window), int(rows_per_slot),
+                chunk, scale * kLog2e, partials, counters, max_chunks, status);
 }
 
 size_t attn_workspace(int64_t batch, int64_t q_heads, int64_t kv_heads_unused, int64_t head_dim, int64_t context) {
@@ -322,8 +332,7 @@ size_t attn_workspace(int64_t batch, int64_t q_heads, int64_t kv_heads_unused, i
   // worst case over G: partial floats per (b, kv head, chunk) = G*(D+2); bound with q_heads*(D+2) per (b, chunk)
   const int chunk = 64;
   const int64_t max_chunks = (context + chunk - 1) / chunk;
-  const size_t cbytes = ((size_t(batch) * q_heads * sizeof(unsigned) + 255) / 256) * 256;
-  return cbytes + size_t(batch) * max_chunks * q_heads * (head_dim + 2) * sizeof(float);
+  return kTicketBytes + size_t(batch) * max_chunks * q_heads * (head_dim + 2) * sizeof(float);
 }
 
 }  // namespace
@@ -335,31 +344,30 @@ extern "C" size_t q3t_decode_attention_workspace_bytes(int64_t batch, int64_t q_
 }
 
 extern "C" int q3t_decode_attention(const void* query, const void* keys, const void* values, const int64_t* positions,
-                                    void* out, int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
-                                    int64_t capacity, int64_t context, float scale, void* workspace,
-                                    size_t workspace_bytes, unsigned* status, void* stream) {
+                                    void* out, int64_t rows, int64_t rows_per_slot, int64_t q_heads, int64_t kv_heads,
+                                    int64_t head_dim, int64_t capacity, int64_t context, int64_t window, float scale,
+                                    void* workspace, size_t workspace_bytes, unsigned* status, void* stream) {
   if (!query || !keys || !values || !positions || !out) return fail(Q3T_EINVAL, "attention: null pointer");
-  if (batch < 1 || batch > 65535 || kv_heads < 1 || kv_heads > 65535 || q_heads % kv_heads)
-    return fail(Q3T_EINVAL, "attention: invalid head geometry");
+  if (rows < 1 || rows > 65535 || rows_per_slot < 1 || rows % rows_per_slot || kv_heads < 1 || kv_heads > 65535 ||
+      q_heads % kv_heads || window < 0)
+    return fail(Q3T_EINVAL, "attention: invalid row or head geometry");
   if (context < 1 || context > capacity) return fail(Q3T_EINVAL, "Attention context must fit the KV arena");
+  if (size_t(rows) * size_t(kv_heads) > kMaxTickets) return fail(Q3T_EUNSUPPORTED, "attention: rows x kv_heads > 65536");
   if (!aligned16(keys) || !aligned16(values) || !aligned16(query))
     return fail(Q3T_EINVAL, "attention: 16-byte alignment");
   const int64_t g = q_heads / kv_heads;
-  const size_t need = attn_workspace(batch, q_heads, kv_heads, head_dim, context);
+  const size_t need = attn_workspace(rows, q_heads, kv_heads, head_dim, context);
   if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
     return fail(Q3T_ESPACE, "attention: workspace needs %zu bytes", need);
-  if (head_dim == 128 && g == 2)
-    return launch_attn<128, 2>(query, keys, values, positions, out, batch, kv_heads, capacity, context, scale,
-                               workspace, status, stream);
-  if (head_dim == 128 && g == 1)
-    return launch_attn<128, 1>(query, keys, values, positions, out, batch, kv_heads, capacity, context, scale,
-                               workspace, status, stream);
-  if (head_dim == 64 && g == 1)
-    return launch_attn<64, 1>(query, keys, values, positions, out, batch, kv_heads, capacity, context, scale,
-                              workspace, status, stream);
-  if (head_dim == 64 && g == 2)
-    return launch_attn<64, 2>(query, keys, values, positions, out, batch, kv_heads, capacity, context, scale,
-                              workspace, status, stream);
+#define Q3T_ATTN(DD, GG)                                                                                       \
+  if (head_dim == DD && g == GG)                                                                               \
+    return launch_attn<DD, GG>(query, keys, values, positions, out, rows, rows_per_slot, kv_heads, capacity, \
+                               context, window, scale, workspace, status, stream);
+  Q3T_ATTN(128, 2)
+  Q3T_ATTN(128, 1)
+  Q3T_ATTN(64, 1)
+  Q3T_ATTN(64, 2)
+#undef Q3T_ATTN
   return fail(Q3T_EUNSUPPORTED, "attention: head_dim %lld with %lld query heads per kv head", (long long)head_dim,
               (long long)g);
 }

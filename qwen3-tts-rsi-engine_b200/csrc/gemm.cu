@@ -339,10 +339,16 @@ int dispatch_bn(const Plan& p, const CUtensorMap& tmw, const CUtensorMap& tmx, c
   }
 }
 
+// Workspace layout: a fixed ticket region (kMaxTiles counters, zero between
+// calls) followed by the fp32 partials. The ticket region never moves, so
+// calls of different shapes sharing one workspace cannot see each other's
+// partials as tickets.
+constexpr size_t kMaxTiles = 16384;
+constexpr size_t kTicketBytes = kMaxTiles * sizeof(unsigned);
+
 size_t workspace_for(const Plan& p, int64_t rows, int64_t out_features) {
-  const size_t counters = size_t(p.n_tiles) * p.m_tiles * sizeof(unsigned);
   const size_t partial = size_t(p.splits) * size_t(rows) * size_t(out_features) * sizeof(float);
-  return ((counters + 255) / 256) * 256 + partial;
+  return kTicketBytes + partial;
 }
 
 }  // namespace
@@ -392,9 +398,9 @@ extern "C" int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t
   a.out_f32 = out_dtype == Q3T_F32;
   a.residual = static_cast<const __nv_bfloat16*>(residual);
   a.res_stride = residual_stride;
-  const size_t counter_bytes = ((size_t(p.n_tiles) * p.m_tiles * sizeof(unsigned) + 255) / 256) * 256;
+  if (size_t(p.n_tiles) * p.m_tiles > kMaxTiles) return fail(Q3T_EUNSUPPORTED, "linear: more than 16384 tiles");
   a.counters = static_cast<unsigned*>(workspace);
-  a.partials = workspace ? reinterpret_cast<float*>(static_cast<char*>(workspace) + counter_bytes) : nullptr;
+  a.partials = workspace ? reinterpret_cast<float*>(static_cast<char*>(workspace) + kTicketBytes) : nullptr;
   a.status = status;
   switch (epilogue) {
     case Q3T_EPI_STORE: return dispatch_bn<Q3T_EPI_STORE>(p, tmw, tmx, a, stream);

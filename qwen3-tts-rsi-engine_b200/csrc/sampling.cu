@@ -117,6 +117,7 @@ struct SampleArgs {
   int64_t uniform_stride;
   uint64_t seed;
   const int64_t* offsets;
+  int64_t offset_add;
   int64_t* tokens;
   int64_t token_stride;
   uint8_t* seen_out;
@@ -299,7 +300,7 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
   if (a.uniforms != nullptr) {
     u = a.uniforms[r * a.uniform_stride];
   } else {
-    const uint64_t off = a.offsets ? uint64_t(a.offsets[r]) : uint64_t(r);
+    const uint64_t off = (a.offsets ? uint64_t(a.offsets[r]) : uint64_t(r)) + uint64_t(a.offset_add);
     const U4 o = philox4x32_10(U4{uint32_t(off), uint32_t(off >> 32), 0u, 0u}, uint32_t(a.seed), uint32_t(a.seed >> 32));
     u = u01(o.x);
   }
@@ -362,7 +363,7 @@ extern "C" int q3t_sample(const void* logits, int logits_dtype, int64_t logits_s
                           int64_t seen_stride, const uint8_t* allowed, const int64_t* steps, int64_t eos,
                           int64_t min_steps, float penalty, float temperature, int64_t top_k, float top_p,
                           const float* uniforms, int64_t uniform_stride, uint64_t seed, const int64_t* philox_offsets,
-                          int64_t* tokens, int64_t token_stride, uint8_t* seen_out, int64_t seen_out_stride,
+                          int64_t philox_add, int64_t* tokens, int64_t token_stride, uint8_t* seen_out, int64_t seen_out_stride,
                           int64_t rows, int64_t width, void* stream) {
   if (!logits || !tokens || rows < 1 || width < 1 || width > kMaxWidth)
     return fail(Q3T_EINVAL, "sample: rows >= 1 and width in 1..4096 required");
@@ -389,6 +390,7 @@ extern "C" int q3t_sample(const void* logits, int logits_dtype, int64_t logits_s
   a.uniform_stride = uniform_stride;
   a.seed = seed;
   a.offsets = philox_offsets;
+  a.offset_add = philox_add;
   a.tokens = tokens;
   a.token_stride = token_stride;
   a.seen_out = seen_out;

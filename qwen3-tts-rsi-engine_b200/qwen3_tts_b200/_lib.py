@@ -45,11 +45,11 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "q3t_qk_norm_rope_kv": (_i32, [_p, _i64, _p, _p, _f32, _p, _p, _i64, _p, _p, _p, _p, _p, _i64, _i64, _i64,
                                    _i64, _i64, _i64, _p, _p]),
     "q3t_decode_attention_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),
-    "q3t_decode_attention": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _sz, _p,
-                                    _p]),
+    "q3t_decode_attention": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32,
+                                    _p, _sz, _p, _p]),
     "q3t_cdf_select": (_i32, [_p, _p, _p, _i64, _i64, _p]),
     "q3t_sample": (_i32, [_p, _i32, _i64, _p, _i64, _p, _p, _i64, _i64, _f32, _f32, _i64, _f32, _p, _i64, _u64,
-                          _p, _p, _i64, _p, _i64, _i64, _i64, _p]),
+                          _p, _i64, _p, _i64, _p, _i64, _i64, _i64, _p]),
     "q3t_philox_uniforms": (_i32, [_u64, _u64, _p, _i64, _p]),
     "q3t_frame_embed": (_i32, [_p, _i64, _p, _i64, _p, _i64, _i64, _p, _i64, _p, _i64, _i64, _p, _p]),
     "q3t_embedding": (_i32, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _p, _p]),

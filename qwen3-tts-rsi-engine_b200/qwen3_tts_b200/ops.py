@@ -312,24 +312,24 @@ def decode_attention_workspace_bytes(batch, q_heads, head_dim, context) -> int:
     return int(_lib.load().q3t_decode_attention_workspace_bytes(batch, q_heads, head_dim, context))
 
 
-def decode_attention(query, keys, values, positions, *, context=None, scale=None, out=None,
-                     workspace: Optional[torch.Tensor] = None, tag: str = "attention"):
-    """GQA attention of one query token per slot over keys 0..positions[b] of that slot."""
+def decode_attention(query, keys, values, positions, *, context=None, scale=None, out=None, rows_per_slot=1,
+                     window=0, workspace: Optional[torch.Tensor] = None, tag: str = "attention"):
+    """GQA attention of query row r over keys [max(0, p-window+1), p] of slot r // rows_per_slot, p = positions[r]."""
     _need_cuda(query, keys, values, positions)
-    batch, q_heads, head_dim = query.shape
+    rows, q_heads, head_dim = query.shape
     slots, kv_heads, capacity, width = keys.shape
-    if (width != head_dim or values.shape != keys.shape or slots < batch or not keys.is_contiguous()
+    if (width != head_dim or values.shape != keys.shape or slots * rows_per_slot < rows or not keys.is_contiguous()
             or not values.is_contiguous() or not query.is_contiguous() or query.dtype != BF16
             or keys.dtype != BF16 or values.dtype != BF16 or positions.dtype != torch.int64):
-        raise ValueError("Expected BF16 query [B,Hq,D] and contiguous BF16 KV arena [slots,Hkv,cap,D]")
+        raise ValueError("Expected BF16 query [rows,Hq,D] and contiguous BF16 KV arena [slots,Hkv,cap,D]")
     context = capacity if context is None else context
     scale = head_dim ** -0.5 if scale is None else scale
     out = torch.empty_like(query) if out is None else out
-    need = decode_attention_workspace_bytes(batch, q_heads, head_dim, context)
+    need = decode_attention_workspace_bytes(rows, q_heads, head_dim, context)
     ws = workspace if workspace is not None else SCRATCH.workspace(need, query.device, tag)
     call("q3t_decode_attention", query.data_ptr(), keys.data_ptr(), values.data_ptr(), positions.data_ptr(),
-         out.data_ptr(), batch, q_heads, kv_heads, head_dim, capacity, context, float(scale), ws.data_ptr(),
-         ws.numel(), status_word(query.device).data_ptr(), _stream())
+         out.data_ptr(), rows, rows_per_slot, q_heads, kv_heads, head_dim, capacity, context, window, float(scale),
+         ws.data_ptr(), ws.numel(), status_word(query.device).data_ptr(), _stream())
     return out
 
 
@@ -349,8 +349,9 @@ def cdf_select(cdf, uniforms):
     return out
 
 
-def sample(logits, *, uniforms=None, seed: int = 0, philox_offsets=None, temperature=0.9, top_k=50, top_p=1.0,
-           seen=None, allowed=None, steps=None, eos=0, min_steps=2, penalty=1.05, seen_out=None, tokens=None):
+def sample(logits, *, uniforms=None, seed: int = 0, philox_offsets=None, philox_add: int = 0, temperature=0.9,
+           top_k=50, top_p=1.0, seen=None, allowed=None, steps=None, eos=0, min_steps=2, penalty=1.05,
+           seen_out=None, tokens=None):
     """Fused categorical sampling (sampling.py:5 + continuous.py:365-370 + sampling_graph.py:14-16)."""
     _need_cuda(logits)
     if logits.ndim != 2 or logits.stride(1) != 1 or logits.dtype not in (BF16, torch.float32):
@@ -359,7 +360,8 @@ def sample(logits, *, uniforms=None, seed: int = 0, philox_offsets=None, tempera
     if uniforms is None and philox_offsets is None:
         raise ValueError("Provide uniforms or Philox offsets")
     if uniforms is not None:
-        if uniforms.dtype != torch.float32 or uniforms.shape[0] != rows or uniforms.device != logits.device:
+        if uniforms.dtype != torch.float32 or uniforms.shape[0] != rows or uniforms.device != logits.device \
+                or uniforms.ndim != 1:
             raise ValueError("Uniforms must be one FP32 value per row")
     if philox_offsets is not None and (philox_offsets.dtype != torch.int64 or philox_offsets.shape[0] != rows):
         raise ValueError("Philox offsets must be one int64 per row")
@@ -372,7 +374,7 @@ def sample(logits, *, uniforms=None, seed: int = 0, philox_offsets=None, tempera
          _ptr(seen), seen.stride(0) if seen is not None else 0, _ptr(allowed), _ptr(steps), int(eos), int(min_steps),
          float(penalty), float(temperature), int(top_k), float(top_p), _ptr(uniforms),
          uniforms.stride(0) if uniforms is not None else 0, int(seed) & ((1 << 64) - 1), _ptr(philox_offsets),
-         tokens.data_ptr(), tokens.stride(0), _ptr(seen_out), seen_out.stride(0) if seen_out is not None else 0, rows,
+         int(philox_add), tokens.data_ptr(), tokens.stride(0), _ptr(seen_out), seen_out.stride(0) if seen_out is not None else 0, rows,
          width, _stream())
     return tokens
 

@@ -1,0 +1,187 @@
+"""Code predictor: the 15-codebook autoregressive chain per frame, one CUDA graph per batch.
+
+Mirrors ``UniformPredictor`` (continuous.py:20-94): step 0 runs the talker
+hidden state and the semantic code's embedding as two tokens at positions
+[0, 1] with a causal mask; step i runs the embedding of code i (codebook i-1
+table) at position i+1; head i samples code i+1 from ``draws[:, i+1]``
+(the request's uniform table) or from Philox (seed, per-row stream offset).
+With ``graph_embeddings`` the frame embedding (talker codec embedding of the
+semantic code plus the 15 predictor embeddings, summed once, plus the text
+embedding) is produced in the same graph (continuous.py:63-67, 590-601).
+
+All 15 steps x 5 layers and the sampling run as ~675 kernels from
+``libq3t_b200.so`` replayed as one graph; the RoPE coefficients of the 16
+fixed positions are precomputed (fixed_predictor_rotary.py).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib, ops
+from .config import PredictorConfig
+from .talker import rope_tables
+from .weights import pack_decoder
+
+BF16 = torch.bfloat16
+
+
+class PredictorStep:
+    def __init__(self, cfg: PredictorConfig, weights: dict, talker_embedding: torch.Tensor, batch: int, device, *,
+                 temperature: float = 0.9, top_k: int = 50, top_p: float = 1.0, philox_seed=None,
+                 record_logits: bool = False):
+        self.cfg, self.w, self.batch = cfg, weights, batch
+        self.device = torch.device(device)
+        self.talker_embedding = talker_embedding
+        self.temperature, self.top_k, self.top_p = temperature, top_k, top_p
+        self.philox_seed = philox_seed
+        dev, B, Hp, Ht = self.device, batch, cfg.hidden, cfg.talker_hidden
+        positions = cfg.groups + 1
+        self.cos, self.sin = rope_tables(positions, cfg.head_dim, cfg.theta, dev)
+        self.inputs = torch.zeros(B, 2, Ht, dtype=BF16, device=dev)          # (hidden, first)
+        self.draws = torch.full((B, 16), 0.5, dtype=torch.float32, device=dev)
+        self.offsets = torch.zeros(B, dtype=torch.long, device=dev)         # Philox stream per row
+        self.codes = torch.zeros(B, cfg.groups + 1, dtype=torch.long, device=dev)
+        self.text = torch.zeros(B, Ht, dtype=BF16, device=dev)
+        self.embeds = torch.zeros(B, Ht, dtype=BF16, device=dev)            # next talker input
+        self.x = torch.zeros(2 * B, Hp, dtype=BF16, device=dev)
+        self.xn = torch.zeros(2 * B, Hp, dtype=BF16, device=dev)
+        self.qkv = torch.zeros(2 * B, cfg.qkv_width, dtype=BF16, device=dev)
+        self.q = torch.zeros(2 * B, cfg.q_heads, cfg.head_dim, dtype=BF16, device=dev)
+        self.attn = torch.zeros(2 * B, cfg.q_heads, cfg.head_dim, dtype=BF16, device=dev)
+        self.act = torch.zeros(2 * B, cfg.ffn, dtype=BF16, device=dev)
+        self.e = torch.zeros(B, Ht, dtype=BF16, device=dev)
+        self.logits = torch.zeros(B, cfg.vocab, dtype=torch.float32, device=dev)
+        # optional per-step logits (parity checks); the head GEMMs write there directly
+        self.step_logits = (torch.zeros(cfg.groups, B, cfg.vocab, dtype=torch.float32, device=dev)
+                            if record_logits else None)
+        self.cache = torch.zeros(2 * cfg.layers, B, cfg.kv_heads, positions, cfg.head_dim, dtype=BF16, device=dev)
+        self.pos0 = torch.tensor([0, 1] * B, dtype=torch.long, device=dev)
+        self.pos = torch.arange(2, positions, dtype=torch.long, device=dev).view(-1, 1).repeat(1, B).contiguous()
+        gemms = [(Ht, Hp), (Hp, cfg.qkv_width), (cfg.q_width, Hp), (Hp, 2 * cfg.ffn), (cfg.ffn, Hp), (Hp, cfg.vocab)]
+        need = max(ops.linear_workspace_bytes(2 * B, k, n) for k, n in gemms)
+        self.ws_linear = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
+        need = ops.decode_attention_workspace_bytes(2 * B, cfg.q_heads, cfg.head_dim, positions)
+        self.ws_attn = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
+        self.status = ops.status_word(dev)
+        self.graph = None
+
+    def _layers(self, rows: int, length: int, positions: torch.Tensor) -> None:
+        cfg, lw = self.cfg, ops.linear
+        x = self.x[:rows]
+        L = cfg.layers
+        for i, layer in enumerate(self.w["layers"]):
+            keys, values = self.cache[i], self.cache[L + i]
+            ops.rms_norm(x, layer.input_norm, cfg.eps, out=self.xn[:rows])
+            lw(self.xn[:rows], layer.qkv, out=self.qkv[:rows], workspace=self.ws_linear)
+            ops.qk_norm_rope_kv(self.qkv[:rows], layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin, positions,
+                                positions, keys, values, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads,
+                                head_dim=cfg.head_dim, length=length, query_out=self.q[:rows])
+            ops.decode_attention(self.q[:rows], keys, values, positions, context=keys.shape[2], rows_per_slot=length,
+                                 out=self.attn[:rows], workspace=self.ws_attn)
+            lw(self.attn[:rows].view(rows, cfg.q_width), layer.o, out=x, epilogue=_lib.EPI_RESIDUAL, residual=x,
+               workspace=self.ws_linear)
+            ops.rms_norm(x, layer.post_norm, cfg.eps, out=self.xn[:rows])
+            lw(self.xn[:rows], layer.gate_up, out=self.act[:rows], epilogue=_lib.EPI_SWIGLU_PAIRED,
+               workspace=self.ws_linear)
+            lw(self.act[:rows], layer.down, out=x, epilogue=_lib.EPI_RESIDUAL, residual=x, workspace=self.ws_linear)
+        ops.rms_norm(x, self.w["norm"], cfg.eps, out=self.xn[:rows])
+
+    def _logits(self, step: int) -> torch.Tensor:
+        return self.logits if self.step_logits is None else self.step_logits[step]
+
+    def _sample(self, step: int) -> None:
+        tokens = self.codes[:, step + 1]
+        logits = self._logits(step)
+        if self.philox_seed is None:
+            ops.sample(logits, uniforms=self.draws[:, step + 1], temperature=self.temperature, top_k=self.top_k,
+                       top_p=self.top_p, tokens=tokens)
+        else:
+            ops.sample(logits, seed=self.philox_seed, philox_offsets=self.offsets, philox_add=step,
+                       temperature=self.temperature, top_k=self.top_k, top_p=self.top_p, tokens=tokens)
+
+    def compute(self) -> None:
+        cfg, w, B, lw = self.cfg, self.w, self.batch, ops.linear
+        lw(self.inputs.view(2 * B, cfg.talker_hidden), w["proj"], w["proj_bias"], out=self.x, workspace=self.ws_linear)
+        self._layers(2 * B, 2, self.pos0)
+        last = self.xn.view(B, 2, cfg.hidden)[:, 1]
+        lw(last, w["heads"][0], out=self._logits(0), out_dtype=torch.float32, workspace=self.ws_linear)
+        self._sample(0)
+        for step in range(1, cfg.groups):
+            ops.embedding(self.codes[:, step], w["embeddings"][step - 1], out=self.e)
+            lw(self.e, w["proj"], w["proj_bias"], out=self.x[:B], workspace=self.ws_linear)
+            self._layers(B, 1, self.pos[step - 1])
+            lw(self.xn[:B], w["heads"][step], out=self._logits(step), out_dtype=torch.float32, workspace=self.ws_linear)
+            self._sample(step)
+        ops.frame_embed(self.codes, self.talker_embedding, w["embeddings"], self.text, out=self.embeds)
+
+    @torch.inference_mode()
+    def capture(self, warmup: int = 2) -> None:
+        stream = torch.cuda.Stream(device=self.device)
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                self.compute()
+        torch.cuda.current_stream().wait_stream(stream)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=stream):
+            self.compute()
+        torch.cuda.synchronize()
+
+    @torch.inference_mode()
+    def run(self, hidden, first_codes, draws=None, text=None, offsets=None, clone: bool = True):
+        """hidden [B, Ht]; first_codes [B] semantic codes -> (codes [B, 16], talker input embeddings [B, Ht])."""
+        B = self.batch
+        self.inputs[:, 0].copy_(hidden)
+        ops.embedding(first_codes.view(-1), self.talker_embedding, out=self.inputs[:, 1])
+        self.codes[:, 0].copy_(first_codes.view(-1))
+        if draws is not None:
+            self.draws.copy_(draws)
+        if offsets is not None:
+            self.offsets.copy_(offsets)
+        if text is not None:
+            self.text.copy_(text)
+        if self.graph is None:
+            self.compute()
+        else:
+            self.graph.replay()
+        if clone:
+            return self.codes.clone(), self.embeds.clone()
+        return self.codes, self.embeds
+
+    def close(self) -> None:
+        if self.graph is not None:
+            torch.cuda.synchronize()
+            self.graph.reset()
+            self.graph = None
+
+
+class CodePredictor:
+    """Predictor weights plus one captured chain per batch size (UniformPredictor.captures)."""
+
+    def __init__(self, cfg: PredictorConfig, weights: dict, talker_embedding: torch.Tensor, device, packed=False,
+                 use_graphs=True, **sampling):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.weights = weights if packed else pack_decoder(weights, self.device)
+        self.talker_embedding = talker_embedding
+        self.use_graphs = use_graphs
+        self.sampling = sampling
+        self.captures: dict[int, PredictorStep] = {}
+
+    def step_for(self, batch: int) -> PredictorStep:
+        step = self.captures.get(batch)
+        if step is None:
+            step = PredictorStep(self.cfg, self.weights, self.talker_embedding, batch, self.device, **self.sampling)
+            if self.use_graphs:
+                step.capture()
+            self.captures[batch] = step
+        return step
+
+    def run(self, hidden, first_codes, draws=None, text=None, offsets=None):
+        return self.step_for(hidden.shape[0]).run(hidden, first_codes, draws=draws, text=text, offsets=offsets)
+
+    def close(self) -> None:
+        for step in self.captures.values():
+            step.close()
+        self.captures.clear()

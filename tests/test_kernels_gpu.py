@@ -323,6 +323,27 @@ def test_decode_attention_ignores_poisoned_tail(ops, cuda):
     torch.testing.assert_close(out.cpu().float(), ref, atol=2e-2, rtol=0)
 
 
+def test_decode_attention_rows_per_slot_and_window(ops, cuda):
+    # predictor first step: 2 query rows per slot at positions (0, 1) - a 2x2 causal mask
+    B, Hq, Hkv, D, cap = 6, 16, 8, 128, 16
+    keys = rnd(110, (B, Hkv, cap, D), 1.0, BF16)
+    values = rnd(111, (B, Hkv, cap, D), 1.0, BF16)
+    q = rnd(112, (2 * B, Hq, D), 1.0, BF16)
+    pos = torch.tensor([0, 1] * B)
+    ref = KV.decode_attention(q, keys, values, pos, rows_per_slot=2)
+    out = ops.decode_attention(q.to(cuda), keys.to(cuda), values.to(cuda), pos.to(cuda), rows_per_slot=2)
+    torch.testing.assert_close(out.cpu().float(), ref, atol=2e-2, rtol=0)
+    # codec transformer: head_dim 64, 8 heads, sliding window 72 over a long history
+    B, H, D, cap = 4, 8, 64, 300
+    keys = rnd(113, (B, H, cap, D), 1.0, BF16)
+    values = rnd(114, (B, H, cap, D), 1.0, BF16)
+    q = rnd(115, (B * 3, H, D), 1.0, BF16)
+    pos = torch.tensor([0, 50, 71, 72, 140, 299, 5, 100, 200, 71, 72, 73])
+    ref = KV.decode_attention(q, keys, values, pos, rows_per_slot=3, window=72)
+    out = ops.decode_attention(q.to(cuda), keys.to(cuda), values.to(cuda), pos.to(cuda), rows_per_slot=3, window=72)
+    torch.testing.assert_close(out.cpu().float(), ref, atol=2e-2, rtol=0)
+
+
 # ------------------------------------------------------------------ sampling
 def boundary_free(tokens_a, tokens_b, limit=1):
     return int((tokens_a != tokens_b).sum()) <= limit
