@@ -69,8 +69,9 @@ def test_tiny_talker_step_matches_oracle(cuda, use_graph):
         for b, p in enumerate(positions):
             torch.testing.assert_close(engine.arena.keys[layer][b, :, p].float().cpu(), cache_b[layer][0][b, :, p],
                                        atol=2e-2, rtol=2e-2)
-            assert torch.equal(engine.arena.values[layer][b, :, p].float().cpu(),
-                               cache_b[layer][1][b, :, p].to(BF16).float())
+            # V is the bf16 GEMM output: equal up to one bf16 rounding of a reordered fp32 sum
+            torch.testing.assert_close(engine.arena.values[layer][b, :, p].float().cpu(),
+                                       cache_b[layer][1][b, :, p], atol=1e-2, rtol=2 ** -7)
     engine.close()
 
 
