@@ -371,3 +371,116 @@ extern "C" int q3t_decode_attention(const void* query, const void* keys, const v
   return fail(Q3T_EUNSUPPORTED, "attention: head_dim %lld with %lld query heads per kv head", (long long)head_dim,
               (long long)g);
 }
+
+// ======================================================================
+// Allocation-free variant.
+//
+// Some callers cannot allocate device memory at all: a host runtime that
+// owns a fixed, pre-reserved memory pool, a foreign-language embedding that
+// links this library but has no CUDA allocator of its own, or code running
+// while allocation is forbidden. For them the split-KV scratch (tickets and
+// chunk partials) lives in one file-scope device array of fixed size instead
+// of a caller workspace. Every GPU that loads this library holds the array
+// (4 MiB) until the process exits.
+//
+// The array is shared by every call on a device and keeps the previous
+// call's contents; each call clears the tickets it uses before its kernel
+// runs. Calls whose kernels overlap on the GPU (different streams, no
+// ordering between them) race on the array and must not be issued.
+// ======================================================================
+#include <mutex>
+
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(4) << 20;  // 4 MiB
+constexpr size_t kStaticTickets = 16384;                  // first 64 KiB
+constexpr size_t kStaticTicketBytes = kStaticTickets * sizeof(unsigned);
+
+__device__ __align__(256) unsigned char g_attention_scratch[kStaticScratchBytes];
+
+std::mutex g_static_mutex;
+void* g_static_address[64] = {nullptr};
+
+// Device address of g_attention_scratch on the current device. The first call
+// on a device resolves it with cudaGetSymbolAddress (that device current).
+int static_scratch(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(Q3T_ECUDA, "attention (no-alloc): no current CUDA device");
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  if (g_static_address[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_attention_scratch);
+    if (err != cudaSuccess || p == nullptr)
+      return fail(Q3T_ECUDA, "attention (no-alloc): cudaGetSymbolAddress failed: %s", cudaGetErrorString(err));
+    g_static_address[dev] = p;
+  }
+  *out = g_static_address[dev];
+  return Q3T_OK;
+}
+
+template <int D, int G>
+int launch_attn_static(const void* q, const void* k, const void* v, const int64_t* pos, void* out, int64_t rows,
+                       int64_t rows_per_slot, int64_t kv_heads, int64_t capacity, int64_t context, int64_t window,
+                       float scale, unsigned* status, void* stream) {
+  using C = AttnCfg<D, G>;
+  const int64_t span = window > 0 && window < context ? window : context;
+  const int chunk = pick_chunk(rows, kv_heads, span);
+  const int max_chunks = int((span + chunk - 1) / chunk);
+  const size_t tickets = size_t(rows) * size_t(kv_heads);
+  const size_t partial_bytes = tickets * size_t(max_chunks) * C::kPart * sizeof(float);
+  if (tickets > kStaticTickets || kStaticTicketBytes + partial_bytes > kStaticScratchBytes)
+    return fail(Q3T_ESPACE,
+                "attention (no-alloc): needs %zu tickets and %zu partial bytes; the static scratch holds %zu tickets "
+                "and %zu bytes",
+                tickets, partial_bytes, kStaticTickets, kStaticScratchBytes - kStaticTicketBytes);
+  void* base = nullptr;
+  int rc = static_scratch(&base);
+  if (rc != Q3T_OK) return rc;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(decode_attention_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
+        cudaSuccess)
+      return check_cuda("attention (no-alloc): set smem");
+    configured[dev] = true;
+  }
+  if (cudaMemsetAsync(base, 0, tickets * sizeof(unsigned), as_stream(stream)) != cudaSuccess)
+    return check_cuda("attention (no-alloc): clear tickets");
+  unsigned* counters = static_cast<unsigned*>(base);
+  float* partials = reinterpret_cast<float*>(static_cast<char*>(base) + kStaticTicketBytes);
+  return launch(decode_attention_kernel<D, G>, dim3(max_chunks, unsigned(kv_heads), unsigned(rows)), dim3(128),
+                size_t(C::kSmem), stream, false, "decode_attention_noalloc", static_cast<const __nv_bfloat16*>(q),
+                static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), pos,
+                static_cast<__nv_bfloat16*>(out), int(kv_heads), capacity, context, int(window), int(rows_per_slot),
+                chunk, scale * kLog2e, partials, counters, max_chunks, status);
+}
+
+}  // namespace
+
+extern "C" int q3t_decode_attention_noalloc(const void* query, const void* keys, const void* values,
+                                            const int64_t* positions, void* out, int64_t rows, int64_t rows_per_slot,
+                                            int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t capacity,
+                                            int64_t context, int64_t window, float scale, unsigned* status,
+                                            void* stream) {
+  if (!query || !keys || !values || !positions || !out) return fail(Q3T_EINVAL, "attention (no-alloc): null pointer");
+  if (rows < 1 || rows > 65535 || rows_per_slot < 1 || rows % rows_per_slot || kv_heads < 1 || kv_heads > 65535 ||
+      q_heads % kv_heads || window < 0)
+    return fail(Q3T_EINVAL, "attention (no-alloc): invalid row or head geometry");
+  if (context < 1 || context > capacity) return fail(Q3T_EINVAL, "Attention context must fit the KV arena");
+  if (!aligned16(keys) || !aligned16(values) || !aligned16(query))
+    return fail(Q3T_EINVAL, "attention (no-alloc): 16-byte alignment");
+  const int64_t g = q_heads / kv_heads;
+#define Q3T_ATTN_STATIC(DD, GG)                                                                                \
+  if (head_dim == DD && g == GG)                                                                               \
+    return launch_attn_static<DD, GG>(query, keys, values, positions, out, rows, rows_per_slot, kv_heads,    \
+                                      capacity, context, window, scale, status, stream);
+  Q3T_ATTN_STATIC(128, 2)
+  Q3T_ATTN_STATIC(128, 1)
+  Q3T_ATTN_STATIC(64, 1)
+  Q3T_ATTN_STATIC(64, 2)
+#undef Q3T_ATTN_STATIC
+  return fail(Q3T_EUNSUPPORTED, "attention (no-alloc): head_dim %lld with %lld query heads per kv head",
+              (long long)head_dim, (long long)g);
+}
