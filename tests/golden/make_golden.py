@@ -23,6 +23,7 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parents[1]))
+sys.path.insert(0, str(HERE.parents[1] / "qwen3-tts-rsi-engine_b200"))
 from tests.golden.inputs import bf16_scores, normal, uniform  # noqa: E402
 
 
@@ -145,6 +146,59 @@ def main(reference: str) -> None:
     np.savez_compressed(HERE / "decode_path.npz", **arrays)
     (HERE / "decode_path.json").write_text(json.dumps(out, indent=1) + "\n")
     print("wrote", HERE / "decode_path.npz", HERE / "decode_path.json")
+    codec_fixtures()
+
+
+TINY_CODEC = dict(codebooks=4, codebook_size=32, codebook_dim=8, semantic_codebooks=1, latent=12, hidden=8,
+                  layers=2, heads=2, head_dim=4, ffn=16, window=6, eps=1e-5, theta=10000.0,
+                  upsampling_ratios=(2,), upsample_rates=(2, 3), decoder_dim=8, layer_scale=0.1)
+CODEC_SCHEDULE = {0: [2, 2, 4, 8, 4], 1: [1, 3, 8, 8]}
+
+
+def codec_fixtures() -> None:
+    """Run the reference's slot-indexed incremental codec (CodecSlots / CodecSlotGraph.compute,
+    IncrementalCodec.run_module) over the oracle's stand-in decoder modules, two interleaved
+    streams with ragged chunks, a slot move and a reset."""
+    from qwen3_tts_engine.codec_slots import CodecSlotGraph, CodecSlots
+    from oracle.codec import CodecDecoder, randomize
+    from qwen3_tts_b200.config import CodecConfig
+
+    cfg = CodecConfig(**TINY_CODEC)
+    decoder = randomize(CodecDecoder(cfg), seed=5)
+    slots = CodecSlots(decoder, 4)
+    codes = {s: torch.from_numpy((uniform(60 + s, (1, cfg.codebooks, 20)) * cfg.codebook_size).astype(np.int64))
+             for s in CODEC_SCHEDULE}
+    slot_of = {0: 1, 1: 3}
+    done = {0: 0, 1: 0}
+    pcm = {0: [], 1: []}
+    graphs = {}
+    with torch.inference_mode():
+        for step in range(max(len(v) for v in CODEC_SCHEDULE.values())):
+            for stream, sched in CODEC_SCHEDULE.items():
+                if step >= len(sched):
+                    continue
+                n = sched[step]
+                graph = graphs.setdefault(n, CodecSlotGraph(slots, 1, n))
+                graph.indices.copy_(torch.tensor([slot_of[stream]]))
+                graph.codes.copy_(codes[stream][:, :, done[stream]:done[stream] + n])
+                pcm[stream].append(graph.compute().clone())
+                done[stream] += n
+            if step == 1:  # compaction: stream 1 moves from slot 3 to slot 2 (CodecSlots.move)
+                slots.move(3, 2)
+                slot_of[1] = 2
+        full = {s: decoder(codes[s]) for s in CODEC_SCHEDULE}
+        # a reset slot decodes like a fresh stream
+        slots.reset(slot_of[0])
+        graph = graphs[4]
+        graph.indices.copy_(torch.tensor([slot_of[0]]))
+        graph.codes.copy_(codes[1][:, :, :4])
+        fresh = graph.compute().clone()
+    arrays = {f"codec_pcm_{s}": torch.cat(pcm[s], -1).numpy() for s in pcm}
+    arrays.update({f"codec_full_{s}": full[s].numpy() for s in full})
+    arrays["codec_fresh_after_reset"] = fresh.numpy()
+    arrays["codec_frames"] = slots.frames.numpy()
+    np.savez_compressed(HERE / "codec.npz", **arrays)
+    print("wrote", HERE / "codec.npz")
 
 
 if __name__ == "__main__":
