@@ -319,6 +319,15 @@ def run_b200(args, dist: Dist):
     e2e_ms = dist.max(e0.elapsed_time(e1))
     h2d = host_in.numel() * 2 + host_pos.numel() * 8 * 2
     d2h = host_tok.numel() * 8
+    if os.environ.get("Q3T_BENCH_DIAG"):
+        for name, g in (("tick_graph", graph), ("step_graph", e2e_graph)):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(args.steps):
+                g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            print(json.dumps({"diag": name, "ms_per_replay": a.elapsed_time(b) / args.steps}), file=sys.stderr)
 
     # ---- roofline of the dominant kernels, timed alone with L2 flushed between launches
     kernels = kernel_rooflines(cfg, engine, step, positions_at_start, dev)

@@ -45,8 +45,10 @@ enum { Q3T_BF16 = 0, Q3T_F32 = 1 };
 enum {
   Q3T_EPI_STORE = 0,        /* out = acc (+ bias), rounded to out dtype */
   Q3T_EPI_RESIDUAL = 1,     /* out = bf16(residual + bf16(acc)) */
-  Q3T_EPI_SWIGLU_PAIRED = 2 /* rows of each 128-row weight tile are [64 gate; 64 up];
+  Q3T_EPI_SWIGLU_PAIRED = 2,/* rows of each 128-row weight tile are [64 gate; 64 up];
                                out[:, f] = bf16(bf16(silu(gate_f)) * up_f) */
+  Q3T_EPI_RESIDUAL_SCALED = 3,/* out = bf16(residual + bf16(scale[n] * bf16(acc + bias))) */
+  Q3T_EPI_GELU = 4          /* out = bf16(gelu_erf(bf16(acc + bias))) */
 };
 
 /* RMSNorm rounding modes. */
@@ -143,22 +145,27 @@ int q3t_snake(const void* x, const void* alpha, const void* inverse_beta, void* 
 /* Replaces torch.nn.functional.linear at qwen3_tts_engine/packed_attention.py:42,85,
  * qwen3_tts_engine/packed_mlp.py:20,27 and the codec head at continuous.py:613.
  * out[r, n] = epilogue(sum_k x[r, k] * weight[n, k] (+ bias[n])). tcgen05 GEMM,
- * weights as the 128-row UMMA operand, rows as N, split-K across SMs.
+ * weights as the 128-row UMMA operand, rows as N, split-K over a thread-block
+ * cluster reduced through distributed shared memory (workspace unused; may be NULL).
+ * Also the codec's convolutions (im2col rows from q3t_conv_gather), its
+ * ConvNeXt pointwise layers (GELU / scaled-residual epilogues) and the layer-scaled
+ * residuals of its transformer.
  * x, weight, bias, residual: bf16; out: bf16 or fp32 (Q3T_EPI_STORE only).
  * Alignment: base pointers 16 B, row strides multiples of 8 elements. */
 size_t q3t_linear_workspace_bytes(int64_t rows, int64_t in_features, int64_t out_features);
 int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t in_features,
                const void* weight, int64_t out_features, const void* bias, void* out,
                int64_t out_stride, int out_dtype, int epilogue, const void* residual,
-               int64_t residual_stride, void* workspace, size_t workspace_bytes, unsigned* status,
-               void* stream);
+               int64_t residual_stride, const void* scale, void* workspace, size_t workspace_bytes,
+               unsigned* status, void* stream);
 
 /* ------------------------------------------------------------------ attention */
 
 /* Replaces the q_norm/k_norm, rotary and cache update of
  * qwen3_tts_engine/packed_attention.py:42-74 (text-only rotary, decode and prefill rows).
  * qkv: [rows, (q_heads + 2*kv_heads)*head_dim] bf16 (row stride qkv_stride);
- * row r belongs to slot r / length and sequence offset r % length.
+ * row r belongs to slot r / length (or slots[r / length] when the slot table is given)
+ * and sequence offset r % length. Null norm weights skip the head norms (codec).
  * cos/sin tables: [table_len, head_dim] bf16; rotary_positions[r] indexes them.
  * cache_positions[r]: KV write position of row r in target [slots, kv_heads, capacity, head_dim].
  * query_out: [rows, q_heads, head_dim]. */
@@ -166,9 +173,9 @@ int q3t_qk_norm_rope_kv(const void* qkv, int64_t qkv_stride, const void* q_norm_
                         const void* k_norm_weight, float eps, const void* cos_table,
                         const void* sin_table, int64_t table_len, const int64_t* rotary_positions,
                         const int64_t* cache_positions, void* query_out, void* target_keys,
-                        void* target_values, int64_t rows, int64_t length, int64_t q_heads,
-                        int64_t kv_heads, int64_t head_dim, int64_t capacity, unsigned* status,
-                        void* stream);
+                        void* target_values, int64_t rows, int64_t length, const int64_t* slots,
+                        int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t capacity,
+                        unsigned* status, void* stream);
 
 /* Replaces torch_npu.npu_fused_infer_attention_score at qwen3_tts_engine/npu_attention.py:21
  * (and SDPA over SlotCache, continuous.py:188-198; the predictor's causal
@@ -176,16 +183,21 @@ int q3t_qk_norm_rope_kv(const void* qkv, int64_t qkv_stride, const void* q_norm_
  * codec_slots.py:73-77). query rows [rows, q_heads, head_dim] bf16; row r
  * reads slot r / rows_per_slot of keys/values [slots, kv_heads, capacity, head_dim]
  * (bf16, contiguous) and sees keys max(0, p - window + 1) .. p with
- * p = positions[r] (window 0 = unbounded). context bounds the grid
- * (positions < context <= capacity). out [rows, q_heads, head_dim] bf16.
+ * p = positions[r] (window 0 = unbounded). With a slot table, row r reads
+ * slot slots[r / rows_per_slot]. ring > 0 makes the arena a ring of `ring`
+ * rows (capacity == ring): position p lives in row p % ring, positions are
+ * unbounded and 1 <= window <= ring (the codec's KV tail, codec_slots.py:27-39).
+ * Otherwise context bounds the grid (positions < context <= capacity).
+ * out [rows, q_heads, head_dim] bf16.
  * Split-KV with an in-kernel combine. */
 size_t q3t_decode_attention_workspace_bytes(int64_t rows, int64_t q_heads, int64_t head_dim,
                                             int64_t context);
 int q3t_decode_attention(const void* query, const void* keys, const void* values,
                          const int64_t* positions, void* out, int64_t rows, int64_t rows_per_slot,
-                         int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t capacity,
-                         int64_t context, int64_t window, float scale, void* workspace,
-                         size_t workspace_bytes, unsigned* status, void* stream);
+                         const int64_t* slots, int64_t ring, int64_t q_heads, int64_t kv_heads,
+                         int64_t head_dim, int64_t capacity, int64_t context, int64_t window,
+                         float scale, void* workspace, size_t workspace_bytes, unsigned* status,
+                         void* stream);
 
 /* No counterpart in the reference: an allocation-free form of
  * q3t_decode_attention for callers that cannot allocate device memory (a
@@ -264,6 +276,53 @@ int q3t_scatter_rows(void* target, int64_t target_rows, const int64_t* indices,
                      const void* source, int ndim, const int64_t* source_shape,
                      const int64_t* source_strides, int elem_size, unsigned* status,
                      void* stream);
+
+/* ------------------------------------------------------------------ incremental codec */
+
+/* Replaces CachedQuantizer.decode (qwen3_tts_engine/cached_quantizer.py:17-30) up to
+ * the output projections: out[(b,t)] = [sum_{q<semantic} table_q[code] | sum_{q>=semantic}
+ * table_q[code]] (fp32 sums in codebook order, rounded once) as [batch*frames, 2*dim] bf16;
+ * tables: pre-normalised codebooks [codebooks, bins, dim] bf16. The caller applies
+ * [W_first | W_rest] with q3t_linear. codes: int64 with element strides (batch, codebook, frame). */
+int q3t_rvq_gather(const int64_t* codes, int64_t b_stride, int64_t cb_stride, int64_t t_stride,
+                   const void* tables, int64_t codebooks, int64_t semantic, int64_t bins,
+                   int64_t dim, int64_t batch, int64_t frames, void* out, unsigned* status,
+                   void* stream);
+
+/* Replaces the causal-conv history concat of IncrementalCodec.run_module
+ * (qwen3_tts_engine/incremental_codec.py:53-65) and the SnakeBeta that precedes a conv
+ * (snake_triton_ascend.py, incremental_codec.py:42-49): im2col rows
+ * col[(b,t), j*C + c] = snake(src(b, t - shift_j, c)) with shift_j = (taps-1-j)*dilation
+ * (reverse = 0) or j*dilation (reverse = 1, transposed convs: [x[t] | x[t-1]]);
+ * negative times read history [slots, history_len, C] of slot slots[b] (or b).
+ * x: time-major [batch, frames, C] (row stride x_stride); alpha/inverse_beta nullable. */
+int q3t_conv_gather(const void* x, int64_t x_stride, int64_t batch, int64_t frames,
+                    int64_t channels, const void* history, int64_t history_len,
+                    const int64_t* slots, int64_t taps, int64_t dilation, int reverse,
+                    const float* alpha, const float* inverse_beta, void* col, void* stream);
+
+/* history = last history_len frames of [history | x] per slot (incremental_codec.py:62). */
+int q3t_conv_history(const void* x, int64_t x_stride, int64_t batch, int64_t frames,
+                     int64_t channels, void* history, int64_t history_len, const int64_t* slots,
+                     void* stream);
+
+/* ConvNeXt depthwise causal conv (kernel 7, history 6) + LayerNorm over channels
+ * (incremental_codec.py:80-84): out [batch*frames, C] bf16. Weights fp32. */
+int q3t_dwconv_layernorm(const void* x, int64_t batch, int64_t frames, int64_t channels,
+                         const void* history, int64_t history_len, const int64_t* slots,
+                         const float* weight, const float* bias, const float* ln_weight,
+                         const float* ln_bias, float eps, void* out, void* stream);
+
+/* Frame positions of a codec chunk (codec_slots.py:70-72, 98): for rows (b, t),
+ * rotary = frames[slot_b] + t, cache = (frames[slot_b] + t) % ring (ring 0: no modulo);
+ * advance != 0 then adds `frames` to frames[slot_b]. */
+int q3t_codec_positions(int64_t* frames_by_slot, const int64_t* slots, int64_t batch,
+                        int64_t frames, int64_t ring, int64_t* rotary_positions,
+                        int64_t* cache_positions, int advance, void* stream);
+
+/* PCM conversion of qwen3_tts_engine/continuous.py:510,535 on the device:
+ * wave = clip(x, -1, 1) (fp32, nullable), pcm = int16(wave * 32767) (nullable). */
+int q3t_pcm16(const void* x, int64_t count, float* wave, int16_t* pcm, void* stream);
 
 #ifdef __cplusplus
 }

@@ -51,7 +51,8 @@ __global__ void __launch_bounds__(128)
     decode_attention_kernel(const __nv_bfloat16* __restrict__ query, const __nv_bfloat16* __restrict__ keys,
                             const __nv_bfloat16* __restrict__ values, const int64_t* __restrict__ positions,
                             __nv_bfloat16* __restrict__ out, int kv_heads, int64_t capacity, int64_t context,
-                            int window, int rows_per_slot, int chunk, float qscale, float* __restrict__ partials,
+                            int window, int rows_per_slot, const int64_t* __restrict__ slots, int64_t ring,
+                            int chunk, float qscale, float* __restrict__ partials,
                             unsigned* __restrict__ counters,
                             int max_chunks, unsigned* status) {
   using C = AttnCfg<D, G>;
@@ -74,7 +75,8 @@ __global__ void __launch_bounds__(128)
   grid_dependency_wait();
 
   int64_t pos = positions[b];
-  if (pos < 0 || pos >= context) {
+  // linear arenas hold positions [0, context); ring arenas any position >= 0
+  if (pos < 0 || (ring == 0 && pos >= context)) {
     if (c == 0 && h == 0 && threadIdx.x == 0) raise_status(status, kStatusBadIndex);
     pos = pos < 0 ? 0 : context - 1;
   }
@@ -86,7 +88,8 @@ __global__ void __launch_bounds__(128)
   const int64_t k_begin = k_lo + int64_t(c) * chunk;
   const int64_t k_end = (k_begin + chunk) < nkeys ? (k_begin + chunk) : nkeys;
   const int ntiles = int((k_end - k_begin + C::kTK - 1) / C::kTK);
-  const int slot = b / rows_per_slot;  // query row b reads the keys of its slot
+  // query row b reads the keys of its slot (through the slot table when given)
+  const int64_t slot = slots != nullptr ? slots[b / rows_per_slot] : int64_t(b / rows_per_slot);
   const size_t head_base = (size_t(slot) * kv_heads + h) * size_t(capacity) * D;
 
   if (threadIdx.x == 0) {
@@ -101,8 +104,20 @@ __global__ void __launch_bounds__(128)
     const uint32_t bytes = uint32_t(n) * D * 2;
     uint64_t* bar = &bars[t & 1];
     mbar_expect_tx(bar, 2 * bytes);
-    bulk_load(kt[t & 1], keys + head_base + size_t(t0) * D, bytes, bar);
-    bulk_load(vt[t & 1], values + head_base + size_t(t0) * D, bytes, bar);
+    if (ring > 0) {
+      // ring-buffered keys: position p lives in row p % ring; a tile wraps at most once
+      const int64_t start = t0 % ring;
+      const int64_t n1 = (ring - start) < n ? (ring - start) : n;
+      bulk_load(kt[t & 1], keys + head_base + size_t(start) * D, uint32_t(n1) * D * 2, bar);
+      bulk_load(vt[t & 1], values + head_base + size_t(start) * D, uint32_t(n1) * D * 2, bar);
+      if (n > n1) {
+        bulk_load(kt[t & 1] + n1 * D, keys + head_base, uint32_t(n - n1) * D * 2, bar);
+        bulk_load(vt[t & 1] + n1 * D, values + head_base, uint32_t(n - n1) * D * 2, bar);
+      }
+    } else {
+      bulk_load(kt[t & 1], keys + head_base + size_t(t0) * D, bytes, bar);
+      bulk_load(vt[t & 1], values + head_base + size_t(t0) * D, bytes, bar);
+    }
   };
   if (threadIdx.x == 0) {
     issue(0);
@@ -303,8 +318,8 @@ int pick_chunk(int64_t batch, int64_t kv_heads, int64_t context) {
 
 template <int D, int G>
 int launch_attn(const void* q, const void* k, const void* v, const int64_t* pos, void* out, int64_t rows,
-                int64_t rows_per_slot, int64_t kv_heads, int64_t capacity, int64_t context, int64_t window,
-                float scale, void* ws, unsigned* status, void* stream) {
+                int64_t rows_per_slot, const int64_t* slots, int64_t ring, int64_t kv_heads, int64_t capacity,
+                int64_t context, int64_t window, float scale, void* ws, unsigned* status, void* stream) {
   using C = AttnCfg<D, G>;
   const int64_t span = window > 0 && window < context ? window : context;
   const int chunk = pick_chunk(rows, kv_heads, span);
@@ -324,7 +339,7 @@ int launch_attn(const void* q, const void* k, const void* v, const int64_t* pos,
                 size_t(C::kSmem), stream, true, "decode_attention", static_cast<const __nv_bfloat16*>(q),
                 static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), pos,
                 static_cast<__nv_bfloat16*>(out), int(kv_heads), capacity, context, int(window), int(rows_per_slot),
-                chunk, scale * kLog2e, partials, counters, max_chunks, status);
+                slots, ring, chunk, scale * kLog2e, partials, counters, max_chunks, status);
 }
 
 size_t attn_workspace(int64_t batch, int64_t q_heads, int64_t kv_heads_unused, int64_t head_dim, int64_t context) {
@@ -344,15 +359,18 @@ extern "C" size_t q3t_decode_attention_workspace_bytes(int64_t batch, int64_t q_
 }
 
 extern "C" int q3t_decode_attention(const void* query, const void* keys, const void* values, const int64_t* positions,
-                                    void* out, int64_t rows, int64_t rows_per_slot, int64_t q_heads, int64_t kv_heads,
-                                    int64_t head_dim, int64_t capacity, int64_t context, int64_t window, float scale,
-                                    void* workspace, size_t workspace_bytes, unsigned* status, void* stream) {
+                                    void* out, int64_t rows, int64_t rows_per_slot, const int64_t* slots, int64_t ring,
+                                    int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t capacity,
+                                    int64_t context, int64_t window, float scale, void* workspace,
+                                    size_t workspace_bytes, unsigned* status, void* stream) {
   if (!query || !keys || !values || !positions || !out) return fail(Q3T_EINVAL, "attention: null pointer");
   if (rows < 1 || rows > 65535 || rows_per_slot < 1 || rows % rows_per_slot || kv_heads < 1 || kv_heads > 65535 ||
       q_heads % kv_heads || window < 0)
     return fail(Q3T_EINVAL, "attention: invalid row or head geometry");
   if (context < 1 || context > capacity) return fail(Q3T_EINVAL, "Attention context must fit the KV arena");
   if (size_t(rows) * size_t(kv_heads) > kMaxTickets) return fail(Q3T_EUNSUPPORTED, "attention: rows x kv_heads > 65536");
+  if (ring < 0 || (ring > 0 && (ring != capacity || window < 1 || window > ring)))
+    return fail(Q3T_EINVAL, "attention: a ring arena needs capacity == ring and 1 <= window <= ring");
   if (!aligned16(keys) || !aligned16(values) || !aligned16(query))
     return fail(Q3T_EINVAL, "attention: 16-byte alignment");
   const int64_t g = q_heads / kv_heads;
@@ -361,8 +379,8 @@ extern "C" int q3t_decode_attention(const void* query, const void* keys, const v
     return fail(Q3T_ESPACE, "attention: workspace needs %zu bytes", need);
 #define Q3T_ATTN(DD, GG)                                                                                       \
   if (head_dim == DD && g == GG)                                                                               \
-    return launch_attn<DD, GG>(query, keys, values, positions, out, rows, rows_per_slot, kv_heads, capacity, \
-                               context, window, scale, workspace, status, stream);
+    return launch_attn<DD, GG>(query, keys, values, positions, out, rows, rows_per_slot, slots, ring, kv_heads, \
+                               capacity, context, window, scale, workspace, status, stream);
   Q3T_ATTN(128, 2)
   Q3T_ATTN(128, 1)
   Q3T_ATTN(64, 1)
@@ -454,7 +472,8 @@ int launch_attn_static(const void* q, const void* k, const void* v, const int64_
                 size_t(C::kSmem), stream, false, "decode_attention_noalloc", static_cast<const __nv_bfloat16*>(q),
                 static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), pos,
                 static_cast<__nv_bfloat16*>(out), int(kv_heads), capacity, context, int(window), int(rows_per_slot),
-                chunk, scale * kLog2e, partials, counters, max_chunks, status);
+                static_cast<const int64_t*>(nullptr), int64_t(0), chunk, scale * kLog2e, partials, counters,
+                max_chunks, status);
 }
 
 }  // namespace

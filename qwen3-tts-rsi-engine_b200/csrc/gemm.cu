@@ -34,8 +34,13 @@ struct Cfg {
   static constexpr int kBBytes = BN * kTileK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
-  // ring + barriers (2 per stage + done) + tmem slot + flags, plus 1 KB alignment slack
-  static constexpr int kSmem = kStages * kStageBytes + 256 + 1024;
+  static constexpr int kRing = kStages * kStageBytes;
+  // split-K reduce buffer: column-major [BN][128 + 4] fp32 (rows of one batch column contiguous)
+  static constexpr int kRedStride = kTileN + 4;
+  static constexpr int kRedBytes = BN * kRedStride * 4;
+  static constexpr int kMain = kRing > kRedBytes ? kRing : kRedBytes;
+  // main area + barriers (2 per stage + done) + tmem slot + flags, plus 1 KB alignment slack
+  static constexpr int kSmem = kMain + 256 + 1024;
 };
 
 struct GemmArgs {
@@ -46,8 +51,7 @@ struct GemmArgs {
   int out_f32;
   const __nv_bfloat16* residual;
   int64_t res_stride;
-  float* partials;      // [splits][rows][out_features]
-  unsigned* counters;   // [n_tiles * m_tiles]
+  const __nv_bfloat16* scale;  // per-feature scale of Q3T_EPI_RESIDUAL_SCALED
   unsigned* status;
 };
 
@@ -62,6 +66,15 @@ __device__ __forceinline__ void store_out(const GemmArgs& a, int m, int n, float
   if constexpr (EPI == Q3T_EPI_RESIDUAL) {
     const float r = __bfloat162float(a.residual[int64_t(m) * a.res_stride + n]);
     static_cast<__nv_bfloat16*>(a.out)[int64_t(m) * a.out_stride + n] = __float2bfloat16_rn(r + bf16r(acc));
+  } else if constexpr (EPI == Q3T_EPI_RESIDUAL_SCALED) {
+    const float r = __bfloat162float(a.residual[int64_t(m) * a.res_stride + n]);
+    const float g = __bfloat162float(a.scale[n]);
+    static_cast<__nv_bfloat16*>(a.out)[int64_t(m) * a.out_stride + n] =
+        __float2bfloat16_rn(r + bf16r(g * bf16r(acc)));
+  } else if constexpr (EPI == Q3T_EPI_GELU) {
+    const float v = bf16r(acc);
+    static_cast<__nv_bfloat16*>(a.out)[int64_t(m) * a.out_stride + n] =
+        __float2bfloat16_rn(0.5f * v * (1.0f + erff(v * 0.70710678118654752f)));
   } else {
     if (a.out_f32)
       static_cast<float*>(a.out)[int64_t(m) * a.out_stride + n] = bf16r(acc);
@@ -70,6 +83,34 @@ __device__ __forceinline__ void store_out(const GemmArgs& a, int m, int n, float
   }
 }
 
+Q3T_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+Q3T_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+Q3T_DEV uint32_t map_peer(uint32_t local_smem, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_smem), "r"(rank));
+  return remote;
+}
+Q3T_DEV float4 ld_peer4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+// One CTA = 128 weight rows x BN activation rows x one K slice. The CTAs of
+// the K slices of one tile form a thread-block cluster (gridDim.y = splits,
+// a power of two <= 8) and reduce their fp32 accumulators through
+// distributed shared memory: each writes its tile column-major into its own
+// shared memory, then CTA of cluster rank r sums rows [r*128/S, (r+1)*128/S)
+// over all peers in rank order (deterministic) and applies the epilogue.
 template <int BN, int EPI>
 __global__ void __launch_bounds__(128, 1)
     linear_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx, GemmArgs a) {
@@ -77,13 +118,13 @@ __global__ void __launch_bounds__(128, 1)
   constexpr int S = C::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kMain);
   uint64_t* empty = full + S;
   uint64_t* done = empty + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* consumed = abort_flag + 1;  // ring slots the MMA issuer has taken
-  int* ticket = const_cast<int*>(consumed + 1);
+  float* red = reinterpret_cast<float*>(smem);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kTileN;
@@ -92,6 +133,7 @@ __global__ void __launch_bounds__(128, 1)
   const int kb0 = int(int64_t(split) * a.kblocks / a.splits);
   const int kb1 = int(int64_t(split + 1) * a.kblocks / a.splits);
   const int nk = kb1 - kb0;
+  const bool clustered = a.splits > 1;
 
   grid_dependency_launch();
   if (threadIdx.x == 0) {
@@ -118,7 +160,8 @@ __global__ void __launch_bounds__(128, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- TMA producer
+      // ---------------- TMA producer: weight tiles of the first ring slots go out before the
+      // dependency wait (weights never depend on the previous kernel), activations after it.
       const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
       const int pre = nk < S ? nk : S;
       for (int i = 0; i < pre; ++i) {
@@ -126,7 +169,7 @@ __global__ void __launch_bounds__(128, 1)
         tma_load_2d(smem + i * C::kStageBytes, &tmw, &full[i], (kb0 + i) * kTileK, n0, pol_w);
       }
       issued = pre;
-      grid_dependency_wait();  // activations come from the previous kernel
+      grid_dependency_wait();
       for (int i = 0; i < pre; ++i)
         tma_load_2d(smem + i * C::kStageBytes + kABytes, &tmx, &full[i], (kb0 + i) * kTileK, m0, pol_x);
       for (int i = pre; i < nk; ++i) {
@@ -166,12 +209,13 @@ __global__ void __launch_bounds__(128, 1)
   }
   grid_dependency_wait();
 
-  // ---------------- epilogue: TMEM -> registers -> partials / output
+  // ---------------- TMEM -> registers
   const bool ok = mbar_wait(done, 0, a.status, kStatusMmaTimeout);
   tc_fence_after();
-  const int n = n0 + warp * 32 + lane;
+  const int r = warp * 32 + lane;  // tile row (output feature n0 + r)
   const uint32_t taddr = tmem + (uint32_t(warp * 32) << 16);
-  if (a.splits == 1 && EPI != Q3T_EPI_SWIGLU_PAIRED) {
+  if (!clustered && EPI != Q3T_EPI_SWIGLU_PAIRED) {
+    const int n = n0 + r;
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 16) {
       float v[16];
@@ -184,71 +228,79 @@ __global__ void __launch_bounds__(128, 1)
         }
       }
     }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
   } else {
-    float* part = a.partials + int64_t(split) * a.rows * a.out_features;
+    // Failure path first: outstanding ring loads must land before the ring
+    // is reused as the reduce buffer (bounded waits).
+    if (threadIdx.x == 0 && *abort_flag)
+      for (int j = *consumed; j < issued; ++j) mbar_wait(&full[j % S], (j / S) & 1, a.status, kStatusTmaTimeout);
+    __syncthreads();
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 16) {
       float v[16];
       tmem_ld16(taddr + c0, v);
-      if (n < a.out_features) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = m0 + c0 + j;
-          if (m < a.rows) part[int64_t(m) * a.out_features + n] = ok ? v[j] : 0.f;
-        }
-      }
+      for (int j = 0; j < 16; ++j) red[(c0 + j) * C::kRedStride + r] = ok ? v[j] : 0.f;
     }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
   }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
-  if (threadIdx.x == 0 && *abort_flag) {
-    // Failure path: wait (bounded) for ring loads that were issued but never
-    // consumed, so no TMA write lands after this CTA's shared memory is gone.
+  if (threadIdx.x == 0 && !clustered && *abort_flag)
     for (int j = *consumed; j < issued; ++j) mbar_wait(&full[j % S], (j / S) & 1, a.status, kStatusTmaTimeout);
-  }
-  if (a.splits == 1 && EPI != Q3T_EPI_SWIGLU_PAIRED) return;
+  if (!clustered && EPI != Q3T_EPI_SWIGLU_PAIRED) return;
 
-  // ---------------- split-K ticket: the last CTA of this tile reduces
-  __threadfence();
-  __syncthreads();
-  const int tile = blockIdx.z * gridDim.x + blockIdx.x;
-  if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(&a.counters[tile], 1u);
-    *ticket = (prev == unsigned(a.splits - 1)) ? 1 : 0;
-  }
-  __syncthreads();
-  if (*ticket != 1) return;
-  __threadfence();
+  // ---------------- split-K reduction across the cluster through DSMEM
+  if (clustered) cluster_sync();  // every peer's tile is in its shared memory
+  const int cs = a.splits;
+  const uint32_t rank = clustered ? cluster_rank() : 0u;
   const int mcount = (a.rows - m0) < BN ? (a.rows - m0) : BN;
-  const int64_t plane = int64_t(a.rows) * a.out_features;
+  const uint32_t red_local = smem_u32(red);
   if constexpr (EPI == Q3T_EPI_SWIGLU_PAIRED) {
-    const int width = a.out_features / 2;
-    for (int e = threadIdx.x; e < mcount * 64; e += blockDim.x) {
-      const int m = m0 + e / 64, f = e % 64;
-      const int ng = n0 + f, nu = n0 + 64 + f;
-      if (nu >= a.out_features) continue;
-      float g = 0.f, u = 0.f;
-      for (int s = 0; s < a.splits; ++s) {
-        g += __ldcg(a.partials + s * plane + int64_t(m) * a.out_features + ng);
-        u += __ldcg(a.partials + s * plane + int64_t(m) * a.out_features + nu);
+    const int nf = 64 / cs;                    // features of this CTA (multiple of 4)
+    const int f0 = int(rank) * nf;
+    const int units = mcount * (nf / 4);
+    for (int u = threadIdx.x; u < units; u += blockDim.x) {
+      const int c = u / (nf / 4);
+      const int f = f0 + (u % (nf / 4)) * 4;
+      float4 g = make_float4(0.f, 0.f, 0.f, 0.f), up = g;
+      for (int p = 0; p < cs; ++p) {
+        const uint32_t base = clustered ? map_peer(red_local, uint32_t(p)) : red_local;
+        const float4 gv = clustered ? ld_peer4(base + uint32_t(c * C::kRedStride + f) * 4u)
+                                    : *reinterpret_cast<const float4*>(red + c * C::kRedStride + f);
+        const float4 uv = clustered ? ld_peer4(base + uint32_t(c * C::kRedStride + 64 + f) * 4u)
+                                    : *reinterpret_cast<const float4*>(red + c * C::kRedStride + 64 + f);
+        g.x += gv.x; g.y += gv.y; g.z += gv.z; g.w += gv.w;
+        up.x += uv.x; up.y += uv.y; up.z += uv.z; up.w += uv.w;
       }
-      g = bf16r(g);
-      u = bf16r(u);
-      static_cast<__nv_bfloat16*>(a.out)[int64_t(m) * a.out_stride + (n0 / 2 + f)] =
-          __float2bfloat16_rn(silu_gate(g, u));
-      (void)width;
+      const int m = m0 + c;
+      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + int64_t(m) * a.out_stride + (n0 / 2 + f);
+      const float gs[4] = {g.x, g.y, g.z, g.w}, us[4] = {up.x, up.y, up.z, up.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (n0 + 64 + f + j < a.out_features) o[j] = __float2bfloat16_rn(silu_gate(bf16r(gs[j]), bf16r(us[j])));
     }
   } else {
-    for (int e = threadIdx.x; e < mcount * kTileN; e += blockDim.x) {
-      const int m = m0 + e / kTileN, nn = n0 + e % kTileN;
-      if (nn >= a.out_features) continue;
-      float acc = 0.f;
-      for (int s = 0; s < a.splits; ++s) acc += __ldcg(a.partials + s * plane + int64_t(m) * a.out_features + nn);
-      store_out<EPI>(a, m, nn, acc);
+    const int nf = kTileN / cs;
+    const int f0 = int(rank) * nf;
+    const int units = mcount * (nf / 4);
+    for (int u = threadIdx.x; u < units; u += blockDim.x) {
+      const int c = u / (nf / 4);
+      const int f = f0 + (u % (nf / 4)) * 4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int p = 0; p < cs; ++p) {
+        const float4 v = ld_peer4(map_peer(red_local, uint32_t(p)) + uint32_t(c * C::kRedStride + f) * 4u);
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+      }
+      const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (n0 + f + j < a.out_features) store_out<EPI>(a, m0 + c, n0 + f + j, vals[j]);
     }
   }
-  if (threadIdx.x == 0) a.counters[tile] = 0u;
+  if (clustered) cluster_sync();  // peers finished reading this CTA's shared memory
 }
 
 // ---------------------------------------------------------------- host side
@@ -302,12 +354,12 @@ Plan plan(int64_t rows, int64_t in_features, int64_t out_features) {
   p.n_tiles = int((out_features + kTileN - 1) / kTileN);
   p.m_tiles = int((rows + p.bn - 1) / p.bn);
   p.kblocks = int((in_features + kTileK - 1) / kTileK);
+  // K splits: a power of two <= 8 (one thread-block cluster per tile), each
+  // split at least two k-blocks, aiming at ~2 resident CTAs per SM.
   const int base = p.n_tiles * p.m_tiles;
   const int target = 2 * sm_count();
-  int splits = (target + base / 2) / base;
-  const int max_split = p.kblocks / 2 > 1 ? p.kblocks / 2 : 1;
-  if (splits > max_split) splits = max_split;
-  if (splits < 1) splits = 1;
+  int splits = 1;
+  while (splits < 8 && base * splits * 2 <= target + target / 8 && p.kblocks >= 4 * splits) splits *= 2;
   p.splits = splits;
   return p;
 }
@@ -324,8 +376,24 @@ int launch_linear(const Plan& p, const CUtensorMap& tmw, const CUtensorMap& tmx,
       return check_cuda("linear: set smem");
     configured[dev] = true;
   }
-  return launch(linear_kernel<BN, EPI>, dim3(p.n_tiles, p.splits, p.m_tiles), dim3(128), size_t(C::kSmem), stream,
-                true, "linear", tmw, tmx, args);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.n_tiles, p.splits, p.m_tiles);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = size_t(C::kSmem);
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = unsigned(p.splits);
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, linear_kernel<BN, EPI>, tmw, tmx, args);
+  if (err != cudaSuccess) return fail(Q3T_ECUDA, "linear launch failed: %s", cudaGetErrorString(err));
+  note_launch();
+  return Q3T_OK;
 }
 
 template <int EPI>
@@ -339,31 +407,22 @@ int dispatch_bn(const Plan& p, const CUtensorMap& tmw, const CUtensorMap& tmx, c
   }
 }
 
-// Workspace layout: a fixed ticket region (kMaxTiles counters, zero between
-// calls) followed by the fp32 partials. The ticket region never moves, so
-// calls of different shapes sharing one workspace cannot see each other's
-// partials as tickets.
-constexpr size_t kMaxTiles = 16384;
-constexpr size_t kTicketBytes = kMaxTiles * sizeof(unsigned);
-
-size_t workspace_for(const Plan& p, int64_t rows, int64_t out_features) {
-  const size_t partial = size_t(p.splits) * size_t(rows) * size_t(out_features) * sizeof(float);
-  return kTicketBytes + partial;
-}
-
 }  // namespace
 
+// The split-K reduction runs through distributed shared memory: no scratch.
 extern "C" size_t q3t_linear_workspace_bytes(int64_t rows, int64_t in_features, int64_t out_features) {
-  if (rows < 1 || in_features < 1 || out_features < 1) return 0;
-  return workspace_for(plan(rows, in_features, out_features), rows, out_features);
+  (void)rows;
+  (void)in_features;
+  (void)out_features;
+  return 0;
 }
 
 extern "C" int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t in_features, const void* weight,
                           int64_t out_features, const void* bias, void* out, int64_t out_stride, int out_dtype,
-                          int epilogue, const void* residual, int64_t residual_stride, void* workspace,
-                          size_t workspace_bytes, unsigned* status, void* stream) {
+                          int epilogue, const void* residual, int64_t residual_stride, const void* scale,
+                          void* workspace, size_t workspace_bytes, unsigned* status, void* stream) {
   if (!x || !weight || !out) return fail(Q3T_EINVAL, "linear: null pointer");
-  if (rows < 1 || rows > 65536 || in_features < 8 || in_features % 8 || out_features < 1 || out_features > (1 << 24))
+  if (rows < 1 || rows > (int64_t(1) << 24) || in_features < 8 || in_features % 8 || out_features < 1 || out_features > (1 << 24))
     return fail(Q3T_EINVAL, "linear: unsupported shape rows=%lld in=%lld out=%lld", (long long)rows,
                 (long long)in_features, (long long)out_features);
   if (x_stride < in_features || x_stride % 8 || !aligned16(x) || !aligned16(weight))
@@ -371,16 +430,18 @@ extern "C" int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t
   if (out_stride < (epilogue == Q3T_EPI_SWIGLU_PAIRED ? out_features / 2 : out_features))
     return fail(Q3T_EINVAL, "linear: out_stride too small");
   if (out_dtype != Q3T_BF16 && out_dtype != Q3T_F32) return fail(Q3T_EINVAL, "linear: out dtype");
-  if (epilogue == Q3T_EPI_RESIDUAL && (residual == nullptr || out_dtype != Q3T_BF16))
+  if ((epilogue == Q3T_EPI_RESIDUAL || epilogue == Q3T_EPI_RESIDUAL_SCALED) &&
+      (residual == nullptr || out_dtype != Q3T_BF16))
     return fail(Q3T_EINVAL, "linear: residual epilogue needs a bf16 residual and bf16 output");
+  if (epilogue == Q3T_EPI_RESIDUAL_SCALED && scale == nullptr)
+    return fail(Q3T_EINVAL, "linear: scaled residual epilogue needs a scale vector");
+  if (epilogue == Q3T_EPI_GELU && out_dtype != Q3T_BF16) return fail(Q3T_EINVAL, "linear: GELU epilogue is bf16");
   if (epilogue == Q3T_EPI_SWIGLU_PAIRED && (out_features % kTileN || out_dtype != Q3T_BF16 || bias != nullptr))
     return fail(Q3T_EINVAL, "linear: paired SwiGLU needs out_features %% 128 == 0, bf16 output, no bias");
-  if (epilogue < Q3T_EPI_STORE || epilogue > Q3T_EPI_SWIGLU_PAIRED) return fail(Q3T_EINVAL, "linear: epilogue");
+  if (epilogue < Q3T_EPI_STORE || epilogue > Q3T_EPI_GELU) return fail(Q3T_EINVAL, "linear: epilogue");
+  (void)workspace;
+  (void)workspace_bytes;
   const Plan p = plan(rows, in_features, out_features);
-  const bool needs_ws = p.splits > 1 || epilogue == Q3T_EPI_SWIGLU_PAIRED;
-  const size_t need = workspace_for(p, rows, out_features);
-  if (needs_ws && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)))
-    return fail(Q3T_ESPACE, "linear: workspace needs %zu bytes", need);
   CUtensorMap tmw, tmx;
   int rc = make_map(&tmw, weight, out_features, in_features, in_features, kTileN);
   if (rc) return rc;
@@ -398,13 +459,13 @@ extern "C" int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t
   a.out_f32 = out_dtype == Q3T_F32;
   a.residual = static_cast<const __nv_bfloat16*>(residual);
   a.res_stride = residual_stride;
-  if (size_t(p.n_tiles) * p.m_tiles > kMaxTiles) return fail(Q3T_EUNSUPPORTED, "linear: more than 16384 tiles");
-  a.counters = static_cast<unsigned*>(workspace);
-  a.partials = workspace ? reinterpret_cast<float*>(static_cast<char*>(workspace) + kTicketBytes) : nullptr;
+  a.scale = static_cast<const __nv_bfloat16*>(scale);
   a.status = status;
   switch (epilogue) {
     case Q3T_EPI_STORE: return dispatch_bn<Q3T_EPI_STORE>(p, tmw, tmx, a, stream);
     case Q3T_EPI_RESIDUAL: return dispatch_bn<Q3T_EPI_RESIDUAL>(p, tmw, tmx, a, stream);
+    case Q3T_EPI_RESIDUAL_SCALED: return dispatch_bn<Q3T_EPI_RESIDUAL_SCALED>(p, tmw, tmx, a, stream);
+    case Q3T_EPI_GELU: return dispatch_bn<Q3T_EPI_GELU>(p, tmw, tmx, a, stream);
     default: return dispatch_bn<Q3T_EPI_SWIGLU_PAIRED>(p, tmw, tmx, a, stream);
   }
 }

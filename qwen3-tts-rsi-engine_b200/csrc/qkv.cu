@@ -20,8 +20,8 @@ __global__ void qk_norm_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, in
                                        const __nv_bfloat16* __restrict__ sin_t, int64_t table_len,
                                        const int64_t* __restrict__ rot_pos, const int64_t* __restrict__ cache_pos,
                                        __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ tk,
-                                       __nv_bfloat16* __restrict__ tv, int length, int q_heads, int kv_heads,
-                                       int64_t capacity, unsigned* status) {
+                                       __nv_bfloat16* __restrict__ tv, int length, const int64_t* __restrict__ slots,
+                                       int q_heads, int kv_heads, int64_t capacity, unsigned* status) {
   constexpr int DL = D / 32;
   grid_dependency_launch();
   grid_dependency_wait();
@@ -74,7 +74,7 @@ __global__ void qk_norm_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, in
     return;
   }
   const int64_t pos = cache_pos[r];
-  const int64_t slot = r / length;
+  const int64_t slot = slots != nullptr ? slots[r / length] : r / length;
   if (pos < 0 || pos >= capacity) {
     if (lane == 0) raise_status(status, kStatusBadIndex);
     return;
@@ -94,8 +94,8 @@ extern "C" int q3t_qk_norm_rope_kv(const void* qkv, int64_t qkv_stride, const vo
                                    const void* k_norm_weight, float eps, const void* cos_table, const void* sin_table,
                                    int64_t table_len, const int64_t* rotary_positions, const int64_t* cache_positions,
                                    void* query_out, void* target_keys, void* target_values, int64_t rows,
-                                   int64_t length, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
-                                   int64_t capacity, unsigned* status, void* stream) {
+                                   int64_t length, const int64_t* slots, int64_t q_heads, int64_t kv_heads,
+                                   int64_t head_dim, int64_t capacity, unsigned* status, void* stream) {
   if (!qkv || (q_norm_weight == nullptr) != (k_norm_weight == nullptr) || !cos_table || !sin_table || !rotary_positions || !cache_positions ||
       !query_out || !target_keys || !target_values)
     return fail(Q3T_EINVAL, "qk_norm_rope_kv: null pointer");
@@ -111,7 +111,7 @@ extern "C" int q3t_qk_norm_rope_kv(const void* qkv, int64_t qkv_stride, const vo
                   static_cast<const __nv_bfloat16*>(cos_table), static_cast<const __nv_bfloat16*>(sin_table),
                   table_len, rotary_positions, cache_positions, static_cast<__nv_bfloat16*>(query_out),
                   static_cast<__nv_bfloat16*>(target_keys), static_cast<__nv_bfloat16*>(target_values), int(length),
-                  int(q_heads), int(kv_heads), capacity, status);
+                  slots, int(q_heads), int(kv_heads), capacity, status);
   if (head_dim == 64)
     return launch(qk_norm_rope_kv_kernel<64>, dim3(unsigned(rows)), block, 0, stream, true, "qk_norm_rope_kv",
                   static_cast<const __nv_bfloat16*>(qkv), qkv_stride, static_cast<const __nv_bfloat16*>(q_norm_weight),
@@ -119,6 +119,6 @@ extern "C" int q3t_qk_norm_rope_kv(const void* qkv, int64_t qkv_stride, const vo
                   static_cast<const __nv_bfloat16*>(cos_table), static_cast<const __nv_bfloat16*>(sin_table),
                   table_len, rotary_positions, cache_positions, static_cast<__nv_bfloat16*>(query_out),
                   static_cast<__nv_bfloat16*>(target_keys), static_cast<__nv_bfloat16*>(target_values), int(length),
-                  int(q_heads), int(kv_heads), capacity, status);
+                  slots, int(q_heads), int(kv_heads), capacity, status);
   return fail(Q3T_EUNSUPPORTED, "qk_norm_rope_kv: head_dim must be 64 or 128");
 }

@@ -262,7 +262,7 @@ def linear_workspace_bytes(rows: int, in_features: int, out_features: int) -> in
 
 
 def linear(x, weight, bias=None, *, out=None, out_dtype=BF16, epilogue: int = _lib.EPI_STORE, residual=None,
-           workspace: Optional[torch.Tensor] = None, tag: str = "linear"):
+           scale=None, workspace: Optional[torch.Tensor] = None, tag: str = "linear"):
     """out = x @ weight.T (+ bias) with a fused epilogue, on tcgen05 tensor cores."""
     _need_cuda(x, weight)
     if x.dtype != BF16 or weight.dtype != BF16 or weight.ndim != 2 or not weight.is_contiguous():
@@ -281,19 +281,17 @@ def linear(x, weight, bias=None, *, out=None, out_dtype=BF16, epilogue: int = _l
     res2 = None
     if residual is not None:
         res2 = residual.reshape(rows, n_out) if residual.is_contiguous() else residual
-    need = linear_workspace_bytes(rows, in_features, weight.shape[0])
-    ws = workspace if workspace is not None else SCRATCH.workspace(need, x.device, tag)
     odt = _lib.Q3T_BF16 if out.dtype == BF16 else _lib.Q3T_F32
     call("q3t_linear", x2.data_ptr(), x2.stride(0), rows, in_features, weight.data_ptr(), weight.shape[0],
          _ptr(bias), out2.data_ptr(), out2.stride(0), odt, epilogue, _ptr(res2),
-         res2.stride(0) if res2 is not None else 0, ws.data_ptr(), ws.numel(), status_word(x.device).data_ptr(),
-         _stream())
+         res2.stride(0) if res2 is not None else 0, _ptr(scale), _ptr(workspace),
+         workspace.numel() if workspace is not None else 0, status_word(x.device).data_ptr(), _stream())
     return out
 
 
 # ------------------------------------------------------------------ attention
 def qk_norm_rope_kv(qkv, q_norm_weight, k_norm_weight, eps, cos_table, sin_table, rotary_positions, cache_positions,
-                    target_keys, target_values, *, q_heads, kv_heads, head_dim, length=1, query_out=None):
+                    target_keys, target_values, *, q_heads, kv_heads, head_dim, length=1, query_out=None, slots=None):
     """Per-head q/k RMSNorm, rotary and KV write for packed QKV rows (packed_attention.py:42-74)."""
     _need_cuda(qkv, cos_table, sin_table, rotary_positions, cache_positions, target_keys, target_values)
     rows = qkv.shape[0]
@@ -304,7 +302,8 @@ def qk_norm_rope_kv(qkv, q_norm_weight, k_norm_weight, eps, cos_table, sin_table
     call("q3t_qk_norm_rope_kv", qkv.data_ptr(), qkv.stride(0), _ptr(q_norm_weight), _ptr(k_norm_weight), float(eps),
          cos_table.data_ptr(), sin_table.data_ptr(), cos_table.shape[0], rotary_positions.data_ptr(),
          cache_positions.data_ptr(), query_out.data_ptr(), target_keys.data_ptr(), target_values.data_ptr(), rows,
-         length, q_heads, kv_heads, head_dim, target_keys.shape[2], status_word(qkv.device).data_ptr(), _stream())
+         length, _ptr(slots), q_heads, kv_heads, head_dim, target_keys.shape[2], status_word(qkv.device).data_ptr(),
+         _stream())
     return query_out
 
 
@@ -313,12 +312,14 @@ def decode_attention_workspace_bytes(batch, q_heads, head_dim, context) -> int:
 
 
 def decode_attention(query, keys, values, positions, *, context=None, scale=None, out=None, rows_per_slot=1,
-                     window=0, workspace: Optional[torch.Tensor] = None, tag: str = "attention"):
-    """GQA attention of query row r over keys [max(0, p-window+1), p] of slot r // rows_per_slot, p = positions[r]."""
+                     window=0, slots=None, ring=0, workspace: Optional[torch.Tensor] = None, tag: str = "attention"):
+    """GQA attention of query row r over keys [max(0, p-window+1), p] of slot r // rows_per_slot
+    (or slots[r // rows_per_slot]), p = positions[r]; ring > 0 stores position p in row p % ring."""
     _need_cuda(query, keys, values, positions)
     rows, q_heads, head_dim = query.shape
-    slots, kv_heads, capacity, width = keys.shape
-    if (width != head_dim or values.shape != keys.shape or slots * rows_per_slot < rows or not keys.is_contiguous()
+    n_slots, kv_heads, capacity, width = keys.shape
+    if (width != head_dim or values.shape != keys.shape or (slots is None and n_slots * rows_per_slot < rows)
+            or not keys.is_contiguous()
             or not values.is_contiguous() or not query.is_contiguous() or query.dtype != BF16
             or keys.dtype != BF16 or values.dtype != BF16 or positions.dtype != torch.int64):
         raise ValueError("Expected BF16 query [rows,Hq,D] and contiguous BF16 KV arena [slots,Hkv,cap,D]")
@@ -328,8 +329,8 @@ def decode_attention(query, keys, values, positions, *, context=None, scale=None
     need = decode_attention_workspace_bytes(rows, q_heads, head_dim, context)
     ws = workspace if workspace is not None else SCRATCH.workspace(need, query.device, tag)
     call("q3t_decode_attention", query.data_ptr(), keys.data_ptr(), values.data_ptr(), positions.data_ptr(),
-         out.data_ptr(), rows, rows_per_slot, q_heads, kv_heads, head_dim, capacity, context, window, float(scale),
-         ws.data_ptr(), ws.numel(), status_word(query.device).data_ptr(), _stream())
+         out.data_ptr(), rows, rows_per_slot, _ptr(slots), int(ring), q_heads, kv_heads, head_dim, capacity, context,
+         window, float(scale), ws.data_ptr(), ws.numel(), status_word(query.device).data_ptr(), _stream())
     return out
 
 
@@ -420,3 +421,57 @@ def scatter_rows(target, indices, source) -> None:
     call("q3t_scatter_rows", target.data_ptr(), target.shape[0], indices.data_ptr(), source.data_ptr(), source.ndim,
          i64_array(source.shape), i64_array(source.stride()), source.element_size(),
          status_word(target.device).data_ptr(), _stream())
+
+
+# ------------------------------------------------------------------ incremental codec
+def rvq_gather(codes, tables, semantic: int, out=None):
+    """[sum of semantic codebook rows | sum of the rest] per (stream, frame) (cached_quantizer.py:17-30).
+
+    codes int64 [B, n_q, T]; tables bf16 [n_q, bins, dim] (normalised codebooks) -> [B*T, 2*dim]."""
+    _need_cuda(codes, tables)
+    B, n_q, T = codes.shape
+    dim = tables.shape[2]
+    out = torch.empty(B * T, 2 * dim, dtype=BF16, device=codes.device) if out is None else out
+    call("q3t_rvq_gather", codes.data_ptr(), codes.stride(0), codes.stride(1), codes.stride(2), tables.data_ptr(),
+         n_q, semantic, tables.shape[1], dim, B, T, out.data_ptr(), status_word(codes.device).data_ptr(), _stream())
+    return out
+
+
+def conv_gather(x, batch: int, frames: int, *, taps: int, dilation: int = 1, reverse: bool = False, history=None,
+                slots=None, alpha=None, inverse_beta=None, out=None):
+    """im2col rows of a causal conv over time-major x [batch*frames, C] with per-slot history."""
+    _need_cuda(x)
+    C = x.shape[-1]
+    H = history.shape[1] if history is not None else 0
+    out = torch.empty(batch * frames, taps * C, dtype=BF16, device=x.device) if out is None else out
+    call("q3t_conv_gather", x.data_ptr(), x.stride(0), batch, frames, C, _ptr(history), H, _ptr(slots), taps,
+         dilation, int(reverse), _ptr(alpha), _ptr(inverse_beta), out.data_ptr(), _stream())
+    return out
+
+
+def conv_history(x, batch: int, frames: int, history, slots=None) -> None:
+    """history[slot] = last H frames of [history[slot] | x[b]]."""
+    _need_cuda(x, history)
+    call("q3t_conv_history", x.data_ptr(), x.stride(0), batch, frames, x.shape[-1], history.data_ptr(),
+         history.shape[1], _ptr(slots), _stream())
+
+
+def dwconv_layernorm(x, batch: int, frames: int, history, slots, weight, bias, ln_weight, ln_bias, eps, out=None):
+    _need_cuda(x)
+    C = x.shape[-1]
+    out = torch.empty_like(x) if out is None else out
+    call("q3t_dwconv_layernorm", x.data_ptr(), batch, frames, C, _ptr(history),
+         history.shape[1] if history is not None else 0, _ptr(slots), weight.data_ptr(), bias.data_ptr(),
+         ln_weight.data_ptr(), ln_bias.data_ptr(), float(eps), out.data_ptr(), _stream())
+    return out
+
+
+def codec_positions(frames_by_slot, slots, batch: int, frames: int, ring: int, rotary, cache, advance: bool) -> None:
+    call("q3t_codec_positions", frames_by_slot.data_ptr(), _ptr(slots), batch, frames, ring, rotary.data_ptr(),
+         cache.data_ptr(), int(advance), _stream())
+
+
+def pcm16(x, wave=None, pcm=None) -> None:
+    """wave = clip(x, -1, 1) (fp32) and/or pcm = int16(wave * 32767) on the device."""
+    _need_cuda(x)
+    call("q3t_pcm16", x.data_ptr(), x.numel(), _ptr(wave), _ptr(pcm), _stream())
