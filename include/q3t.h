@@ -156,8 +156,16 @@ size_t q3t_linear_workspace_bytes(int64_t rows, int64_t in_features, int64_t out
 int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t in_features,
                const void* weight, int64_t out_features, const void* bias, void* out,
                int64_t out_stride, int out_dtype, int epilogue, const void* residual,
-               int64_t residual_stride, const void* scale, void* workspace, size_t workspace_bytes,
-               unsigned* status, void* stream);
+               int64_t residual_stride, const void* scale, const void* weight_tiles,
+               void* workspace, size_t workspace_bytes, unsigned* status, void* stream);
+
+/* Pre-swizzled weight layout for q3t_linear (pass it as weight_tiles, weight may
+ * then be NULL): tile (n, k) of 128 rows x 64 columns is the contiguous 16 KB image
+ * of the 128-byte-swizzled shared-memory tile, tiles ordered [n][k], zero padded.
+ * Each pipeline stage then streams one contiguous 16 KB block from HBM. */
+size_t q3t_weight_tiles_bytes(int64_t out_features, int64_t in_features);
+int q3t_pack_weight_tiles(const void* weight, int64_t out_features, int64_t in_features, void* tiles,
+                          void* stream);
 
 /* ------------------------------------------------------------------ attention */
 
@@ -188,16 +196,17 @@ int q3t_qk_norm_rope_kv(const void* qkv, int64_t qkv_stride, const void* q_norm_
  * rows (capacity == ring): position p lives in row p % ring, positions are
  * unbounded and 1 <= window <= ring (the codec's KV tail, codec_slots.py:27-39).
  * Otherwise context bounds the grid (positions < context <= capacity).
- * out [rows, q_heads, head_dim] bf16.
+ * arena_slots: the slot extent of keys/values. out [rows, q_heads, head_dim] bf16.
+ * Linear arenas run on tensor-core fragments (mma.sync) with TMA-swizzled K/V tiles.
  * Split-KV with an in-kernel combine. */
 size_t q3t_decode_attention_workspace_bytes(int64_t rows, int64_t q_heads, int64_t head_dim,
                                             int64_t context);
 int q3t_decode_attention(const void* query, const void* keys, const void* values,
                          const int64_t* positions, void* out, int64_t rows, int64_t rows_per_slot,
                          const int64_t* slots, int64_t ring, int64_t q_heads, int64_t kv_heads,
-                         int64_t head_dim, int64_t capacity, int64_t context, int64_t window,
-                         float scale, void* workspace, size_t workspace_bytes, unsigned* status,
-                         void* stream);
+                         int64_t head_dim, int64_t arena_slots, int64_t capacity, int64_t context,
+                         int64_t window, float scale, void* workspace, size_t workspace_bytes,
+                         unsigned* status, void* stream);
 
 /* No counterpart in the reference: an allocation-free form of
  * q3t_decode_attention for callers that cannot allocate device memory (a

@@ -12,6 +12,7 @@
 // of (key l/G, head l%G); softmax is online (base-2 exponent, q pre-scaled by
 // scale*log2(e)). Chunks of a slot combine through fp32 partials and an
 // atomic ticket: the last chunk CTA merges them in chunk order.
+#include "attention.cuh"
 #include "common.cuh"
 #include "host.cuh"
 
@@ -360,13 +361,15 @@ extern "C" size_t q3t_decode_attention_workspace_bytes(int64_t batch, int64_t q_
 
 extern "C" int q3t_decode_attention(const void* query, const void* keys, const void* values, const int64_t* positions,
                                     void* out, int64_t rows, int64_t rows_per_slot, const int64_t* slots, int64_t ring,
-                                    int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t capacity,
-                                    int64_t context, int64_t window, float scale, void* workspace,
+                                    int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t arena_slots,
+                                    int64_t capacity, int64_t context, int64_t window, float scale, void* workspace,
                                     size_t workspace_bytes, unsigned* status, void* stream) {
   if (!query || !keys || !values || !positions || !out) return fail(Q3T_EINVAL, "attention: null pointer");
   if (rows < 1 || rows > 65535 || rows_per_slot < 1 || rows % rows_per_slot || kv_heads < 1 || kv_heads > 65535 ||
-      q_heads % kv_heads || window < 0)
+      q_heads % kv_heads || window < 0 || arena_slots < 1)
     return fail(Q3T_EINVAL, "attention: invalid row or head geometry");
+  if (slots == nullptr && arena_slots * rows_per_slot < rows)
+    return fail(Q3T_EINVAL, "attention: more query rows than arena slots");
   if (context < 1 || context > capacity) return fail(Q3T_EINVAL, "Attention context must fit the KV arena");
   if (size_t(rows) * size_t(kv_heads) > kMaxTickets) return fail(Q3T_EUNSUPPORTED, "attention: rows x kv_heads > 65536");
   if (ring < 0 || (ring > 0 && (ring != capacity || window < 1 || window > ring)))
@@ -377,6 +380,34 @@ extern "C" int q3t_decode_attention(const void* query, const void* keys, const v
   const size_t need = attn_workspace(rows, q_heads, kv_heads, head_dim, context);
   if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
     return fail(Q3T_ESPACE, "attention: workspace needs %zu bytes", need);
+  if (ring == 0 && attention_mma_supported(head_dim, g)) {
+    // linear arenas: tensor-core kernel (TMA-swizzled K/V tiles, mma.sync fragments)
+    const int64_t span = window > 0 && window < context ? window : context;
+    AttentionCall call;
+    call.query = query;
+    call.keys = keys;
+    call.values = values;
+    call.positions = positions;
+    call.out = out;
+    call.rows = rows;
+    call.rows_per_slot = rows_per_slot;
+    call.slots = slots;
+    call.q_heads = q_heads;
+    call.kv_heads = kv_heads;
+    call.head_dim = head_dim;
+    call.arena_slots = arena_slots;
+    call.capacity = capacity;
+    call.context = context;
+    call.window = window;
+    call.scale = scale;
+    call.chunk = pick_chunk(rows, kv_heads, span);
+    call.max_chunks = int((span + call.chunk - 1) / call.chunk);
+    call.counters = static_cast<unsigned*>(workspace);
+    call.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kTicketBytes);
+    call.status = status;
+    call.stream = stream;
+    return launch_attention_mma(call);
+  }
 #define Q3T_ATTN(DD, GG)                                                                                       \
   if (head_dim == DD && g == GG)                                                                               \
     return launch_attn<DD, GG>(query, keys, values, positions, out, rows, rows_per_slot, slots, ring, kv_heads, \

@@ -1,0 +1,30 @@
+// Launch description shared by the decode-attention kernels.
+#pragma once
+
+#include <stdint.h>
+
+namespace q3t {
+
+struct AttentionCall {
+  const void* query;
+  const void* keys;
+  const void* values;
+  const int64_t* positions;
+  void* out;
+  int64_t rows, rows_per_slot;
+  const int64_t* slots;
+  int64_t q_heads, kv_heads, head_dim;
+  int64_t arena_slots, capacity, context, window;
+  float scale;
+  int chunk, max_chunks;
+  float* partials;
+  unsigned* counters;
+  unsigned* status;
+  void* stream;
+};
+
+// Tensor-core (mma.sync) kernel for linear arenas: head_dim 64/128, 1 or 2 query heads per kv head.
+bool attention_mma_supported(int64_t head_dim, int64_t group);
+int launch_attention_mma(const AttentionCall& call);
+
+}  // namespace q3t

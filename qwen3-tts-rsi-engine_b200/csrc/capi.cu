@@ -1,5 +1,6 @@
 // Library-wide entry points: ABI version, error strings, launch accounting.
 #include <atomic>
+#include <mutex>
 #include <stdio.h>
 
 #include "host.cuh"
@@ -37,6 +38,39 @@ int sm_count() {
     g_sms[dev] = n;
   }
   return g_sms[dev];
+}
+
+namespace {
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiled tiled_encoder() {
+  static EncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+  });
+  return fn;
+}
+}  // namespace
+
+int make_map_bf16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t stride_elems, int box_cols,
+                  int box_rows) {
+  EncodeTiled enc = tiled_encoder();
+  if (enc == nullptr) return fail(Q3T_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(stride_elems) * 2};
+  cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(Q3T_EINVAL, "tensor map encode failed (%d)", int(r));
+  return Q3T_OK;
 }
 
 }  // namespace q3t

@@ -19,6 +19,7 @@
 #include "host.cuh"
 
 #include <mutex>
+#include <string.h>
 
 using namespace q3t;
 
@@ -45,6 +46,9 @@ struct Cfg {
 
 struct GemmArgs {
   int rows, in_features, out_features, kblocks, splits;
+  // Q3T_WEIGHTS_TILED: weight tile (n-tile, k-block) is the contiguous 16 KB
+  // swizzled shared-memory image at tiles + (n-tile * kblocks + k-block) * 16 KB
+  const uint8_t* tiles;
   const __nv_bfloat16* bias;
   void* out;
   int64_t out_stride;
@@ -80,6 +84,18 @@ __device__ __forceinline__ void store_out(const GemmArgs& a, int m, int n, float
       static_cast<float*>(a.out)[int64_t(m) * a.out_stride + n] = bf16r(acc);
     else
       static_cast<__nv_bfloat16*>(a.out)[int64_t(m) * a.out_stride + n] = __float2bfloat16_rn(acc);
+  }
+}
+
+// Weight tile (k-block kb, rows n0..n0+127) into a ring slot: one contiguous
+// 16 KB bulk copy from the pre-swizzled tile layout, or a 2-D TMA tile load.
+Q3T_DEV void load_weights(uint8_t* dst, const CUtensorMap* tmw, const GemmArgs& a, uint64_t* bar, int kb, int n0,
+                          uint64_t pol) {
+  if (a.tiles != nullptr) {
+    const size_t tile = size_t(n0 / kTileN) * size_t(a.kblocks) + size_t(kb);
+    bulk_load(dst, a.tiles + tile * size_t(kABytes), uint32_t(kABytes), bar);
+  } else {
+    tma_load_2d(dst, tmw, bar, kb * kTileK, n0, pol);
   }
 }
 
@@ -145,7 +161,7 @@ __global__ void __launch_bounds__(128, 1)
     *abort_flag = 0;
     *consumed = 0;
     fence_mbar_init();
-    prefetch_tmap(&tmw);
+    if (a.tiles == nullptr) prefetch_tmap(&tmw);
     prefetch_tmap(&tmx);
   }
   if (warp == 1) {
@@ -166,7 +182,7 @@ __global__ void __launch_bounds__(128, 1)
       const int pre = nk < S ? nk : S;
       for (int i = 0; i < pre; ++i) {
         mbar_expect_tx(&full[i], C::kStageBytes);
-        tma_load_2d(smem + i * C::kStageBytes, &tmw, &full[i], (kb0 + i) * kTileK, n0, pol_w);
+        load_weights(smem + i * C::kStageBytes, &tmw, a, &full[i], kb0 + i, n0, pol_w);
       }
       issued = pre;
       grid_dependency_wait();
@@ -179,7 +195,7 @@ __global__ void __launch_bounds__(128, 1)
           break;
         }
         mbar_expect_tx(&full[s], C::kStageBytes);
-        tma_load_2d(smem + s * C::kStageBytes, &tmw, &full[s], (kb0 + i) * kTileK, n0, pol_w);
+        load_weights(smem + s * C::kStageBytes, &tmw, a, &full[s], kb0 + i, n0, pol_w);
         tma_load_2d(smem + s * C::kStageBytes + kABytes, &tmx, &full[s], (kb0 + i) * kTileK, m0, pol_x);
         issued = i + 1;
       }
@@ -303,6 +319,32 @@ __global__ void __launch_bounds__(128, 1)
   if (clustered) cluster_sync();  // peers finished reading this CTA's shared memory
 }
 
+// Weight [N, K] row-major -> tiles [ceil(N/128)][ceil(K/64)] of the 128-byte-swizzled
+// shared-memory image (row r, 16-byte chunk j stored at chunk j ^ (r % 8)); padding is zero.
+__global__ void pack_tiles_kernel(const __nv_bfloat16* __restrict__ w, int64_t n, int64_t k, int64_t kblocks,
+                                  int64_t total_chunks, uint4* __restrict__ tiles) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total_chunks;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    // i enumerates destination 16-byte chunks in storage order
+    const int64_t tile = i / (kTileN * 8), within = i % (kTileN * 8);
+    const int r = int(within / 8), pos = int(within % 8);
+    const int j = pos ^ (r & 7);  // logical chunk stored at this position
+    const int64_t nt = tile / kblocks, kb = tile % kblocks;
+    const int64_t row = nt * kTileN + r, col = kb * kTileK + int64_t(j) * 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (row < n) {
+      if (col + 8 <= k) {
+        v = *reinterpret_cast<const uint4*>(w + row * k + col);
+      } else {
+        __nv_bfloat16 e[8];
+        for (int q = 0; q < 8; ++q) e[q] = (col + q < k) ? w[row * k + col + q] : __float2bfloat16_rn(0.f);
+        v = *reinterpret_cast<const uint4*>(e);
+      }
+    }
+    tiles[i] = v;
+  }
+}
+
 // ---------------------------------------------------------------- host side
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -409,6 +451,25 @@ int dispatch_bn(const Plan& p, const CUtensorMap& tmw, const CUtensorMap& tmx, c
 
 }  // namespace
 
+extern "C" size_t q3t_weight_tiles_bytes(int64_t out_features, int64_t in_features) {
+  if (out_features < 1 || in_features < 1) return 0;
+  return size_t((out_features + kTileN - 1) / kTileN) * size_t((in_features + kTileK - 1) / kTileK) * kABytes;
+}
+
+extern "C" int q3t_pack_weight_tiles(const void* weight, int64_t out_features, int64_t in_features, void* tiles,
+                                     void* stream) {
+  if (!weight || !tiles || out_features < 1 || in_features < 8 || in_features % 8 || !aligned16(weight) ||
+      !aligned16(tiles))
+    return fail(Q3T_EINVAL, "pack_weight_tiles: invalid arguments");
+  const int64_t kblocks = (in_features + kTileK - 1) / kTileK;
+  const int64_t chunks = int64_t(q3t_weight_tiles_bytes(out_features, in_features) / 16);
+  int64_t blocks = (chunks + 255) / 256;
+  if (blocks > int64_t(sm_count()) * 16) blocks = int64_t(sm_count()) * 16;
+  return launch(pack_tiles_kernel, dim3(unsigned(blocks)), dim3(256), 0, stream, false, "pack_weight_tiles",
+                static_cast<const __nv_bfloat16*>(weight), out_features, in_features, kblocks, chunks,
+                static_cast<uint4*>(tiles));
+}
+
 // The split-K reduction runs through distributed shared memory: no scratch.
 extern "C" size_t q3t_linear_workspace_bytes(int64_t rows, int64_t in_features, int64_t out_features) {
   (void)rows;
@@ -420,12 +481,14 @@ extern "C" size_t q3t_linear_workspace_bytes(int64_t rows, int64_t in_features, 
 extern "C" int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t in_features, const void* weight,
                           int64_t out_features, const void* bias, void* out, int64_t out_stride, int out_dtype,
                           int epilogue, const void* residual, int64_t residual_stride, const void* scale,
-                          void* workspace, size_t workspace_bytes, unsigned* status, void* stream) {
-  if (!x || !weight || !out) return fail(Q3T_EINVAL, "linear: null pointer");
+                          const void* weight_tiles, void* workspace, size_t workspace_bytes, unsigned* status,
+                          void* stream) {
+  if (!x || (!weight && !weight_tiles) || !out) return fail(Q3T_EINVAL, "linear: null pointer");
   if (rows < 1 || rows > (int64_t(1) << 24) || in_features < 8 || in_features % 8 || out_features < 1 || out_features > (1 << 24))
     return fail(Q3T_EINVAL, "linear: unsupported shape rows=%lld in=%lld out=%lld", (long long)rows,
                 (long long)in_features, (long long)out_features);
-  if (x_stride < in_features || x_stride % 8 || !aligned16(x) || !aligned16(weight))
+  if (x_stride < in_features || x_stride % 8 || !aligned16(x) || (weight && !aligned16(weight)) ||
+      (weight_tiles && !aligned16(weight_tiles)))
     return fail(Q3T_EINVAL, "linear: x/weight need 16-byte aligned rows");
   if (out_stride < (epilogue == Q3T_EPI_SWIGLU_PAIRED ? out_features / 2 : out_features))
     return fail(Q3T_EINVAL, "linear: out_stride too small");
@@ -443,8 +506,13 @@ extern "C" int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t
   (void)workspace_bytes;
   const Plan p = plan(rows, in_features, out_features);
   CUtensorMap tmw, tmx;
-  int rc = make_map(&tmw, weight, out_features, in_features, in_features, kTileN);
-  if (rc) return rc;
+  int rc = Q3T_OK;
+  if (weight_tiles == nullptr) {
+    rc = make_map(&tmw, weight, out_features, in_features, in_features, kTileN);
+    if (rc) return rc;
+  } else {
+    memset(&tmw, 0, sizeof(tmw));
+  }
   rc = make_map(&tmx, x, rows, in_features, x_stride, p.bn);
   if (rc) return rc;
   GemmArgs a;
@@ -460,6 +528,7 @@ extern "C" int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t
   a.residual = static_cast<const __nv_bfloat16*>(residual);
   a.res_stride = residual_stride;
   a.scale = static_cast<const __nv_bfloat16*>(scale);
+  a.tiles = static_cast<const uint8_t*>(weight_tiles);
   a.status = status;
   switch (epilogue) {
     case Q3T_EPI_STORE: return dispatch_bn<Q3T_EPI_STORE>(p, tmw, tmx, a, stream);

@@ -3,6 +3,7 @@
 // attribute so a kernel may start while its predecessor drains.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdint.h>
@@ -19,6 +20,11 @@ int check_cuda(const char* what);
 void note_launch();
 // Number of SMs of the current device (cached per device).
 int sm_count();
+
+// 2-D bf16 tensor map over a row-major matrix: dims {cols, rows}, row stride in
+// elements, box {box_cols, box_rows}, 128-byte swizzle (box_cols * 2 <= 128).
+int make_map_bf16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t stride_elems,
+                  int box_cols, int box_rows);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 

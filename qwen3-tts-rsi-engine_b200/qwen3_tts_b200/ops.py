@@ -261,20 +261,48 @@ def linear_workspace_bytes(rows: int, in_features: int, out_features: int) -> in
     return int(_lib.load().q3t_linear_workspace_bytes(rows, in_features, out_features))
 
 
+class TiledWeight:
+    """A [out, in] weight in the pre-swizzled tile layout of q3t_pack_weight_tiles."""
+
+    def __init__(self, tiles: torch.Tensor, out_features: int, in_features: int):
+        self.tiles, self.out_features, self.in_features = tiles, out_features, in_features
+        self.shape = (out_features, in_features)
+        self.dtype = BF16
+        self.device = tiles.device
+
+    def numel(self) -> int:
+        return self.out_features * self.in_features
+
+
+def pack_tiles(weight: torch.Tensor) -> TiledWeight:
+    """Re-layout a contiguous bf16 [out, in] weight as contiguous swizzled 16 KB tiles."""
+    _need_cuda(weight)
+    if weight.dtype != BF16 or weight.ndim != 2 or not weight.is_contiguous():
+        raise ValueError("pack_tiles expects a contiguous BF16 [out, in] weight")
+    n, k = weight.shape
+    nbytes = int(_lib.load().q3t_weight_tiles_bytes(n, k))
+    tiles = torch.empty(nbytes, dtype=torch.uint8, device=weight.device)
+    call("q3t_pack_weight_tiles", weight.data_ptr(), n, k, tiles.data_ptr(), _stream())
+    return TiledWeight(tiles, n, k)
+
+
 def linear(x, weight, bias=None, *, out=None, out_dtype=BF16, epilogue: int = _lib.EPI_STORE, residual=None,
            scale=None, workspace: Optional[torch.Tensor] = None, tag: str = "linear"):
-    """out = x @ weight.T (+ bias) with a fused epilogue, on tcgen05 tensor cores."""
-    _need_cuda(x, weight)
-    if x.dtype != BF16 or weight.dtype != BF16 or weight.ndim != 2 or not weight.is_contiguous():
+    """out = x @ weight.T (+ bias) with a fused epilogue, on tcgen05 tensor cores.
+
+    `weight` is a contiguous bf16 [out, in] tensor or a TiledWeight."""
+    tiled = isinstance(weight, TiledWeight)
+    _need_cuda(x, weight.tiles if tiled else weight)
+    if x.dtype != BF16 or (not tiled and (weight.dtype != BF16 or weight.ndim != 2 or not weight.is_contiguous())):
         raise ValueError("linear expects BF16 activations and a contiguous BF16 [out, in] weight")
-    in_features = weight.shape[1]
+    n_rows_w, in_features = weight.shape
     if x.shape[-1] != in_features or x.stride(-1) != 1:
         raise ValueError("linear: activation width must match the weight")
     rows = x.numel() // in_features if x.is_contiguous() else x.shape[0]
     x2 = x.reshape(rows, in_features) if x.is_contiguous() else x
     if x2.ndim != 2:
         raise ValueError("linear: non-contiguous activations must be 2-D")
-    n_out = weight.shape[0] // 2 if epilogue == _lib.EPI_SWIGLU_PAIRED else weight.shape[0]
+    n_out = n_rows_w // 2 if epilogue == _lib.EPI_SWIGLU_PAIRED else n_rows_w
     if out is None:
         out = torch.empty(*x.shape[:-1], n_out, dtype=out_dtype, device=x.device)
     out2 = out.reshape(rows, n_out) if out.is_contiguous() else out
@@ -282,10 +310,11 @@ def linear(x, weight, bias=None, *, out=None, out_dtype=BF16, epilogue: int = _l
     if residual is not None:
         res2 = residual.reshape(rows, n_out) if residual.is_contiguous() else residual
     odt = _lib.Q3T_BF16 if out.dtype == BF16 else _lib.Q3T_F32
-    call("q3t_linear", x2.data_ptr(), x2.stride(0), rows, in_features, weight.data_ptr(), weight.shape[0],
+    call("q3t_linear", x2.data_ptr(), x2.stride(0), rows, in_features, None if tiled else weight.data_ptr(), n_rows_w,
          _ptr(bias), out2.data_ptr(), out2.stride(0), odt, epilogue, _ptr(res2),
-         res2.stride(0) if res2 is not None else 0, _ptr(scale), _ptr(workspace),
-         workspace.numel() if workspace is not None else 0, status_word(x.device).data_ptr(), _stream())
+         res2.stride(0) if res2 is not None else 0, _ptr(scale), weight.tiles.data_ptr() if tiled else None,
+         _ptr(workspace), workspace.numel() if workspace is not None else 0, status_word(x.device).data_ptr(),
+         _stream())
     return out
 
 
@@ -329,8 +358,8 @@ def decode_attention(query, keys, values, positions, *, context=None, scale=None
     need = decode_attention_workspace_bytes(rows, q_heads, head_dim, context)
     ws = workspace if workspace is not None else SCRATCH.workspace(need, query.device, tag)
     call("q3t_decode_attention", query.data_ptr(), keys.data_ptr(), values.data_ptr(), positions.data_ptr(),
-         out.data_ptr(), rows, rows_per_slot, _ptr(slots), int(ring), q_heads, kv_heads, head_dim, capacity, context,
-         window, float(scale), ws.data_ptr(), ws.numel(), status_word(query.device).data_ptr(), _stream())
+         out.data_ptr(), rows, rows_per_slot, _ptr(slots), int(ring), q_heads, kv_heads, head_dim, n_slots, capacity,
+         context, window, float(scale), ws.data_ptr(), ws.numel(), status_word(query.device).data_ptr(), _stream())
     return out
 
 

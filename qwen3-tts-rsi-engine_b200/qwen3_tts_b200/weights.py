@@ -89,23 +89,39 @@ class PackedLayer:
     down: torch.Tensor
 
 
-def pack_decoder(weights: dict, device) -> dict:
-    """Kernel layouts on `device` (bf16, contiguous)."""
+def pack_decoder(weights: dict, device, tiled: bool = True) -> dict:
+    """Kernel layouts on `device` (bf16, contiguous).
+
+    With ``tiled`` the projection matrices are re-laid out as contiguous
+    pre-swizzled 16 KB GEMM tiles (``ops.pack_tiles``), so every pipeline stage
+    of the weight-streaming GEMM reads one contiguous block of HBM."""
+    from . import ops
+
     def dev(t):
         return t.to(device=device, dtype=torch.bfloat16).contiguous()
 
+    def mat(t):
+        t = dev(t)
+        return ops.pack_tiles(t) if tiled else t
+
     layers = [PackedLayer(
         input_norm=dev(l["input_norm"]),
-        qkv=dev(torch.cat([l["q"], l["k"], l["v"]], dim=0)),
+        qkv=mat(torch.cat([l["q"], l["k"], l["v"]], dim=0)),
         q_norm=dev(l["q_norm"]),
         k_norm=dev(l["k_norm"]),
-        o=dev(l["o"]),
+        o=mat(l["o"]),
         post_norm=dev(l["post_norm"]),
-        gate_up=dev(interleave_gate_up(l["gate"], l["up"])),
-        down=dev(l["down"]),
+        gate_up=mat(interleave_gate_up(l["gate"], l["up"])),
+        down=mat(l["down"]),
     ) for l in weights["layers"]]
     packed = {"layers": layers, "norm": dev(weights["norm"])}
-    for key in ("head", "embedding", "heads", "embeddings", "proj", "proj_bias"):
+    for key in ("embedding", "embeddings", "proj_bias"):
         if key in weights:
             packed[key] = dev(weights[key])
+    if "head" in weights:
+        packed["head"] = mat(weights["head"])
+    if "proj" in weights:
+        packed["proj"] = mat(weights["proj"])
+    if "heads" in weights:
+        packed["heads"] = [mat(h) for h in weights["heads"]]
     return packed

@@ -19,6 +19,7 @@ BF16 = torch.bfloat16
 
 def snr_db(ref, got):
     ref, got = ref.double(), got.double()
+    ref, got = ref.detach(), got.detach()
     return 10 * math.log10(float((ref ** 2).sum()) / max(float(((got - ref) ** 2).sum()), 1e-30))
 
 

@@ -213,6 +213,21 @@ def test_linear_store_bf16(ops, cuda, rows, k, n):
     assert_status_clean(ops, cuda)
 
 
+@pytest.mark.parametrize("rows,k,n", [(1, 2048, 4096), (32, 2048, 12288), (33, 6144, 2048), (64, 96, 200),
+                                      (300, 1024, 2048)])
+def test_linear_tiled_weights_equal_row_major(ops, cuda, rows, k, n):
+    from qwen3_tts_b200 import _lib
+    x = rnd(35, (rows, k), 1.0, BF16).to(cuda)
+    w = rnd(36, (n, k), 0.02, BF16).to(cuda)
+    tiled = ops.pack_tiles(w)
+    ref = ops.linear(x, w, out_dtype=torch.float32)
+    got = ops.linear(x, tiled, out_dtype=torch.float32)
+    assert torch.equal(got, ref)  # same tiles, same MMA order: bit-identical
+    if n % 128 == 0:
+        got = ops.linear(x, tiled, epilogue=_lib.EPI_SWIGLU_PAIRED)
+        assert torch.equal(got, ops.linear(x, w, epilogue=_lib.EPI_SWIGLU_PAIRED))
+
+
 def test_linear_fp32_bias_residual_and_strided_input(ops, cuda):
     from qwen3_tts_b200 import _lib
     rows, k, n = 24, 2048, 3072

@@ -29,7 +29,8 @@ def _call_both(lib, q, k, v, pos, context):
     need = ops.decode_attention_workspace_bytes(rows, q_heads, head_dim, context)
     workspace = torch.zeros(need, dtype=torch.uint8, device=q.device)
     rc = lib.q3t_decode_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), ref.data_ptr(), rows, 1,
-                                  None, 0, q_heads, kv_heads, head_dim, capacity, context, 0, head_dim ** -0.5,
+                                  None, 0, q_heads, kv_heads, head_dim, slots, capacity, context, 0,
+                                  head_dim ** -0.5,
                                   workspace.data_ptr(), workspace.numel(), status.data_ptr(), stream)
     assert rc == 0
     out = torch.full_like(q, float("nan"))
