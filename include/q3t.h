@@ -48,7 +48,8 @@ enum {
   Q3T_EPI_SWIGLU_PAIRED = 2,/* rows of each 128-row weight tile are [64 gate; 64 up];
                                out[:, f] = bf16(bf16(silu(gate_f)) * up_f) */
   Q3T_EPI_RESIDUAL_SCALED = 3,/* out = bf16(residual + bf16(scale[n] * bf16(acc + bias))) */
-  Q3T_EPI_GELU = 4          /* out = bf16(gelu_erf(bf16(acc + bias))) */
+  Q3T_EPI_GELU = 4,         /* out = bf16(gelu_erf(bf16(acc + bias))) */
+  Q3T_EPI_SILU = 5          /* out = bf16(silu(bf16(acc + bias))) - text_projection fc1 + act */
 };
 
 /* RMSNorm rounding modes. */
@@ -329,9 +330,55 @@ int q3t_codec_positions(int64_t* frames_by_slot, const int64_t* slots, int64_t b
                         int64_t frames, int64_t ring, int64_t* rotary_positions,
                         int64_t* cache_positions, int advance, void* stream);
 
-/* PCM conversion of qwen3_tts_engine/continuous.py:510,535 on the device:
- * wave = clip(x, -1, 1) (fp32, nullable), pcm = int16(wave * 32767) (nullable). */
-int q3t_pcm16(const void* x, int64_t count, float* wave, int16_t* pcm, void* stream);
+/* PCM conversion of qwen3_tts_engine/continuous.py:531-533 on the device:
+ * wave = clip(x, -1, 1) (fp32, nullable), pcm = int16(wave * 32767) (nullable).
+ * A nonfinite input sample raises status bit 16 (the reference raises
+ * "Native codec emitted nonfinite audio" at continuous.py:530-531). */
+int q3t_pcm16(const void* x, int64_t count, float* wave, int16_t* pcm, unsigned* status, void* stream);
+
+/* ---------------------------------------------------------------- engine slots
+ * Device-resident request state of ContinuousModel (RequestState,
+ * qwen3_tts_engine/continuous.py:232-247): slot i holds the i-th active
+ * request; arrays are [slots, ...]. Rows >= *active (a device int64) are graph
+ * padding and receive the reference's padding values (continuous.py:580-583,
+ * 599-604).
+ *
+ * q3t_tick_gather replaces the per-tick torch.cat/stack of continuous.py:575-606:
+ *   pred_inputs[b] = (hidden_state[b], codec_embedding[tokens[b]])  [rows, 2, hidden] bf16
+ *   codes[b * codes_stride] = tokens[b]
+ *   draws[b, :16] = tables[b, frames[b], :]; talker_uniform[b] = tables[b, frames[b] + 1, 0]
+ *   steps[b] = frames[b] + 1
+ *   text[b] = frames[b] < trailing_len[b] ? trailing[b, frames[b]] : pad[b]
+ *   step_positions[b] = positions[b]; step_rotary[b] = rotary[b]
+ * tables: [slots, table_rows, 16] fp32 (random_table, sampling.py:17-19). */
+int q3t_tick_gather(const int64_t* active, const int64_t* tokens, const void* hidden_state,
+                    const void* codec_embedding, int64_t vocab, const float* tables, int64_t table_rows,
+                    const int64_t* frames, const void* trailing, int64_t trailing_rows,
+                    const int64_t* trailing_len, const void* pad, const int64_t* positions,
+                    const int64_t* rotary, void* pred_inputs, int64_t* codes, int64_t codes_stride,
+                    float* draws, float* talker_uniform, int64_t* steps, void* text,
+                    int64_t* step_positions, int64_t* step_rotary, int64_t rows, int64_t hidden,
+                    unsigned* status, void* stream);
+
+/* Write-back of continuous.py:618-635 for rows b < *active:
+ *   ring[b, frames[b] % ring_depth, :] = codes[b, :codebooks]  (CodecCodeBuffer.write,
+ *   codec_code_buffer.py:12-17); hidden_state[b] = step_hidden[b];
+ *   frames[b] += 1; positions[b] += 1; rotary[b] += 1. */
+int q3t_tick_commit(const int64_t* active, const int64_t* codes, int64_t codes_stride, int64_t codebooks,
+                    const void* step_hidden, void* hidden_state, int64_t* ring, int64_t ring_depth,
+                    int64_t* frames, int64_t* positions, int64_t* rotary, int64_t rows, int64_t hidden,
+                    void* stream);
+
+/* CodecCodeBuffer.write (codec_code_buffer.py:12-17): ring[i, frame_indices[i] % depth] = codes[i]
+ * for i < count; ring [slots, depth, codebooks] int64. */
+int q3t_code_ring_write(const int64_t* codes, int64_t codes_stride, const int64_t* frame_indices,
+                        int64_t* ring, int64_t ring_depth, int64_t codebooks, int64_t count, void* stream);
+
+/* CodecCodeBuffer.read (codec_code_buffer.py:19-27):
+ * out[i, c, t] = ring[indices[i], (starts[i] + t) % depth, c], out [batch, codebooks, length]. */
+int q3t_code_ring_read(const int64_t* ring, int64_t slots, int64_t ring_depth, int64_t codebooks,
+                       const int64_t* indices, const int64_t* starts, int64_t batch, int64_t length,
+                       int64_t* out, unsigned* status, void* stream);
 
 #ifdef __cplusplus
 }

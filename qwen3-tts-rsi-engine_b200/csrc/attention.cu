@@ -72,7 +72,6 @@ __global__ void __launch_bounds__(128)
 
   const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  grid_dependency_launch();
   grid_dependency_wait();
 
   int64_t pos = positions[b];

@@ -85,7 +85,6 @@ __global__ void __launch_bounds__(128)
   const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
-  grid_dependency_launch();
   grid_dependency_wait();
 
   int64_t pos = positions[b];

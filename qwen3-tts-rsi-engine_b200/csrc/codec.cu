@@ -205,13 +205,17 @@ __global__ void codec_positions_kernel(int64_t* __restrict__ frames, const int64
 // ------------------------------------------------------------------ PCM16 (continuous.py:535)
 // pcm = int16(clip(x, -1, 1) * 32767) (truncation toward zero); wave = clip(x, -1, 1).
 __global__ void pcm16_kernel(const __nv_bfloat16* __restrict__ x, int64_t n, float* __restrict__ wave,
-                             int16_t* __restrict__ pcm) {
+                             int16_t* __restrict__ pcm, unsigned* status) {
   grid_dependency_wait();
+  bool finite = true;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
-    const float v = fminf(fmaxf(__bfloat162float(x[i]), -1.0f), 1.0f);
+    const float raw = __bfloat162float(x[i]);
+    finite = finite && isfinite(raw);
+    const float v = fminf(fmaxf(raw, -1.0f), 1.0f);
     if (wave) wave[i] = v;
     if (pcm) pcm[i] = int16_t(v * 32767.0f);
   }
+  if (__any_sync(0xffffffffu, !finite) && (threadIdx.x & 31) == 0) raise_status(status, kStatusNonFinite);
 }
 
 }  // namespace
@@ -279,8 +283,8 @@ extern "C" int q3t_codec_positions(int64_t* frames_by_slot, const int64_t* slots
                 int(batch), int(frames), ring, rotary_positions, cache_positions, advance);
 }
 
-extern "C" int q3t_pcm16(const void* x, int64_t count, float* wave, int16_t* pcm, void* stream) {
+extern "C" int q3t_pcm16(const void* x, int64_t count, float* wave, int16_t* pcm, unsigned* status, void* stream) {
   if (!x || count < 1 || (!wave && !pcm)) return fail(Q3T_EINVAL, "pcm16: invalid arguments");
   return launch(pcm16_kernel, dim3(grid_for(count, 256)), dim3(256), 0, stream, true, "pcm16",
-                static_cast<const __nv_bfloat16*>(x), count, wave, pcm);
+                static_cast<const __nv_bfloat16*>(x), count, wave, pcm, status);
 }

@@ -59,6 +59,7 @@ enum : unsigned {
   kStatusMmaTimeout = 1u << 1,
   kStatusFlagTimeout = 1u << 2,
   kStatusBadIndex = 1u << 3,
+  kStatusNonFinite = 1u << 4,
 };
 // Two seconds: every kernel here finishes in well under a millisecond.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
@@ -149,10 +150,17 @@ Q3T_DEV void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t
 }
 
 // ---------------------------------------------------------------- programmatic dependent launch
-// Wait for the preceding kernel in the stream (no-op without the PDL attribute).
-Q3T_DEV void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-// Allow the next kernel in the stream to begin launching.
-Q3T_DEV void grid_dependency_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Wait for the preceding kernel in the stream to complete (no-op without the
+// PDL attribute), then allow the next kernel to begin launching: its CTAs may
+// become resident while this grid runs and do their dependency-free prologue
+// (barrier setup, weight prefetch) before their own wait. Triggering only
+// after the wait keeps at most two grids of the chain resident at a time, and
+// since the trigger fires once every CTA of this grid has executed it, the
+// early CTAs never take launch slots from this grid.
+Q3T_DEV void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 // ---------------------------------------------------------------- tcgen05 / TMEM
 Q3T_DEV void tmem_alloc(uint32_t* smem_result, uint32_t ncols) {

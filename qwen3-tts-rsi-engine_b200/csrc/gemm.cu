@@ -6,9 +6,10 @@
 // rows in the N dimension ("swap-AB"): one CTA owns 128 output features x BN
 // rows, streams its 128 x K weight slab through a TMA/mbarrier ring into
 // 128-byte-swizzled shared memory and accumulates in TMEM. K is split across
-// CTAs so that ~2 CTAs per SM stream weights; each split writes fp32 partials
-// and the last CTA of a tile (atomic ticket) sums them in fixed split order
-// (deterministic) and applies the fused epilogue.
+// the CTAs of a thread-block cluster (1..8 splits) so that ~2 CTAs per SM
+// stream weights; each CTA parks its fp32 tile in shared memory and the
+// cluster reduces the tiles through distributed shared memory in fixed rank
+// order (deterministic, no global scratch) and applies the fused epilogue.
 //
 // Roles (128 threads): warp0.lane0 = TMA producer, warp1 = TMEM owner and
 // lane0 = MMA issuer, all four warps = epilogue (warp w reads TMEM lanes
@@ -79,6 +80,9 @@ __device__ __forceinline__ void store_out(const GemmArgs& a, int m, int n, float
     const float v = bf16r(acc);
     static_cast<__nv_bfloat16*>(a.out)[int64_t(m) * a.out_stride + n] =
         __float2bfloat16_rn(0.5f * v * (1.0f + erff(v * 0.70710678118654752f)));
+  } else if constexpr (EPI == Q3T_EPI_SILU) {
+    const float v = bf16r(acc);
+    static_cast<__nv_bfloat16*>(a.out)[int64_t(m) * a.out_stride + n] = __float2bfloat16_rn(v / (1.0f + expf(-v)));
   } else {
     if (a.out_f32)
       static_cast<float*>(a.out)[int64_t(m) * a.out_stride + n] = bf16r(acc);
@@ -151,7 +155,6 @@ __global__ void __launch_bounds__(128, 1)
   const int nk = kb1 - kb0;
   const bool clustered = a.splits > 1;
 
-  grid_dependency_launch();
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
@@ -498,10 +501,11 @@ extern "C" int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t
     return fail(Q3T_EINVAL, "linear: residual epilogue needs a bf16 residual and bf16 output");
   if (epilogue == Q3T_EPI_RESIDUAL_SCALED && scale == nullptr)
     return fail(Q3T_EINVAL, "linear: scaled residual epilogue needs a scale vector");
-  if (epilogue == Q3T_EPI_GELU && out_dtype != Q3T_BF16) return fail(Q3T_EINVAL, "linear: GELU epilogue is bf16");
+  if ((epilogue == Q3T_EPI_GELU || epilogue == Q3T_EPI_SILU) && out_dtype != Q3T_BF16)
+    return fail(Q3T_EINVAL, "linear: GELU/SiLU epilogues are bf16");
   if (epilogue == Q3T_EPI_SWIGLU_PAIRED && (out_features % kTileN || out_dtype != Q3T_BF16 || bias != nullptr))
     return fail(Q3T_EINVAL, "linear: paired SwiGLU needs out_features %% 128 == 0, bf16 output, no bias");
-  if (epilogue < Q3T_EPI_STORE || epilogue > Q3T_EPI_GELU) return fail(Q3T_EINVAL, "linear: epilogue");
+  if (epilogue < Q3T_EPI_STORE || epilogue > Q3T_EPI_SILU) return fail(Q3T_EINVAL, "linear: epilogue");
   (void)workspace;
   (void)workspace_bytes;
   const Plan p = plan(rows, in_features, out_features);
@@ -535,6 +539,7 @@ extern "C" int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t
     case Q3T_EPI_RESIDUAL: return dispatch_bn<Q3T_EPI_RESIDUAL>(p, tmw, tmx, a, stream);
     case Q3T_EPI_RESIDUAL_SCALED: return dispatch_bn<Q3T_EPI_RESIDUAL_SCALED>(p, tmw, tmx, a, stream);
     case Q3T_EPI_GELU: return dispatch_bn<Q3T_EPI_GELU>(p, tmw, tmx, a, stream);
+    case Q3T_EPI_SILU: return dispatch_bn<Q3T_EPI_SILU>(p, tmw, tmx, a, stream);
     default: return dispatch_bn<Q3T_EPI_SWIGLU_PAIRED>(p, tmw, tmx, a, stream);
   }
 }

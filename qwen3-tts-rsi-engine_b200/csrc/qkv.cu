@@ -23,7 +23,6 @@ __global__ void qk_norm_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, in
                                        __nv_bfloat16* __restrict__ tv, int length, const int64_t* __restrict__ slots,
                                        int q_heads, int kv_heads, int64_t capacity, unsigned* status) {
   constexpr int DL = D / 32;
-  grid_dependency_launch();
   grid_dependency_wait();
   const int64_t r = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

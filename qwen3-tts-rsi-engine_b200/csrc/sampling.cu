@@ -136,7 +136,6 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
   __shared__ int cand_i[kMaxWidth];
   __shared__ int cand_n;
   __shared__ uint8_t removed[kMaxWidth];
-  grid_dependency_launch();
   grid_dependency_wait();
 
   const int64_t r = blockIdx.x;

@@ -417,6 +417,18 @@ class CodecSlots:
         self._validate(indices, codes)
         return self._graph(len(indices), codes.shape[-1]).run(torch.tensor(indices, device=self.device), codes)
 
+    def decode_groups(self, groups, on_output=None):
+        """Decode several (indices, codes) groups in order (codec_slots.py:241-305 surface).
+
+        Every group is enqueued on the current stream; `on_output(i, output)` is
+        called as each group's (wave, pcm) clone is enqueued. Returns the outputs."""
+        outputs = []
+        for index, (indices, codes) in enumerate(groups):
+            outputs.append(self.decode(indices, codes))
+            if on_output is not None:
+                on_output(index, outputs[-1])
+        return outputs
+
     def reset(self, slot: int) -> None:
         self.state.reset(slot)
 
@@ -430,3 +442,38 @@ class CodecSlots:
         for step in self.graphs.values():
             step.close()
         self.graphs.clear()
+
+
+class CodecGraph:
+    """Windowed (non-incremental) decode of whole code windows (codec_graph.py:10-29).
+
+    ``decode(codes [b, codebooks, T])`` returns the audio of all T frames decoded
+    from a fresh stream, as the reference's full-sequence decoder call does. The
+    causal decoder's output for a window equals that of an incremental decode of
+    the same frames from zeroed state, so the window runs through a private
+    CodecSlots arena of `max_batch` slots: the slots are reset, then the frames
+    go through in chunks of up to `chunk` frames (one captured graph per
+    (batch, chunk length)) and the chunk outputs are concatenated."""
+
+    def __init__(self, cfg: CodecConfig, packed: dict, device, max_batch: int = 4, chunk: int = 56,
+                 use_graphs: bool = True):
+        self.slots = CodecSlots(cfg, packed, max_batch, device, max_chunk_frames=chunk, use_graphs=use_graphs)
+        self.chunk = chunk
+        self.captures = self.slots.graphs
+
+    @torch.inference_mode()
+    def decode(self, codes: torch.Tensor):
+        batch, _, frames = codes.shape
+        if not 1 <= batch <= self.slots.slots or frames < 1:
+            raise ValueError("Window batch must fit the codec graph arena")
+        self.slots.reset_range(0, batch)
+        indices = list(range(batch))
+        waves, pcms = [], []
+        for start in range(0, frames, self.chunk):
+            wave, pcm = self.slots.decode(indices, codes[..., start:start + self.chunk].contiguous())
+            waves.append(wave)
+            pcms.append(pcm)
+        return torch.cat(waves, -1), torch.cat(pcms, -1)
+
+    def close(self) -> None:
+        self.slots.close()

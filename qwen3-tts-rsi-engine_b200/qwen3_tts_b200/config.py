@@ -96,3 +96,55 @@ def tiny_talker(layers: int = 2) -> TalkerConfig:
 
 def tiny_predictor(layers: int = 2) -> PredictorConfig:
     return replace(PREDICTOR, layers=layers, hidden=256, ffn=512, vocab=2048, talker_hidden=256)
+
+
+@dataclass(frozen=True)
+class PromptConfig:
+    """CustomVoice prompt geometry (custom_voice_prompt.py:23-70).
+
+    Text ids are embedded by a [text_vocab, text_hidden] table and mapped to the
+    talker width by ``text_projection`` (fc1 text_hidden -> text_hidden with
+    SiLU, fc2 -> hidden, both with bias). Codec-side control ids (think tags,
+    language ids, speaker ids, codec pad/bos) index the talker's codec
+    embedding; they all sit in the last 1024 ids the sampler masks out.
+    The special text ids follow the Qwen chat template the reference tokenizes
+    (role tokens first, five template tokens last).
+    """
+    text_vocab: int = 151936
+    text_hidden: int = 2048
+    hidden: int = 2048
+    im_start: int = 151644
+    im_end: int = 151645
+    assistant: int = 77091
+    user: int = 872
+    newline: int = 198
+    tts_pad: int = 151671
+    tts_bos: int = 151672
+    tts_eos: int = 151673
+    codec_pad: int = 2148
+    codec_bos: int = 2149
+    codec_think: int = 2154
+    codec_nothink: int = 2155
+    codec_think_bos: int = 2156
+    codec_think_eos: int = 2157
+    languages: tuple = (("english", 2050), ("chinese", 2055), ("japanese", 2058), ("korean", 2064))
+    speakers: tuple = (("voice_a", 3000), ("voice_b", 3001))
+    dialects: tuple = ()   # (speaker, dialect-language) pairs; a dialect speaker's Chinese/auto
+                           # prompts use the dialect's language id
+
+    @property
+    def language_ids(self) -> dict:
+        return dict(self.languages)
+
+    @property
+    def speaker_ids(self) -> dict:
+        return dict(self.speakers)
+
+
+PROMPT = PromptConfig()
+
+
+def tiny_prompt(hidden: int = 256) -> PromptConfig:
+    """Reduced text vocabulary and width for CPU-checkable parity (special ids remapped)."""
+    return replace(PROMPT, text_vocab=1024, text_hidden=hidden, hidden=hidden, im_start=1000, im_end=1001,
+                   assistant=1002, user=1003, newline=1004, tts_pad=1005, tts_bos=1006, tts_eos=1007)

@@ -500,7 +500,49 @@ def codec_positions(frames_by_slot, slots, batch: int, frames: int, ring: int, r
          cache.data_ptr(), int(advance), _stream())
 
 
+STATUS_NONFINITE = 1 << 4
+
+
 def pcm16(x, wave=None, pcm=None) -> None:
-    """wave = clip(x, -1, 1) (fp32) and/or pcm = int16(wave * 32767) on the device."""
+    """wave = clip(x, -1, 1) (fp32) and/or pcm = int16(wave * 32767) on the device;
+    a nonfinite sample raises STATUS_NONFINITE in the device status word."""
     _need_cuda(x)
-    call("q3t_pcm16", x.data_ptr(), x.numel(), _ptr(wave), _ptr(pcm), _stream())
+    call("q3t_pcm16", x.data_ptr(), x.numel(), _ptr(wave), _ptr(pcm), status_word(x.device).data_ptr(), _stream())
+
+
+# ------------------------------------------------------------------ engine slot state
+def tick_gather(active, tokens, hidden_state, codec_embedding, tables, frames, trailing, trailing_len, pad, positions,
+                rotary, *, pred_inputs, codes, draws, talker_uniform, steps, text, step_positions, step_rotary,
+                rows: int) -> None:
+    """State arrays -> one tick's predictor/talker inputs (continuous.py:575-606)."""
+    hidden = hidden_state.shape[-1]
+    call("q3t_tick_gather", active.data_ptr(), tokens.data_ptr(), hidden_state.data_ptr(), codec_embedding.data_ptr(),
+         codec_embedding.shape[0], tables.data_ptr(), tables.shape[1], frames.data_ptr(), trailing.data_ptr(),
+         trailing.shape[1], trailing_len.data_ptr(), pad.data_ptr(), positions.data_ptr(), rotary.data_ptr(),
+         pred_inputs.data_ptr(), codes.data_ptr(), codes.stride(0), draws.data_ptr(), talker_uniform.data_ptr(),
+         steps.data_ptr(), text.data_ptr(), step_positions.data_ptr(), step_rotary.data_ptr(), rows, hidden,
+         status_word(tokens.device).data_ptr(), _stream())
+
+
+def tick_commit(active, codes, step_hidden, hidden_state, ring, frames, positions, rotary, *, rows: int) -> None:
+    """Step outputs -> state arrays and the code ring (continuous.py:618-635)."""
+    call("q3t_tick_commit", active.data_ptr(), codes.data_ptr(), codes.stride(0), ring.shape[2], step_hidden.data_ptr(),
+         hidden_state.data_ptr(), ring.data_ptr(), ring.shape[1], frames.data_ptr(), positions.data_ptr(),
+         rotary.data_ptr(), rows, hidden_state.shape[-1], _stream())
+
+
+def code_ring_write(ring, codes, frame_indices) -> None:
+    """ring[i, frame_indices[i] % depth] = codes[i] (codec_code_buffer.py:12-17)."""
+    _need_cuda(ring, codes, frame_indices)
+    call("q3t_code_ring_write", codes.data_ptr(), codes.stride(0), frame_indices.data_ptr(), ring.data_ptr(),
+         ring.shape[1], ring.shape[2], codes.shape[0], _stream())
+
+
+def code_ring_read(ring, indices, starts, length: int, out=None):
+    """[batch, codebooks, length] codes of retained frames (codec_code_buffer.py:19-27)."""
+    _need_cuda(ring, indices, starts)
+    batch = indices.numel()
+    out = torch.empty(batch, ring.shape[2], length, dtype=torch.long, device=ring.device) if out is None else out
+    call("q3t_code_ring_read", ring.data_ptr(), ring.shape[0], ring.shape[1], ring.shape[2], indices.data_ptr(),
+         starts.data_ptr(), batch, length, out.data_ptr(), status_word(ring.device).data_ptr(), _stream())
+    return out

@@ -176,6 +176,101 @@ class TalkerStep:
             self.graph = None
 
 
+class TalkerPrefill:
+    """Batched padded prefill straight into arena slots (PrefillGraph, prefill_graph.py:18-78).
+
+    ``batch`` prompts padded to ``length`` run the full causal stack; row
+    (b, t) writes its K/V at position t of arena slot ``slots[b]`` and attends
+    keys 0..t of that slot. Returns the final-norm hidden state and fp32 logits
+    of each prompt's last real token (continuous.py:455-458)."""
+
+    def __init__(self, cfg: DecoderConfig, weights: dict, arena: SlotArena, batch: int, length: int, cos, sin,
+                 norm_mode: int = _lib.NORM_REFERENCE):
+        if length > arena.capacity:
+            raise ValueError("Prompt longer than the KV arena")
+        self.cfg, self.w, self.arena = cfg, weights, arena
+        self.batch, self.length = batch, length
+        self.cos, self.sin, self.norm_mode = cos, sin, norm_mode
+        dev = arena.device
+        R, H = batch * length, cfg.hidden
+        self.inputs = torch.zeros(R, H, dtype=BF16, device=dev)
+        self.slots = torch.zeros(batch, dtype=torch.long, device=dev)
+        self.last = torch.zeros(batch, dtype=torch.long, device=dev)          # row index b*L + len_b - 1
+        self.positions = torch.arange(length, device=dev).repeat(batch).contiguous()
+        self.h = torch.zeros(R, H, dtype=BF16, device=dev)
+        self.xn = torch.zeros(R, H, dtype=BF16, device=dev)
+        self.qkv = torch.zeros(R, cfg.qkv_width, dtype=BF16, device=dev)
+        self.q = torch.zeros(R, cfg.q_heads, cfg.head_dim, dtype=BF16, device=dev)
+        self.attn = torch.zeros(R, cfg.q_heads, cfg.head_dim, dtype=BF16, device=dev)
+        self.act = torch.zeros(R, cfg.ffn, dtype=BF16, device=dev)
+        self.hidden = torch.zeros(batch, H, dtype=BF16, device=dev)
+        self.logits = torch.zeros(batch, cfg.vocab, dtype=torch.float32, device=dev)
+        need = ops.decode_attention_workspace_bytes(R, cfg.q_heads, cfg.head_dim, length)
+        self.ws_attn = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
+        self.status = ops.status_word(dev)
+        self.graph = None
+
+    def compute(self) -> None:
+        cfg, w, R, L = self.cfg, self.w, self.batch * self.length, self.length
+        res_in = self.inputs
+        for i, layer in enumerate(w["layers"]):
+            ops.rms_norm(res_in, layer.input_norm, cfg.eps, self.norm_mode, out=self.xn)
+            ops.linear(self.xn, layer.qkv, out=self.qkv)
+            ops.qk_norm_rope_kv(self.qkv, layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin, self.positions,
+                                self.positions, self.arena.keys[i], self.arena.values[i], q_heads=cfg.q_heads,
+                                kv_heads=cfg.kv_heads, head_dim=cfg.head_dim, length=L, query_out=self.q,
+                                slots=self.slots)
+            ops.decode_attention(self.q, self.arena.keys[i], self.arena.values[i], self.positions, context=L,
+                                 rows_per_slot=L, slots=self.slots, out=self.attn, workspace=self.ws_attn)
+            ops.linear(self.attn.view(R, cfg.q_width), layer.o, out=self.h, epilogue=_lib.EPI_RESIDUAL,
+                       residual=res_in)
+            ops.rms_norm(self.h, layer.post_norm, cfg.eps, self.norm_mode, out=self.xn)
+            ops.linear(self.xn, layer.gate_up, out=self.act, epilogue=_lib.EPI_SWIGLU_PAIRED)
+            ops.linear(self.act, layer.down, out=self.h, epilogue=_lib.EPI_RESIDUAL, residual=self.h)
+            res_in = self.h
+        ops.embedding(self.last, self.h, out=self.xn[:self.batch])       # last real row of each prompt
+        ops.rms_norm(self.xn[:self.batch], w["norm"], cfg.eps, self.norm_mode, out=self.hidden)
+        ops.linear(self.hidden, w["head"], out=self.logits)
+
+    @torch.inference_mode()
+    def capture(self, warmup: int = 2) -> None:
+        """Capture after warm-up; warm-up writes only to scratch slot rows that are
+        restored (slots default to 0..batch-1; their first `length` positions are saved)."""
+        saved = self.arena.packed[:, :self.batch, :, :self.length].clone()
+        self.slots.copy_(torch.arange(self.batch, device=self.slots.device))
+        self.last.copy_(torch.arange(self.batch, device=self.last.device) * self.length + self.length - 1)
+        stream = torch.cuda.Stream(device=self.inputs.device)
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                self.compute()
+        torch.cuda.current_stream().wait_stream(stream)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=stream):
+            self.compute()
+        torch.cuda.synchronize()
+        self.arena.packed[:, :self.batch, :, :self.length].copy_(saved)
+
+    @torch.inference_mode()
+    def run(self, embeds, lengths, slots):
+        """embeds [batch, length, H] (right-padded), lengths [batch], slots [batch] -> (hidden, logits)."""
+        self.inputs.copy_(embeds.reshape(self.batch * self.length, -1))
+        self.slots.copy_(slots)
+        self.last.copy_(torch.arange(self.batch, device=self.last.device) * self.length + lengths - 1)
+        if self.graph is None:
+            self.compute()
+        else:
+            self.graph.replay()
+        return self.hidden.clone(), self.logits.clone()
+
+    def close(self) -> None:
+        if self.graph is not None:
+            torch.cuda.synchronize()
+            self.graph.reset()
+            self.graph = None
+
+
 class TalkerDecoder:
     """Talker weights, arena and per-bucket step graphs."""
 
