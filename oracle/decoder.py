@@ -146,7 +146,10 @@ def predictor_frame(cfg, weights, hidden, first, draws, tables, mode="fp32", *, 
         if forced_codes is not None:
             token = forced_codes[:, step:step + 1]
     subcodes = torch.cat(codes, dim=-1)
+    # The frame embedding sums the codes the frame actually carries: the forced ones
+    # under teacher forcing, else this chain's own draws (continuous.py:590-597).
+    carried = forced_codes if forced_codes is not None else subcodes
     acc = first.float()
     for i in range(cfg.groups):
-        acc = acc + weights["embeddings"][i][subcodes[:, i]].float()
+        acc = acc + weights["embeddings"][i][carried[:, i]].float()
     return subcodes, acc, torch.stack(all_logits)

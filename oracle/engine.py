@@ -58,14 +58,19 @@ class RequestOracle:
         self.seen = torch.zeros(talker_cfg.vocab, dtype=torch.bool)
         self.token = None
         self.gaps: list[float] = []
+        self.labels: list[tuple] = []   # (frame, draw kind, step, engine token, best token) per gap
 
     def _head(self, hidden):
         logits = hidden @ self.tw["head"].float().T
         return bf(logits) if self.mode == "bf16" else logits
 
+    def _record(self, scores, token, kind, step):
+        self.gaps.append(gap(scores, token))
+        self.labels.append((self.frames, kind, step, int(token), int(scores.argmax())))
+
     def first(self, engine_token: int) -> None:
         scores = semantic_scores(self.logits, self.seen, 0, self.allowed, self.tc.eos)
-        self.gaps.append(gap(scores, engine_token))
+        self._record(scores, engine_token, "first", 0)
         self.seen[engine_token] = True
         self.token = engine_token
 
@@ -80,13 +85,13 @@ class RequestOracle:
                                                    self.ptables, self.mode, top_k=1,
                                                    forced_codes=torch.tensor([codes[1:]]))
         for step in range(self.pc.groups):
-            self.gaps.append(gap(logits[step, 0].float(), codes[1 + step]))
+            self._record(logits[step, 0].float(), codes[1 + step], "predictor", step)
         embeds = bf(bf(acc) + self.pad) if self.mode == "bf16" else acc + self.pad
         hidden, logits = OD.talker_decode_step(self.tc, self.tw, embeds, torch.tensor([self.position]),
                                                torch.tensor([0]), self.cache, self.ttables, self.mode)
         self.hidden = hidden[0]
         scores = semantic_scores(logits[0], self.seen, self.frames + 1, self.allowed, self.tc.eos)
-        self.gaps.append(gap(scores, engine_next))
+        self._record(scores, engine_next, "talker", 0)
         self.seen[engine_next] = True
         self.token = engine_next
         self.frames += 1

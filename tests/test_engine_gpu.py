@@ -105,7 +105,7 @@ def test_engine_ticks_match_teacher_forced_oracle(cuda):
 
     # teacher-forced oracle over every request's frames (including the cancelled one)
     table_codec = tw["embedding"].float()
-    gaps = []
+    gaps, labels = [], []
     for name, frames in log.items():
         payload = PAYLOADS[name]
         ids = P.text_ids(prcfg, payload)
@@ -118,6 +118,7 @@ def test_engine_ticks_match_teacher_forced_oracle(cuda):
         for frame, codes, token in frames:
             oracle.frame(codes, token)
         gaps.extend(oracle.gaps)
+        labels.extend((name,) + label for label in oracle.labels)
         if name in results:
             codes = torch.tensor([c for _, c, _ in frames]).T[None]          # [1, 16, frames]
             ref = OC.IncrementalOracle(decoder).decode(codes, OC.IncrementalOracle(decoder).new_state())
@@ -126,8 +127,9 @@ def test_engine_ticks_match_teacher_forced_oracle(cuda):
             assert got.shape == ref.shape
             assert snr_db(ref, got) >= 40.0, name
     gaps = np.array(gaps)
-    assert np.all(gaps <= 5e-2), float(gaps.max())
-    assert (gaps == 0).mean() >= 0.9, float((gaps == 0).mean())
+    worst = [(float(gaps[i]),) + labels[i] for i in np.argsort(-gaps)[:12] if gaps[i] > 0]
+    assert np.all(gaps <= 5e-2), worst
+    assert (gaps == 0).mean() >= 0.9, (float((gaps == 0).mean()), worst)
 
 
 def test_engine_prompt_matches_oracle(cuda):
