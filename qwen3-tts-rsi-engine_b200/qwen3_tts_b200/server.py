@@ -1,0 +1,349 @@
+"""Streaming speech service over the continuous engine (SpeechService, server.py:44-252).
+
+One model-owner thread does all device work; HTTP handlers never touch the
+GPU. Requests arrive on ``POST /v1/audio/speech`` and are answered as
+server-sent events:
+
+* ``speech.audio.delta`` ``{audio: base64 PCM16LE, sample_rate, channels: 1}``
+  (streamed chunks when ``streaming`` is on, then the not-yet-sent tail),
+* ``speech.audio.done`` ``{finish_reason, codec_frames}``,
+* ``speech.audio.error`` ``{error: {message}}`` if the request fails mid-stream.
+
+Two scheduling modes, as in the reference: ``run`` groups queued requests into
+micro-batches for a ``generate(payloads[, emit])`` model, and
+``run_continuous`` drives ``tick(submissions, emit, cancelled)`` of a
+continuous model, admitting up to ``prefill_per_tick`` new requests every
+``prefill_interval`` ticks (cancellations are passed on every tick).
+
+``model_factory(model_path, device)`` builds the model on the owner thread; the
+dispatcher in ``dispatcher.py`` provides a factory that fronts one engine
+process per GPU.
+"""
+from __future__ import annotations
+
+import argparse
+import asyncio
+import base64
+import json
+import logging
+import threading
+from concurrent.futures import ThreadPoolExecutor
+from functools import partial
+from pathlib import Path
+
+LOGGER = logging.getLogger(__name__)
+MAX_INPUT_CHARS = 10000
+
+
+class AudioChannel:
+    """Bounded per-request audio queue fed from the model-owner thread.
+
+    ``emit`` blocks the owner thread for at most 30 s when the client falls
+    behind (16 queued chunks); a timeout or a closed loop marks the channel
+    failed and later chunks are dropped."""
+
+    def __init__(self, loop, depth: int = 16):
+        self.loop = loop
+        self.queue = asyncio.Queue(maxsize=depth)
+        self.closed = threading.Event()
+        self.error = None
+
+    def emit(self, pcm: bytes, sample_rate: int) -> None:
+        if self.closed.is_set():
+            return
+        future = asyncio.run_coroutine_threadsafe(self.queue.put((pcm, sample_rate)), self.loop)
+        try:
+            future.result(timeout=30)
+        except Exception as error:  # the client stopped reading or the loop is gone
+            future.cancel()
+            self.error = error
+            self.closed.set()
+
+    def close(self) -> None:
+        self.closed.set()
+        while not self.queue.empty():
+            self.queue.get_nowait()
+
+
+def normalize(payload, speakers, languages) -> dict:
+    """Validate one request body; raises ValueError/TypeError with the reason (HTTP 400)."""
+    if not isinstance(payload, dict):
+        raise ValueError("Request must be an object")
+    text = payload.get("input")
+    if not isinstance(text, str) or not text.strip():
+        raise ValueError("Nonempty input text is required")
+    if len(text) > MAX_INPUT_CHARS:
+        raise ValueError(f"Input exceeds {MAX_INPUT_CHARS} characters")
+    if payload.get("response_format", "pcm") != "pcm" or payload.get("stream_format", "sse") != "sse":
+        raise ValueError("This endpoint requires PCM over SSE")
+    request = {"input": text, "voice": str(payload.get("voice", "Ryan")).lower(),
+               "language": str(payload.get("language", "English")).lower(),
+               "instructions": payload.get("instructions", ""), "seed": payload.get("seed", 42),
+               "max_new_tokens": payload.get("max_new_tokens", 2048)}
+    if payload.get("input_ids") is not None:
+        ids = payload["input_ids"]
+        if not isinstance(ids, list) or not all(type(i) is int and i >= 0 for i in ids):
+            raise ValueError("input_ids must be a list of non-negative integers")
+        request["input_ids"] = ids
+    if request["voice"] not in speakers or request["language"] not in languages:
+        raise ValueError("Unsupported speaker or language")
+    if not isinstance(request["instructions"], str):
+        raise ValueError("Instructions must be text")
+    if type(request["seed"]) is not int or not 0 <= request["seed"] < 2 ** 32:
+        raise ValueError("Seed must be an unsigned 32-bit integer")
+    if type(request["max_new_tokens"]) is not int or not 2 <= request["max_new_tokens"] <= 4096:
+        raise ValueError("max_new_tokens must be an integer in [2,4096]")
+    return request
+
+
+def sse(event: dict) -> bytes:
+    return ("data: " + json.dumps(event) + "\n\n").encode()
+
+
+def delta(pcm: bytes, sample_rate: int) -> dict:
+    return {"type": "speech.audio.delta", "audio": base64.b64encode(pcm).decode(), "sample_rate": sample_rate,
+            "channels": 1}
+
+
+class SpeechService:
+    def __init__(self, options, model_factory):
+        self.options = options
+        self.model_factory = model_factory
+        self.queue: asyncio.Queue = asyncio.Queue(maxsize=options.queue_size)
+        self.executor = ThreadPoolExecutor(max_workers=1, thread_name_prefix="model-owner")
+        self.model = None
+        self.worker = None
+        self.failure = None
+
+    @property
+    def streaming(self) -> bool:
+        return bool(getattr(self.options, "streaming", False))
+
+    async def start(self, app) -> None:
+        loop = asyncio.get_running_loop()
+        self.model = await loop.run_in_executor(self.executor, self.model_factory, str(self.options.model),
+                                                self.options.device)
+        loop_fn = self.run_continuous if getattr(self.options, "continuous", False) else self.run
+        self.worker = asyncio.create_task(loop_fn())
+
+    async def stop(self, app) -> None:
+        if self.worker is not None:
+            self.worker.cancel()
+            await asyncio.gather(self.worker, return_exceptions=True)
+        if self.model is not None:
+            await asyncio.get_running_loop().run_in_executor(self.executor, self.model.close)
+        self.executor.shutdown(wait=True, cancel_futures=True)
+
+    # ------------------------------------------------------------------ micro-batch mode
+    async def run(self) -> None:
+        loop = asyncio.get_running_loop()
+        while True:
+            batch = [await self.queue.get()]
+            if getattr(self.options, "batch_wait_ms", 0):
+                await asyncio.sleep(self.options.batch_wait_ms / 1000)
+            while len(batch) < self.options.max_batch_size and not self.queue.empty():
+                batch.append(self.queue.get_nowait())
+            groups: dict = {}
+            for entry in batch:
+                if not entry[1].cancelled():
+                    groups.setdefault((entry[0]["seed"], entry[0]["max_new_tokens"]), []).append(entry)
+            for group in groups.values():
+                operation = self.model.generate
+                if self.streaming:
+                    operation = partial(operation, emit=lambda i, pcm, rate, g=group: g[i][2].emit(pcm, rate))
+                try:
+                    outputs = await loop.run_in_executor(self.executor, operation, [p for p, _, _ in group])
+                    if len(outputs) != len(group):
+                        raise RuntimeError("Model batch output count mismatch")
+                    for (_, future, channel), output in zip(group, outputs):
+                        self._resolve(future, channel, output)
+                except Exception as error:
+                    LOGGER.exception("Model batch failed")
+                    for _, future, _ in group:
+                        if not future.done():
+                            future.set_exception(error)
+            for _ in batch:
+                self.queue.task_done()
+
+    @staticmethod
+    def _resolve(future, channel, output) -> None:
+        if future.done():
+            return
+        if channel.error is not None:
+            future.set_exception(channel.error)
+        else:
+            future.set_result(output)
+
+    # ------------------------------------------------------------------ continuous mode
+    async def run_continuous(self) -> None:
+        loop = asyncio.get_running_loop()
+        pending: dict = {}
+        next_id, ticks = 0, 0
+        interval = getattr(self.options, "prefill_interval", 1)
+        budget = getattr(self.options, "prefill_per_tick", 4)
+        while True:
+            cancelled = [i for i, (_, future, _) in pending.items() if future.cancelled()]
+            for identifier in cancelled:
+                del pending[identifier]
+                self.queue.task_done()
+            submissions = []
+
+            def admit(entry):
+                nonlocal next_id
+                if entry[1].cancelled():
+                    self.queue.task_done()
+                    return
+                pending[next_id] = entry
+                submissions.append((next_id, entry[0]))
+                next_id += 1
+
+            if not pending and not cancelled:
+                admit(await self.queue.get())   # idle: block for the next request
+                if not submissions:
+                    continue
+            if not pending or ticks % interval == 0 or submissions:
+                while (len(pending) < self.options.max_batch_size and len(submissions) < budget
+                       and not self.queue.empty()):
+                    admit(self.queue.get_nowait())
+
+            def emit(identifier, pcm, rate):
+                entry = pending.get(identifier)
+                if entry is not None and self.streaming:
+                    entry[2].emit(pcm, rate)
+
+            try:
+                outputs = await loop.run_in_executor(self.executor, self.model.tick, submissions, emit, cancelled)
+            except asyncio.CancelledError:
+                for _, future, channel in pending.values():
+                    channel.close()
+                    future.cancel()
+                raise
+            except Exception as error:
+                LOGGER.exception("Continuous model failed")
+                self.failure = error
+                for _, future, _ in pending.values():
+                    if not future.done():
+                        future.set_exception(error)
+                    self.queue.task_done()
+                return
+            ticks += 1
+            for identifier, output in outputs:
+                _, future, channel = pending.pop(identifier)
+                self._resolve(future, channel, output)
+                self.queue.task_done()
+
+    # ------------------------------------------------------------------ HTTP
+    async def health(self, incoming):
+        from aiohttp import web
+        state = "failed" if self.failure else "ready" if self.model else "starting"
+        body = {"status": state, "queued": self.queue.qsize(), "backend": "b200",
+                "audio_delivery": "codec-windows" if self.streaming else "complete-waveform"}
+        return web.json_response(body, status=503 if self.failure else 200)
+
+    async def speech(self, incoming):
+        from aiohttp import web
+        if self.failure is not None:
+            return web.json_response({"error": "Model worker failed"}, status=503)
+        try:
+            request = normalize(await incoming.json(), self.model.speakers, self.model.languages)
+        except (ValueError, TypeError) as error:
+            return web.json_response({"error": str(error)}, status=400)
+        loop = asyncio.get_running_loop()
+        future = loop.create_future()
+        channel = AudioChannel(loop)
+        try:
+            self.queue.put_nowait((request, future, channel))
+        except asyncio.QueueFull:
+            return web.json_response({"error": "Request queue full"}, status=503)
+        response = web.StreamResponse(headers={"Content-Type": "text/event-stream"})
+        try:
+            await response.prepare(incoming)
+            sent = 0
+            while self.streaming:
+                chunk = asyncio.ensure_future(channel.queue.get())
+                try:
+                    done, _ = await asyncio.wait((future, chunk), return_when=asyncio.FIRST_COMPLETED)
+                finally:
+                    if not chunk.done():
+                        chunk.cancel()
+                        await asyncio.gather(chunk, return_exceptions=True)
+                if chunk not in done:
+                    break
+                pcm, rate = chunk.result()
+                await response.write(sse(delta(pcm, rate)))
+                sent += len(pcm)
+            output = await future
+            if sent > len(output["pcm"]):
+                raise RuntimeError("Streaming output exceeded final waveform length")
+            await response.write(sse(delta(output["pcm"][sent:], output["sample_rate"])))
+            await response.write(sse({"type": "speech.audio.done", "finish_reason": output["finish_reason"],
+                                      "codec_frames": output["codec_frames"]}))
+        except asyncio.CancelledError:
+            future.cancel()
+            raise
+        except ConnectionResetError:
+            future.cancel()
+        except Exception as error:
+            await response.write(sse({"type": "speech.audio.error", "error": {"message": str(error)}}))
+        finally:
+            channel.close()
+            if not future.done():
+                future.cancel()
+        return response
+
+
+def engine_factory(options):
+    """Model factory for one GPU (``--gpus 1``) or the multi-GPU dispatcher."""
+    kwargs = dict(max_slots=options.max_batch_size, codec_left_context=options.codec_left_context,
+                  codec_batch_size=options.codec_batch_size, codec_chunk_frames=options.codec_chunk_frames,
+                  incremental_codec=True, seed=options.seed, prewarm_codec=options.prewarm_codec,
+                  decode_bucket_step=options.decode_bucket_step)
+    if options.gpus > 1:
+        from .dispatcher import Dispatcher
+        return lambda model, device: Dispatcher.start(options.gpus, kwargs, per_engine=options.max_batch_size)
+
+    def build(model, device):
+        from .continuous import ContinuousModel
+        return ContinuousModel(None, device, **kwargs)
+    return build
+
+
+def main(argv=None) -> None:
+    from aiohttp import web
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    parser.add_argument("--model", type=Path, default=Path("random-init"))
+    parser.add_argument("--device", default="cuda:0")
+    parser.add_argument("--gpus", type=int, default=1, help="engine processes, one per GPU")
+    parser.add_argument("--seed", type=int, default=0, help="random-init weight seed")
+    parser.add_argument("--host", default="127.0.0.1")
+    parser.add_argument("--port", type=int, default=8097)
+    parser.add_argument("--max-batch-size", type=int, default=64, help="slots per engine (power of two)")
+    parser.add_argument("--queue-size", type=int, default=512)
+    parser.add_argument("--streaming", action="store_true")
+    parser.add_argument("--prefill-per-tick", type=int, default=4)
+    parser.add_argument("--prefill-interval", type=int, default=1)
+    parser.add_argument("--codec-left-context", type=int, default=72)
+    parser.add_argument("--codec-batch-size", type=int, choices=[1, 2, 4, 8], default=4)
+    parser.add_argument("--codec-chunk-frames", type=int, choices=[8, 16], default=8)
+    parser.add_argument("--decode-bucket-step", type=int, default=0)
+    parser.add_argument("--prewarm-codec", action="store_true")
+    options = parser.parse_args(argv)
+    options.continuous = True
+    if options.max_batch_size < 1 or options.max_batch_size & (options.max_batch_size - 1):
+        parser.error("Continuous slots must be a power of two")
+    if options.prefill_per_tick < 1 or not 1 <= options.prefill_interval <= 64 or options.queue_size < 1:
+        parser.error("Invalid admission or queue settings")
+    logging.basicConfig(level=logging.INFO)
+    factory = engine_factory(options)
+    options.max_batch_size *= max(1, options.gpus)   # requests in flight across all engines
+    service = SpeechService(options, factory)
+    app = web.Application(client_max_size=1024 * 1024)
+    app.router.add_get("/health", service.health)
+    app.router.add_post("/v1/audio/speech", service.speech)
+    app.on_startup.append(service.start)
+    app.on_cleanup.append(service.stop)
+    web.run_app(app, host=options.host, port=options.port, handler_cancellation=True)
+
+
+if __name__ == "__main__":
+    main()
