@@ -316,16 +316,6 @@ int pick_chunk(int64_t batch, int64_t kv_heads, int64_t context) {
   return chunk;
 }
 
-// Persistent tensor-core kernel: chunks of 256 keys (4 TMA tiles) unless the
-// work would not give every resident CTA (two per SM) about four items at the
-// bucket's full context; smaller chunks cost more partial stores and merges.
-int pick_stream_chunk(int64_t batch, int64_t kv_heads, int64_t context) {
-  const int64_t target = 8LL * sm_count();
-  int chunk = 256;
-  while (chunk > 64 && batch * kv_heads * ((context + chunk - 1) / chunk) < target) chunk >>= 1;
-  return chunk;
-}
-
 template <int D, int G>
 int launch_attn(const void* q, const void* k, const void* v, const int64_t* pos, void* out, int64_t rows,
                 int64_t rows_per_slot, const int64_t* slots, int64_t ring, int64_t kv_heads, int64_t capacity,
@@ -409,12 +399,9 @@ extern "C" int q3t_decode_attention(const void* query, const void* keys, const v
     call.context = context;
     call.window = window;
     call.scale = scale;
-    if (size_t(rows) * size_t(kv_heads) > kMaxTickets - 2)
-      return fail(Q3T_EUNSUPPORTED, "attention: rows x kv_heads > 65534");
-    call.chunk = pick_stream_chunk(rows, kv_heads, span);
+    call.chunk = pick_chunk(rows, kv_heads, span);
     call.max_chunks = int((span + call.chunk - 1) / call.chunk);
     call.counters = static_cast<unsigned*>(workspace);
-    call.work = call.counters + (kMaxTickets - 2);
     call.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kTicketBytes);
     call.status = status;
     call.stream = stream;

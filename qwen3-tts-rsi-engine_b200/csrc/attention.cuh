@@ -18,8 +18,7 @@ struct AttentionCall {
   float scale;
   int chunk, max_chunks;
   float* partials;
-  unsigned* counters;  // one chunk ticket per (row, kv head)
-  unsigned* work;      // two counters: next work item, CTAs finished (both zero between calls)
+  unsigned* counters;  // one chunk ticket per (row, kv head), zero between calls
   unsigned* status;
   void* stream;
 };
