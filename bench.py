@@ -48,6 +48,12 @@ def parse_args():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--layers", type=int, default=28, help="talker depth (28 = the benchmarked model)")
+    p.add_argument("--op-costs", action="store_true",
+                   help="print the in-graph cost of each talker-layer op (28 chained launches per op) and exit")
+    p.add_argument("--workload", choices=["step", "serving"], default="step",
+                   help="step: BASELINE config 2 (default); serving: BASELINE config 5, end-to-end ContinuousModel")
+    p.add_argument("--concurrency", type=int, default=32, help="serving: requests in flight (closed loop)")
+    p.add_argument("--requests", type=int, default=128, help="serving: synthetic requests per timed pass")
     return p.parse_args()
 
 
@@ -380,12 +386,13 @@ def kernel_rooflines(cfg, engine, step, positions, dev):
     t = timed(lambda: ops.decode_attention(step.q, engine.arena.keys[0], engine.arena.values[0], pos,
                                            context=step.context, out=step.attn, workspace=step.ws_attn))
     out["decode_attention"] = {"seconds": t, "bytes": kv_bytes + q_bytes, "per_step": cfg.layers}
-    for name, w, x, o, epi, res in (
-            ("linear_gate_up", layer.gate_up, step.xn, step.act, _lib.EPI_SWIGLU_PAIRED, None),
-            ("linear_qkv", layer.qkv, step.xn, step.qkv, _lib.EPI_STORE, None),
-            ("linear_down", layer.down, step.act, step.h, _lib.EPI_RESIDUAL, step.h),
-            ("linear_o", layer.o, step.attn.view(B, -1), step.h, _lib.EPI_RESIDUAL, step.h)):
-        t = timed(lambda: ops.linear(x, w, out=o, epilogue=epi, residual=res, workspace=step.ws_linear))
+    eps = cfg.eps if layer.folded else None   # QKV and gate/up carry the folded RMSNorm
+    for name, w, x, o, epi, res, norm in (
+            ("linear_gate_up", layer.gate_up, step.h, step.act, _lib.EPI_SWIGLU_PAIRED, None, eps),
+            ("linear_qkv", layer.qkv, step.h, step.qkv, _lib.EPI_STORE, None, eps),
+            ("linear_down", layer.down, step.act, step.h, _lib.EPI_RESIDUAL, step.h, None),
+            ("linear_o", layer.o, step.attn.view(B, -1), step.h, _lib.EPI_RESIDUAL, step.h, None)):
+        t = timed(lambda: ops.linear(x, w, out=o, epilogue=epi, residual=res, row_norm_eps=norm))
         nbytes = w.numel() * 2 + x.numel() * 2 + o.numel() * 2 * (2 if res is not None else 1)
         out[name] = {"seconds": t, "bytes": nbytes, "per_step": cfg.layers}
     del flush
@@ -413,8 +420,159 @@ def run_reference(args, dist: Dist):
     }
 
 
+def op_costs(args) -> None:
+    """In-graph cost of each op of a talker layer: one CUDA graph of 28 back-to-back launches
+    of the same op cycling through the 28 layers' weights and KV (nothing stays in L2), timed
+    with CUDA events; one JSON line per op (us per launch, achieved GB/s)."""
+    from qwen3_tts_b200 import _lib, ops
+    from qwen3_tts_b200.config import TALKER
+    from qwen3_tts_b200.talker import TalkerDecoder
+    from qwen3_tts_b200.weights import decoder_weights
+
+    dev = torch.device("cuda:0")
+    cfg, L = TALKER, TALKER.layers
+    work = Workload(args.seed)
+    positions = work.positions.to(dev)
+    engine = TalkerDecoder(cfg, decoder_weights(cfg, args.seed, dev), SLOTS, CAPACITY, dev, use_graphs=False)
+    step = engine.step_for(SLOTS, CAPACITY)
+    for plane in engine.arena.keys + engine.arena.values:
+        plane.normal_()
+    W = engine.weights["layers"]
+    eps = cfg.eps if W[0].folded else None
+
+    def graph_us(fn, replays=10):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for i in range(L):
+                fn(i)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            for i in range(L):
+                fn(i)
+        graph.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(replays):
+            graph.replay()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) * 1e3 / (L * replays)
+
+    kv = int(((work.positions + 1).sum()).item()) * cfg.kv_heads * cfg.head_dim * 2 * 2
+    B = SLOTS
+    costs = {
+        "linear_qkv": (lambda i: ops.linear(step.h, W[i].qkv, out=step.qkv, row_norm_eps=eps), W[0].qkv.numel() * 2),
+        "qk_norm_rope_kv": (lambda i: ops.qk_norm_rope_kv(
+            step.qkv, W[i].q_norm, W[i].k_norm, cfg.eps, engine.cos, engine.sin, positions, positions,
+            engine.arena.keys[i], engine.arena.values[i], q_heads=cfg.q_heads, kv_heads=cfg.kv_heads,
+            head_dim=cfg.head_dim, query_out=step.q), B * cfg.qkv_width * 2 * 2),
+        "decode_attention": (lambda i: ops.decode_attention(
+            step.q, engine.arena.keys[i], engine.arena.values[i], positions, context=CAPACITY, out=step.attn,
+            workspace=step.ws_attn), kv),
+        "decode_attention_qkv (fused q/k norm, RoPE, KV write)": (lambda i: ops.decode_attention_qkv(
+            step.qkv, W[i].q_norm, W[i].k_norm, cfg.eps, engine.cos, engine.sin, positions, engine.arena.keys[i],
+            engine.arena.values[i], positions, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
+            context=CAPACITY, out=step.attn, workspace=step.ws_attn), kv),
+        "linear_o": (lambda i: ops.linear(step.attn.view(B, -1), W[i].o, out=step.h, epilogue=_lib.EPI_RESIDUAL,
+                                          residual=step.h), W[0].o.numel() * 2),
+        "linear_gate_up": (lambda i: ops.linear(step.h, W[i].gate_up, out=step.act, epilogue=_lib.EPI_SWIGLU_PAIRED,
+                                                row_norm_eps=eps), W[0].gate_up.numel() * 2),
+        "linear_down": (lambda i: ops.linear(step.act, W[i].down, out=step.h, epilogue=_lib.EPI_RESIDUAL,
+                                             residual=step.h), W[0].down.numel() * 2),
+    }
+    total = 0.0
+    step_ops = {"linear_qkv", "decode_attention_qkv (fused q/k norm, RoPE, KV write)", "linear_o", "linear_gate_up",
+                "linear_down"}
+    for name, (fn, nbytes) in costs.items():
+        us = graph_us(fn)
+        total += us if name in step_ops else 0.0
+        print(json.dumps({"op": name, "us_per_launch": round(us, 2), "GBps": round(nbytes / us / 1e3, 1)}))
+    print(json.dumps({"layer_us (ops of the decode step)": round(total, 1), "step_ms_28_layers": round(total * L / 1e3, 3),
+                      "status": ops.read_status(dev)}))
+
+
+def serving_requests(seed: int, count: int):
+    """BASELINE config 5 synthetic requests: text ids U[0, 151936) of length U[20, 200], one of two
+    speakers, target audio frames U[50, 400] (max_new_tokens = target + 1, so each ends at its target)."""
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for i in range(count):
+        length = int(torch.randint(20, 201, (1,), generator=g))
+        ids = torch.randint(0, 151936, (length,), generator=g).tolist()
+        target = int(torch.randint(50, 401, (1,), generator=g))
+        out.append({"input": "", "input_ids": ids, "voice": ("voice_a", "voice_b")[i % 2], "language": "english",
+                    "instructions": "", "max_new_tokens": target + 1, "seed": seed * 1000 + i})
+    return out
+
+
+def run_serving(args) -> dict:
+    """Closed-loop serving through ContinuousModel.tick at `concurrency` requests in flight.
+
+    A first pass over the same request set captures every graph shape (untimed); the
+    second pass is timed on the host clock (the engine synchronises once per tick).
+    frames/s = codec frames delivered / wall time; TTFA = submission -> first PCM chunk;
+    RTF = mean request latency / mean request audio duration."""
+    from qwen3_tts_b200.continuous import ContinuousModel
+    dev = torch.device("cuda:0")
+    slots = 1 << max(0, (args.concurrency - 1).bit_length())
+    model = ContinuousModel(None, dev, max_slots=slots, initial_capacity=1024, seed=args.seed, codec_batch_size=4)
+    requests = serving_requests(args.seed, args.requests)
+
+    def one_pass():
+        pending = list(enumerate(requests))
+        submitted, first_audio, done, frames = {}, {}, {}, 0
+        in_flight = 0
+
+        def emit(identifier, pcm, rate):
+            first_audio.setdefault(identifier, time.perf_counter())
+
+        start = time.perf_counter()
+        while pending or in_flight:
+            subs = []
+            while pending and in_flight + len(subs) < args.concurrency:
+                subs.append(pending.pop(0))
+            now = time.perf_counter()
+            for identifier, _ in subs:
+                submitted[identifier] = now
+            in_flight += len(subs)
+            for identifier, result in model.tick(subs, emit=emit):
+                done[identifier] = time.perf_counter()
+                frames += result["codec_frames"]
+                in_flight -= 1
+        wall = time.perf_counter() - start
+        ttfa = sorted(first_audio[i] - submitted[i] for i in submitted)
+        latency = [done[i] - submitted[i] for i in submitted]
+        audio_s = [(requests[i]["max_new_tokens"] - 1) / 12.5 for i in submitted]
+        return {"frames": frames, "wall_s": wall, "ttfa": ttfa, "rtf": float(np.mean(latency) / np.mean(audio_s))}
+
+    one_pass()                       # graph capture for every (batch, context) and codec shape met
+    res = one_pass()
+    model.close()
+    ttfa = res["ttfa"]
+    pct = lambda q: ttfa[min(len(ttfa) - 1, int(q * len(ttfa)))]
+    return {"frames_per_s": res["frames"] / res["wall_s"], "frames": res["frames"], "wall_s": res["wall_s"],
+            "ttfa_p50_ms": pct(0.5) * 1e3, "ttfa_p95_ms": pct(0.95) * 1e3, "rtf": res["rtf"], "slots": slots}
+
+
 def main():
     args = parse_args()
+    if args.op_costs:
+        op_costs(args)
+        return
+    if args.workload == "serving":
+        res = run_serving(args)
+        print(json.dumps({
+            "metric": f"codec frames/s (end-to-end serving, C={args.concurrency})", "value": res["frames_per_s"],
+            "unit": UNIT, "n_gpus": 1, "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic (BASELINE config 5 request recipe, seeded random-init weights)",
+            "config": {"workload": "BASELINE config 5: talker -> code predictor -> incremental codec, closed loop",
+                       "concurrency": args.concurrency, "requests": args.requests, "slots": res["slots"]},
+            "ttfa_p50_ms": res["ttfa_p50_ms"], "ttfa_p95_ms": res["ttfa_p95_ms"], "rtf": res["rtf"],
+            "frames": res["frames"], "wall_s": res["wall_s"]}))
+        return
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", 0))
         if rank != 0:

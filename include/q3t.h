@@ -160,6 +160,19 @@ int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t in_feature
                int64_t residual_stride, const void* scale, const void* weight_tiles,
                void* workspace, size_t workspace_bytes, unsigned* status, void* stream);
 
+/* q3t_linear with the preceding RMSNorm folded in (qwen3_tts_engine/operators.py:16-23
+ * followed by the projection at packed_attention.py:42 / packed_mlp.py:20):
+ *   out[r, n] = epilogue(rsqrt(mean_k x[r, k]^2 + eps) * sum_k x[r, k] * weight[n, k] (+ bias[n]))
+ * with the norm weight pre-multiplied into the projection by the caller
+ * (weight[n, k] = W[n, k] * norm_weight[k], rounded to bf16). x is the raw
+ * residual stream; the row sums of squares are taken from the activation tiles
+ * the GEMM streams anyway, so no normalised copy of x is written. eps > 0. */
+int q3t_linear_rownorm(const void* x, int64_t x_stride, int64_t rows, int64_t in_features,
+                       const void* weight, int64_t out_features, const void* bias, void* out,
+                       int64_t out_stride, int out_dtype, int epilogue, const void* residual,
+                       int64_t residual_stride, const void* scale, float eps, const void* weight_tiles,
+                       unsigned* status, void* stream);
+
 /* Pre-swizzled weight layout for q3t_linear (pass it as weight_tiles, weight may
  * then be NULL): tile (n, k) of 128 rows x 64 columns is the contiguous 16 KB image
  * of the 128-byte-swizzled shared-memory tile, tiles ordered [n][k], zero padded.
@@ -208,6 +221,21 @@ int q3t_decode_attention(const void* query, const void* keys, const void* values
                          int64_t head_dim, int64_t arena_slots, int64_t capacity, int64_t context,
                          int64_t window, float scale, void* workspace, size_t workspace_bytes,
                          unsigned* status, void* stream);
+
+/* Talker decode step attention with the per-head q/k RMSNorm, RoPE and the
+ * K/V write of PackedAttention.forward (packed_attention.py:42-74) fused in:
+ * reads the raw QKV projection rows qkv [rows, (q_heads + 2 kv_heads) * head_dim]
+ * (row stride qkv_stride), normalises (q_norm/k_norm, nullable) and rotates them
+ * at rotary_positions with the cos/sin tables, writes the new key/value of row b
+ * at positions[b] of arena slot b, and attends over keys 0..positions[b]
+ * (one query row per slot, no window). Same workspace as q3t_decode_attention. */
+int q3t_decode_attention_qkv(const void* qkv, int64_t qkv_stride, const void* q_norm_weight,
+                             const void* k_norm_weight, float eps, const void* cos_table,
+                             const void* sin_table, int64_t table_len, const int64_t* rotary_positions,
+                             void* keys, void* values, const int64_t* positions, void* out, int64_t rows,
+                             int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t arena_slots,
+                             int64_t capacity, int64_t context, float scale, void* workspace,
+                             size_t workspace_bytes, unsigned* status, void* stream);
 
 /* No counterpart in the reference: an allocation-free form of
  * q3t_decode_attention for callers that cannot allocate device memory (a

@@ -8,10 +8,14 @@ q_norm/k_norm, rotate-half RoPE, cache update and GQA attention
 Layer internals belong to qwen-tts==0.1.1 (absent here), so they are restated
 from those call sites: this part of the oracle is unpinned.
 
-Two precisions:
+Three precisions:
   mode="fp32"  every op in fp32 from the bf16 weights (the parity truth);
   mode="bf16"  fp32 math with bf16 rounding at each point the reference's
-               bf16 tensors round (linear outputs, norms, RoPE ops, residuals).
+               bf16 tensors round (linear outputs, norms, RoPE ops, residuals);
+  mode="bf16f" as "bf16", with the input and post-attention RMSNorms folded
+               into the following projections the way the GPU path computes
+               them (norm weight premultiplied into the bf16 weight, row scale
+               on the fp32 product).
 """
 from __future__ import annotations
 
@@ -21,21 +25,38 @@ from .elementwise import bf, rope_tables
 from .sampling import categorical
 
 
+def _rounds(mode):
+    return mode in ("bf16", "bf16f")
+
+
 def _r(x, mode):
-    return bf(x) if mode == "bf16" else x
+    return bf(x) if _rounds(mode) else x
 
 
 def _rms(x, w, eps, mode):
     r = 1.0 / torch.sqrt(x.pow(2).mean(-1, keepdim=True) + eps)
-    if mode == "bf16":
+    if _rounds(mode):
         return bf(w.float() * bf(x * r))
     return w.float() * (x * r)
+
+
+def _normed_proj(h, norm_w, weight, eps, mode):
+    """RMSNorm of h followed by a projection. In mode "bf16f" the norm weight is
+    folded into the projection (bf16(W * w)) and the row scale rsqrt(mean(h^2)+eps)
+    multiplies the fp32 product before the bf16 rounding: the GPU's fused
+    q3t_linear_rownorm path. The other modes normalise first (operators.py:16-23)."""
+    if mode == "bf16f":
+        r = 1.0 / torch.sqrt(h.pow(2).mean(-1, keepdim=True) + eps)
+        folded = bf(weight.float() * norm_w.float()[None, :])
+        return bf((h @ folded.T) * r)
+    x = _rms(h, norm_w, eps, mode)
+    return _r(x @ weight.float().T, mode)
 
 
 def _rope(x, cos, sin, mode):
     half = x.shape[-1] // 2
     rot = torch.cat([-x[..., half:], x[..., :half]], dim=-1)
-    if mode == "bf16":
+    if _rounds(mode):
         return bf(bf(x * cos) + bf(rot * sin))
     return x * cos + rot * sin
 
@@ -55,10 +76,9 @@ def layer_forward(cfg, w, h, rot_pos, cache_k, cache_v, cache_pos, tables, mode)
     attends to cache positions 0..cache_pos[b, t]."""
     B, L, H = h.shape
     D, Hq, Hkv = cfg.head_dim, cfg.q_heads, cfg.kv_heads
-    x = _rms(h, w["input_norm"], cfg.eps, mode)
-    q = _r(x @ w["q"].float().T, mode).view(B, L, Hq, D)
-    k = _r(x @ w["k"].float().T, mode).view(B, L, Hkv, D)
-    v = _r(x @ w["v"].float().T, mode).view(B, L, Hkv, D)
+    q = _normed_proj(h, w["input_norm"], w["q"], cfg.eps, mode).view(B, L, Hq, D)
+    k = _normed_proj(h, w["input_norm"], w["k"], cfg.eps, mode).view(B, L, Hkv, D)
+    v = _normed_proj(h, w["input_norm"], w["v"], cfg.eps, mode).view(B, L, Hkv, D)
     q = _rms(q, w["q_norm"], cfg.eps, mode)
     k = _rms(k, w["k_norm"], cfg.eps, mode)
     cos = tables.cos[rot_pos][:, :, None, :]
@@ -81,9 +101,8 @@ def layer_forward(cfg, w, h, rot_pos, cache_k, cache_v, cache_pos, tables, mode)
             attn[b, t] = torch.einsum("hn,hnd->hd", torch.softmax(s, -1), vv)
     attn = _r(attn, mode).reshape(B, L, Hq * D)
     h = _r(h + _r(attn @ w["o"].float().T, mode), mode)
-    x = _rms(h, w["post_norm"], cfg.eps, mode)
-    gate = _r(x @ w["gate"].float().T, mode)
-    up = _r(x @ w["up"].float().T, mode)
+    gate = _normed_proj(h, w["post_norm"], w["gate"], cfg.eps, mode)
+    up = _normed_proj(h, w["post_norm"], w["up"], cfg.eps, mode)
     act = _r(_r(torch.nn.functional.silu(gate), mode) * up, mode)
     h = _r(h + _r(act @ w["down"].float().T, mode), mode)
     return h

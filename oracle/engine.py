@@ -41,7 +41,7 @@ def gap(scores, token: int) -> float:
 
 class RequestOracle:
     def __init__(self, talker_cfg, predictor_cfg, talker_w, predictor_w, inputs_embeds, pad, table, capacity,
-                 mode="bf16"):
+                 mode="bf16f"):
         self.tc, self.pc, self.tw, self.pw = talker_cfg, predictor_cfg, talker_w, predictor_w
         self.mode, self.pad, self.table = mode, pad.float(), table
         self.allowed = allowed_mask(talker_cfg.vocab, talker_cfg.eos)
@@ -62,7 +62,7 @@ class RequestOracle:
 
     def _head(self, hidden):
         logits = hidden @ self.tw["head"].float().T
-        return bf(logits) if self.mode == "bf16" else logits
+        return bf(logits) if self.mode in ("bf16", "bf16f") else logits
 
     def _record(self, scores, token, kind, step):
         self.gaps.append(gap(scores, token))
@@ -86,7 +86,7 @@ class RequestOracle:
                                                    forced_codes=torch.tensor([codes[1:]]))
         for step in range(self.pc.groups):
             self._record(logits[step, 0].float(), codes[1 + step], "predictor", step)
-        embeds = bf(bf(acc) + self.pad) if self.mode == "bf16" else acc + self.pad
+        embeds = bf(bf(acc) + self.pad) if self.mode in ("bf16", "bf16f") else acc + self.pad
         hidden, logits = OD.talker_decode_step(self.tc, self.tw, embeds, torch.tensor([self.position]),
                                                torch.tensor([0]), self.cache, self.ttables, self.mode)
         self.hidden = hidden[0]

@@ -358,6 +358,56 @@ extern "C" size_t q3t_decode_attention_workspace_bytes(int64_t batch, int64_t q_
   return attn_workspace(batch, q_heads, 0, head_dim, context);
 }
 
+extern "C" int q3t_decode_attention_qkv(const void* qkv, int64_t qkv_stride, const void* q_norm_weight,
+                                        const void* k_norm_weight, float eps, const void* cos_table,
+                                        const void* sin_table, int64_t table_len, const int64_t* rotary_positions,
+                                        void* keys, void* values, const int64_t* positions, void* out, int64_t rows,
+                                        int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t arena_slots,
+                                        int64_t capacity, int64_t context, float scale, void* workspace,
+                                        size_t workspace_bytes, unsigned* status, void* stream) {
+  if (!qkv || !cos_table || !sin_table || !rotary_positions || !keys || !values || !positions || !out)
+    return fail(Q3T_EINVAL, "attention_qkv: null pointer");
+  if (rows < 1 || rows > 65535 || kv_heads < 1 || q_heads % kv_heads || arena_slots < rows || table_len < 1)
+    return fail(Q3T_EINVAL, "attention_qkv: invalid row or head geometry");
+  if (context < 1 || context > capacity) return fail(Q3T_EINVAL, "Attention context must fit the KV arena");
+  if (size_t(rows) * size_t(kv_heads) > kMaxTickets) return fail(Q3T_EUNSUPPORTED, "attention: rows x kv_heads > 65536");
+  const int64_t g = q_heads / kv_heads;
+  if (!attention_mma_supported(head_dim, g))
+    return fail(Q3T_EUNSUPPORTED, "attention_qkv: head_dim %lld with %lld query heads per kv head",
+                (long long)head_dim, (long long)g);
+  if (qkv_stride < (q_heads + 2 * kv_heads) * head_dim || qkv_stride % 8 || !aligned16(qkv) || !aligned16(keys) ||
+      !aligned16(values))
+    return fail(Q3T_EINVAL, "attention_qkv: 16-byte aligned rows required");
+  const size_t need = attn_workspace(rows, q_heads, kv_heads, head_dim, context);
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
+    return fail(Q3T_ESPACE, "attention: workspace needs %zu bytes", need);
+  AttentionCall call;
+  call.query = qkv;
+  call.keys = keys;
+  call.values = values;
+  call.positions = positions;
+  call.out = out;
+  call.rows = rows;
+  call.rows_per_slot = 1;
+  call.slots = nullptr;
+  call.q_heads = q_heads;
+  call.kv_heads = kv_heads;
+  call.head_dim = head_dim;
+  call.arena_slots = arena_slots;
+  call.capacity = capacity;
+  call.context = context;
+  call.window = 0;
+  call.scale = scale;
+  call.chunk = pick_chunk(rows, kv_heads, context);
+  call.max_chunks = int((context + call.chunk - 1) / call.chunk);
+  call.counters = static_cast<unsigned*>(workspace);
+  call.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kTicketBytes);
+  call.status = status;
+  call.stream = stream;
+  return launch_attention_fused(call, qkv, qkv_stride, q_norm_weight, k_norm_weight, eps, cos_table, sin_table,
+                                table_len, rotary_positions);
+}
+
 extern "C" int q3t_decode_attention(const void* query, const void* keys, const void* values, const int64_t* positions,
                                     void* out, int64_t rows, int64_t rows_per_slot, const int64_t* slots, int64_t ring,
                                     int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t arena_slots,

@@ -26,5 +26,9 @@ struct AttentionCall {
 // Tensor-core (mma.sync) kernel for linear arenas: head_dim 64/128, 1 or 2 query heads per kv head.
 bool attention_mma_supported(int64_t head_dim, int64_t group);
 int launch_attention_mma(const AttentionCall& call);
+// Decode variant reading the raw QKV projection (per-head norm, RoPE and K/V write fused).
+int launch_attention_fused(const AttentionCall& call, const void* qkv, int64_t qkv_stride, const void* q_norm,
+                           const void* k_norm, float eps, const void* cos, const void* sin, int64_t table_len,
+                           const int64_t* rot_pos);
 
 }  // namespace q3t

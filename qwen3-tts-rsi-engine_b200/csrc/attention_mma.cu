@@ -66,14 +66,63 @@ Q3T_DEV uint32_t keep_keys(uint32_t v, int key_lo, int valid) {
   return v;
 }
 
-template <int D, int G>
+// Decode step with the per-head q/k RMSNorm, RoPE and the K/V write fused in
+// (FUSED = true): the kernel reads the raw QKV projection row instead of a
+// finished query. Every chunk CTA of (row, kv head) normalises and rotates its
+// G query heads in shared memory; the CTA of the last chunk (the one whose key
+// range contains the row's position p) also builds the new key/value of p,
+// stores them to the arena and patches them into its shared tile before using
+// it, so no other CTA of the launch depends on that write.
+struct FusedQKV {
+  const __nv_bfloat16* qkv;     // [rows, (q_heads + 2 kv_heads) * D], row stride qkv_stride
+  int64_t qkv_stride;
+  const __nv_bfloat16* q_norm;  // [D] or null (no per-head norm)
+  const __nv_bfloat16* k_norm;
+  float eps;
+  const __nv_bfloat16* cos;     // [table_len, D]
+  const __nv_bfloat16* sin;
+  int64_t table_len;
+  const int64_t* rot_pos;       // [rows]
+  __nv_bfloat16* keys;          // arena [slots, kv_heads, capacity, D] (row b = slot b)
+  __nv_bfloat16* values;
+};
+
+// Per-head RMSNorm (optional weight) and rotate-half RoPE of D values, one warp,
+// lane l holding dims [l*D/32, (l+1)*D/32); bf16 rounding after each op as the
+// standalone q/k kernel does.
+template <int D>
+Q3T_DEV void norm_rope(float (&x)[D / 32], const __nv_bfloat16* w, float eps, const __nv_bfloat16* cs,
+                       const __nv_bfloat16* sn, int lane) {
+  constexpr int DL = D / 32;
+  float y[DL];
+  if (w != nullptr) {
+    float ss = 0.f;
+#pragma unroll
+    for (int d = 0; d < DL; ++d) ss += x[d] * x[d];
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / float(D) + eps);
+#pragma unroll
+    for (int d = 0; d < DL; ++d) y[d] = bf16r(__bfloat162float(w[lane * DL + d]) * bf16r(x[d] * inv));
+  } else {
+#pragma unroll
+    for (int d = 0; d < DL; ++d) y[d] = x[d];
+  }
+#pragma unroll
+  for (int d = 0; d < DL; ++d) {
+    const float partner = __shfl_xor_sync(0xffffffffu, y[d], 16);
+    const float rot = lane < 16 ? -partner : partner;
+    x[d] = bf16r(bf16r(y[d] * __bfloat162float(cs[lane * DL + d])) + bf16r(rot * __bfloat162float(sn[lane * DL + d])));
+  }
+}
+
+template <int D, int G, bool FUSED>
 __global__ void __launch_bounds__(128, 3)
     decode_attention_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                                 const __nv_bfloat16* __restrict__ query, const int64_t* __restrict__ positions,
                                 __nv_bfloat16* __restrict__ out, int kv_heads, int64_t capacity, int64_t context,
                                 int window, int rows_per_slot, const int64_t* __restrict__ slots, int chunk,
                                 float qscale, float* __restrict__ partials, unsigned* __restrict__ counters,
-                                int max_chunks, unsigned* status) {
+                                int max_chunks, unsigned* status, const FusedQKV f) {
   using C = MmaCfg<D, G>;
   constexpr int S = C::kStages;
   constexpr int KS = D / 16;  // k-steps of S = Q K^T
@@ -84,7 +133,7 @@ __global__ void __launch_bounds__(128, 3)
   __shared__ __align__(16) __nv_bfloat16 qs[G * D];
   __shared__ float wm[4][G], wl[4][G];
   __shared__ float wo[4][G][D];
-  __shared__ int tile_ok, last_flag;
+  __shared__ int last_flag;
 
   const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -92,6 +141,7 @@ __global__ void __launch_bounds__(128, 3)
   grid_dependency_wait();
 
   int64_t pos = positions[b];
+  const bool pos_ok = pos >= 0 && pos < context;
   if (pos < 0 || pos >= context) {
     if (c == 0 && h == 0 && threadIdx.x == 0) raise_status(status, kStatusBadIndex);
     pos = pos < 0 ? 0 : context - 1;
@@ -119,8 +169,11 @@ __global__ void __launch_bounds__(128, 3)
     const int s = t % S;
     const uint64_t pol = policy_evict_first();
     mbar_expect_tx(&full[s], C::kStageBytes + (t == 0 ? C::kQBytes : 0));
-    if (t == 0)  // the query rows ride on the first tile's barrier
-      bulk_load(qs, query + (int64_t(b) * kv_heads + h) * G * D, uint32_t(C::kQBytes), &full[0]);
+    if (t == 0) {  // the query rows ride on the first tile's barrier
+      const __nv_bfloat16* qsrc = FUSED ? f.qkv + int64_t(b) * f.qkv_stride + int64_t(h) * G * D
+                                        : query + (int64_t(b) * kv_heads + h) * G * D;
+      bulk_load(qs, qsrc, uint32_t(C::kQBytes), &full[0]);
+    }
     const int y = int(row0 + int64_t(t) * C::kTile);
 #pragma unroll
     for (int bx = 0; bx < C::kBoxes; ++bx) {
@@ -130,6 +183,38 @@ __global__ void __launch_bounds__(128, 3)
   };
   if (threadIdx.x == 0)
     for (int t = 0; t < ntiles && t < S; ++t) issue(t);
+
+  // ---- fused: rotary row, and (last chunk only) the new key/value of position p
+  constexpr int DL = D / 32;
+  const bool owns_p = FUSED && c == active - 1;
+  const int t_p = int((pos - k_begin) / C::kTile);   // tile of this chunk holding p (last chunk)
+  float knew[DL], vnew[DL];
+  int64_t rp = 0;
+  if constexpr (FUSED) {
+    rp = f.rot_pos[b];
+    if (rp < 0 || rp >= f.table_len) {
+      if (c == 0 && h == 0 && threadIdx.x == 0) raise_status(status, kStatusBadIndex);
+      rp = rp < 0 ? 0 : f.table_len - 1;
+    }
+    if (owns_p && warp == 3) {
+      const int q_heads = kv_heads * G;
+      const __nv_bfloat16* row = f.qkv + int64_t(b) * f.qkv_stride;
+#pragma unroll
+      for (int d = 0; d < DL; ++d) {
+        knew[d] = __bfloat162float(row[int64_t(q_heads + h) * D + lane * DL + d]);
+        vnew[d] = __bfloat162float(row[int64_t(q_heads + kv_heads + h) * D + lane * DL + d]);
+      }
+      norm_rope<D>(knew, f.k_norm, f.eps, f.cos + rp * D, f.sin + rp * D, lane);
+      if (pos_ok) {
+        const size_t dst = ((size_t(slot) * kv_heads + h) * size_t(capacity) + size_t(pos)) * D + lane * DL;
+#pragma unroll
+        for (int d = 0; d < DL; ++d) {
+          f.keys[dst + d] = __float2bfloat16_rn(knew[d]);
+          f.values[dst + d] = __float2bfloat16_rn(vnew[d]);
+        }
+      }
+    }
+  }
 
   uint32_t qa[KS][2];  // Q as the A fragment (rows g < G real, rows >= G and g+8 zero), filled at tile 0
   float o[NT][4];
@@ -141,13 +226,37 @@ __global__ void __launch_bounds__(128, 3)
   int failed = -1;
   for (int t = 0; t < ntiles; ++t) {
     const int s = t % S;
-    if (threadIdx.x == 0) tile_ok = mbar_wait(&full[s], (t / S) & 1, status, kStatusTmaTimeout) ? 1 : 0;
-    __syncthreads();
-    if (!tile_ok) {
-      failed = t;
-      break;
+    // Every thread waits for the stage itself (bounded); a timeout is made uniform by the
+    // end-of-tile barrier below, which is the only CTA barrier per tile.
+    const bool tile_ok = mbar_wait(&full[s], (t / S) & 1, status, kStatusTmaTimeout);
+    if constexpr (FUSED) {
+      if (t == 0 || (owns_p && t == t_p)) {  // CTA-uniform condition
+        if (t == 0 && warp < G) {            // warp w finishes query head w in place
+          float x[DL];
+          __nv_bfloat16* qh = qs + warp * D + lane * DL;
+#pragma unroll
+          for (int d = 0; d < DL; ++d) x[d] = __bfloat162float(qh[d]);
+          norm_rope<D>(x, f.q_norm, f.eps, f.cos + rp * D, f.sin + rp * D, lane);
+#pragma unroll
+          for (int d = 0; d < DL; ++d) qh[d] = __float2bfloat16_rn(x[d]);
+        }
+        if (owns_p && t == t_p && warp == 3) {  // the freshly built K/V of p replace the stale arena row
+          const int rr = int(pos - k_begin) - t_p * C::kTile;
+          const int col = (lane * DL) % 64, bx = (lane * DL) / 64;
+          const int off = bx * C::kBoxBytes + rr * 128 + ((((col >> 3) ^ (rr & 7)) & 7) << 4) + (col & 7) * 2;
+          __nv_bfloat16 kb[DL], vb[DL];
+#pragma unroll
+          for (int d = 0; d < DL; ++d) {
+            kb[d] = __float2bfloat16_rn(knew[d]);
+            vb[d] = __float2bfloat16_rn(vnew[d]);
+          }
+          memcpy(stage_k(s) + off, kb, sizeof(kb));
+          memcpy(stage_v(s) + off, vb, sizeof(vb));
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // before TMA refills this stage
+        }
+        __syncthreads();
+      }
     }
-    mbar_wait(&full[s], (t / S) & 1, status, kStatusTmaTimeout);
     if (t == 0) {
       const bool real = g < G;
       const __nv_bfloat16* qp = qs + (real ? g : 0) * D;
@@ -223,7 +332,11 @@ __global__ void __launch_bounds__(128, 3)
         mma_rows8(o[2 * np + 1], pa0, pa2, v2, v3);
       }
     }
-    __syncthreads();  // all warps are done with stage s
+    // all warps are done with stage s (and agree whether it ever landed)
+    if (__syncthreads_or(!tile_ok)) {
+      failed = t;
+      break;
+    }
     if (threadIdx.x == 0 && t + S < ntiles) issue(t + S);
   }
   if (failed >= 0) {
@@ -271,14 +384,18 @@ __global__ void __launch_bounds__(128, 3)
   }
   if (active == 1) return;
 
-  // ---- chunk combine: the last CTA of this (row, kv head) merges in chunk order
-  __threadfence();
+  // ---- chunk combine: the last CTA of this (row, kv head) merges in chunk order.
+  // The barrier orders every thread's partial stores before thread 0's device-scope
+  // fence and ticket (release); the last CTA fences again before reading (acquire).
   __syncthreads();
   unsigned* counter = counters + size_t(b) * kv_heads + h;
-  if (threadIdx.x == 0) last_flag = (atomicAdd(counter, 1u) == unsigned(active - 1));
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last_flag = (atomicAdd(counter, 1u) == unsigned(active - 1));
+    if (last_flag) __threadfence();
+  }
   __syncthreads();
   if (!last_flag) return;
-  __threadfence();
   const float* base = partials + (size_t(b) * kv_heads + h) * max_chunks * C::kPart;
   for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
     const int gg = e / D, d = e % D;
@@ -297,14 +414,14 @@ __global__ void __launch_bounds__(128, 3)
   if (threadIdx.x == 0) *counter = 0u;
 }
 
-template <int D, int G>
-int launch_mma(const AttentionCall& a) {
+template <int D, int G, bool FUSED>
+int launch_mma(const AttentionCall& a, const FusedQKV& f) {
   using C = MmaCfg<D, G>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(decode_attention_mma_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(decode_attention_mma_kernel<D, G, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::kSmem) != cudaSuccess)
       return check_cuda("attention: set smem");
     configured[dev] = true;
@@ -315,11 +432,11 @@ int launch_mma(const AttentionCall& a) {
   if (rc) return rc;
   rc = make_map_bf16(&tmv, a.values, arena_rows, D, D, 64, C::kTile);
   if (rc) return rc;
-  return launch(decode_attention_mma_kernel<D, G>, dim3(a.max_chunks, unsigned(a.kv_heads), unsigned(a.rows)),
+  return launch(decode_attention_mma_kernel<D, G, FUSED>, dim3(a.max_chunks, unsigned(a.kv_heads), unsigned(a.rows)),
                 dim3(128), size_t(C::kSmem), a.stream, true, "decode_attention_mma", tmk, tmv,
                 static_cast<const __nv_bfloat16*>(a.query), a.positions, static_cast<__nv_bfloat16*>(a.out),
                 int(a.kv_heads), a.capacity, a.context, int(a.window), int(a.rows_per_slot), a.slots, a.chunk,
-                a.scale * kLog2e, a.partials, a.counters, a.max_chunks, a.status);
+                a.scale * kLog2e, a.partials, a.counters, a.max_chunks, a.status, f);
 }
 
 }  // namespace
@@ -332,11 +449,35 @@ bool attention_mma_supported(int64_t head_dim, int64_t group) {
 
 int launch_attention_mma(const AttentionCall& a) {
   const int64_t g = a.q_heads / a.kv_heads;
-  if (a.head_dim == 128 && g == 2) return launch_mma<128, 2>(a);
-  if (a.head_dim == 128 && g == 1) return launch_mma<128, 1>(a);
-  if (a.head_dim == 64 && g == 2) return launch_mma<64, 2>(a);
-  if (a.head_dim == 64 && g == 1) return launch_mma<64, 1>(a);
+  const FusedQKV none = {};
+  if (a.head_dim == 128 && g == 2) return launch_mma<128, 2, false>(a, none);
+  if (a.head_dim == 128 && g == 1) return launch_mma<128, 1, false>(a, none);
+  if (a.head_dim == 64 && g == 2) return launch_mma<64, 2, false>(a, none);
+  if (a.head_dim == 64 && g == 1) return launch_mma<64, 1, false>(a, none);
   return fail(Q3T_EUNSUPPORTED, "attention (mma): unsupported head geometry");
+}
+
+int launch_attention_fused(const AttentionCall& a, const void* qkv, int64_t qkv_stride, const void* q_norm,
+                           const void* k_norm, float eps, const void* cos, const void* sin, int64_t table_len,
+                           const int64_t* rot_pos) {
+  FusedQKV f;
+  f.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  f.qkv_stride = qkv_stride;
+  f.q_norm = static_cast<const __nv_bfloat16*>(q_norm);
+  f.k_norm = static_cast<const __nv_bfloat16*>(k_norm);
+  f.eps = eps;
+  f.cos = static_cast<const __nv_bfloat16*>(cos);
+  f.sin = static_cast<const __nv_bfloat16*>(sin);
+  f.table_len = table_len;
+  f.rot_pos = rot_pos;
+  f.keys = static_cast<__nv_bfloat16*>(const_cast<void*>(a.keys));
+  f.values = static_cast<__nv_bfloat16*>(const_cast<void*>(a.values));
+  const int64_t g = a.q_heads / a.kv_heads;
+  if (a.head_dim == 128 && g == 2) return launch_mma<128, 2, true>(a, f);
+  if (a.head_dim == 128 && g == 1) return launch_mma<128, 1, true>(a, f);
+  if (a.head_dim == 64 && g == 2) return launch_mma<64, 2, true>(a, f);
+  if (a.head_dim == 64 && g == 1) return launch_mma<64, 1, true>(a, f);
+  return fail(Q3T_EUNSUPPORTED, "attention (fused): unsupported head geometry");
 }
 
 }  // namespace q3t

@@ -32,6 +32,8 @@ constexpr int kABytes = kTileN * kTileK * 2;
 
 template <int BN>
 struct Cfg {
+  // (Measured: three stages at BN <= 32, which would let a CTA of the next kernel
+  // become resident beside two of this one, ran the talker GEMMs ~10% slower.)
   static constexpr int kStages = BN <= 16 ? 6 : BN <= 32 ? 5 : BN <= 64 ? 4 : BN <= 128 ? 3 : 2;
   static constexpr int kBBytes = BN * kTileK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -41,8 +43,9 @@ struct Cfg {
   static constexpr int kRedStride = kTileN + 4;
   static constexpr int kRedBytes = BN * kRedStride * 4;
   static constexpr int kMain = kRing > kRedBytes ? kRing : kRedBytes;
-  // main area + barriers (2 per stage + done) + tmem slot + flags, plus 1 KB alignment slack
-  static constexpr int kSmem = kMain + 256 + 1024;
+  // main area + barriers (2 per stage + done) + tmem slot + flags, row scales [BN] of the
+  // folded RMSNorm, plus 1 KB alignment slack
+  static constexpr int kSmem = kMain + 256 + 1024 + 1024;
 };
 
 struct GemmArgs {
@@ -57,6 +60,8 @@ struct GemmArgs {
   const __nv_bfloat16* residual;
   int64_t res_stride;
   const __nv_bfloat16* scale;  // per-feature scale of Q3T_EPI_RESIDUAL_SCALED
+  int row_norm;                // scale row m by 1/sqrt(mean_k x[m,k]^2 + norm_eps) (folded RMSNorm)
+  float norm_eps;
   unsigned* status;
 };
 
@@ -116,6 +121,11 @@ Q3T_DEV uint32_t map_peer(uint32_t local_smem, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_smem), "r"(rank));
   return remote;
 }
+Q3T_DEV float ld_peer1(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
 Q3T_DEV float4 ld_peer4(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
@@ -127,10 +137,11 @@ Q3T_DEV float4 ld_peer4(uint32_t addr) {
 
 // One CTA = 128 weight rows x BN activation rows x one K slice. The CTAs of
 // the K slices of one tile form a thread-block cluster (gridDim.y = splits,
-// a power of two <= 8) and reduce their fp32 accumulators through
+// 1..8) and reduce their fp32 accumulators through
 // distributed shared memory: each writes its tile column-major into its own
-// shared memory, then CTA of cluster rank r sums rows [r*128/S, (r+1)*128/S)
-// over all peers in rank order (deterministic) and applies the epilogue.
+// shared memory, then CTA of cluster rank r sums its share of the tile's
+// feature quads over all peers in rank order (deterministic) and applies the
+// epilogue.
 template <int BN, int EPI>
 __global__ void __launch_bounds__(128, 1)
     linear_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx, GemmArgs a) {
@@ -145,6 +156,7 @@ __global__ void __launch_bounds__(128, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* consumed = abort_flag + 1;  // ring slots the MMA issuer has taken
   float* red = reinterpret_cast<float*>(smem);
+  float* rnorm = reinterpret_cast<float*>(smem + C::kMain + 256);  // [BN] row scales (row_norm)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kTileN;
@@ -158,7 +170,8 @@ __global__ void __launch_bounds__(128, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      // a slot is free once the MMAs read it and, with row_norm, warps 2 and 3 summed its rows
+      mbar_init(&empty[s], a.row_norm ? 3 : 1);
     }
     mbar_init(done, 1);
     *abort_flag = 0;
@@ -226,6 +239,43 @@ __global__ void __launch_bounds__(128, 1)
     }
     __syncwarp();
   }
+
+  // ---------------- folded RMSNorm: warps 2 and 3 (idle during the main loop) sum the
+  // squares of every activation row from the ring slots as they land, over this CTA's K slice
+  constexpr int RPT = BN > 64 ? BN / 64 : 1;  // activation rows per thread
+  float ss[RPT];
+#pragma unroll
+  for (int q = 0; q < RPT; ++q) ss[q] = 0.f;
+  if (a.row_norm && warp >= 2) {
+    const int t2 = threadIdx.x - 64;
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % S;
+      if (!mbar_wait(&full[s], (i / S) & 1, a.status, kStatusTmaTimeout)) {
+        *abort_flag = 1;
+        break;
+      }
+      const uint8_t* xb = smem + s * C::kStageBytes + kABytes;
+#pragma unroll
+      for (int q = 0; q < RPT; ++q) {
+        const int m = t2 + 64 * q;
+        if (m < BN) {
+          const uint4* row = reinterpret_cast<const uint4*>(xb + m * 128);  // the 64 k of row m, chunk-permuted
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint4 v = row[c];
+            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float lo = __uint_as_float(w4[e] << 16), hi = __uint_as_float(w4[e] & 0xFFFF0000u);
+              ss[q] += lo * lo + hi * hi;
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+  }
   grid_dependency_wait();
 
   // ---------------- TMEM -> registers
@@ -235,6 +285,15 @@ __global__ void __launch_bounds__(128, 1)
   const uint32_t taddr = tmem + (uint32_t(warp * 32) << 16);
   if (!clustered && EPI != Q3T_EPI_SWIGLU_PAIRED) {
     const int n = n0 + r;
+    if (a.row_norm) {
+      if (warp >= 2)
+#pragma unroll
+        for (int q = 0; q < RPT; ++q) {
+          const int m = threadIdx.x - 64 + 64 * q;
+          if (m < BN) rnorm[m] = 1.0f / sqrtf(ss[q] / float(a.in_features) + a.norm_eps);
+        }
+      __syncthreads();
+    }
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 16) {
       float v[16];
@@ -243,7 +302,7 @@ __global__ void __launch_bounds__(128, 1)
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int m = m0 + c0 + j;
-          if (m < a.rows) store_out<EPI>(a, m, n, v[j]);
+          if (m < a.rows) store_out<EPI>(a, m, n, a.row_norm ? v[j] * rnorm[c0 + j] : v[j]);
         }
       }
     }
@@ -263,6 +322,12 @@ __global__ void __launch_bounds__(128, 1)
 #pragma unroll
       for (int j = 0; j < 16; ++j) red[(c0 + j) * C::kRedStride + r] = ok ? v[j] : 0.f;
     }
+    if (a.row_norm && warp >= 2)  // this CTA's partial row sums ride in the padding column
+#pragma unroll
+      for (int q = 0; q < RPT; ++q) {
+        const int m = threadIdx.x - 64 + 64 * q;
+        if (m < BN) red[m * C::kRedStride + kTileN] = ss[q];
+      }
     tc_fence_before();
     __syncthreads();
     if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
@@ -277,22 +342,55 @@ __global__ void __launch_bounds__(128, 1)
   const uint32_t rank = clustered ? cluster_rank() : 0u;
   const int mcount = (a.rows - m0) < BN ? (a.rows - m0) : BN;
   const uint32_t red_local = smem_u32(red);
+  // Row scale of the folded RMSNorm for activation row c: the K slices' partial sums of
+  // squares (each CTA's padding column) added in rank order, so every CTA of the
+  // cluster computes the same value; loaded together with the accumulator tiles.
+  auto row_scale = [&](int c) -> float {
+    float total = 0.f;
+    const uint32_t off = uint32_t(c * C::kRedStride + kTileN) * 4u;
+    for (int p0 = 0; p0 < cs; p0 += 4) {
+      float v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        v[j] = p0 + j < cs ? (clustered ? ld_peer1(map_peer(red_local, uint32_t(p0 + j)) + off)
+                                        : red[c * C::kRedStride + kTileN])
+                           : 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) total += v[j];
+    }
+    return 1.0f / sqrtf(total / float(a.in_features) + a.norm_eps);
+  };
   if constexpr (EPI == Q3T_EPI_SWIGLU_PAIRED) {
-    const int nf = 64 / cs;                    // features of this CTA (multiple of 4)
-    const int f0 = int(rank) * nf;
-    const int units = mcount * (nf / 4);
+    // this CTA finalises feature quads [q0, q1) of the 16 gate/up quad pairs
+    const int q0 = int(rank) * 16 / cs, nq = (int(rank) + 1) * 16 / cs - q0;
+    const int f0 = q0 * 4;
+    const int units = mcount * nq;
     for (int u = threadIdx.x; u < units; u += blockDim.x) {
-      const int c = u / (nf / 4);
-      const int f = f0 + (u % (nf / 4)) * 4;
+      const int c = u / nq;
+      const int f = f0 + (u % nq) * 4;
       float4 g = make_float4(0.f, 0.f, 0.f, 0.f), up = g;
-      for (int p = 0; p < cs; ++p) {
-        const uint32_t base = clustered ? map_peer(red_local, uint32_t(p)) : red_local;
-        const float4 gv = clustered ? ld_peer4(base + uint32_t(c * C::kRedStride + f) * 4u)
-                                    : *reinterpret_cast<const float4*>(red + c * C::kRedStride + f);
-        const float4 uv = clustered ? ld_peer4(base + uint32_t(c * C::kRedStride + 64 + f) * 4u)
-                                    : *reinterpret_cast<const float4*>(red + c * C::kRedStride + 64 + f);
-        g.x += gv.x; g.y += gv.y; g.z += gv.z; g.w += gv.w;
-        up.x += uv.x; up.y += uv.y; up.z += uv.z; up.w += uv.w;
+      for (int p0 = 0; p0 < cs; p0 += 2) {  // both halves of two peers in flight, then the adds (rank order)
+        float4 gv[2], uv[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const bool live = p0 + j < cs;
+          const uint32_t base = clustered ? map_peer(red_local, uint32_t(live ? p0 + j : 0)) : red_local;
+          gv[j] = clustered ? ld_peer4(base + uint32_t(c * C::kRedStride + f) * 4u)
+                            : *reinterpret_cast<const float4*>(red + c * C::kRedStride + f);
+          uv[j] = clustered ? ld_peer4(base + uint32_t(c * C::kRedStride + 64 + f) * 4u)
+                            : *reinterpret_cast<const float4*>(red + c * C::kRedStride + 64 + f);
+          if (!live) gv[j] = uv[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          g.x += gv[j].x; g.y += gv[j].y; g.z += gv[j].z; g.w += gv[j].w;
+          up.x += uv[j].x; up.y += uv[j].y; up.z += uv[j].z; up.w += uv[j].w;
+        }
+      }
+      if (a.row_norm) {
+        const float rn = row_scale(c);
+        g.x *= rn; g.y *= rn; g.z *= rn; g.w *= rn;
+        up.x *= rn; up.y *= rn; up.z *= rn; up.w *= rn;
       }
       const int m = m0 + c;
       __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + int64_t(m) * a.out_stride + (n0 / 2 + f);
@@ -302,18 +400,27 @@ __global__ void __launch_bounds__(128, 1)
         if (n0 + 64 + f + j < a.out_features) o[j] = __float2bfloat16_rn(silu_gate(bf16r(gs[j]), bf16r(us[j])));
     }
   } else {
-    const int nf = kTileN / cs;
-    const int f0 = int(rank) * nf;
-    const int units = mcount * (nf / 4);
+    // this CTA finalises feature quads [q0, q1) of the tile's 32
+    const int q0 = int(rank) * 32 / cs, nq = (int(rank) + 1) * 32 / cs - q0;
+    const int f0 = q0 * 4;
+    const int units = mcount * nq;
     for (int u = threadIdx.x; u < units; u += blockDim.x) {
-      const int c = u / (nf / 4);
-      const int f = f0 + (u % (nf / 4)) * 4;
+      const int c = u / nq;
+      const int f = f0 + (u % nq) * 4;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int p = 0; p < cs; ++p) {
-        const float4 v = ld_peer4(map_peer(red_local, uint32_t(p)) + uint32_t(c * C::kRedStride + f) * 4u);
-        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+      const uint32_t off = uint32_t(c * C::kRedStride + f) * 4u;
+      for (int p0 = 0; p0 < cs; p0 += 4) {  // four remote loads in flight, then the adds (rank order)
+        float4 v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          v[j] = p0 + j < cs ? ld_peer4(map_peer(red_local, uint32_t(p0 + j)) + off) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc.x += v[j].x; acc.y += v[j].y; acc.z += v[j].z; acc.w += v[j].w;
+        }
       }
-      const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+      const float rn = a.row_norm ? row_scale(c) : 1.f;
+      const float vals[4] = {acc.x * rn, acc.y * rn, acc.z * rn, acc.w * rn};
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         if (n0 + f + j < a.out_features) store_out<EPI>(a, m0 + c, n0 + f + j, vals[j]);
@@ -393,6 +500,7 @@ struct Plan {
   int bn, n_tiles, m_tiles, kblocks, splits;
 };
 
+
 Plan plan(int64_t rows, int64_t in_features, int64_t out_features) {
   Plan p;
   p.bn = pick_bn(rows);
@@ -400,7 +508,9 @@ Plan plan(int64_t rows, int64_t in_features, int64_t out_features) {
   p.m_tiles = int((rows + p.bn - 1) / p.bn);
   p.kblocks = int((in_features + kTileK - 1) / kTileK);
   // K splits: a power of two <= 8 (one thread-block cluster per tile), each
-  // split at least two k-blocks, aiming at ~2 resident CTAs per SM.
+  // split at least two k-blocks, aiming at ~2 resident CTAs per SM. (Measured:
+  // 16-CTA and 3- or 9-CTA clusters that fill the SMs more evenly ran the
+  // talker GEMMs 1.6-2x slower in a dependent launch chain.)
   const int base = p.n_tiles * p.m_tiles;
   const int target = 2 * sm_count();
   int splits = 1;
@@ -481,12 +591,14 @@ extern "C" size_t q3t_linear_workspace_bytes(int64_t rows, int64_t in_features, 
   return 0;
 }
 
-extern "C" int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t in_features, const void* weight,
-                          int64_t out_features, const void* bias, void* out, int64_t out_stride, int out_dtype,
-                          int epilogue, const void* residual, int64_t residual_stride, const void* scale,
-                          const void* weight_tiles, void* workspace, size_t workspace_bytes, unsigned* status,
-                          void* stream) {
+namespace {
+
+int linear_impl(const void* x, int64_t x_stride, int64_t rows, int64_t in_features, const void* weight,
+                int64_t out_features, const void* bias, void* out, int64_t out_stride, int out_dtype, int epilogue,
+                const void* residual, int64_t residual_stride, const void* scale, float row_norm_eps,
+                const void* weight_tiles, void* workspace, size_t workspace_bytes, unsigned* status, void* stream) {
   if (!x || (!weight && !weight_tiles) || !out) return fail(Q3T_EINVAL, "linear: null pointer");
+  if (!(row_norm_eps >= 0.f)) return fail(Q3T_EINVAL, "linear: row-norm eps must be >= 0");
   if (rows < 1 || rows > (int64_t(1) << 24) || in_features < 8 || in_features % 8 || out_features < 1 || out_features > (1 << 24))
     return fail(Q3T_EINVAL, "linear: unsupported shape rows=%lld in=%lld out=%lld", (long long)rows,
                 (long long)in_features, (long long)out_features);
@@ -533,6 +645,8 @@ extern "C" int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t
   a.res_stride = residual_stride;
   a.scale = static_cast<const __nv_bfloat16*>(scale);
   a.tiles = static_cast<const uint8_t*>(weight_tiles);
+  a.row_norm = row_norm_eps > 0.f ? 1 : 0;
+  a.norm_eps = row_norm_eps;
   a.status = status;
   switch (epilogue) {
     case Q3T_EPI_STORE: return dispatch_bn<Q3T_EPI_STORE>(p, tmw, tmx, a, stream);
@@ -542,4 +656,25 @@ extern "C" int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t
     case Q3T_EPI_SILU: return dispatch_bn<Q3T_EPI_SILU>(p, tmw, tmx, a, stream);
     default: return dispatch_bn<Q3T_EPI_SWIGLU_PAIRED>(p, tmw, tmx, a, stream);
   }
+}
+
+}  // namespace
+
+extern "C" int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t in_features, const void* weight,
+                          int64_t out_features, const void* bias, void* out, int64_t out_stride, int out_dtype,
+                          int epilogue, const void* residual, int64_t residual_stride, const void* scale,
+                          const void* weight_tiles, void* workspace, size_t workspace_bytes, unsigned* status,
+                          void* stream) {
+  return linear_impl(x, x_stride, rows, in_features, weight, out_features, bias, out, out_stride, out_dtype, epilogue,
+                     residual, residual_stride, scale, 0.f, weight_tiles, workspace, workspace_bytes, status, stream);
+}
+
+extern "C" int q3t_linear_rownorm(const void* x, int64_t x_stride, int64_t rows, int64_t in_features,
+                                  const void* weight, int64_t out_features, const void* bias, void* out,
+                                  int64_t out_stride, int out_dtype, int epilogue, const void* residual,
+                                  int64_t residual_stride, const void* scale, float eps, const void* weight_tiles,
+                                  unsigned* status, void* stream) {
+  if (!(eps > 0.f)) return fail(Q3T_EINVAL, "linear_rownorm: eps must be positive");
+  return linear_impl(x, x_stride, rows, in_features, weight, out_features, bias, out, out_stride, out_dtype, epilogue,
+                     residual, residual_stride, scale, eps, weight_tiles, nullptr, 0, status, stream);
 }

@@ -27,7 +27,7 @@ import torch
 from . import _lib, ops
 from .config import CodecConfig
 from .talker import rope_tables
-from .weights import interleave_gate_up
+from .weights import fold_norm, interleave_gate_up
 
 BF16 = torch.bfloat16
 RING = 128
@@ -92,13 +92,19 @@ def pack_codec(decoder, device) -> dict:
     tr = decoder.pre_transformer
     layers = []
     for layer in tr.layers:
+        input_norm = layer.input_layernorm.weight.detach().to(dev, BF16).contiguous()
+        post_norm = layer.post_attention_layernorm.weight.detach().to(dev, BF16).contiguous()
+        qkv = torch.cat([layer.q_proj.weight, layer.k_proj.weight, layer.v_proj.weight]).detach().to(dev, BF16)
+        gate_up = interleave_gate_up(layer.gate_proj.weight.detach(), layer.up_proj.weight.detach()).to(dev, BF16)
         layers.append({
-            "input_norm": layer.input_layernorm.weight.detach().to(dev, BF16).contiguous(),
-            "qkv": torch.cat([layer.q_proj.weight, layer.k_proj.weight, layer.v_proj.weight]).detach().to(dev, BF16).contiguous(),
+            "input_norm": input_norm,
+            # the RMSNorm weights are folded into the projections that follow them;
+            # the GEMMs apply the row RMS themselves (q3t_linear_rownorm)
+            "qkv": fold_norm(qkv, input_norm).contiguous(),
             "o": layer.o_proj.weight.detach().to(dev, BF16).contiguous(),
             "attn_scale": layer.attn_scale.detach().to(dev, BF16).contiguous(),
-            "post_norm": layer.post_attention_layernorm.weight.detach().to(dev, BF16).contiguous(),
-            "gate_up": interleave_gate_up(layer.gate_proj.weight.detach(), layer.up_proj.weight.detach()).to(dev, BF16),
+            "post_norm": post_norm,
+            "gate_up": fold_norm(gate_up, post_norm).contiguous(),
             "down": layer.down_proj.weight.detach().to(dev, BF16).contiguous(),
             "mlp_scale": layer.mlp_scale.detach().to(dev, BF16).contiguous(),
         })
@@ -278,8 +284,7 @@ class CodecStep:
         L = cfg.layers
         for i, layer in enumerate(tr["layers"]):
             keys, values = st.kv[i], st.kv[L + i]
-            ops.rms_norm(b["h"], layer["input_norm"], cfg.eps, out=b["xn"])
-            ops.linear(b["xn"], layer["qkv"], out=b["qkv"])
+            ops.linear(b["h"], layer["qkv"], out=b["qkv"], row_norm_eps=cfg.eps)
             q = ops.qk_norm_rope_kv(b["qkv"], None, None, cfg.eps, self.cos, self.sin, self.rot, self.cache, keys,
                                     values, q_heads=cfg.heads, kv_heads=cfg.heads, head_dim=cfg.head_dim, length=T,
                                     query_out=b["q"].view(R, cfg.heads, cfg.head_dim), slots=self.indices)
@@ -288,8 +293,8 @@ class CodecStep:
                                  workspace=self.ws_attn)
             ops.linear(b["attn"], layer["o"], out=b["h"], epilogue=_lib.EPI_RESIDUAL_SCALED, residual=b["h"],
                        scale=layer["attn_scale"])
-            ops.rms_norm(b["h"], layer["post_norm"], cfg.eps, out=b["xn"])
-            ops.linear(b["xn"], layer["gate_up"], out=b["act"], epilogue=_lib.EPI_SWIGLU_PAIRED)
+            ops.linear(b["h"], layer["gate_up"], out=b["act"], epilogue=_lib.EPI_SWIGLU_PAIRED,
+                       row_norm_eps=cfg.eps)
             ops.linear(b["act"], layer["down"], out=b["h"], epilogue=_lib.EPI_RESIDUAL_SCALED, residual=b["h"],
                        scale=layer["mlp_scale"])
         ops.rms_norm(b["h"], tr["norm"], cfg.eps, out=b["xn"])

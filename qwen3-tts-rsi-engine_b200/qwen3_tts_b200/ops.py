@@ -287,10 +287,14 @@ def pack_tiles(weight: torch.Tensor) -> TiledWeight:
 
 
 def linear(x, weight, bias=None, *, out=None, out_dtype=BF16, epilogue: int = _lib.EPI_STORE, residual=None,
-           scale=None, workspace: Optional[torch.Tensor] = None, tag: str = "linear"):
+           scale=None, row_norm_eps: Optional[float] = None, workspace: Optional[torch.Tensor] = None,
+           tag: str = "linear"):
     """out = x @ weight.T (+ bias) with a fused epilogue, on tcgen05 tensor cores.
 
-    `weight` is a contiguous bf16 [out, in] tensor or a TiledWeight."""
+    `weight` is a contiguous bf16 [out, in] tensor or a TiledWeight. With
+    `row_norm_eps`, row r of the product is scaled by rsqrt(mean(x[r]^2) + eps):
+    an RMSNorm of x folded into the GEMM (the norm weight must already be
+    multiplied into `weight`, see weights.fold_norm)."""
     tiled = isinstance(weight, TiledWeight)
     _need_cuda(x, weight.tiles if tiled else weight)
     if x.dtype != BF16 or (not tiled and (weight.dtype != BF16 or weight.ndim != 2 or not weight.is_contiguous())):
@@ -310,6 +314,12 @@ def linear(x, weight, bias=None, *, out=None, out_dtype=BF16, epilogue: int = _l
     if residual is not None:
         res2 = residual.reshape(rows, n_out) if residual.is_contiguous() else residual
     odt = _lib.Q3T_BF16 if out.dtype == BF16 else _lib.Q3T_F32
+    if row_norm_eps is not None:
+        call("q3t_linear_rownorm", x2.data_ptr(), x2.stride(0), rows, in_features,
+             None if tiled else weight.data_ptr(), n_rows_w, _ptr(bias), out2.data_ptr(), out2.stride(0), odt,
+             epilogue, _ptr(res2), res2.stride(0) if res2 is not None else 0, _ptr(scale), float(row_norm_eps),
+             weight.tiles.data_ptr() if tiled else None, status_word(x.device).data_ptr(), _stream())
+        return out
     call("q3t_linear", x2.data_ptr(), x2.stride(0), rows, in_features, None if tiled else weight.data_ptr(), n_rows_w,
          _ptr(bias), out2.data_ptr(), out2.stride(0), odt, epilogue, _ptr(res2),
          res2.stride(0) if res2 is not None else 0, _ptr(scale), weight.tiles.data_ptr() if tiled else None,
@@ -360,6 +370,31 @@ def decode_attention(query, keys, values, positions, *, context=None, scale=None
     call("q3t_decode_attention", query.data_ptr(), keys.data_ptr(), values.data_ptr(), positions.data_ptr(),
          out.data_ptr(), rows, rows_per_slot, _ptr(slots), int(ring), q_heads, kv_heads, head_dim, n_slots, capacity,
          context, window, float(scale), ws.data_ptr(), ws.numel(), status_word(query.device).data_ptr(), _stream())
+    return out
+
+
+def decode_attention_qkv(qkv, q_norm_weight, k_norm_weight, eps, cos_table, sin_table, rotary_positions, keys,
+                         values, positions, *, q_heads, kv_heads, head_dim, context=None, scale=None, out=None,
+                         workspace: Optional[torch.Tensor] = None, tag: str = "attention"):
+    """Decode attention straight from the QKV projection rows: per-head q/k RMSNorm, RoPE and the
+    K/V write of each row's position fused into the attention kernel (one query row per slot)."""
+    _need_cuda(qkv, cos_table, sin_table, rotary_positions, keys, values, positions)
+    rows = qkv.shape[0]
+    n_slots, kvh, capacity, width = keys.shape
+    if (qkv.ndim != 2 or qkv.stride(1) != 1 or qkv.dtype != BF16 or width != head_dim or kvh != kv_heads
+            or values.shape != keys.shape or not keys.is_contiguous() or not values.is_contiguous()
+            or keys.dtype != BF16 or positions.dtype != torch.int64 or rotary_positions.dtype != torch.int64):
+        raise ValueError("Expected BF16 QKV rows and a contiguous BF16 KV arena [slots, Hkv, cap, D]")
+    context = capacity if context is None else context
+    scale = head_dim ** -0.5 if scale is None else scale
+    out = torch.empty(rows, q_heads, head_dim, dtype=BF16, device=qkv.device) if out is None else out
+    need = decode_attention_workspace_bytes(rows, q_heads, head_dim, context)
+    ws = workspace if workspace is not None else SCRATCH.workspace(need, qkv.device, tag)
+    call("q3t_decode_attention_qkv", qkv.data_ptr(), qkv.stride(0), _ptr(q_norm_weight), _ptr(k_norm_weight),
+         float(eps), cos_table.data_ptr(), sin_table.data_ptr(), cos_table.shape[0], rotary_positions.data_ptr(),
+         keys.data_ptr(), values.data_ptr(), positions.data_ptr(), out.data_ptr(), rows, q_heads, kv_heads, head_dim,
+         n_slots, capacity, context, float(scale), ws.data_ptr(), ws.numel(), status_word(qkv.device).data_ptr(),
+         _stream())
     return out
 
 

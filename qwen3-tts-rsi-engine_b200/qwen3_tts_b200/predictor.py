@@ -71,8 +71,11 @@ class PredictorStep:
         L = cfg.layers
         for i, layer in enumerate(self.w["layers"]):
             keys, values = self.cache[i], self.cache[L + i]
-            ops.rms_norm(x, layer.input_norm, cfg.eps, out=self.xn[:rows])
-            lw(self.xn[:rows], layer.qkv, out=self.qkv[:rows], workspace=self.ws_linear)
+            if layer.folded:
+                lw(x, layer.qkv, out=self.qkv[:rows], row_norm_eps=cfg.eps)
+            else:
+                ops.rms_norm(x, layer.input_norm, cfg.eps, out=self.xn[:rows])
+                lw(self.xn[:rows], layer.qkv, out=self.qkv[:rows], workspace=self.ws_linear)
             ops.qk_norm_rope_kv(self.qkv[:rows], layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin, positions,
                                 positions, keys, values, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads,
                                 head_dim=cfg.head_dim, length=length, query_out=self.q[:rows])
@@ -80,9 +83,12 @@ class PredictorStep:
                                  out=self.attn[:rows], workspace=self.ws_attn)
             lw(self.attn[:rows].view(rows, cfg.q_width), layer.o, out=x, epilogue=_lib.EPI_RESIDUAL, residual=x,
                workspace=self.ws_linear)
-            ops.rms_norm(x, layer.post_norm, cfg.eps, out=self.xn[:rows])
-            lw(self.xn[:rows], layer.gate_up, out=self.act[:rows], epilogue=_lib.EPI_SWIGLU_PAIRED,
-               workspace=self.ws_linear)
+            if layer.folded:
+                lw(x, layer.gate_up, out=self.act[:rows], epilogue=_lib.EPI_SWIGLU_PAIRED, row_norm_eps=cfg.eps)
+            else:
+                ops.rms_norm(x, layer.post_norm, cfg.eps, out=self.xn[:rows])
+                lw(self.xn[:rows], layer.gate_up, out=self.act[:rows], epilogue=_lib.EPI_SWIGLU_PAIRED,
+                   workspace=self.ws_linear)
             lw(self.act[:rows], layer.down, out=x, epilogue=_lib.EPI_RESIDUAL, residual=x, workspace=self.ws_linear)
         ops.rms_norm(x, self.w["norm"], cfg.eps, out=self.xn[:rows])
 

@@ -6,10 +6,12 @@ one KV arena holds every slot's keys and values, a decode step runs the whole
 (batch bucket, context bucket) with static input buffers, so any slot
 assignment replays the same graph (positions live in device buffers).
 
-Per layer the step launches eight kernels, all from ``libq3t_b200.so``:
-RMSNorm -> QKV GEMM -> q/k norm + RoPE + KV write -> ragged GQA attention ->
-O GEMM (+ residual) -> RMSNorm -> gate/up GEMM (+ SwiGLU) -> down GEMM
-(+ residual); then the final norm and the LM head (fp32 logits).
+Per layer the step launches five kernels, all from ``libq3t_b200.so``:
+QKV GEMM (input RMSNorm folded in) -> ragged GQA attention (q/k norm, RoPE
+and the KV write fused in) -> O GEMM (+ residual) -> gate/up GEMM
+(post-attention RMSNorm folded in, + SwiGLU) -> down GEMM (+ residual); then
+the final norm and the LM head (fp32 logits). With unfolded weights the two
+norms, and with ``fused_attention=False`` the q/k kernel, run separately.
 """
 from __future__ import annotations
 
@@ -71,7 +73,7 @@ class TalkerStep:
     """Static-buffer decode step for `batch` slots attending over `context` keys."""
 
     def __init__(self, cfg: DecoderConfig, weights: dict, arena: SlotArena, batch: int, context: int, cos, sin,
-                 norm_mode: int = _lib.NORM_REFERENCE):
+                 norm_mode: int = _lib.NORM_REFERENCE, fused_attention: bool = True):
         if not 1 <= context <= arena.capacity:
             raise ValueError("Attention context must fit the KV arena")
         if batch > arena.slots:
@@ -80,6 +82,7 @@ class TalkerStep:
         self.batch, self.context = batch, context
         self.cos, self.sin = cos, sin
         self.norm_mode = norm_mode
+        self.fused_attention = fused_attention   # q/k norm, RoPE and KV write inside the attention kernel
         dev = arena.device
         B, H = batch, cfg.hidden
         self.inputs = torch.zeros(B, H, dtype=BF16, device=dev)
@@ -108,17 +111,29 @@ class TalkerStep:
         lw = ops.linear
         res_in = self.inputs
         for i, layer in enumerate(w["layers"]):
-            ops.rms_norm(res_in, layer.input_norm, cfg.eps, self.norm_mode, out=self.xn)
-            lw(self.xn, layer.qkv, out=self.qkv, workspace=self.ws_linear)
-            ops.qk_norm_rope_kv(self.qkv, layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin, self.rotary,
-                                self.positions, self.arena.keys[i], self.arena.values[i], q_heads=cfg.q_heads,
-                                kv_heads=cfg.kv_heads, head_dim=cfg.head_dim, query_out=self.q)
-            ops.decode_attention(self.q, self.arena.keys[i], self.arena.values[i], self.positions,
-                                 context=self.context, out=self.attn, workspace=self.ws_attn)
+            if layer.folded:
+                lw(res_in, layer.qkv, out=self.qkv, row_norm_eps=cfg.eps)
+            else:
+                ops.rms_norm(res_in, layer.input_norm, cfg.eps, self.norm_mode, out=self.xn)
+                lw(self.xn, layer.qkv, out=self.qkv, workspace=self.ws_linear)
+            if self.fused_attention:
+                ops.decode_attention_qkv(self.qkv, layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin,
+                                         self.rotary, self.arena.keys[i], self.arena.values[i], self.positions,
+                                         q_heads=cfg.q_heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
+                                         context=self.context, out=self.attn, workspace=self.ws_attn)
+            else:
+                ops.qk_norm_rope_kv(self.qkv, layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin, self.rotary,
+                                    self.positions, self.arena.keys[i], self.arena.values[i], q_heads=cfg.q_heads,
+                                    kv_heads=cfg.kv_heads, head_dim=cfg.head_dim, query_out=self.q)
+                ops.decode_attention(self.q, self.arena.keys[i], self.arena.values[i], self.positions,
+                                     context=self.context, out=self.attn, workspace=self.ws_attn)
             lw(self.attn.view(B, cfg.q_width), layer.o, out=self.h, epilogue=_lib.EPI_RESIDUAL, residual=res_in,
                workspace=self.ws_linear)
-            ops.rms_norm(self.h, layer.post_norm, cfg.eps, self.norm_mode, out=self.xn)
-            lw(self.xn, layer.gate_up, out=self.act, epilogue=_lib.EPI_SWIGLU_PAIRED, workspace=self.ws_linear)
+            if layer.folded:
+                lw(self.h, layer.gate_up, out=self.act, epilogue=_lib.EPI_SWIGLU_PAIRED, row_norm_eps=cfg.eps)
+            else:
+                ops.rms_norm(self.h, layer.post_norm, cfg.eps, self.norm_mode, out=self.xn)
+                lw(self.xn, layer.gate_up, out=self.act, epilogue=_lib.EPI_SWIGLU_PAIRED, workspace=self.ws_linear)
             lw(self.act, layer.down, out=self.h, epilogue=_lib.EPI_RESIDUAL, residual=self.h,
                workspace=self.ws_linear)
             res_in = self.h
@@ -126,7 +141,8 @@ class TalkerStep:
         lw(self.hidden, w["head"], out=self.logits, workspace=self.ws_linear)
 
     def launches_per_step(self) -> int:
-        return 8 * self.cfg.layers + 2
+        per_layer = (6 if self.w["layers"][0].folded else 8) - (1 if self.fused_attention else 0)
+        return per_layer * self.cfg.layers + 2
 
     # ---------------------------------------------------------------- graph capture / replay
     @torch.inference_mode()
@@ -214,8 +230,11 @@ class TalkerPrefill:
         cfg, w, R, L = self.cfg, self.w, self.batch * self.length, self.length
         res_in = self.inputs
         for i, layer in enumerate(w["layers"]):
-            ops.rms_norm(res_in, layer.input_norm, cfg.eps, self.norm_mode, out=self.xn)
-            ops.linear(self.xn, layer.qkv, out=self.qkv)
+            if layer.folded:
+                ops.linear(res_in, layer.qkv, out=self.qkv, row_norm_eps=cfg.eps)
+            else:
+                ops.rms_norm(res_in, layer.input_norm, cfg.eps, self.norm_mode, out=self.xn)
+                ops.linear(self.xn, layer.qkv, out=self.qkv)
             ops.qk_norm_rope_kv(self.qkv, layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin, self.positions,
                                 self.positions, self.arena.keys[i], self.arena.values[i], q_heads=cfg.q_heads,
                                 kv_heads=cfg.kv_heads, head_dim=cfg.head_dim, length=L, query_out=self.q,
@@ -224,8 +243,11 @@ class TalkerPrefill:
                                  rows_per_slot=L, slots=self.slots, out=self.attn, workspace=self.ws_attn)
             ops.linear(self.attn.view(R, cfg.q_width), layer.o, out=self.h, epilogue=_lib.EPI_RESIDUAL,
                        residual=res_in)
-            ops.rms_norm(self.h, layer.post_norm, cfg.eps, self.norm_mode, out=self.xn)
-            ops.linear(self.xn, layer.gate_up, out=self.act, epilogue=_lib.EPI_SWIGLU_PAIRED)
+            if layer.folded:
+                ops.linear(self.h, layer.gate_up, out=self.act, epilogue=_lib.EPI_SWIGLU_PAIRED, row_norm_eps=cfg.eps)
+            else:
+                ops.rms_norm(self.h, layer.post_norm, cfg.eps, self.norm_mode, out=self.xn)
+                ops.linear(self.xn, layer.gate_up, out=self.act, epilogue=_lib.EPI_SWIGLU_PAIRED)
             ops.linear(self.act, layer.down, out=self.h, epilogue=_lib.EPI_RESIDUAL, residual=self.h)
             res_in = self.h
         ops.embedding(self.last, self.h, out=self.xn[:self.batch])       # last real row of each prompt

@@ -87,14 +87,24 @@ class PackedLayer:
     post_norm: torch.Tensor
     gate_up: torch.Tensor
     down: torch.Tensor
+    folded: bool = False   # input/post norm weights are premultiplied into qkv/gate_up
 
 
-def pack_decoder(weights: dict, device, tiled: bool = True) -> dict:
+def fold_norm(weight: torch.Tensor, norm_weight: torch.Tensor) -> torch.Tensor:
+    """W[n, k] * w[k] in fp32, rounded to bf16: the RMSNorm weight moved into the next projection."""
+    return (weight.float() * norm_weight.float()[None, :].to(weight.device)).to(torch.bfloat16)
+
+
+def pack_decoder(weights: dict, device, tiled: bool = True, fold_norms: bool = True) -> dict:
     """Kernel layouts on `device` (bf16, contiguous).
 
     With ``tiled`` the projection matrices are re-laid out as contiguous
     pre-swizzled 16 KB GEMM tiles (``ops.pack_tiles``), so every pipeline stage
-    of the weight-streaming GEMM reads one contiguous block of HBM."""
+    of the weight-streaming GEMM reads one contiguous block of HBM. With
+    ``fold_norms`` the input and post-attention RMSNorm weights are folded
+    into the QKV and gate/up projections; the step then runs those GEMMs on the
+    raw residual stream with the row RMS applied in the GEMM
+    (``q3t_linear_rownorm``) and launches no separate norm kernels."""
     from . import ops
 
     def dev(t):
@@ -104,15 +114,19 @@ def pack_decoder(weights: dict, device, tiled: bool = True) -> dict:
         t = dev(t)
         return ops.pack_tiles(t) if tiled else t
 
+    def maybe_fold(w, norm):
+        return fold_norm(dev(w), dev(norm)) if fold_norms else w
+
     layers = [PackedLayer(
         input_norm=dev(l["input_norm"]),
-        qkv=mat(torch.cat([l["q"], l["k"], l["v"]], dim=0)),
+        qkv=mat(maybe_fold(torch.cat([l["q"], l["k"], l["v"]], dim=0), l["input_norm"])),
         q_norm=dev(l["q_norm"]),
         k_norm=dev(l["k_norm"]),
         o=mat(l["o"]),
         post_norm=dev(l["post_norm"]),
-        gate_up=mat(interleave_gate_up(l["gate"], l["up"])),
+        gate_up=mat(maybe_fold(interleave_gate_up(l["gate"], l["up"]), l["post_norm"])),
         down=mat(l["down"]),
+        folded=fold_norms,
     ) for l in weights["layers"]]
     packed = {"layers": layers, "norm": dev(weights["norm"])}
     for key in ("embedding", "embeddings", "proj_bias"):

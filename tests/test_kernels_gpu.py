@@ -259,6 +259,70 @@ def test_linear_paired_swiglu(ops, cuda, rows):
     torch.testing.assert_close(out.cpu().float(), ref.float(), atol=1e-2, rtol=2e-2)
 
 
+@pytest.mark.parametrize("rows,k,n", [(1, 2048, 4096), (32, 2048, 4096), (32, 2048, 12288), (64, 1024, 2048),
+                                      (100, 2048, 640), (300, 256, 1024)])
+def test_linear_rownorm_equals_rmsnorm_then_linear(ops, cuda, rows, k, n):
+    """The folded RMSNorm GEMM (norm weight premultiplied, row RMS taken from the streamed
+    activation tiles, summed over the split-K cluster in rank order) against the fp32
+    reference rsqrt(mean(x^2)+eps) * (x @ bf16(W*w)^T), for one-CTA and clustered splits,
+    BN 16..256, and the STORE / RESIDUAL / paired-SwiGLU epilogues."""
+    from qwen3_tts_b200 import _lib
+    from qwen3_tts_b200.weights import fold_norm
+    eps = 1e-6
+    x = rnd(70 + rows, (rows, k), 1.0, BF16)
+    w = rnd(71, (n, k), 0.02, BF16)
+    g = (1.0 + rnd(72, (k,), 0.1, torch.float32)).to(BF16)
+    folded = fold_norm(w, g)
+    r = 1.0 / torch.sqrt(x.float().pow(2).mean(-1, keepdim=True) + eps)
+    prod = (x.float() @ folded.float().T) * r
+    out = ops.linear(x.to(cuda), ops.pack_tiles(folded.to(cuda)), row_norm_eps=eps)
+    # bf16 output of an fp32-accumulated, fp32-scaled dot product: one rounding plus order effects
+    torch.testing.assert_close(out.cpu().float(), prod, atol=2e-3 * math.sqrt(k / 64), rtol=1e-2)
+    res = rnd(73, (rows, n), 1.0, BF16)
+    out = ops.linear(x.to(cuda), folded.to(cuda), epilogue=_lib.EPI_RESIDUAL, residual=res.to(cuda), row_norm_eps=eps)
+    ref = (res.float() + prod.to(BF16).float()).to(BF16)
+    torch.testing.assert_close(out.cpu().float(), ref.float(), atol=2e-2, rtol=1e-2)
+    if n % 128 == 0:
+        out = ops.linear(x.to(cuda), folded.to(cuda), epilogue=_lib.EPI_SWIGLU_PAIRED, row_norm_eps=eps)
+        gate = prod.view(rows, n // 128, 2, 64)[:, :, 0].reshape(rows, n // 2).to(BF16)
+        up = prod.view(rows, n // 128, 2, 64)[:, :, 1].reshape(rows, n // 2).to(BF16)
+        ref = E.swiglu(torch.cat([gate, up], dim=-1))
+        torch.testing.assert_close(out.cpu().float(), ref.float(), atol=2e-2, rtol=2e-2)
+    assert_status_clean(ops, cuda)
+
+
+@pytest.mark.parametrize("rows,q_heads,kv_heads,head_dim,capacity,norms", [
+    (32, 16, 8, 128, 2304, True), (5, 16, 8, 128, 128, True), (7, 8, 8, 128, 640, False), (4, 4, 2, 64, 300, True)])
+def test_fused_qkv_attention_equals_separate_kernels(ops, cuda, rows, q_heads, kv_heads, head_dim, capacity, norms):
+    """q3t_decode_attention_qkv (q/k norm + RoPE + KV write inside the attention kernel)
+    against q3t_qk_norm_rope_kv followed by q3t_decode_attention: the same per-op bf16
+    rounding, so the outputs and the arena rows written are bit-identical."""
+    from qwen3_tts_b200.talker import rope_tables
+    gen = torch.Generator().manual_seed(rows * 7 + head_dim)
+    width = (q_heads + 2 * kv_heads) * head_dim
+    qkv = torch.randn(rows, width + 64, generator=gen).to(BF16).to(cuda)[:, :width]   # strided rows
+    keys = torch.randn(rows, kv_heads, capacity, head_dim, generator=gen).to(BF16).to(cuda)
+    values = torch.randn(rows, kv_heads, capacity, head_dim, generator=gen).to(BF16).to(cuda)
+    positions = torch.randint(0, capacity, (rows,), generator=gen).to(cuda)
+    positions[0] = 0
+    positions[-1] = capacity - 1
+    rotary = (positions + 3).contiguous()
+    qn = (1 + 0.1 * torch.randn(head_dim, generator=gen)).to(BF16).to(cuda) if norms else None
+    kn = (1 + 0.1 * torch.randn(head_dim, generator=gen)).to(BF16).to(cuda) if norms else None
+    cos, sin = rope_tables(capacity + 8, head_dim, 1e6, cuda)
+    k1, v1 = keys.clone(), values.clone()
+    q = ops.qk_norm_rope_kv(qkv, qn, kn, 1e-6, cos, sin, rotary, positions, k1, v1, q_heads=q_heads,
+                            kv_heads=kv_heads, head_dim=head_dim)
+    ref = ops.decode_attention(q, k1, v1, positions, context=capacity)
+    k2, v2 = keys.clone(), values.clone()
+    got = ops.decode_attention_qkv(qkv, qn, kn, 1e-6, cos, sin, rotary, k2, v2, positions, q_heads=q_heads,
+                                   kv_heads=kv_heads, head_dim=head_dim, context=capacity)
+    torch.cuda.synchronize()
+    assert torch.equal(k2, k1) and torch.equal(v2, v1)
+    assert torch.equal(got, ref)
+    assert_status_clean(ops, cuda)
+
+
 def test_linear_graph_replay_is_deterministic(ops, cuda):
     x = rnd(60, (32, 2048), 1.0, BF16).to(cuda)
     w = rnd(61, (6144, 2048), 0.02, BF16).to(cuda)

@@ -32,7 +32,7 @@ def check_chain(cfg, weights, talker_emb, step, hidden, first_codes, draws_fn, t
     gpu_logits = step.step_logits.cpu()
     first = talker_emb[first_codes].float()
     tables = OD.Tables(cfg.groups + 1, cfg.head_dim, cfg.theta)
-    _, _, ref_logits = OD.predictor_frame(cfg, weights, hidden.float(), first, None, tables, mode="bf16",
+    _, _, ref_logits = OD.predictor_frame(cfg, weights, hidden.float(), first, None, tables, mode="bf16f",
                                           uniforms_fn=draws_fn, forced_codes=codes[:, 1:], top_p=top_p)
     # per-step logits under teacher forcing: bf16-emulating oracle, same rounding points
     scale = ref_logits.abs().max()

@@ -52,7 +52,7 @@ def test_tiny_talker_step_matches_oracle(cuda, use_graph):
         cuda, cfg, 5, 128, positions, use_graph=use_graph)
     # bf16-emulating oracle: same rounding points, only accumulation order differs
     cache_b = [(k.clone(), v.clone()) for k, v in cache]
-    h_ref, l_ref = OD.talker_decode_step(cfg, weights, embeds, pos, delta, cache_b, tables, mode="bf16")
+    h_ref, l_ref = OD.talker_decode_step(cfg, weights, embeds, pos, delta, cache_b, tables, mode="bf16f")
     torch.testing.assert_close(hidden.float(), h_ref, atol=3e-2, rtol=3e-2)
     torch.testing.assert_close(logits, l_ref, atol=2e-2, rtol=2e-2)
     # fp32 truth: logits within 1e-2 relative of the logit scale
@@ -103,7 +103,7 @@ def test_full_width_talker_layers(cuda):
         cuda, cfg, 32, 640, positions, seed=9)
     from qwen3_tts_b200 import ops
     assert ops.read_status(cuda) == 0
-    h_ref, l_ref = OD.talker_decode_step(cfg, weights, embeds, pos, delta, cache, tables, mode="bf16")
+    h_ref, l_ref = OD.talker_decode_step(cfg, weights, embeds, pos, delta, cache, tables, mode="bf16f")
     # Logits within 1e-2 relative (normwise, ||diff||_2 / ||ref||_2); elementwise
     # the bf16 rounding chain of two full-width layers differs in a handful of
     # entries by a few bf16 ulps of the hidden state, so the max-abs bound is 6e-2.
