@@ -296,7 +296,11 @@ __global__ void __launch_bounds__(128, 3)
     float mt = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
     mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
     mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
-    const float m_new = fmaxf(m_run, mt);
+    // Lazy rescaling: the running reference max only moves when a score exceeds it by
+    // more than 2^8 (p stays <= 256, exact in fp32 and bf16's range); the final O / L
+    // and the chunk merge are invariant to the reference chosen. Most tiles then skip
+    // the 2 x D/8 rescale multiplies (the skip is warp-uniform).
+    const float m_new = (m_run == -INFINITY || mt > m_run + 8.f) ? fmaxf(m_run, mt) : m_run;
     const float alpha = m_new == -INFINITY ? 1.f : exp2f(m_run - m_new);
     float p[4];
 #pragma unroll
@@ -305,12 +309,14 @@ __global__ void __launch_bounds__(128, 3)
     ps += __shfl_xor_sync(0xffffffffu, ps, 1);
     ps += __shfl_xor_sync(0xffffffffu, ps, 2);
     l_run = l_run * alpha + ps;
-    m_run = m_new;
+    if (__any_sync(0xffffffffu, m_new != m_run)) {
 #pragma unroll
-    for (int n = 0; n < NT; ++n) {
-      o[n][0] *= alpha;
-      o[n][1] *= alpha;
+      for (int n = 0; n < NT; ++n) {
+        o[n][0] *= alpha;
+        o[n][1] *= alpha;
+      }
     }
+    m_run = m_new;
     const uint32_t pa0 = pack_bf16x2(p[0], p[1]), pa2 = pack_bf16x2(p[2], p[3]);
 
     // ---- O += P V (keys of this warp; stale rows past the chunk end are zeroed)
