@@ -173,6 +173,17 @@ int q3t_linear_rownorm(const void* x, int64_t x_stride, int64_t rows, int64_t in
                        int64_t residual_stride, const void* scale, float eps, const void* weight_tiles,
                        unsigned* status, void* stream);
 
+/* q3t_linear (eps == 0) or q3t_linear_rownorm (eps > 0) that also pulls the next
+ * kernel's weights into L2 while it runs: [prefetch, prefetch + prefetch_bytes)
+ * is split over the CTAs and requested before the dependency wait, so the next
+ * GEMM of a decode chain streams its weights from L2 (a hint only: no ordering,
+ * no completion). prefetch 16-byte aligned, prefetch_bytes % 16 == 0; NULL or 0 = none. */
+int q3t_linear_prefetch(const void* x, int64_t x_stride, int64_t rows, int64_t in_features,
+                        const void* weight, int64_t out_features, const void* bias, void* out,
+                        int64_t out_stride, int out_dtype, int epilogue, const void* residual,
+                        int64_t residual_stride, const void* scale, float eps, const void* weight_tiles,
+                        const void* prefetch, size_t prefetch_bytes, unsigned* status, void* stream);
+
 /* Pre-swizzled weight layout for q3t_linear (pass it as weight_tiles, weight may
  * then be NULL): tile (n, k) of 128 rows x 64 columns is the contiguous 16 KB image
  * of the 128-byte-swizzled shared-memory tile, tiles ordered [n][k], zero padded.

@@ -108,12 +108,18 @@ def layer_forward(cfg, w, h, rot_pos, cache_k, cache_v, cache_pos, tables, mode)
     return h
 
 
-def decoder_forward(cfg, weights, h, rot_pos, cache, cache_pos, tables, mode="fp32"):
-    """All layers then the final norm. cache: list of (K, V) per layer."""
+def decoder_layers(cfg, weights, h, rot_pos, cache, cache_pos, tables, mode="fp32"):
+    """All layers, without the final norm. cache: list of (K, V) per layer."""
     h = h.float()
     for w, (ck, cv) in zip(weights["layers"], cache):
         h = layer_forward(cfg, w, h, rot_pos, ck, cv, cache_pos, tables, mode)
-    return _rms(h, weights["norm"], cfg.eps, mode)
+    return h
+
+
+def decoder_forward(cfg, weights, h, rot_pos, cache, cache_pos, tables, mode="fp32"):
+    """All layers then the final norm. cache: list of (K, V) per layer."""
+    return _rms(decoder_layers(cfg, weights, h, rot_pos, cache, cache_pos, tables, mode), weights["norm"], cfg.eps,
+                mode)
 
 
 def new_cache(cfg, batch, capacity):
@@ -156,8 +162,13 @@ def predictor_frame(cfg, weights, hidden, first, draws, tables, mode="fp32", *, 
             x = weights["embeddings"][step - 1][token[:, 0]].float()[:, None, :]
             pos = torch.full((B, 1), step + 1)
         x = _r(x @ weights["proj"].float().T + weights["proj_bias"].float(), mode)
-        out = decoder_forward(cfg, weights, x, pos, cache, pos, tables, mode)
-        logits = _r(out[:, -1] @ weights["heads"][step].float().T, mode)
+        if mode == "bf16f":
+            # the predictor's final norm feeds only the heads: folded into them on the GPU
+            out = decoder_layers(cfg, weights, x, pos, cache, pos, tables, mode)
+            logits = _normed_proj(out[:, -1], weights["norm"], weights["heads"][step], cfg.eps, mode)
+        else:
+            out = decoder_forward(cfg, weights, x, pos, cache, pos, tables, mode)
+            logits = _r(out[:, -1] @ weights["heads"][step].float().T, mode)
         u = draws[:, step + 1] if uniforms_fn is None else uniforms_fn(step)
         token = categorical(logits, u, temperature=temperature, top_k=top_k, top_p=top_p)
         codes.append(token)

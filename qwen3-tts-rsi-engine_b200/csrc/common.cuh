@@ -140,6 +140,11 @@ Q3T_DEV void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, 
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
+// L2 prefetch hint for a global range (16-byte aligned address, bytes % 16 == 0); no completion.
+Q3T_DEV void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
+}
 // Untiled bulk copy global -> shared; both addresses 16-byte aligned, bytes % 16 == 0.
 Q3T_DEV void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(

@@ -20,6 +20,7 @@
 #include "host.cuh"
 
 #include <mutex>
+#include <stdlib.h>
 #include <string.h>
 
 using namespace q3t;
@@ -62,6 +63,10 @@ struct GemmArgs {
   const __nv_bfloat16* scale;  // per-feature scale of Q3T_EPI_RESIDUAL_SCALED
   int row_norm;                // scale row m by 1/sqrt(mean_k x[m,k]^2 + norm_eps) (folded RMSNorm)
   float norm_eps;
+  // L2 prefetch hint: bytes the NEXT kernel of the chain will stream (its weights),
+  // split evenly over this grid's CTAs and requested at kernel start
+  const uint8_t* prefetch;
+  uint64_t prefetch_bytes;
   unsigned* status;
 };
 
@@ -69,30 +74,88 @@ __device__ __forceinline__ float silu_gate(float g, float u) {
   return bf16r(bf16r(g / (1.0f + expf(-g))) * u);
 }
 
-// Stores one output element according to the epilogue (non-SwiGLU).
+__host__ __device__ constexpr bool has_residual(int epi) { return epi == Q3T_EPI_RESIDUAL || epi == Q3T_EPI_RESIDUAL_SCALED; }
+
+// Final value of one output element (non-SwiGLU epilogues) from its accumulator
+// (bias already added), its residual input r and its per-feature scale g.
 template <int EPI>
-__device__ __forceinline__ void store_out(const GemmArgs& a, int m, int n, float acc) {
-  if (a.bias != nullptr) acc += __bfloat162float(a.bias[n]);
+__device__ __forceinline__ float epilogue_value(float acc, float r, float g) {
   if constexpr (EPI == Q3T_EPI_RESIDUAL) {
-    const float r = __bfloat162float(a.residual[int64_t(m) * a.res_stride + n]);
-    static_cast<__nv_bfloat16*>(a.out)[int64_t(m) * a.out_stride + n] = __float2bfloat16_rn(r + bf16r(acc));
+    return r + bf16r(acc);
   } else if constexpr (EPI == Q3T_EPI_RESIDUAL_SCALED) {
-    const float r = __bfloat162float(a.residual[int64_t(m) * a.res_stride + n]);
-    const float g = __bfloat162float(a.scale[n]);
-    static_cast<__nv_bfloat16*>(a.out)[int64_t(m) * a.out_stride + n] =
-        __float2bfloat16_rn(r + bf16r(g * bf16r(acc)));
+    return r + bf16r(g * bf16r(acc));
   } else if constexpr (EPI == Q3T_EPI_GELU) {
     const float v = bf16r(acc);
-    static_cast<__nv_bfloat16*>(a.out)[int64_t(m) * a.out_stride + n] =
-        __float2bfloat16_rn(0.5f * v * (1.0f + erff(v * 0.70710678118654752f)));
+    return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
   } else if constexpr (EPI == Q3T_EPI_SILU) {
     const float v = bf16r(acc);
-    static_cast<__nv_bfloat16*>(a.out)[int64_t(m) * a.out_stride + n] = __float2bfloat16_rn(v / (1.0f + expf(-v)));
+    return v / (1.0f + expf(-v));
   } else {
-    if (a.out_f32)
-      static_cast<float*>(a.out)[int64_t(m) * a.out_stride + n] = bf16r(acc);
-    else
-      static_cast<__nv_bfloat16*>(a.out)[int64_t(m) * a.out_stride + n] = __float2bfloat16_rn(acc);
+    return acc;
+  }
+}
+
+template <int EPI>
+__device__ __forceinline__ void store_value(const GemmArgs& a, int m, int n, float v) {
+  if (EPI == Q3T_EPI_STORE && a.out_f32)
+    static_cast<float*>(a.out)[int64_t(m) * a.out_stride + n] = bf16r(v);
+  else
+    static_cast<__nv_bfloat16*>(a.out)[int64_t(m) * a.out_stride + n] = __float2bfloat16_rn(v);
+}
+
+// Output elements (m_first + j, n), j < 16, of one feature n. All residual inputs
+// are loaded before the first store: the residual may alias the output, and
+// interleaved load/store pairs would serialise one memory round trip per element.
+template <int EPI>
+__device__ __forceinline__ void store_rows16(const GemmArgs& a, int m_first, int n, const float* v,
+                                             const float* rscale) {
+  const bool hb = a.bias != nullptr;
+  const float bias = hb ? __bfloat162float(a.bias[n]) : 0.f;
+  const float g = EPI == Q3T_EPI_RESIDUAL_SCALED ? __bfloat162float(a.scale[n]) : 0.f;
+  float r[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+    r[j] = (has_residual(EPI) && m_first + j < a.rows)
+               ? __bfloat162float(a.residual[int64_t(m_first + j) * a.res_stride + n])
+               : 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if (m_first + j >= a.rows) break;
+    float acc = rscale != nullptr ? v[j] * rscale[j] : v[j];
+    if (hb) acc += bias;
+    store_value<EPI>(a, m_first + j, n, epilogue_value<EPI>(acc, r[j], g));
+  }
+}
+
+// Epilogue inputs of output elements (m, n_first + j), j < 4: residual, bias and per-feature
+// scale, loaded up front so that their latency overlaps the split-K partial loads.
+struct Inputs4 {
+  float r[4], bias[4], g[4];
+};
+template <int EPI>
+__device__ __forceinline__ Inputs4 load_inputs4(const GemmArgs& a, int m, int n_first) {
+  Inputs4 in;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const bool live = n_first + j < a.out_features;
+    in.r[j] = (has_residual(EPI) && live) ? __bfloat162float(a.residual[int64_t(m) * a.res_stride + n_first + j])
+                                          : 0.f;
+    in.bias[j] = (a.bias != nullptr && live) ? __bfloat162float(a.bias[n_first + j]) : 0.f;
+    in.g[j] = (EPI == Q3T_EPI_RESIDUAL_SCALED && live) ? __bfloat162float(a.scale[n_first + j]) : 0.f;
+  }
+  return in;
+}
+
+// Output elements (m, n_first + j), j < 4, of one activation row (features bounded by out_features).
+template <int EPI>
+__device__ __forceinline__ void store_features4(const GemmArgs& a, int m, int n_first, const float* v,
+                                                const Inputs4& in) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (n_first + j >= a.out_features) break;
+    float acc = v[j];
+    if (a.bias != nullptr) acc += in.bias[j];
+    store_value<EPI>(a, m, n_first + j, epilogue_value<EPI>(acc, in.r[j], in.g[j]));
   }
 }
 
@@ -189,6 +252,17 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   int issued = 0;  // producer only
+  if (a.prefetch != nullptr && threadIdx.x == 64) {
+    // this CTA's share of the next kernel's weights, in 16-byte units, pulled into L2
+    const uint64_t ctas = uint64_t(gridDim.x) * gridDim.y * gridDim.z;
+    const uint64_t id = blockIdx.x + uint64_t(gridDim.x) * (blockIdx.y + uint64_t(gridDim.y) * blockIdx.z);
+    const uint64_t units = a.prefetch_bytes / 16, per = (units + ctas - 1) / ctas;
+    const uint64_t u0 = id * per, u1 = u0 + per < units ? u0 + per : units;
+    for (uint64_t u = u0; u < u1; u += 2048) {  // 32 KB requests
+      const uint64_t n = u1 - u < 2048 ? u1 - u : 2048;
+      prefetch_l2(a.prefetch + u * 16, uint32_t(n * 16));
+    }
+  }
 
   if (warp == 0) {
     if (lane == 0) {
@@ -298,13 +372,7 @@ __global__ void __launch_bounds__(128, 1)
     for (int c0 = 0; c0 < BN; c0 += 16) {
       float v[16];
       tmem_ld16(taddr + c0, v);
-      if (ok && n < a.out_features) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = m0 + c0 + j;
-          if (m < a.rows) store_out<EPI>(a, m, n, a.row_norm ? v[j] * rnorm[c0 + j] : v[j]);
-        }
-      }
+      if (ok && n < a.out_features) store_rows16<EPI>(a, m0 + c0, n, v, a.row_norm ? rnorm + c0 : nullptr);
     }
     tc_fence_before();
     __syncthreads();
@@ -342,22 +410,17 @@ __global__ void __launch_bounds__(128, 1)
   const uint32_t rank = clustered ? cluster_rank() : 0u;
   const int mcount = (a.rows - m0) < BN ? (a.rows - m0) : BN;
   const uint32_t red_local = smem_u32(red);
-  // Row scale of the folded RMSNorm for activation row c: the K slices' partial sums of
-  // squares (each CTA's padding column) added in rank order, so every CTA of the
-  // cluster computes the same value; loaded together with the accumulator tiles.
-  auto row_scale = [&](int c) -> float {
+  // Every peer's partial quad (and, with the folded RMSNorm, its partial sum of squares of
+  // the row, kept in the padding column) is requested at once, after the unit's global
+  // epilogue inputs; the partials are then added in rank order, so every CTA of the
+  // cluster computes the same row scale and the result does not depend on timing.
+  constexpr int kMaxSplits = 8;
+  const uint32_t ss_col = uint32_t(kTileN) * 4u;
+  auto scale_of = [&](const float* ss) -> float {
     float total = 0.f;
-    const uint32_t off = uint32_t(c * C::kRedStride + kTileN) * 4u;
-    for (int p0 = 0; p0 < cs; p0 += 4) {
-      float v[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        v[j] = p0 + j < cs ? (clustered ? ld_peer1(map_peer(red_local, uint32_t(p0 + j)) + off)
-                                        : red[c * C::kRedStride + kTileN])
-                           : 0.f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) total += v[j];
-    }
+    for (int j = 0; j < kMaxSplits; ++j)
+      if (j < cs) total += ss[j];
     return 1.0f / sqrtf(total / float(a.in_features) + a.norm_eps);
   };
   if constexpr (EPI == Q3T_EPI_SWIGLU_PAIRED) {
@@ -368,27 +431,34 @@ __global__ void __launch_bounds__(128, 1)
     for (int u = threadIdx.x; u < units; u += blockDim.x) {
       const int c = u / nq;
       const int f = f0 + (u % nq) * 4;
-      float4 g = make_float4(0.f, 0.f, 0.f, 0.f), up = g;
-      for (int p0 = 0; p0 < cs; p0 += 2) {  // both halves of two peers in flight, then the adds (rank order)
-        float4 gv[2], uv[2];
+      const uint32_t row = uint32_t(c * C::kRedStride) * 4u;
+      float4 gv[kMaxSplits], uv[kMaxSplits];
+      float ss[kMaxSplits];
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const bool live = p0 + j < cs;
-          const uint32_t base = clustered ? map_peer(red_local, uint32_t(live ? p0 + j : 0)) : red_local;
-          gv[j] = clustered ? ld_peer4(base + uint32_t(c * C::kRedStride + f) * 4u)
-                            : *reinterpret_cast<const float4*>(red + c * C::kRedStride + f);
-          uv[j] = clustered ? ld_peer4(base + uint32_t(c * C::kRedStride + 64 + f) * 4u)
-                            : *reinterpret_cast<const float4*>(red + c * C::kRedStride + 64 + f);
-          if (!live) gv[j] = uv[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < kMaxSplits; ++j) {
+        if (j < cs) {
+          if (clustered) {
+            const uint32_t base = map_peer(red_local, uint32_t(j)) + row;
+            gv[j] = ld_peer4(base + uint32_t(f) * 4u);
+            uv[j] = ld_peer4(base + uint32_t(64 + f) * 4u);
+            ss[j] = a.row_norm ? ld_peer1(base + ss_col) : 0.f;
+          } else {
+            gv[j] = *reinterpret_cast<const float4*>(red + c * C::kRedStride + f);
+            uv[j] = *reinterpret_cast<const float4*>(red + c * C::kRedStride + 64 + f);
+            ss[j] = a.row_norm ? red[c * C::kRedStride + kTileN] : 0.f;
+          }
         }
+      }
+      float4 g = make_float4(0.f, 0.f, 0.f, 0.f), up = g;
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
+      for (int j = 0; j < kMaxSplits; ++j) {
+        if (j < cs) {
           g.x += gv[j].x; g.y += gv[j].y; g.z += gv[j].z; g.w += gv[j].w;
           up.x += uv[j].x; up.y += uv[j].y; up.z += uv[j].z; up.w += uv[j].w;
         }
       }
       if (a.row_norm) {
-        const float rn = row_scale(c);
+        const float rn = scale_of(ss);
         g.x *= rn; g.y *= rn; g.z *= rn; g.w *= rn;
         up.x *= rn; up.y *= rn; up.z *= rn; up.w *= rn;
       }
@@ -400,30 +470,39 @@ __global__ void __launch_bounds__(128, 1)
         if (n0 + 64 + f + j < a.out_features) o[j] = __float2bfloat16_rn(silu_gate(bf16r(gs[j]), bf16r(us[j])));
     }
   } else {
-    // this CTA finalises feature quads [q0, q1) of the tile's 32
+    // this CTA finalises feature quads [q0, q1) of the tile's 32 (clustered only)
     const int q0 = int(rank) * 32 / cs, nq = (int(rank) + 1) * 32 / cs - q0;
     const int f0 = q0 * 4;
     const int units = mcount * nq;
     for (int u = threadIdx.x; u < units; u += blockDim.x) {
       const int c = u / nq;
       const int f = f0 + (u % nq) * 4;
+      const Inputs4 in = load_inputs4<EPI>(a, m0 + c, n0 + f);
+      const uint32_t row = uint32_t(c * C::kRedStride) * 4u;
+      float4 v[kMaxSplits];
+      float ss[kMaxSplits];
+#pragma unroll
+      for (int j = 0; j < kMaxSplits; ++j) {
+        if (j < cs) {
+          const uint32_t base = map_peer(red_local, uint32_t(j)) + row;
+          v[j] = ld_peer4(base + uint32_t(f) * 4u);
+          ss[j] = a.row_norm ? ld_peer1(base + ss_col) : 0.f;
+        }
+      }
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      const uint32_t off = uint32_t(c * C::kRedStride + f) * 4u;
-      for (int p0 = 0; p0 < cs; p0 += 4) {  // four remote loads in flight, then the adds (rank order)
-        float4 v[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          v[j] = p0 + j < cs ? ld_peer4(map_peer(red_local, uint32_t(p0 + j)) + off) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < kMaxSplits; ++j) {
+        if (j < cs) {
           acc.x += v[j].x; acc.y += v[j].y; acc.z += v[j].z; acc.w += v[j].w;
         }
       }
-      const float rn = a.row_norm ? row_scale(c) : 1.f;
-      const float vals[4] = {acc.x * rn, acc.y * rn, acc.z * rn, acc.w * rn};
+      float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+      if (a.row_norm) {
+        const float rn = scale_of(ss);
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (n0 + f + j < a.out_features) store_out<EPI>(a, m0 + c, n0 + f + j, vals[j]);
+        for (int j = 0; j < 4; ++j) vals[j] *= rn;
+      }
+      store_features4<EPI>(a, m0 + c, n0 + f, vals, in);
     }
   }
   if (clustered) cluster_sync();  // peers finished reading this CTA's shared memory
@@ -508,13 +587,22 @@ Plan plan(int64_t rows, int64_t in_features, int64_t out_features) {
   p.m_tiles = int((rows + p.bn - 1) / p.bn);
   p.kblocks = int((in_features + kTileK - 1) / kTileK);
   // K splits: a power of two <= 8 (one thread-block cluster per tile), each
-  // split at least two k-blocks, aiming at ~2 resident CTAs per SM. (Measured:
-  // 16-CTA and 3- or 9-CTA clusters that fill the SMs more evenly ran the
-  // talker GEMMs 1.6-2x slower in a dependent launch chain.)
+  // split at least four k-blocks, at most ~1.33 CTAs per SM in total. (Measured
+  // in dependent launch chains of the decode GEMMs at 32 and 64 rows: splits of
+  // 2-3 k-blocks, or grids beyond ~200 CTAs, ran 5-50% slower than this rule's
+  // pick for every talker and predictor projection but one, within 5%; 16-CTA
+  // and 3- or 9-CTA clusters ran 1.6-2x slower.)
   const int base = p.n_tiles * p.m_tiles;
-  const int target = 2 * sm_count();
+  const int target = sm_count() + sm_count() / 3;
   int splits = 1;
-  while (splits < 8 && base * splits * 2 <= target + target / 8 && p.kblocks >= 4 * splits) splits *= 2;
+  while (splits < 8 && base * splits * 2 <= target && p.kblocks >= 4 * splits * 2) splits *= 2;
+#ifdef Q3T_TUNING
+  // tuning builds only: force the split count (a power of two <= 8, >= 2 k-blocks per split)
+  if (const char* forced = getenv("Q3T_SPLITS")) {
+    const int s = atoi(forced);
+    if (s >= 1 && s <= 8 && (s & (s - 1)) == 0 && p.kblocks >= 2 * s) splits = s;
+  }
+#endif
   p.splits = splits;
   return p;
 }
@@ -596,8 +684,11 @@ namespace {
 int linear_impl(const void* x, int64_t x_stride, int64_t rows, int64_t in_features, const void* weight,
                 int64_t out_features, const void* bias, void* out, int64_t out_stride, int out_dtype, int epilogue,
                 const void* residual, int64_t residual_stride, const void* scale, float row_norm_eps,
-                const void* weight_tiles, void* workspace, size_t workspace_bytes, unsigned* status, void* stream) {
+                const void* weight_tiles, const void* prefetch, size_t prefetch_bytes, unsigned* status,
+                void* stream) {
   if (!x || (!weight && !weight_tiles) || !out) return fail(Q3T_EINVAL, "linear: null pointer");
+  if (prefetch != nullptr && (!aligned16(prefetch) || prefetch_bytes % 16))
+    return fail(Q3T_EINVAL, "linear: prefetch range needs 16-byte alignment and size");
   if (!(row_norm_eps >= 0.f)) return fail(Q3T_EINVAL, "linear: row-norm eps must be >= 0");
   if (rows < 1 || rows > (int64_t(1) << 24) || in_features < 8 || in_features % 8 || out_features < 1 || out_features > (1 << 24))
     return fail(Q3T_EINVAL, "linear: unsupported shape rows=%lld in=%lld out=%lld", (long long)rows,
@@ -618,8 +709,6 @@ int linear_impl(const void* x, int64_t x_stride, int64_t rows, int64_t in_featur
   if (epilogue == Q3T_EPI_SWIGLU_PAIRED && (out_features % kTileN || out_dtype != Q3T_BF16 || bias != nullptr))
     return fail(Q3T_EINVAL, "linear: paired SwiGLU needs out_features %% 128 == 0, bf16 output, no bias");
   if (epilogue < Q3T_EPI_STORE || epilogue > Q3T_EPI_SILU) return fail(Q3T_EINVAL, "linear: epilogue");
-  (void)workspace;
-  (void)workspace_bytes;
   const Plan p = plan(rows, in_features, out_features);
   CUtensorMap tmw, tmx;
   int rc = Q3T_OK;
@@ -647,6 +736,8 @@ int linear_impl(const void* x, int64_t x_stride, int64_t rows, int64_t in_featur
   a.tiles = static_cast<const uint8_t*>(weight_tiles);
   a.row_norm = row_norm_eps > 0.f ? 1 : 0;
   a.norm_eps = row_norm_eps;
+  a.prefetch = prefetch_bytes ? static_cast<const uint8_t*>(prefetch) : nullptr;
+  a.prefetch_bytes = prefetch_bytes;
   a.status = status;
   switch (epilogue) {
     case Q3T_EPI_STORE: return dispatch_bn<Q3T_EPI_STORE>(p, tmw, tmx, a, stream);
@@ -665,8 +756,10 @@ extern "C" int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t
                           int epilogue, const void* residual, int64_t residual_stride, const void* scale,
                           const void* weight_tiles, void* workspace, size_t workspace_bytes, unsigned* status,
                           void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
   return linear_impl(x, x_stride, rows, in_features, weight, out_features, bias, out, out_stride, out_dtype, epilogue,
-                     residual, residual_stride, scale, 0.f, weight_tiles, workspace, workspace_bytes, status, stream);
+                     residual, residual_stride, scale, 0.f, weight_tiles, nullptr, 0, status, stream);
 }
 
 extern "C" int q3t_linear_rownorm(const void* x, int64_t x_stride, int64_t rows, int64_t in_features,
@@ -677,4 +770,14 @@ extern "C" int q3t_linear_rownorm(const void* x, int64_t x_stride, int64_t rows,
   if (!(eps > 0.f)) return fail(Q3T_EINVAL, "linear_rownorm: eps must be positive");
   return linear_impl(x, x_stride, rows, in_features, weight, out_features, bias, out, out_stride, out_dtype, epilogue,
                      residual, residual_stride, scale, eps, weight_tiles, nullptr, 0, status, stream);
+}
+
+extern "C" int q3t_linear_prefetch(const void* x, int64_t x_stride, int64_t rows, int64_t in_features,
+                                   const void* weight, int64_t out_features, const void* bias, void* out,
+                                   int64_t out_stride, int out_dtype, int epilogue, const void* residual,
+                                   int64_t residual_stride, const void* scale, float eps, const void* weight_tiles,
+                                   const void* prefetch, size_t prefetch_bytes, unsigned* status, void* stream) {
+  if (!(eps >= 0.f)) return fail(Q3T_EINVAL, "linear_prefetch: eps must be >= 0");
+  return linear_impl(x, x_stride, rows, in_features, weight, out_features, bias, out, out_stride, out_dtype, epilogue,
+                     residual, residual_stride, scale, eps, weight_tiles, prefetch, prefetch_bytes, status, stream);
 }

@@ -180,16 +180,40 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
         }
       }
       __syncthreads();
-      if (threadIdx.x == 0) {
-        int rem = sel_remaining;
-        int d = 255;
-        for (; d > 0; --d) {
-          const int cnt = int(hist[d]);
-          if (cnt >= rem) break;
-          rem -= cnt;
+      if (threadIdx.x < 32) {
+        // The digit is the first bin, from the top, at which the cumulative count
+        // reaches `remaining`. Lane l holds bins 255-8l .. 248-8l; a warp scan finds
+        // the lane, which then walks its eight bins.
+        const int lane = threadIdx.x;
+        const int rem = sel_remaining;
+        const int top = 255 - 8 * lane;
+        int cnt[8], local = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          cnt[q] = int(hist[top - q]);
+          local += cnt[q];
         }
-        sel_prefix = prefix | (uint32_t(d) << shift);
-        sel_remaining = rem;
+        int incl = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += v;
+        }
+        const int excl = incl - local;
+        __syncwarp();
+        if (excl < rem && rem <= incl) {
+          int r2 = rem - excl, d = top - 7;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            if (cnt[q] >= r2) {
+              d = top - q;
+              break;
+            }
+            r2 -= cnt[q];
+          }
+          sel_prefix = prefix | (uint32_t(d) << shift);
+          sel_remaining = r2;
+        }
       }
       __syncthreads();
     }

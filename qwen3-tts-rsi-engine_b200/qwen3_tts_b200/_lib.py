@@ -47,6 +47,8 @@ SIGNATURES: dict[str, tuple[object, list]] = {
                                   _p, _p]),
     "q3t_linear": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _p, _p, _i64, _i32, _i32, _p, _i64, _p, _p, _p, _sz,
                           _p, _p]),
+    "q3t_linear_prefetch": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _p, _p, _i64, _i32, _i32, _p, _i64, _p, _f32,
+                                   _p, _p, _sz, _p, _p]),
     "q3t_weight_tiles_bytes": (_sz, [_i64, _i64]),
     "q3t_pack_weight_tiles": (_i32, [_p, _i64, _i64, _p, _p]),
     "q3t_qk_norm_rope_kv": (_i32, [_p, _i64, _p, _p, _f32, _p, _p, _i64, _p, _p, _p, _p, _p, _i64, _i64, _p, _i64,

@@ -288,13 +288,15 @@ def pack_tiles(weight: torch.Tensor) -> TiledWeight:
 
 def linear(x, weight, bias=None, *, out=None, out_dtype=BF16, epilogue: int = _lib.EPI_STORE, residual=None,
            scale=None, row_norm_eps: Optional[float] = None, workspace: Optional[torch.Tensor] = None,
-           tag: str = "linear"):
+           prefetch=None, tag: str = "linear"):
     """out = x @ weight.T (+ bias) with a fused epilogue, on tcgen05 tensor cores.
 
     `weight` is a contiguous bf16 [out, in] tensor or a TiledWeight. With
     `row_norm_eps`, row r of the product is scaled by rsqrt(mean(x[r]^2) + eps):
     an RMSNorm of x folded into the GEMM (the norm weight must already be
-    multiplied into `weight`, see weights.fold_norm)."""
+    multiplied into `weight`, see weights.fold_norm). `prefetch` (a weight
+    tensor or TiledWeight, normally the next GEMM's) is pulled into L2 while
+    this GEMM runs (q3t_linear_prefetch)."""
     tiled = isinstance(weight, TiledWeight)
     _need_cuda(x, weight.tiles if tiled else weight)
     if x.dtype != BF16 or (not tiled and (weight.dtype != BF16 or weight.ndim != 2 or not weight.is_contiguous())):
@@ -314,6 +316,16 @@ def linear(x, weight, bias=None, *, out=None, out_dtype=BF16, epilogue: int = _l
     if residual is not None:
         res2 = residual.reshape(rows, n_out) if residual.is_contiguous() else residual
     odt = _lib.Q3T_BF16 if out.dtype == BF16 else _lib.Q3T_F32
+    if prefetch is not None:
+        pre = prefetch.tiles if isinstance(prefetch, TiledWeight) else prefetch
+        _need_cuda(pre)
+        call("q3t_linear_prefetch", x2.data_ptr(), x2.stride(0), rows, in_features,
+             None if tiled else weight.data_ptr(), n_rows_w, _ptr(bias), out2.data_ptr(), out2.stride(0), odt,
+             epilogue, _ptr(res2), res2.stride(0) if res2 is not None else 0, _ptr(scale),
+             float(row_norm_eps) if row_norm_eps is not None else 0.0, weight.tiles.data_ptr() if tiled else None,
+             pre.data_ptr(), (pre.numel() * pre.element_size()) // 16 * 16, status_word(x.device).data_ptr(),
+             _stream())
+        return out
     if row_norm_eps is not None:
         call("q3t_linear_rownorm", x2.data_ptr(), x2.stride(0), rows, in_features,
              None if tiled else weight.data_ptr(), n_rows_w, _ptr(bias), out2.data_ptr(), out2.stride(0), odt,

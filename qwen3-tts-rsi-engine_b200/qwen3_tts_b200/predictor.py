@@ -9,9 +9,13 @@ With ``graph_embeddings`` the frame embedding (talker codec embedding of the
 semantic code plus the 15 predictor embeddings, summed once, plus the text
 embedding) is produced in the same graph (continuous.py:63-67, 590-601).
 
-All 15 steps x 5 layers and the sampling run as ~675 kernels from
+All 15 steps x 5 layers and the sampling run as ~425 kernels from
 ``libq3t_b200.so`` replayed as one graph; the RoPE coefficients of the 16
-fixed positions are precomputed (fixed_predictor_rotary.py).
+fixed positions are precomputed (fixed_predictor_rotary.py). With the packed
+weights of ``pack_decoder`` a step i >= 1 gathers its input row from the
+pre-projected codebook table (proj and bias applied once at load), runs q/k
+norm, RoPE and the K/V write inside the attention kernel, and the final
+RMSNorm is folded into the codebook heads.
 """
 from __future__ import annotations
 
@@ -63,34 +67,63 @@ class PredictorStep:
         need = ops.decode_attention_workspace_bytes(2 * B, cfg.q_heads, cfg.head_dim, positions)
         self.ws_attn = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
         self.status = ops.status_word(dev)
+        self.prefetch_weights = True  # GEMMs pull the next GEMM's weights into L2
         self.graph = None
 
-    def _layers(self, rows: int, length: int, positions: torch.Tensor) -> None:
+    def _layers(self, rows: int, length: int, positions: torch.Tensor, tail=None) -> None:
+        """The decoder layers on x[:rows]; `tail` is the weight used after them (L2 prefetch target)."""
         cfg, lw = self.cfg, ops.linear
         x = self.x[:rows]
         L = cfg.layers
-        for i, layer in enumerate(self.w["layers"]):
+        layers = self.w["layers"]
+        # each GEMM pulls the next GEMM's weights into L2 while it runs
+        pf = (lambda t: t) if self.prefetch_weights else (lambda t: None)
+        for i, layer in enumerate(layers):
             keys, values = self.cache[i], self.cache[L + i]
+            following = layers[i + 1].qkv if i + 1 < L else tail
             if layer.folded:
-                lw(x, layer.qkv, out=self.qkv[:rows], row_norm_eps=cfg.eps)
+                lw(x, layer.qkv, out=self.qkv[:rows], row_norm_eps=cfg.eps, prefetch=pf(layer.o))
             else:
                 ops.rms_norm(x, layer.input_norm, cfg.eps, out=self.xn[:rows])
-                lw(self.xn[:rows], layer.qkv, out=self.qkv[:rows], workspace=self.ws_linear)
-            ops.qk_norm_rope_kv(self.qkv[:rows], layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin, positions,
-                                positions, keys, values, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads,
-                                head_dim=cfg.head_dim, length=length, query_out=self.q[:rows])
-            ops.decode_attention(self.q[:rows], keys, values, positions, context=keys.shape[2], rows_per_slot=length,
-                                 out=self.attn[:rows], workspace=self.ws_attn)
+                lw(self.xn[:rows], layer.qkv, out=self.qkv[:rows], workspace=self.ws_linear, prefetch=pf(layer.o))
+            if length == 1:
+                # one query row per slot: q/k norm, RoPE and the K/V write run inside attention
+                ops.decode_attention_qkv(self.qkv[:rows], layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin,
+                                         positions, keys, values, positions, q_heads=cfg.q_heads,
+                                         kv_heads=cfg.kv_heads, head_dim=cfg.head_dim, context=keys.shape[2],
+                                         out=self.attn[:rows], workspace=self.ws_attn)
+            else:
+                ops.qk_norm_rope_kv(self.qkv[:rows], layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin,
+                                    positions, positions, keys, values, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads,
+                                    head_dim=cfg.head_dim, length=length, query_out=self.q[:rows])
+                ops.decode_attention(self.q[:rows], keys, values, positions, context=keys.shape[2],
+                                     rows_per_slot=length, out=self.attn[:rows], workspace=self.ws_attn)
             lw(self.attn[:rows].view(rows, cfg.q_width), layer.o, out=x, epilogue=_lib.EPI_RESIDUAL, residual=x,
-               workspace=self.ws_linear)
+               workspace=self.ws_linear, prefetch=pf(layer.gate_up))
             if layer.folded:
-                lw(x, layer.gate_up, out=self.act[:rows], epilogue=_lib.EPI_SWIGLU_PAIRED, row_norm_eps=cfg.eps)
+                lw(x, layer.gate_up, out=self.act[:rows], epilogue=_lib.EPI_SWIGLU_PAIRED, row_norm_eps=cfg.eps,
+                   prefetch=pf(layer.down))
             else:
                 ops.rms_norm(x, layer.post_norm, cfg.eps, out=self.xn[:rows])
                 lw(self.xn[:rows], layer.gate_up, out=self.act[:rows], epilogue=_lib.EPI_SWIGLU_PAIRED,
-                   workspace=self.ws_linear)
-            lw(self.act[:rows], layer.down, out=x, epilogue=_lib.EPI_RESIDUAL, residual=x, workspace=self.ws_linear)
-        ops.rms_norm(x, self.w["norm"], cfg.eps, out=self.xn[:rows])
+                   workspace=self.ws_linear, prefetch=pf(layer.down))
+            lw(self.act[:rows], layer.down, out=x, epilogue=_lib.EPI_RESIDUAL, residual=x, workspace=self.ws_linear,
+               prefetch=pf(following) if following is not None else None)
+        if not self.w.get("heads_folded", False):
+            ops.rms_norm(x, self.w["norm"], self.cfg.eps, out=self.xn[:rows])
+
+    def _head(self, step: int, last: slice) -> None:
+        """Codebook head `step` on the last decoder row of every slot (`last` picks those rows of
+        x / xn). With folded heads the final RMSNorm weight is inside the head matrix and the GEMM
+        applies the row RMS to the raw residual rows itself."""
+        w = self.w
+        following = w["layers"][0].qkv if self.prefetch_weights and step + 1 < self.cfg.groups else None
+        if w.get("heads_folded", False):
+            ops.linear(self.x[last], w["heads"][step], out=self._logits(step), out_dtype=torch.float32,
+                       row_norm_eps=self.cfg.eps, prefetch=following)
+        else:
+            ops.linear(self.xn[last], w["heads"][step], out=self._logits(step), out_dtype=torch.float32,
+                       workspace=self.ws_linear, prefetch=following)
 
     def _logits(self, step: int) -> torch.Tensor:
         return self.logits if self.step_logits is None else self.step_logits[step]
@@ -108,15 +141,18 @@ class PredictorStep:
     def compute(self) -> None:
         cfg, w, B, lw = self.cfg, self.w, self.batch, ops.linear
         lw(self.inputs.view(2 * B, cfg.talker_hidden), w["proj"], w["proj_bias"], out=self.x, workspace=self.ws_linear)
-        self._layers(2 * B, 2, self.pos0)
-        last = self.xn.view(B, 2, cfg.hidden)[:, 1]
-        lw(last, w["heads"][0], out=self._logits(0), out_dtype=torch.float32, workspace=self.ws_linear)
+        self._layers(2 * B, 2, self.pos0, tail=w["heads"][0])
+        self._head(0, slice(1, 2 * B, 2))  # second row of every slot
         self._sample(0)
+        tables = w.get("proj_tables")
         for step in range(1, cfg.groups):
-            ops.embedding(self.codes[:, step], w["embeddings"][step - 1], out=self.e)
-            lw(self.e, w["proj"], w["proj_bias"], out=self.x[:B], workspace=self.ws_linear)
-            self._layers(B, 1, self.pos[step - 1])
-            lw(self.xn[:B], w["heads"][step], out=self._logits(step), out_dtype=torch.float32, workspace=self.ws_linear)
+            if tables is not None:  # projected row of codebook table step-1 (proj and bias applied at load)
+                ops.embedding(self.codes[:, step], tables[step - 1], out=self.x[:B])
+            else:
+                ops.embedding(self.codes[:, step], w["embeddings"][step - 1], out=self.e)
+                lw(self.e, w["proj"], w["proj_bias"], out=self.x[:B], workspace=self.ws_linear)
+            self._layers(B, 1, self.pos[step - 1], tail=w["heads"][step])
+            self._head(step, slice(0, B))
             self._sample(step)
         ops.frame_embed(self.codes, self.talker_embedding, w["embeddings"], self.text, out=self.embeds)
 

@@ -83,6 +83,7 @@ class TalkerStep:
         self.cos, self.sin = cos, sin
         self.norm_mode = norm_mode
         self.fused_attention = fused_attention   # q/k norm, RoPE and KV write inside the attention kernel
+        self.prefetch_weights = True             # GEMMs pull the next GEMM's weights into L2
         dev = arena.device
         B, H = batch, cfg.hidden
         self.inputs = torch.zeros(B, H, dtype=BF16, device=dev)
@@ -110,12 +111,16 @@ class TalkerStep:
         cfg, w, B = self.cfg, self.w, self.batch
         lw = ops.linear
         res_in = self.inputs
-        for i, layer in enumerate(w["layers"]):
+        layers = w["layers"]
+        # each GEMM pulls the next GEMM's weights into L2 while it runs
+        pf = (lambda t: t) if self.prefetch_weights else (lambda t: None)
+        for i, layer in enumerate(layers):
+            following = layers[i + 1].qkv if i + 1 < len(layers) else w["head"]
             if layer.folded:
-                lw(res_in, layer.qkv, out=self.qkv, row_norm_eps=cfg.eps)
+                lw(res_in, layer.qkv, out=self.qkv, row_norm_eps=cfg.eps, prefetch=pf(layer.o))
             else:
                 ops.rms_norm(res_in, layer.input_norm, cfg.eps, self.norm_mode, out=self.xn)
-                lw(self.xn, layer.qkv, out=self.qkv, workspace=self.ws_linear)
+                lw(self.xn, layer.qkv, out=self.qkv, workspace=self.ws_linear, prefetch=pf(layer.o))
             if self.fused_attention:
                 ops.decode_attention_qkv(self.qkv, layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin,
                                          self.rotary, self.arena.keys[i], self.arena.values[i], self.positions,
@@ -128,14 +133,16 @@ class TalkerStep:
                 ops.decode_attention(self.q, self.arena.keys[i], self.arena.values[i], self.positions,
                                      context=self.context, out=self.attn, workspace=self.ws_attn)
             lw(self.attn.view(B, cfg.q_width), layer.o, out=self.h, epilogue=_lib.EPI_RESIDUAL, residual=res_in,
-               workspace=self.ws_linear)
+               workspace=self.ws_linear, prefetch=pf(layer.gate_up))
             if layer.folded:
-                lw(self.h, layer.gate_up, out=self.act, epilogue=_lib.EPI_SWIGLU_PAIRED, row_norm_eps=cfg.eps)
+                lw(self.h, layer.gate_up, out=self.act, epilogue=_lib.EPI_SWIGLU_PAIRED, row_norm_eps=cfg.eps,
+                   prefetch=pf(layer.down))
             else:
                 ops.rms_norm(self.h, layer.post_norm, cfg.eps, self.norm_mode, out=self.xn)
-                lw(self.xn, layer.gate_up, out=self.act, epilogue=_lib.EPI_SWIGLU_PAIRED, workspace=self.ws_linear)
+                lw(self.xn, layer.gate_up, out=self.act, epilogue=_lib.EPI_SWIGLU_PAIRED, workspace=self.ws_linear,
+                   prefetch=pf(layer.down))
             lw(self.act, layer.down, out=self.h, epilogue=_lib.EPI_RESIDUAL, residual=self.h,
-               workspace=self.ws_linear)
+               workspace=self.ws_linear, prefetch=pf(following))
             res_in = self.h
         ops.rms_norm(res_in, w["norm"], cfg.eps, self.norm_mode, out=self.hidden)
         lw(self.hidden, w["head"], out=self.logits, workspace=self.ws_linear)

@@ -137,5 +137,13 @@ def pack_decoder(weights: dict, device, tiled: bool = True, fold_norms: bool = T
     if "proj" in weights:
         packed["proj"] = mat(weights["proj"])
     if "heads" in weights:
-        packed["heads"] = [mat(h) for h in weights["heads"]]
+        # the predictor's final norm feeds only the codebook heads: fold it into them too
+        packed["heads"] = [mat(maybe_fold(h, weights["norm"])) for h in weights["heads"]]
+        packed["heads_folded"] = fold_norms
+    if "proj" in weights and "embeddings" in weights:
+        # Step i >= 1 of the predictor projects one row of codebook table i-1: project
+        # every row once here, so that the step gathers the projected row instead.
+        packed["proj_tables"] = torch.stack([
+            ops.linear(packed["embeddings"][g], packed["proj"], packed["proj_bias"])
+            for g in range(packed["embeddings"].shape[0])]).contiguous()
     return packed

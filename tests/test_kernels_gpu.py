@@ -244,6 +244,29 @@ def test_linear_fp32_bias_residual_and_strided_input(ops, cuda):
     torch.testing.assert_close(out.cpu().float(), ref.float(), atol=1e-2, rtol=1e-2)
 
 
+@pytest.mark.parametrize("rows,k,n", [(32, 1024, 4096), (5000, 192, 192), (7680, 96, 96)])
+def test_linear_inplace_residual_and_l2_prefetch(ops, cuda, rows, k, n):
+    """In-place residual epilogue (out aliases the residual, as the codec's residual units and the
+    decoder's O/down projections run it) against the fp32 reference, and q3t_linear_prefetch
+    (next weights pulled into L2) bit-identical to the plain GEMM, with and without the row norm."""
+    from qwen3_tts_b200 import _lib
+    x = rnd(60 + rows, (rows, k), 1.0, BF16)
+    w = rnd(61, (n, k), 0.02, BF16)
+    res = rnd(62, (rows, n), 1.0, BF16)
+    ref = (res.float() + torch_linear(x, w).to(BF16).float()).to(BF16)
+    xd, wd, nxt = x.to(cuda), ops.pack_tiles(w.to(cuda)), ops.pack_tiles(rnd(63, (2048, 1024), 0.02, BF16).to(cuda))
+    y = res.to(cuda)
+    ops.linear(xd, wd, out=y, epilogue=_lib.EPI_RESIDUAL, residual=y)
+    torch.testing.assert_close(y.cpu().float(), ref.float(), atol=2e-2, rtol=1e-2)
+    y2 = res.to(cuda)
+    ops.linear(xd, wd, out=y2, epilogue=_lib.EPI_RESIDUAL, residual=y2, prefetch=nxt)
+    assert torch.equal(y, y2)
+    a = ops.linear(xd, wd, out_dtype=torch.float32, row_norm_eps=1e-6)
+    b = ops.linear(xd, wd, out_dtype=torch.float32, row_norm_eps=1e-6, prefetch=nxt)
+    assert torch.equal(a, b)
+    assert_status_clean(ops, cuda)
+
+
 @pytest.mark.parametrize("rows", [1, 32, 64, 130])
 def test_linear_paired_swiglu(ops, cuda, rows):
     from qwen3_tts_b200 import _lib
