@@ -49,7 +49,9 @@ enum {
                                out[:, f] = bf16(bf16(silu(gate_f)) * up_f) */
   Q3T_EPI_RESIDUAL_SCALED = 3,/* out = bf16(residual + bf16(scale[n] * bf16(acc + bias))) */
   Q3T_EPI_GELU = 4,         /* out = bf16(gelu_erf(bf16(acc + bias))) */
-  Q3T_EPI_SILU = 5          /* out = bf16(silu(bf16(acc + bias))) - text_projection fc1 + act */
+  Q3T_EPI_SILU = 5,         /* out = bf16(silu(bf16(acc + bias))) - text_projection fc1 + act */
+  Q3T_EPI_SNAKE = 6         /* out = snake_bf16(bf16(acc + bias), alpha[n], inverse_beta[n]): the SnakeBeta
+                               of the codec's next conv (q3t_conv_linear only) */
 };
 
 /* RMSNorm rounding modes. */
@@ -349,6 +351,28 @@ int q3t_conv_gather(const void* x, int64_t x_stride, int64_t batch, int64_t fram
                     int64_t channels, const void* history, int64_t history_len,
                     const int64_t* slots, int64_t taps, int64_t dilation, int reverse,
                     const float* alpha, const float* inverse_beta, void* col, void* stream);
+
+/* Padded input of an implicit causal conv (the history concat of
+ * incremental_codec.py:53-65 and the preceding SnakeBeta, without im2col):
+ * xs[b, p, c] = snake([history[slots[b]] | x[b]][p, c]) for p < history_len + frames,
+ * as bf16 [batch, history_len + frames, channels]; alpha/inverse_beta nullable (identity). */
+int q3t_conv_pad(const void* x, int64_t x_stride, int64_t batch, int64_t frames, int64_t channels,
+                 const void* history, int64_t history_len, const int64_t* slots, const float* alpha,
+                 const float* inverse_beta, void* xs, void* stream);
+
+/* Causal conv (kernel `taps`, `dilation`) as an implicit tcgen05 GEMM over q3t_conv_pad's
+ * buffer xs [batch, pad + frames, channels]: k-block (tap j, 64 channels) streams frames
+ * t + j*dilation (or t + (taps-1-j)*dilation with reverse: transposed convs' [x[t] | x[t-1]])
+ * of its stream straight from xs through a 3-D TMA map, so no im2col copy is written.
+ *   out[b*frames + t, n] = epilogue(sum_{j,c} W[n, j*Cp + c] * xs[b, t + shift_j, c] (+ bias[n]))
+ * weight_tiles: q3t_pack_weight_tiles of W [out_features, taps*Cp], channels zero-padded per
+ * tap to Cp = 64 * ceil(channels / 64). Epilogues STORE, RESIDUAL(_SCALED), GELU, SILU and
+ * SNAKE (alpha / inverse_beta fp32 [out_features]); bf16 output. pad >= (taps-1)*dilation. */
+int q3t_conv_linear(const void* xs, int64_t batch, int64_t frames, int64_t pad, int64_t channels,
+                    int64_t taps, int64_t dilation, int reverse, const void* weight_tiles,
+                    int64_t out_features, const void* bias, void* out, int64_t out_stride, int epilogue,
+                    const void* residual, int64_t residual_stride, const void* scale,
+                    const float* snake_alpha, const float* snake_inv, unsigned* status, void* stream);
 
 /* history = last history_len frames of [history | x] per slot (incremental_codec.py:62). */
 int q3t_conv_history(const void* x, int64_t x_stride, int64_t batch, int64_t frames,

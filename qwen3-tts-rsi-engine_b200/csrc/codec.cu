@@ -23,15 +23,6 @@ int grid_for(int64_t total, int threads) {
   return int(blocks < 1 ? 1 : (blocks > cap ? cap : blocks));
 }
 
-// bf16 SnakeBeta with rounding after every op (snake_triton_ascend.py:20-24).
-Q3T_DEV float snake_bf16(float x, float a, float inv) {
-  const float phase = bf16r(x * a);
-  const float sine = bf16r(sinf(phase));
-  const float square = bf16r(sine * sine);
-  const float scaled = bf16r(inv * square);
-  return bf16r(x + scaled);
-}
-
 // ------------------------------------------------------------------ RVQ (cached_quantizer.py:17-30)
 // out[row] = [ sum_{q < semantic} table_q[code_q] | sum_{q >= semantic} table_q[code_q] ]
 // (fp32 sums in codebook order, one rounding each); the caller applies
@@ -104,12 +95,62 @@ __global__ void conv_gather_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
   }
 }
 
-// new history = last H frames of [old history | x]; one thread per (stream, 8 channels),
-// ascending frame order so the in-place shift reads before it overwrites.
+// Padded input of an implicit causal conv (q3t_conv_linear):
+// xs[b, p, c] = f(seq_b[p]), seq_b = [history[slot_b] (H frames) | x[b*T .. b*T + T)],
+// f = SnakeBeta (alpha != null) or identity; one thread per (row, 8 channels).
+__global__ void conv_pad_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int T, int C,
+                                const __nv_bfloat16* __restrict__ hist, int H, const int64_t* __restrict__ slots,
+                                const float* __restrict__ alpha, const float* __restrict__ inv,
+                                __nv_bfloat16* __restrict__ xs, int64_t rows) {
+  grid_dependency_wait();
+  const int cv = C / 8;
+  const int64_t total = rows * cv;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int c = int(i % cv) * 8;
+    const int64_t row = i / cv;
+    const int64_t b = row / (H + T);
+    const int p = int(row % (H + T));
+    uint4 raw;
+    if (p >= H) {
+      raw = *reinterpret_cast<const uint4*>(x + (b * T + (p - H)) * x_stride + c);
+    } else if (hist != nullptr) {
+      const int64_t slot = slots ? slots[b] : b;
+      raw = *reinterpret_cast<const uint4*>(hist + (slot * H + p) * int64_t(C) + c);
+    } else {
+      raw = make_uint4(0, 0, 0, 0);
+    }
+    if (alpha != nullptr) {
+      float f[8];
+      unpack8(raw, f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) f[k] = snake_bf16(f[k], alpha[c + k], inv[c + k]);
+      raw = pack8(f);
+    }
+    *reinterpret_cast<uint4*>(xs + row * int64_t(C) + c) = raw;
+  }
+}
+
+// new history = last H frames of [old history | x]. With T >= H every new frame comes from
+// x: one thread per (stream, frame, 8 channels). Otherwise one thread per (stream, 8 channels)
+// walks the frames in ascending order, so the in-place shift reads before it overwrites.
 __global__ void conv_history_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride, int B, int T, int C,
                                     __nv_bfloat16* __restrict__ hist, int H, const int64_t* __restrict__ slots) {
   grid_dependency_wait();
   const int cv = C / 8;
+  if (T >= H) {
+    const int64_t total = int64_t(B) * H * cv;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total;
+         i += int64_t(gridDim.x) * blockDim.x) {
+      const int c = int(i % cv) * 8;
+      const int64_t bk = i / cv;
+      const int64_t b = bk / H;
+      const int k = int(bk % H);
+      const int64_t slot = slots ? slots[b] : b;
+      *reinterpret_cast<uint4*>(hist + (slot * H + k) * int64_t(C) + c) =
+          *reinterpret_cast<const uint4*>(x + (b * T + (T - H + k)) * x_stride + c);
+    }
+    return;
+  }
   const int64_t total = int64_t(B) * cv;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
     const int64_t b = i / cv;
@@ -252,11 +293,27 @@ extern "C" int q3t_conv_gather(const void* x, int64_t x_stride, int64_t batch, i
                 reverse, alpha, inverse_beta, static_cast<__nv_bfloat16*>(col), rows);
 }
 
+extern "C" int q3t_conv_pad(const void* x, int64_t x_stride, int64_t batch, int64_t frames, int64_t channels,
+                            const void* history, int64_t history_len, const int64_t* slots, const float* alpha,
+                            const float* inverse_beta, void* xs, void* stream) {
+  if (!x || !xs || batch < 1 || frames < 1 || channels < 8 || channels % 8 || x_stride % 8 || x_stride < channels ||
+      history_len < 0 || ((alpha == nullptr) != (inverse_beta == nullptr)))
+    return fail(Q3T_EINVAL, "conv_pad: invalid arguments");
+  if (!aligned16(x) || !aligned16(xs) || (history && !aligned16(history)))
+    return fail(Q3T_EINVAL, "conv_pad: 16-byte alignment");
+  const int64_t rows = batch * (history_len + frames);
+  return launch(conv_pad_kernel, dim3(grid_for(rows * (channels / 8), 256)), dim3(256), 0, stream, true, "conv_pad",
+                static_cast<const __nv_bfloat16*>(x), x_stride, int(frames), int(channels),
+                static_cast<const __nv_bfloat16*>(history), int(history_len), slots, alpha, inverse_beta,
+                static_cast<__nv_bfloat16*>(xs), rows);
+}
+
 extern "C" int q3t_conv_history(const void* x, int64_t x_stride, int64_t batch, int64_t frames, int64_t channels,
                                 void* history, int64_t history_len, const int64_t* slots, void* stream) {
   if (!x || !history || batch < 1 || frames < 1 || channels < 8 || channels % 8 || history_len < 1 || x_stride % 8)
     return fail(Q3T_EINVAL, "conv_history: invalid arguments");
-  return launch(conv_history_kernel, dim3(grid_for(batch * (channels / 8), 128)), dim3(128), 0, stream, true,
+  const int64_t work = frames >= history_len ? batch * history_len * (channels / 8) : batch * (channels / 8);
+  return launch(conv_history_kernel, dim3(grid_for(work, 128)), dim3(128), 0, stream, true,
                 "conv_history", static_cast<const __nv_bfloat16*>(x), x_stride, int(batch), int(frames),
                 int(channels), static_cast<__nv_bfloat16*>(history), int(history_len), slots);
 }

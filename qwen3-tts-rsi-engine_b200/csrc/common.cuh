@@ -21,6 +21,14 @@ namespace q3t {
 
 // ---------------------------------------------------------------- numerics
 Q3T_DEV float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+// bf16 SnakeBeta x + inv * sin(a * x)^2 with rounding after every op (snake_triton_ascend.py:20-24).
+Q3T_DEV float snake_bf16(float x, float a, float inv) {
+  const float phase = bf16r(x * a);
+  const float sine = bf16r(sinf(phase));
+  const float square = bf16r(sine * sine);
+  const float scaled = bf16r(inv * square);
+  return bf16r(x + scaled);
+}
 Q3T_DEV float ld_bf16(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
 // Unpack 8 bf16 (one 16-byte vector) to fp32.
@@ -140,6 +148,32 @@ Q3T_DEV void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, 
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
+// 3-D tiled tensor load; the same alignment rule for x.
+Q3T_DEV void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
+                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+// Tiled tensor stores from shared memory (bulk-group completion); the coordinates are
+// non-negative and x * element size is a multiple of 16 bytes. Out-of-range parts are clipped.
+Q3T_DEV void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(smem_u32(smem_src))
+               : "memory");
+}
+Q3T_DEV void tma_store_3d(const CUtensorMap* map, const void* smem_src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z), "r"(smem_u32(smem_src))
+               : "memory");
+}
+Q3T_DEV void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until every committed bulk store has finished READING its shared-memory source.
+Q3T_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // L2 prefetch hint for a global range (16-byte aligned address, bytes % 16 == 0); no completion.
 Q3T_DEV void prefetch_l2(const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)

@@ -67,6 +67,18 @@ struct GemmArgs {
   // split evenly over this grid's CTAs and requested at kernel start
   const uint8_t* prefetch;
   uint64_t prefetch_bytes;
+  // Implicit causal convolution (conv_taps > 0): the activations are a padded buffer
+  // [batch, pad + frames, channels] (3-D tensor map); k-block kb covers tap j = kb / conv_cblocks,
+  // channels (kb % conv_cblocks) * 64 + [0, 64), and reads frames t + shift(j) of the stream, with
+  // shift(j) = j * dilation, or (taps - 1 - j) * dilation when conv_reverse. The m-tiles of a stream
+  // (conv_tiles of them) cover its frames; output row = stream * conv_frames + frame.
+  int conv_taps, conv_dil, conv_reverse, conv_cblocks, conv_frames, conv_tiles;
+  const float* snake_alpha;  // per-feature SnakeBeta parameters of Q3T_EPI_SNAKE
+  const float* snake_inv;
+  // Staged epilogue (one-CTA tiles, bf16 output): the residual tile arrives by one TMA load
+  // (tmr) and the finished [BN x 128] tile leaves by one TMA store (tmo), both through the
+  // idle ring; 3-D maps {features, frames, streams} in conv mode, so stores clip per stream.
+  int tma_out;
   unsigned* status;
 };
 
@@ -90,6 +102,8 @@ __device__ __forceinline__ float epilogue_value(float acc, float r, float g) {
   } else if constexpr (EPI == Q3T_EPI_SILU) {
     const float v = bf16r(acc);
     return v / (1.0f + expf(-v));
+  } else if constexpr (EPI == Q3T_EPI_SNAKE) {  // r = alpha[n], g = 1 / beta[n]
+    return snake_bf16(bf16r(acc), r, g);
   } else {
     return acc;
   }
@@ -107,20 +121,23 @@ __device__ __forceinline__ void store_value(const GemmArgs& a, int m, int n, flo
 // are loaded before the first store: the residual may alias the output, and
 // interleaved load/store pairs would serialise one memory round trip per element.
 template <int EPI>
-__device__ __forceinline__ void store_rows16(const GemmArgs& a, int m_first, int n, const float* v,
+__device__ __forceinline__ void store_rows16(const GemmArgs& a, int m_first, int m_end, int n, const float* v,
                                              const float* rscale) {
   const bool hb = a.bias != nullptr;
   const float bias = hb ? __bfloat162float(a.bias[n]) : 0.f;
-  const float g = EPI == Q3T_EPI_RESIDUAL_SCALED ? __bfloat162float(a.scale[n]) : 0.f;
+  const float g = EPI == Q3T_EPI_RESIDUAL_SCALED ? __bfloat162float(a.scale[n])
+                  : EPI == Q3T_EPI_SNAKE         ? a.snake_inv[n]
+                                                 : 0.f;
+  const float alpha = EPI == Q3T_EPI_SNAKE ? a.snake_alpha[n] : 0.f;
   float r[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j)
-    r[j] = (has_residual(EPI) && m_first + j < a.rows)
+    r[j] = (has_residual(EPI) && m_first + j < m_end)
                ? __bfloat162float(a.residual[int64_t(m_first + j) * a.res_stride + n])
-               : 0.f;
+               : alpha;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    if (m_first + j >= a.rows) break;
+    if (m_first + j >= m_end) break;
     float acc = rscale != nullptr ? v[j] * rscale[j] : v[j];
     if (hb) acc += bias;
     store_value<EPI>(a, m_first + j, n, epilogue_value<EPI>(acc, r[j], g));
@@ -142,6 +159,10 @@ __device__ __forceinline__ Inputs4 load_inputs4(const GemmArgs& a, int m, int n_
                                           : 0.f;
     in.bias[j] = (a.bias != nullptr && live) ? __bfloat162float(a.bias[n_first + j]) : 0.f;
     in.g[j] = (EPI == Q3T_EPI_RESIDUAL_SCALED && live) ? __bfloat162float(a.scale[n_first + j]) : 0.f;
+    if (EPI == Q3T_EPI_SNAKE && live) {
+      in.r[j] = a.snake_alpha[n_first + j];
+      in.g[j] = a.snake_inv[n_first + j];
+    }
   }
   return in;
 }
@@ -207,7 +228,8 @@ Q3T_DEV float4 ld_peer4(uint32_t addr) {
 // epilogue.
 template <int BN, int EPI>
 __global__ void __launch_bounds__(128, 1)
-    linear_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx, GemmArgs a) {
+    linear_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
+                  const __grid_constant__ CUtensorMap tmo, const __grid_constant__ CUtensorMap tmr, GemmArgs a) {
   using C = Cfg<BN>;
   constexpr int S = C::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -215,7 +237,8 @@ __global__ void __launch_bounds__(128, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kMain);
   uint64_t* empty = full + S;
   uint64_t* done = empty + S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* epi_bar = done + 1;  // residual tile of the staged epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* consumed = abort_flag + 1;  // ring slots the MMA issuer has taken
   float* red = reinterpret_cast<float*>(smem);
@@ -224,7 +247,13 @@ __global__ void __launch_bounds__(128, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kTileN;
   const int split = blockIdx.y;
-  const int m0 = blockIdx.z * BN;
+  // activation tile: rows [m0, m0 + BN) of a plain GEMM, or frames [t0, t0 + BN) of stream
+  // conv_b of an implicit conv; output rows below m_end exist
+  const int conv_b = a.conv_taps ? int(blockIdx.z) / a.conv_tiles : 0;
+  const int t0 = a.conv_taps ? (int(blockIdx.z) % a.conv_tiles) * BN : 0;
+  const int m0 = a.conv_taps ? conv_b * a.conv_frames + t0 : int(blockIdx.z) * BN;
+  const int m_end = a.conv_taps ? conv_b * a.conv_frames + (a.conv_frames < t0 + BN ? a.conv_frames : t0 + BN)
+                                : a.rows;
   const int kb0 = int(int64_t(split) * a.kblocks / a.splits);
   const int kb1 = int(int64_t(split + 1) * a.kblocks / a.splits);
   const int nk = kb1 - kb0;
@@ -237,11 +266,16 @@ __global__ void __launch_bounds__(128, 1)
       mbar_init(&empty[s], a.row_norm ? 3 : 1);
     }
     mbar_init(done, 1);
+    mbar_init(epi_bar, 1);
     *abort_flag = 0;
     *consumed = 0;
     fence_mbar_init();
     if (a.tiles == nullptr) prefetch_tmap(&tmw);
     prefetch_tmap(&tmx);
+    if (a.tma_out) {
+      prefetch_tmap(&tmo);
+      if (has_residual(EPI)) prefetch_tmap(&tmr);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -269,6 +303,15 @@ __global__ void __launch_bounds__(128, 1)
       // ---------------- TMA producer: weight tiles of the first ring slots go out before the
       // dependency wait (weights never depend on the previous kernel), activations after it.
       const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
+      auto load_act = [&](uint8_t* dst, uint64_t* bar, int kb) {
+        if (a.conv_taps) {
+          const int j = kb / a.conv_cblocks, cb = kb - j * a.conv_cblocks;
+          const int shift = (a.conv_reverse ? a.conv_taps - 1 - j : j) * a.conv_dil;
+          tma_load_3d(dst, &tmx, bar, cb * kTileK, t0 + shift, conv_b, pol_x);
+        } else {
+          tma_load_2d(dst, &tmx, bar, kb * kTileK, m0, pol_x);
+        }
+      };
       const int pre = nk < S ? nk : S;
       for (int i = 0; i < pre; ++i) {
         mbar_expect_tx(&full[i], C::kStageBytes);
@@ -277,7 +320,7 @@ __global__ void __launch_bounds__(128, 1)
       issued = pre;
       grid_dependency_wait();
       for (int i = 0; i < pre; ++i)
-        tma_load_2d(smem + i * C::kStageBytes + kABytes, &tmx, &full[i], (kb0 + i) * kTileK, m0, pol_x);
+        load_act(smem + i * C::kStageBytes + kABytes, &full[i], kb0 + i);
       for (int i = pre; i < nk; ++i) {
         const int s = i % S;
         if (*abort_flag || !mbar_wait(&empty[s], ((i / S) & 1) ^ 1, a.status, kStatusMmaTimeout)) {
@@ -286,7 +329,7 @@ __global__ void __launch_bounds__(128, 1)
         }
         mbar_expect_tx(&full[s], C::kStageBytes);
         load_weights(smem + s * C::kStageBytes, &tmw, a, &full[s], kb0 + i, n0, pol_w);
-        tma_load_2d(smem + s * C::kStageBytes + kABytes, &tmx, &full[s], (kb0 + i) * kTileK, m0, pol_x);
+        load_act(smem + s * C::kStageBytes + kABytes, &full[s], kb0 + i);
         issued = i + 1;
       }
     }
@@ -368,11 +411,64 @@ __global__ void __launch_bounds__(128, 1)
         }
       __syncthreads();
     }
+    // block-uniform: every thread saw the accumulator complete and no load was abandoned
+    if (a.tma_out && __syncthreads_and(ok && !*abort_flag)) {
+      // Staged epilogue: the ring is idle (every load was consumed by the MMAs), so it holds
+      // the [BN rows x 128 features] bf16 tile; thread r owns feature n0 + r of every row.
+      __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(smem);
+      bool res_ok = true;
+      if constexpr (has_residual(EPI)) {
+        if (threadIdx.x == 0) {
+          mbar_expect_tx(epi_bar, uint32_t(BN * kTileN * 2));
+          if (a.conv_taps)
+            tma_load_3d(stage, &tmr, epi_bar, n0, t0, conv_b, policy_evict_first());
+          else
+            tma_load_2d(stage, &tmr, epi_bar, n0, m0, policy_evict_first());
+        }
+        res_ok = mbar_wait(epi_bar, 0, a.status, kStatusTmaTimeout);
+      }
+      const bool live = n < a.out_features;
+      const bool hb = a.bias != nullptr;
+      const float bias = hb && live ? __bfloat162float(a.bias[n]) : 0.f;
+      const float g = !live                             ? 0.f
+                      : EPI == Q3T_EPI_RESIDUAL_SCALED ? __bfloat162float(a.scale[n])
+                      : EPI == Q3T_EPI_SNAKE           ? a.snake_inv[n]
+                                                       : 0.f;
+      const float alpha = EPI == Q3T_EPI_SNAKE && live ? a.snake_alpha[n] : 0.f;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        float v[16];
+        tmem_ld16(taddr + c0, v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          __nv_bfloat16* slot = stage + (c0 + j) * kTileN + r;
+          const float rr = has_residual(EPI) ? __bfloat162float(*slot) : alpha;
+          float acc = a.row_norm ? v[j] * rnorm[c0 + j] : v[j];
+          if (hb) acc += bias;
+          *slot = __float2bfloat16_rn(epilogue_value<EPI>(acc, rr, g));
+        }
+      }
+      fence_async_shared();  // the tile's generic-proxy writes, before the TMA store reads them
+      tc_fence_before();
+      __syncthreads();
+      if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
+      if (threadIdx.x == 0 && res_ok) {
+        if (a.conv_taps)
+          tma_store_3d(&tmo, stage, n0, t0, conv_b);
+        else
+          tma_store_2d(&tmo, stage, n0, m0);
+        bulk_commit_group();
+        bulk_wait_read0();  // the tile must stay until the store engine has read it
+      } else if (threadIdx.x == 0 && has_residual(EPI)) {
+        mbar_wait(epi_bar, 0, a.status, kStatusTmaTimeout);  // a late residual load lands before exit
+      }
+      return;
+    }
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 16) {
       float v[16];
       tmem_ld16(taddr + c0, v);
-      if (ok && n < a.out_features) store_rows16<EPI>(a, m0 + c0, n, v, a.row_norm ? rnorm + c0 : nullptr);
+      if (ok && n < a.out_features) store_rows16<EPI>(a, m0 + c0, m_end, n, v, a.row_norm ? rnorm + c0 : nullptr);
     }
     tc_fence_before();
     __syncthreads();
@@ -408,7 +504,7 @@ __global__ void __launch_bounds__(128, 1)
   if (clustered) cluster_sync();  // every peer's tile is in its shared memory
   const int cs = a.splits;
   const uint32_t rank = clustered ? cluster_rank() : 0u;
-  const int mcount = (a.rows - m0) < BN ? (a.rows - m0) : BN;
+  const int mcount = (m_end - m0) < BN ? (m_end - m0) : BN;
   const uint32_t red_local = smem_u32(red);
   // Every peer's partial quad (and, with the folded RMSNorm, its partial sum of squares of
   // the row, kept in the padding column) is requested at once, after the unit's global
@@ -567,6 +663,21 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int
   return Q3T_OK;
 }
 
+// 3-D bf16 map over a padded conv buffer [batch, frames, channels]: box {64, box_rows, 1}, 128-byte swizzle.
+int make_map_3d(CUtensorMap* map, const void* base, int64_t batch, int64_t frames, int64_t channels, int box_rows) {
+  EncodeTiled enc = encoder();
+  if (enc == nullptr) return fail(Q3T_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {cuuint64_t(channels), cuuint64_t(frames), cuuint64_t(batch)};
+  cuuint64_t strides[2] = {cuuint64_t(channels) * 2, cuuint64_t(frames) * cuuint64_t(channels) * 2};
+  cuuint32_t box[3] = {cuuint32_t(kTileK), cuuint32_t(box_rows), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(Q3T_EINVAL, "tensor map encode failed (%d)", int(r));
+  return Q3T_OK;
+}
+
 int pick_bn(int64_t rows) {
   if (rows <= 16) return 16;
   if (rows <= 32) return 32;
@@ -579,23 +690,51 @@ struct Plan {
   int bn, n_tiles, m_tiles, kblocks, splits;
 };
 
+// Tensor maps of one launch: weights (row-major path only), activations, and the staged
+// epilogue's output and residual (zeroed when unused).
+struct Maps {
+  CUtensorMap w, x, o, r;
+};
 
-Plan plan(int64_t rows, int64_t in_features, int64_t out_features) {
-  Plan p;
-  p.bn = pick_bn(rows);
-  p.n_tiles = int((out_features + kTileN - 1) / kTileN);
-  p.m_tiles = int((rows + p.bn - 1) / p.bn);
-  p.kblocks = int((in_features + kTileK - 1) / kTileK);
-  // K splits: a power of two <= 8 (one thread-block cluster per tile), each
-  // split at least four k-blocks, at most ~1.33 CTAs per SM in total. (Measured
-  // in dependent launch chains of the decode GEMMs at 32 and 64 rows: splits of
-  // 2-3 k-blocks, or grids beyond ~200 CTAs, ran 5-50% slower than this rule's
-  // pick for every talker and predictor projection but one, within 5%; 16-CTA
-  // and 3- or 9-CTA clusters ran 1.6-2x slower.)
+// Maps of the staged epilogue: out (and the residual) as bf16 {features, rows} (frames == 0) or
+// {features, frames, streams} maps with a {128, bn} box, no swizzle. False = not eligible
+// (alignment, stride or encode), and the kernel then stores element by element.
+bool staged_maps(Maps& m, int bn, int64_t out_features, const void* out, int64_t out_stride, const void* residual,
+                 int64_t res_stride, int64_t rows, int64_t batch, int64_t frames) {
+  EncodeTiled enc = encoder();
+  if (enc == nullptr) return false;
+  auto make = [&](CUtensorMap* map, const void* base, int64_t stride) -> bool {
+    if (!aligned16(base) || stride % 8 || stride < out_features) return false;
+    cuuint64_t dims[3] = {cuuint64_t(out_features), cuuint64_t(frames ? frames : rows), cuuint64_t(batch)};
+    cuuint64_t strides[2] = {cuuint64_t(stride) * 2, cuuint64_t(frames) * cuuint64_t(stride) * 2};
+    cuuint32_t box[3] = {cuuint32_t(kTileN), cuuint32_t(bn), 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, frames ? 3 : 2, const_cast<void*>(base), dims, strides, box,
+               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  };
+  if (!make(&m.o, out, out_stride)) return false;
+  if (residual != nullptr && !make(&m.r, residual, res_stride)) return false;
+  return true;
+}
+
+
+// K splits: a power of two <= 8 (one thread-block cluster per tile), at most
+// ~1.33 CTAs per SM in total, each split at least two k-blocks, and at least
+// four once the grid exceeds 64 CTAs. (Measured in dependent launch chains of
+// the talker, predictor and codec projections at 8-128 rows: this pick was the
+// fastest split or within 5% of it for every shape; grids beyond ~200 CTAs, or
+// 2-k-block splits on grids of 128+, ran 10-50% slower; 16-CTA and 3- or 9-CTA
+// clusters ran 1.6-2x slower.)
+void choose_splits(Plan& p) {
   const int base = p.n_tiles * p.m_tiles;
   const int target = sm_count() + sm_count() / 3;
   int splits = 1;
-  while (splits < 8 && base * splits * 2 <= target && p.kblocks >= 4 * splits * 2) splits *= 2;
+  while (splits < 8) {
+    const int next = splits * 2, ctas = base * next, per_split = p.kblocks / next;
+    if (ctas > target || per_split < 2 || (ctas > 64 && per_split < 4)) break;
+    splits = next;
+  }
 #ifdef Q3T_TUNING
   // tuning builds only: force the split count (a power of two <= 8, >= 2 k-blocks per split)
   if (const char* forced = getenv("Q3T_SPLITS")) {
@@ -604,11 +743,20 @@ Plan plan(int64_t rows, int64_t in_features, int64_t out_features) {
   }
 #endif
   p.splits = splits;
+}
+
+Plan plan(int64_t rows, int64_t in_features, int64_t out_features) {
+  Plan p;
+  p.bn = pick_bn(rows);
+  p.n_tiles = int((out_features + kTileN - 1) / kTileN);
+  p.m_tiles = int((rows + p.bn - 1) / p.bn);
+  p.kblocks = int((in_features + kTileK - 1) / kTileK);
+  choose_splits(p);
   return p;
 }
 
 template <int BN, int EPI>
-int launch_linear(const Plan& p, const CUtensorMap& tmw, const CUtensorMap& tmx, const GemmArgs& args, void* stream) {
+int launch_linear(const Plan& p, const Maps& m, const GemmArgs& args, void* stream) {
   using C = Cfg<BN>;
   static bool configured[64] = {false};
   int dev = 0;
@@ -633,20 +781,20 @@ int launch_linear(const Plan& p, const CUtensorMap& tmw, const CUtensorMap& tmx,
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, linear_kernel<BN, EPI>, tmw, tmx, args);
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, linear_kernel<BN, EPI>, m.w, m.x, m.o, m.r, args);
   if (err != cudaSuccess) return fail(Q3T_ECUDA, "linear launch failed: %s", cudaGetErrorString(err));
   note_launch();
   return Q3T_OK;
 }
 
 template <int EPI>
-int dispatch_bn(const Plan& p, const CUtensorMap& tmw, const CUtensorMap& tmx, const GemmArgs& args, void* stream) {
+int dispatch_bn(const Plan& p, const Maps& m, const GemmArgs& args, void* stream) {
   switch (p.bn) {
-    case 16: return launch_linear<16, EPI>(p, tmw, tmx, args, stream);
-    case 32: return launch_linear<32, EPI>(p, tmw, tmx, args, stream);
-    case 64: return launch_linear<64, EPI>(p, tmw, tmx, args, stream);
-    case 128: return launch_linear<128, EPI>(p, tmw, tmx, args, stream);
-    default: return launch_linear<256, EPI>(p, tmw, tmx, args, stream);
+    case 16: return launch_linear<16, EPI>(p, m, args, stream);
+    case 32: return launch_linear<32, EPI>(p, m, args, stream);
+    case 64: return launch_linear<64, EPI>(p, m, args, stream);
+    case 128: return launch_linear<128, EPI>(p, m, args, stream);
+    default: return launch_linear<256, EPI>(p, m, args, stream);
   }
 }
 
@@ -708,19 +856,19 @@ int linear_impl(const void* x, int64_t x_stride, int64_t rows, int64_t in_featur
     return fail(Q3T_EINVAL, "linear: GELU/SiLU epilogues are bf16");
   if (epilogue == Q3T_EPI_SWIGLU_PAIRED && (out_features % kTileN || out_dtype != Q3T_BF16 || bias != nullptr))
     return fail(Q3T_EINVAL, "linear: paired SwiGLU needs out_features %% 128 == 0, bf16 output, no bias");
-  if (epilogue < Q3T_EPI_STORE || epilogue > Q3T_EPI_SILU) return fail(Q3T_EINVAL, "linear: epilogue");
+  if (epilogue < Q3T_EPI_STORE || epilogue > Q3T_EPI_SILU)
+    return fail(Q3T_EINVAL, "linear: epilogue (the Snake epilogue needs q3t_conv_linear)");
   const Plan p = plan(rows, in_features, out_features);
-  CUtensorMap tmw, tmx;
+  Maps maps;
+  memset(&maps, 0, sizeof(maps));
   int rc = Q3T_OK;
   if (weight_tiles == nullptr) {
-    rc = make_map(&tmw, weight, out_features, in_features, in_features, kTileN);
+    rc = make_map(&maps.w, weight, out_features, in_features, in_features, kTileN);
     if (rc) return rc;
-  } else {
-    memset(&tmw, 0, sizeof(tmw));
   }
-  rc = make_map(&tmx, x, rows, in_features, x_stride, p.bn);
+  rc = make_map(&maps.x, x, rows, in_features, x_stride, p.bn);
   if (rc) return rc;
-  GemmArgs a;
+  GemmArgs a = {};
   a.rows = int(rows);
   a.in_features = int(in_features);
   a.out_features = int(out_features);
@@ -738,14 +886,16 @@ int linear_impl(const void* x, int64_t x_stride, int64_t rows, int64_t in_featur
   a.norm_eps = row_norm_eps;
   a.prefetch = prefetch_bytes ? static_cast<const uint8_t*>(prefetch) : nullptr;
   a.prefetch_bytes = prefetch_bytes;
+  a.tma_out = p.splits == 1 && p.bn >= 64 && epilogue != Q3T_EPI_SWIGLU_PAIRED && out_dtype == Q3T_BF16 &&
+              staged_maps(maps, p.bn, out_features, out, out_stride, residual, residual_stride, rows, 1, 0);
   a.status = status;
   switch (epilogue) {
-    case Q3T_EPI_STORE: return dispatch_bn<Q3T_EPI_STORE>(p, tmw, tmx, a, stream);
-    case Q3T_EPI_RESIDUAL: return dispatch_bn<Q3T_EPI_RESIDUAL>(p, tmw, tmx, a, stream);
-    case Q3T_EPI_RESIDUAL_SCALED: return dispatch_bn<Q3T_EPI_RESIDUAL_SCALED>(p, tmw, tmx, a, stream);
-    case Q3T_EPI_GELU: return dispatch_bn<Q3T_EPI_GELU>(p, tmw, tmx, a, stream);
-    case Q3T_EPI_SILU: return dispatch_bn<Q3T_EPI_SILU>(p, tmw, tmx, a, stream);
-    default: return dispatch_bn<Q3T_EPI_SWIGLU_PAIRED>(p, tmw, tmx, a, stream);
+    case Q3T_EPI_STORE: return dispatch_bn<Q3T_EPI_STORE>(p, maps, a, stream);
+    case Q3T_EPI_RESIDUAL: return dispatch_bn<Q3T_EPI_RESIDUAL>(p, maps, a, stream);
+    case Q3T_EPI_RESIDUAL_SCALED: return dispatch_bn<Q3T_EPI_RESIDUAL_SCALED>(p, maps, a, stream);
+    case Q3T_EPI_GELU: return dispatch_bn<Q3T_EPI_GELU>(p, maps, a, stream);
+    case Q3T_EPI_SILU: return dispatch_bn<Q3T_EPI_SILU>(p, maps, a, stream);
+    default: return dispatch_bn<Q3T_EPI_SWIGLU_PAIRED>(p, maps, a, stream);
   }
 }
 
@@ -780,4 +930,73 @@ extern "C" int q3t_linear_prefetch(const void* x, int64_t x_stride, int64_t rows
   if (!(eps >= 0.f)) return fail(Q3T_EINVAL, "linear_prefetch: eps must be >= 0");
   return linear_impl(x, x_stride, rows, in_features, weight, out_features, bias, out, out_stride, out_dtype, epilogue,
                      residual, residual_stride, scale, eps, weight_tiles, prefetch, prefetch_bytes, status, stream);
+}
+
+extern "C" int q3t_conv_linear(const void* xs, int64_t batch, int64_t frames, int64_t pad, int64_t channels,
+                               int64_t taps, int64_t dilation, int reverse, const void* weight_tiles,
+                               int64_t out_features, const void* bias, void* out, int64_t out_stride, int epilogue,
+                               const void* residual, int64_t residual_stride, const void* scale,
+                               const float* snake_alpha, const float* snake_inv, unsigned* status, void* stream) {
+  if (!xs || !weight_tiles || !out) return fail(Q3T_EINVAL, "conv_linear: null pointer");
+  if (batch < 1 || batch > 65535 || frames < 1 || frames > (1 << 24) || channels < 8 || channels % 8 ||
+      taps < 1 || taps > 64 || dilation < 1 || pad < 0 || out_features < 1 || out_features > (1 << 24))
+    return fail(Q3T_EINVAL, "conv_linear: unsupported geometry");
+  if (pad < (taps - 1) * dilation) return fail(Q3T_EINVAL, "conv_linear: pad must cover (taps - 1) * dilation");
+  if (!aligned16(xs) || !aligned16(weight_tiles)) return fail(Q3T_EINVAL, "conv_linear: 16-byte alignment");
+  if (out_stride < out_features) return fail(Q3T_EINVAL, "conv_linear: out_stride too small");
+  if (has_residual(epilogue) && residual == nullptr)
+    return fail(Q3T_EINVAL, "conv_linear: residual epilogue needs a residual");
+  if (epilogue == Q3T_EPI_RESIDUAL_SCALED && scale == nullptr)
+    return fail(Q3T_EINVAL, "conv_linear: scaled residual epilogue needs a scale vector");
+  if (epilogue == Q3T_EPI_SNAKE && (snake_alpha == nullptr || snake_inv == nullptr))
+    return fail(Q3T_EINVAL, "conv_linear: Snake epilogue needs alpha and inverse beta");
+  if (epilogue == Q3T_EPI_SWIGLU_PAIRED || epilogue < Q3T_EPI_STORE || epilogue > Q3T_EPI_SNAKE)
+    return fail(Q3T_EINVAL, "conv_linear: epilogue");
+  if (int64_t(batch) * ((frames + 255) / 256) > 65535 * 256) return fail(Q3T_EINVAL, "conv_linear: too many rows");
+  Plan p;
+  p.bn = pick_bn(frames);
+  const int64_t tiles = (frames + p.bn - 1) / p.bn;
+  p.n_tiles = int((out_features + kTileN - 1) / kTileN);
+  p.m_tiles = int(batch * tiles);
+  const int cblocks = int((channels + kTileK - 1) / kTileK);
+  p.kblocks = int(taps) * cblocks;
+  choose_splits(p);
+  if (p.m_tiles > 65535) return fail(Q3T_EINVAL, "conv_linear: too many row tiles");
+  Maps maps;
+  memset(&maps, 0, sizeof(maps));
+  int rc = make_map_3d(&maps.x, xs, batch, pad + frames, channels, p.bn);
+  if (rc) return rc;
+  GemmArgs a = {};
+  a.rows = int(batch * frames);
+  a.in_features = p.kblocks * kTileK;
+  a.out_features = int(out_features);
+  a.kblocks = p.kblocks;
+  a.splits = p.splits;
+  a.tiles = static_cast<const uint8_t*>(weight_tiles);
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.out = out;
+  a.out_stride = out_stride;
+  a.residual = static_cast<const __nv_bfloat16*>(residual);
+  a.res_stride = residual_stride;
+  a.scale = static_cast<const __nv_bfloat16*>(scale);
+  a.conv_taps = int(taps);
+  a.conv_dil = int(dilation);
+  a.conv_reverse = reverse ? 1 : 0;
+  a.conv_cblocks = cblocks;
+  a.conv_frames = int(frames);
+  a.conv_tiles = int(tiles);
+  a.snake_alpha = snake_alpha;
+  a.snake_inv = snake_inv;
+  a.tma_out = p.splits == 1 && p.bn >= 64 &&
+              staged_maps(maps, p.bn, out_features, out, out_stride, residual, residual_stride, batch * frames,
+                          batch, frames);
+  a.status = status;
+  switch (epilogue) {
+    case Q3T_EPI_STORE: return dispatch_bn<Q3T_EPI_STORE>(p, maps, a, stream);
+    case Q3T_EPI_RESIDUAL: return dispatch_bn<Q3T_EPI_RESIDUAL>(p, maps, a, stream);
+    case Q3T_EPI_RESIDUAL_SCALED: return dispatch_bn<Q3T_EPI_RESIDUAL_SCALED>(p, maps, a, stream);
+    case Q3T_EPI_GELU: return dispatch_bn<Q3T_EPI_GELU>(p, maps, a, stream);
+    case Q3T_EPI_SILU: return dispatch_bn<Q3T_EPI_SILU>(p, maps, a, stream);
+    default: return dispatch_bn<Q3T_EPI_SNAKE>(p, maps, a, stream);
+  }
 }

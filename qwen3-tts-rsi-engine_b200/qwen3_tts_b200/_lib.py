@@ -14,7 +14,7 @@ LIBRARY_PATH = _HERE / "libq3t_b200.so"
 
 Q3T_OK, Q3T_EINVAL, Q3T_EUNSUPPORTED, Q3T_ECUDA, Q3T_ESPACE = 0, -1, -2, -3, -4
 Q3T_BF16, Q3T_F32 = 0, 1
-EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU_PAIRED, EPI_RESIDUAL_SCALED, EPI_GELU, EPI_SILU = 0, 1, 2, 3, 4, 5
+EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU_PAIRED, EPI_RESIDUAL_SCALED, EPI_GELU, EPI_SILU, EPI_SNAKE = 0, 1, 2, 3, 4, 5, 6
 NORM_REFERENCE, NORM_NATIVE = 0, 1
 
 _p = ctypes.c_void_p
@@ -67,6 +67,9 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "q3t_scatter_rows": (_i32, [_p, _i64, _p, _p, _i32, _p, _p, _i32, _p, _p]),
     "q3t_rvq_gather": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "q3t_conv_gather": (_i32, [_p, _i64, _i64, _i64, _i64, _p, _i64, _p, _i64, _i64, _i32, _p, _p, _p, _p]),
+    "q3t_conv_pad": (_i32, [_p, _i64, _i64, _i64, _i64, _p, _i64, _p, _p, _p, _p, _p]),
+    "q3t_conv_linear": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _p, _i64, _p, _p, _i64, _i32, _p, _i64,
+                               _p, _p, _p, _p, _p]),
     "q3t_conv_history": (_i32, [_p, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),
     "q3t_dwconv_layernorm": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _p, _p, _p, _p, _p, _f32, _p, _p]),
     "q3t_codec_positions": (_i32, [_p, _p, _i64, _i64, _i64, _p, _p, _i32, _p]),

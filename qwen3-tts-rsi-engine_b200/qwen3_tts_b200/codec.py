@@ -12,11 +12,15 @@ their new codes [batch, codebooks, frames], and per slot the engine keeps
   (positions are absolute frame indices; the window of 72 sees 71 history keys),
 * the frame counter.
 
-Activations are time-major [batch * frames, channels] bf16. Each convolution
-is ``q3t_conv_gather`` (im2col rows with history and the preceding SnakeBeta
-fused) followed by the tcgen05 GEMM ``q3t_linear``; a transposed conv of
-stride r is one GEMM whose r * C_out outputs per input frame are the
-upsampled sequence. One CUDA graph is captured per (batch, frames) key.
+Activations are time-major [batch * frames, channels] bf16. Each causal
+convolution is ``q3t_conv_pad`` (the slot's history then the new frames, with
+the preceding SnakeBeta applied, written once) followed by the implicit tcgen05
+GEMM ``q3t_conv_linear``, whose activation tiles are tap-shifted rows of that
+buffer (no im2col copy); a transposed conv of stride r is one such GEMM over
+[x[t] | x[t-1]] whose r * C_out outputs per input frame are the upsampled
+sequence. A residual unit's second SnakeBeta runs in the epilogue of its
+dilated conv, so its 1x1 conv reads that output directly. One CUDA graph is
+captured per (batch, frames) key.
 """
 from __future__ import annotations
 
@@ -47,8 +51,8 @@ def _conv(module, device):
     c_out, c_in, k = w.shape
     weight = w.permute(0, 2, 1).reshape(c_out, k * c_in).to(device=device, dtype=BF16).contiguous()
     bias = module.conv.bias.detach().to(device=device, dtype=BF16).contiguous() if module.conv.bias is not None else None
-    return {"w": weight, "b": bias, "k": k, "d": module.conv.dilation[0], "pad": module.padding, "c_in": c_in,
-            "c_out": c_out}
+    return {"w": weight, "tiles": ops.conv_weight_tiles(weight, k) if k > 1 else None, "b": bias, "k": k,
+            "d": module.conv.dilation[0], "pad": module.padding, "c_in": c_in, "c_out": c_out}
 
 
 def _tconv(module, device):
@@ -64,7 +68,8 @@ def _tconv(module, device):
         rows.append(torch.cat([w[:, :, j + m * r].T for m in range(taps)], dim=1))  # [C_out, taps*C_in]
     weight = torch.cat(rows, dim=0).to(device=device, dtype=BF16).contiguous()
     bias = module.conv.bias.detach().repeat(r).to(device=device, dtype=BF16).contiguous()
-    return {"w": weight, "b": bias, "r": r, "taps": taps, "c_in": c_in, "c_out": c_out}
+    return {"w": weight, "tiles": ops.conv_weight_tiles(weight, taps) if taps > 1 else None, "b": bias, "r": r,
+            "taps": taps, "c_in": c_in, "c_out": c_out}
 
 
 def _linear(module, device):
@@ -219,12 +224,17 @@ class CodecStep:
             self.buf[name] = t
         return t
 
+    def _xs(self, hist_name, rows, channels):
+        """Padded conv input [batch * (history + frames), channels] for the conv with history `hist_name`."""
+        H = self.state.histories[hist_name].shape[1]
+        return self._b(hist_name + ".xs", self.batch * H + rows, channels)
+
     def _allocate(self, dev):
         cfg, p, B, T = self.cfg, self.p, self.batch, self.frames
         R = B * T
         self._b("rvq", R, 2 * cfg.codebook_dim)
         self._b("x0", R, cfg.codebook_dim)
-        self._b("col_pre", R, 3 * cfg.codebook_dim)
+        self._xs("pre_conv", R, cfg.codebook_dim)
         self._b("lat", R, cfg.latent)
         self._b("h", R, cfg.hidden)
         self._b("xn", R, cfg.hidden)
@@ -241,33 +251,35 @@ class CodecStep:
             self._b(f"up{i}", rows, C)
             self._b(f"up{i}.ln", rows, C)
             self._b(f"up{i}.pw1", rows, 4 * C)
-        C = p["conv0"]["c_in"]
-        self._b("col0", rows, 7 * C)
+        self._xs("conv0", rows, p["conv0"]["c_in"])
         self._b("d0", rows, p["conv0"]["c_out"])
         for i, blk in enumerate(p["blocks"]):
             t = blk["tconv"]
-            self._b(f"b{i}.col", rows, t["taps"] * t["c_in"])
+            self._xs(f"b{i}.tconv", rows, t["c_in"])
             rows *= t["r"]
             C = t["c_out"]
             self._b(f"b{i}.y", rows, C)
-            self._b(f"b{i}.col7", rows, 7 * C)
-            self._b(f"b{i}.h", rows, C)
+            for u in range(len(blk["units"])):
+                self._xs(f"b{i}.u{u}.conv1", rows, C)
             self._b(f"b{i}.col1", rows, C)
-        self._b("colf", rows, 7 * p["final_conv"]["c_in"])
+        self._xs("final", rows, p["final_conv"]["c_in"])
         self._b("out", rows, 1)
 
     # ------------------------------------------------------------------ kernels of one call
     def _conv(self, x, rows_in, conv, hist_name, *, snake=None, out=None, epilogue=_lib.EPI_STORE, residual=None,
-              col_name=None):
+              out_snake=None, reverse=False):
+        """Causal conv (or, with `reverse`, the [x[t] | x[t-1]] transposed conv) of x with the slot
+        histories: pad (+ SnakeBeta) -> history update -> implicit GEMM."""
         B, T = self.batch, rows_in // self.batch
-        hist = self.state.histories.get(hist_name) if hist_name else None
+        hist = self.state.histories[hist_name]
         alpha, inv = snake if snake is not None else (None, None)
-        col = self.buf[col_name]
-        ops.conv_gather(x, B, T, taps=conv["k"], dilation=conv["d"], history=hist, slots=self.indices, alpha=alpha,
-                        inverse_beta=inv, out=col)
-        ops.linear(col, conv["w"], conv["b"], out=out, epilogue=epilogue, residual=residual)
-        if hist is not None:
-            ops.conv_history(x, B, T, hist, slots=self.indices)
+        xs = self.buf[hist_name + ".xs"]
+        ops.conv_pad(x, B, T, history=hist, slots=self.indices, alpha=alpha, inverse_beta=inv, out=xs)
+        ops.conv_history(x, B, T, hist, slots=self.indices)
+        taps = conv["taps"] if reverse else conv["k"]
+        ops.conv_linear(xs, B, T, hist.shape[1], conv["tiles"], taps=taps, dilation=1 if reverse else conv["d"],
+                        reverse=reverse, bias=conv["b"], out=out, epilogue=epilogue, residual=residual,
+                        snake=out_snake)
 
     def compute(self) -> None:
         cfg, p, st, b = self.cfg, self.p, self.state, self.buf
@@ -276,7 +288,7 @@ class CodecStep:
         # RVQ dequantisation and the pre-transformer causal conv
         ops.rvq_gather(self.codes, p["rvq_tables"], cfg.semantic_codebooks, out=b["rvq"])
         ops.linear(b["rvq"], p["rvq_proj"], out=b["x0"])
-        self._conv(b["x0"], R, p["pre_conv"], "pre_conv", out=b["lat"], col_name="col_pre")
+        self._conv(b["x0"], R, p["pre_conv"], "pre_conv", out=b["lat"])
         # sliding-window transformer
         tr = p["transformer"]
         ops.linear(b["lat"], *tr["input_proj"], out=b["h"])
@@ -314,27 +326,22 @@ class CodecStep:
                        scale=up["gamma"])
             x = y
         # decoder: causal conv, 4 blocks (Snake -> transposed conv -> 3 residual units), Snake, conv
-        self._conv(x, rows, p["conv0"], "conv0", out=b["d0"], col_name="col0")
+        self._conv(x, rows, p["conv0"], "conv0", out=b["d0"])
         x = b["d0"]
         for i, blk in enumerate(p["blocks"]):
             t = blk["tconv"]
-            alpha, inv = blk["snake"]
-            ops.conv_gather(x, B, rows // B, taps=t["taps"], dilation=1, reverse=True,
-                            history=st.histories[f"b{i}.tconv"], slots=self.indices, alpha=alpha, inverse_beta=inv,
-                            out=b[f"b{i}.col"])
             y = b[f"b{i}.y"]
-            ops.linear(b[f"b{i}.col"], t["w"], t["b"], out=y.view(rows, t["r"] * t["c_out"]))
-            ops.conv_history(x, B, rows // B, st.histories[f"b{i}.tconv"], slots=self.indices)
+            self._conv(x, rows, t, f"b{i}.tconv", snake=blk["snake"], out=y.view(rows, t["r"] * t["c_out"]),
+                       reverse=True)
             rows *= t["r"]
             for u, unit in enumerate(blk["units"]):
-                self._conv(y, rows, unit["conv1"], f"b{i}.u{u}.conv1", snake=unit["snake1"], out=b[f"b{i}.h"],
-                           col_name=f"b{i}.col7")
-                a2, i2 = unit["snake2"]
-                ops.conv_gather(b[f"b{i}.h"], B, rows // B, taps=1, alpha=a2, inverse_beta=i2, out=b[f"b{i}.col1"])
+                # dilated conv with the unit's second SnakeBeta in its epilogue, then the 1x1 conv + residual
+                self._conv(y, rows, unit["conv1"], f"b{i}.u{u}.conv1", snake=unit["snake1"], out=b[f"b{i}.col1"],
+                           epilogue=_lib.EPI_SNAKE, out_snake=unit["snake2"])
                 ops.linear(b[f"b{i}.col1"], unit["conv2"]["w"], unit["conv2"]["b"], out=y,
                            epilogue=_lib.EPI_RESIDUAL, residual=y)
             x = y
-        self._conv(x, rows, p["final_conv"], "final", snake=p["final_snake"], out=b["out"], col_name="colf")
+        self._conv(x, rows, p["final_conv"], "final", snake=p["final_snake"], out=b["out"])
         ops.pcm16(b["out"], wave=self.wave, pcm=self.pcm)
 
     @torch.inference_mode()

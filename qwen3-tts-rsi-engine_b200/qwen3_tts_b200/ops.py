@@ -525,6 +525,52 @@ def conv_gather(x, batch: int, frames: int, *, taps: int, dilation: int = 1, rev
     return out
 
 
+def conv_pad(x, batch: int, frames: int, *, history=None, slots=None, alpha=None, inverse_beta=None, out=None):
+    """Padded input of an implicit causal conv: snake([history[slot] | x[b]]) as [batch*(H+frames), C]."""
+    _need_cuda(x)
+    C = x.shape[-1]
+    H = history.shape[1] if history is not None else 0
+    out = torch.empty(batch * (H + frames), C, dtype=BF16, device=x.device) if out is None else out
+    if out.shape != (batch * (H + frames), C) or not out.is_contiguous():
+        raise ValueError("conv_pad: out must be a contiguous [batch*(history+frames), channels] buffer")
+    call("q3t_conv_pad", x.data_ptr(), x.stride(0), batch, frames, C, _ptr(history), H, _ptr(slots), _ptr(alpha),
+         _ptr(inverse_beta), out.data_ptr(), _stream())
+    return out
+
+
+def conv_weight_tiles(weight: torch.Tensor, taps: int) -> TiledWeight:
+    """Conv weight [C_out, taps*C_in] (K ordered (tap, channel)) -> tiles of q3t_conv_linear, with the
+    channels of every tap zero-padded to a multiple of 64."""
+    c_out, k = weight.shape
+    c_in = k // taps
+    cp = -(-c_in // 64) * 64
+    if cp != c_in:
+        padded = torch.zeros(c_out, taps, cp, dtype=weight.dtype, device=weight.device)
+        padded[:, :, :c_in] = weight.view(c_out, taps, c_in)
+        weight = padded.view(c_out, taps * cp)
+    return pack_tiles(weight.contiguous())
+
+
+def conv_linear(xs, batch: int, frames: int, pad: int, weight: TiledWeight, *, taps: int, dilation: int = 1,
+                reverse: bool = False, bias=None, out=None, epilogue: int = _lib.EPI_STORE, residual=None, scale=None,
+                snake=None):
+    """Causal conv over conv_pad's buffer as an implicit GEMM (q3t_conv_linear) -> [batch*frames, C_out]."""
+    _need_cuda(xs, weight.tiles)
+    C = xs.shape[-1]
+    if not isinstance(weight, TiledWeight) or weight.in_features != taps * (-(-C // 64) * 64):
+        raise ValueError("conv_linear: weight must be conv_weight_tiles of [C_out, taps*C_in]")
+    if xs.shape != (batch * (pad + frames), C) or not xs.is_contiguous():
+        raise ValueError("conv_linear: xs must be conv_pad's [batch*(pad+frames), channels] buffer")
+    n = weight.out_features
+    out = torch.empty(batch * frames, n, dtype=BF16, device=xs.device) if out is None else out
+    alpha, inv = snake if snake is not None else (None, None)
+    call("q3t_conv_linear", xs.data_ptr(), batch, frames, pad, C, taps, dilation, int(reverse), weight.tiles.data_ptr(),
+         n, _ptr(bias), out.data_ptr(), out.stride(0), epilogue, _ptr(residual),
+         residual.stride(0) if residual is not None else 0, _ptr(scale), _ptr(alpha), _ptr(inv),
+         status_word(xs.device).data_ptr(), _stream())
+    return out
+
+
 def conv_history(x, batch: int, frames: int, history, slots=None) -> None:
     """history[slot] = last H frames of [history[slot] | x[b]]."""
     _need_cuda(x, history)

@@ -267,6 +267,44 @@ def test_linear_inplace_residual_and_l2_prefetch(ops, cuda, rows, k, n):
     assert_status_clean(ops, cuda)
 
 
+@pytest.mark.parametrize("batch,frames,C,N,taps,dil,reverse", [
+    (2, 40, 128, 256, 7, 3, False), (3, 300, 96, 96, 7, 9, False), (2, 64, 192, 384, 2, 1, True),
+    (1, 5, 512, 1024, 3, 1, False), (4, 700, 16, 1, 7, 1, False), (2, 1100, 32, 64, 7, 1, False)])
+def test_conv_linear_matches_gather_then_linear(ops, cuda, batch, frames, C, N, taps, dil, reverse):
+    """Implicit-GEMM causal conv (q3t_conv_pad + q3t_conv_linear: tap-shifted 3-D TMA rows of the
+    padded buffer, channels zero-padded to 64 per tap) against im2col (q3t_conv_gather) + GEMM, with
+    per-slot histories, SnakeBeta on the input, and the STORE / RESIDUAL / SNAKE epilogues."""
+    from qwen3_tts_b200 import _lib
+    H = (taps - 1) * dil
+    x = rnd(80 + frames, (batch * frames, C), 1.0, BF16).to(cuda)
+    hist = rnd(81, (batch + 2, H, C), 1.0, BF16).to(cuda)
+    slots = torch.tensor(list(range(batch + 1, 0, -1))[:batch], dtype=torch.long, device=cuda)
+    alpha = (0.5 + torch.rand(C, generator=torch.Generator().manual_seed(82))).to(cuda)
+    inv = (0.5 + torch.rand(C, generator=torch.Generator().manual_seed(83))).to(cuda)
+    w = rnd(84, (N, taps * C), 0.05, BF16).to(cuda)
+    bias = rnd(85, (N,), 0.1, BF16).to(cuda)
+    col = ops.conv_gather(x, batch, frames, taps=taps, dilation=dil, reverse=reverse, history=hist, slots=slots,
+                          alpha=alpha, inverse_beta=inv)
+    ref32 = col.float() @ w.float().T + bias.float()
+    xs = ops.conv_pad(x, batch, frames, history=hist, slots=slots, alpha=alpha, inverse_beta=inv)
+    tiles = ops.conv_weight_tiles(w, taps)
+    got = ops.conv_linear(xs, batch, frames, H, tiles, taps=taps, dilation=dil, reverse=reverse, bias=bias)
+    k = taps * C
+    torch.testing.assert_close(got.float(), ref32, atol=2e-3 * math.sqrt(k / 64) + 1e-2, rtol=1e-2)
+    res = rnd(86, (batch * frames, N), 1.0, BF16).to(cuda)
+    y = res.clone()
+    ops.conv_linear(xs, batch, frames, H, tiles, taps=taps, dilation=dil, reverse=reverse, bias=bias, out=y,
+                    epilogue=_lib.EPI_RESIDUAL, residual=y)
+    assert torch.equal(y, (res.float() + got.float()).to(BF16))
+    a2 = (0.5 + torch.rand(N, generator=torch.Generator().manual_seed(87))).to(cuda)
+    i2 = (0.5 + torch.rand(N, generator=torch.Generator().manual_seed(88))).to(cuda)
+    snaked = ops.conv_linear(xs, batch, frames, H, tiles, taps=taps, dilation=dil, reverse=reverse, bias=bias,
+                             epilogue=_lib.EPI_SNAKE, snake=(a2, i2))
+    if N % 8 == 0:  # the same SnakeBeta applied by the gather to the stored conv output
+        assert torch.equal(snaked, ops.conv_gather(got, batch, frames, taps=1, alpha=a2, inverse_beta=i2))
+    assert_status_clean(ops, cuda)
+
+
 @pytest.mark.parametrize("rows", [1, 32, 64, 130])
 def test_linear_paired_swiglu(ops, cuda, rows):
     from qwen3_tts_b200 import _lib
