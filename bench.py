@@ -48,6 +48,8 @@ def parse_args():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--layers", type=int, default=28, help="talker depth (28 = the benchmarked model)")
+    p.add_argument("--slots", type=int, default=SLOTS,
+                   help="step workload: concurrent slots (32 = BASELINE config 2; 64 = the C=64 roofline target)")
     p.add_argument("--op-costs", action="store_true",
                    help="print the in-graph cost of each talker-layer op (28 chained launches per op) and exit")
     p.add_argument("--workload", choices=["step", "serving"], default="step",
@@ -93,9 +95,9 @@ class Dist:
 class Workload:
     """Seeded ragged contexts and the eviction/admission schedule."""
 
-    def __init__(self, seed: int, slots: int = SLOTS):
+    def __init__(self, seed: int, slots: int = None):
         self.g = torch.Generator().manual_seed(seed)
-        self.slots = slots
+        self.slots = slots = SLOTS if slots is None else slots
         self.positions = torch.randint(64, 2049, (slots,), generator=self.g)
 
     def admit(self):
@@ -407,10 +409,10 @@ def run_reference(args, dist: Dist):
     per_step, threads = cpu_decode_sample(TALKER, work.positions, args.warmup + args.steps, layers, args.seed)
     value = SLOTS / per_step
     return {
-        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+        "metric": f"codec frames/s (talker decode step, C={SLOTS})", "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "BASELINE config 2: talker decode step, 32 slots, ctx U[64,2048]",
+        "config": {"workload": f"BASELINE config 2: talker decode step, {SLOTS} slots, ctx U[64,2048]",
                    "model": "qwen3-tts talker 28L h2048 (random init)", "global_batch": SLOTS,
                    "parallelism": "cpu"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
@@ -439,6 +441,9 @@ def op_costs(args) -> None:
         plane.normal_()
     W = engine.weights["layers"]
     eps = cfg.eps if W[0].folded else None
+    # the step's split-KV plan, as TalkerStep.compute makes it once per step
+    ops.attention_plan(positions, step.ws_attn, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
+                       context=CAPACITY)
 
     def graph_us(fn, replays=10):
         side = torch.cuda.Stream()
@@ -558,7 +563,11 @@ def run_serving(args) -> dict:
 
 
 def main():
+    global SLOTS
     args = parse_args()
+    if args.slots < 1 or args.slots > 64:
+        raise SystemExit("--slots must be within 1..64")
+    SLOTS = args.slots
     if args.op_costs:
         op_costs(args)
         return
@@ -599,14 +608,14 @@ def main():
     step_bytes = cfg.weight_bytes() + kv_step
     e2e_value = SLOTS * res["e2e_steps"] * dist.world / (res["e2e_ms"] / 1e3)
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
+        "metric": f"codec frames/s (talker decode step, C={SLOTS})", "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": res["elapsed_ms"] / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights)",
-        "config": {"workload": "BASELINE config 2: talker decode step, 32 slots, ctx U[64,2048], "
+        "config": {"workload": f"BASELINE config 2: talker decode step, {SLOTS} slots, ctx U[64,2048], "
                                "greedy, evict/admit 4 slots every 16 steps",
                    "layers": cfg.layers, "global_batch": SLOTS * dist.world, "slots_per_gpu": SLOTS,
                    "parallelism": f"replicas x{dist.world} (request-level data parallel)",
-                   "l2": "inputs > L2 (6.7 GB streamed per step)",
+                   "l2": f"inputs > L2 ({step_bytes / 1e9:.1f} GB streamed per step)",
                    "hbm_fraction_step": step_bytes / (res["elapsed_ms"] / args.steps / 1e3) / (peak * 1e9),
                    "bytes_per_step": step_bytes},
         "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -622,8 +631,8 @@ def main():
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         per_step, threads = cpu_decode_sample(cfg, positions, 3, 2, args.seed)
         line["cpu_baseline"] = {"value": SLOTS / per_step, "unit": UNIT, "cores": threads, "kind": "port",
-                                "sample": "oracle fp32 talker, 2 of 28 layers at full width, 32 slots, same "
-                                          "contexts, median of 3 steps scaled by 14"}
+                                "sample": f"oracle fp32 talker, 2 of 28 layers at full width, {SLOTS} slots, "
+                                          "same contexts, median of 3 steps scaled by 14"}
     if dist.rank == 0:
         print(json.dumps(line))
     dist.close()

@@ -235,6 +235,17 @@ int q3t_decode_attention(const void* query, const void* keys, const void* values
                          int64_t window, float scale, void* workspace, size_t workspace_bytes,
                          unsigned* status, void* stream);
 
+/* Chunk plan of the decode attention for this batch (once per decode step, before the
+ * layers): with the query positions of the step's rows, writes into the attention
+ * workspace the keys per split-KV chunk that let one wave of resident CTAs cover all
+ * (row, kv head) pairs (a power of two times the default chunk). Later
+ * q3t_decode_attention / _qkv calls on the same workspace (one query row per slot, no
+ * window) use it; without a plan, or with a stale one, results are identical and only
+ * the split differs. positions: int64 [rows]. */
+int q3t_attention_plan(const int64_t* positions, int64_t rows, int64_t q_heads, int64_t kv_heads,
+                       int64_t head_dim, int64_t context, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
 /* Talker decode step attention with the per-head q/k RMSNorm, RoPE and the
  * K/V write of PackedAttention.forward (packed_attention.py:42-74) fused in:
  * reads the raw QKV projection rows qkv [rows, (q_heads + 2 kv_heads) * head_dim]

@@ -303,10 +303,40 @@ __global__ void __launch_bounds__(128)
 }
 
 // Workspace layout: a fixed ticket region (one counter per (row, kv head),
-// zero between calls) followed by the chunk partials; fixed so that calls of
-// different shapes sharing a workspace never read partials as tickets.
+// zero between calls; its last word holds the chunk plan of q3t_attention_plan)
+// followed by the chunk partials; fixed so that calls of different shapes
+// sharing a workspace never read partials as tickets.
 constexpr size_t kMaxTickets = 65536;
 constexpr size_t kTicketBytes = kMaxTickets * sizeof(unsigned);
+constexpr size_t kPlanSlot = kMaxTickets - 1;
+
+// Keys per chunk for one wave of `wave` resident CTAs over this batch's contexts: the keys of
+// all (row, kv head) pairs per CTA, rounded up to chunk_min * 2^k (at most the context and
+// kMaxPlannedChunk: inside a decode step the attention's last CTAs are not overlapped by the
+// next kernel, so longer chunks lengthen the tail; measured on the talker step at 32 and 64 slots).
+constexpr int64_t kMaxPlannedChunk = 1024;
+__global__ void attention_plan_kernel(const int64_t* __restrict__ positions, int rows, int kv_heads, int64_t context,
+                                      int chunk_min, int wave, unsigned* __restrict__ plan) {
+  __shared__ unsigned long long total;
+  grid_dependency_wait();
+  if (threadIdx.x == 0) total = 0ull;
+  __syncthreads();
+  unsigned long long mine = 0ull;
+  for (int i = threadIdx.x; i < rows; i += blockDim.x) {
+    const int64_t p = positions[i];
+    mine += uint64_t(p < 0 ? 0 : (p >= context ? context - 1 : p)) + 1ull;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mine += __shfl_xor_sync(0xffffffffu, mine, o);
+  if ((threadIdx.x & 31) == 0 && mine != 0ull) atomicAdd(&total, mine);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned long long per_cta = (total * uint64_t(kv_heads) + uint64_t(wave) - 1) / uint64_t(wave);
+    int64_t chunk = chunk_min;
+    while (uint64_t(chunk) < per_cta && chunk < context && chunk < kMaxPlannedChunk) chunk <<= 1;
+    *plan = unsigned(chunk);
+  }
+}
 
 int pick_chunk(int64_t batch, int64_t kv_heads, int64_t context) {
   // Enough CTAs to cover every SM a few times at the bucket's full context.
@@ -370,7 +400,7 @@ extern "C" int q3t_decode_attention_qkv(const void* qkv, int64_t qkv_stride, con
   if (rows < 1 || rows > 65535 || kv_heads < 1 || q_heads % kv_heads || arena_slots < rows || table_len < 1)
     return fail(Q3T_EINVAL, "attention_qkv: invalid row or head geometry");
   if (context < 1 || context > capacity) return fail(Q3T_EINVAL, "Attention context must fit the KV arena");
-  if (size_t(rows) * size_t(kv_heads) > kMaxTickets) return fail(Q3T_EUNSUPPORTED, "attention: rows x kv_heads > 65536");
+  if (size_t(rows) * size_t(kv_heads) > kPlanSlot) return fail(Q3T_EUNSUPPORTED, "attention: rows x kv_heads > 65535");
   const int64_t g = q_heads / kv_heads;
   if (!attention_mma_supported(head_dim, g))
     return fail(Q3T_EUNSUPPORTED, "attention_qkv: head_dim %lld with %lld query heads per kv head",
@@ -381,7 +411,7 @@ extern "C" int q3t_decode_attention_qkv(const void* qkv, int64_t qkv_stride, con
   const size_t need = attn_workspace(rows, q_heads, kv_heads, head_dim, context);
   if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
     return fail(Q3T_ESPACE, "attention: workspace needs %zu bytes", need);
-  AttentionCall call;
+  AttentionCall call = {};
   call.query = qkv;
   call.keys = keys;
   call.values = values;
@@ -402,6 +432,7 @@ extern "C" int q3t_decode_attention_qkv(const void* qkv, int64_t qkv_stride, con
   call.max_chunks = int((context + call.chunk - 1) / call.chunk);
   call.counters = static_cast<unsigned*>(workspace);
   call.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kTicketBytes);
+  call.plan = call.counters + kPlanSlot;
   call.status = status;
   call.stream = stream;
   return launch_attention_fused(call, qkv, qkv_stride, q_norm_weight, k_norm_weight, eps, cos_table, sin_table,
@@ -420,7 +451,7 @@ extern "C" int q3t_decode_attention(const void* query, const void* keys, const v
   if (slots == nullptr && arena_slots * rows_per_slot < rows)
     return fail(Q3T_EINVAL, "attention: more query rows than arena slots");
   if (context < 1 || context > capacity) return fail(Q3T_EINVAL, "Attention context must fit the KV arena");
-  if (size_t(rows) * size_t(kv_heads) > kMaxTickets) return fail(Q3T_EUNSUPPORTED, "attention: rows x kv_heads > 65536");
+  if (size_t(rows) * size_t(kv_heads) > kPlanSlot) return fail(Q3T_EUNSUPPORTED, "attention: rows x kv_heads > 65535");
   if (ring < 0 || (ring > 0 && (ring != capacity || window < 1 || window > ring)))
     return fail(Q3T_EINVAL, "attention: a ring arena needs capacity == ring and 1 <= window <= ring");
   if (!aligned16(keys) || !aligned16(values) || !aligned16(query))
@@ -432,7 +463,7 @@ extern "C" int q3t_decode_attention(const void* query, const void* keys, const v
   if (ring == 0 && attention_mma_supported(head_dim, g)) {
     // linear arenas: tensor-core kernel (TMA-swizzled K/V tiles, mma.sync fragments)
     const int64_t span = window > 0 && window < context ? window : context;
-    AttentionCall call;
+    AttentionCall call = {};
     call.query = query;
     call.keys = keys;
     call.values = values;
@@ -453,6 +484,7 @@ extern "C" int q3t_decode_attention(const void* query, const void* keys, const v
     call.max_chunks = int((span + call.chunk - 1) / call.chunk);
     call.counters = static_cast<unsigned*>(workspace);
     call.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kTicketBytes);
+    call.plan = (window == 0 && rows_per_slot == 1) ? call.counters + kPlanSlot : nullptr;
     call.status = status;
     call.stream = stream;
     return launch_attention_mma(call);
@@ -582,4 +614,18 @@ extern "C" int q3t_decode_attention_noalloc(const void* query, const void* keys,
 #undef Q3T_ATTN_STATIC
   return fail(Q3T_EUNSUPPORTED, "attention (no-alloc): head_dim %lld with %lld query heads per kv head",
               (long long)head_dim, (long long)g);
+}
+
+extern "C" int q3t_attention_plan(const int64_t* positions, int64_t rows, int64_t q_heads, int64_t kv_heads,
+                                  int64_t head_dim, int64_t context, void* workspace, size_t workspace_bytes,
+                                  void* stream) {
+  if (!positions || !workspace || rows < 1 || rows > 65535 || kv_heads < 1 || q_heads % kv_heads || context < 1)
+    return fail(Q3T_EINVAL, "attention_plan: invalid arguments");
+  if (workspace_bytes < kTicketBytes || !aligned16(workspace))
+    return fail(Q3T_ESPACE, "attention_plan: workspace needs %zu bytes", kTicketBytes);
+  const int wave = attention_wave_ctas(head_dim, q_heads / kv_heads, true);
+  if (wave < 1) return fail(Q3T_EUNSUPPORTED, "attention_plan: unsupported head geometry");
+  return launch(attention_plan_kernel, dim3(1), dim3(256), 0, stream, true, "attention_plan", positions, int(rows),
+                int(kv_heads), context, pick_chunk(rows, kv_heads, context), wave,
+                static_cast<unsigned*>(workspace) + kPlanSlot);
 }

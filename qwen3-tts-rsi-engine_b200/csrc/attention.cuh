@@ -19,12 +19,15 @@ struct AttentionCall {
   int chunk, max_chunks;
   float* partials;
   unsigned* counters;  // one chunk ticket per (row, kv head), zero between calls
+  const unsigned* plan;  // keys per chunk planned for this batch (q3t_attention_plan), or null
   unsigned* status;
   void* stream;
 };
 
 // Tensor-core (mma.sync) kernel for linear arenas: head_dim 64/128, 1 or 2 query heads per kv head.
 bool attention_mma_supported(int64_t head_dim, int64_t group);
+// Resident CTAs of the tensor-core kernel on this device (one wave), 0 when unknown.
+int attention_wave_ctas(int64_t head_dim, int64_t group, bool fused);
 int launch_attention_mma(const AttentionCall& call);
 // Decode variant reading the raw QKV projection (per-head norm, RoPE and K/V write fused).
 int launch_attention_fused(const AttentionCall& call, const void* qkv, int64_t qkv_stride, const void* q_norm,

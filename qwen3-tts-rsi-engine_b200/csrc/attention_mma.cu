@@ -120,8 +120,9 @@ __global__ void __launch_bounds__(128, 3)
     decode_attention_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                                 const __nv_bfloat16* __restrict__ query, const int64_t* __restrict__ positions,
                                 __nv_bfloat16* __restrict__ out, int kv_heads, int64_t capacity, int64_t context,
-                                int window, int rows_per_slot, const int64_t* __restrict__ slots, int chunk,
-                                float qscale, float* __restrict__ partials, unsigned* __restrict__ counters,
+                                int window, int rows_per_slot, const int64_t* __restrict__ slots, int chunk_min,
+                                const unsigned* __restrict__ plan, float qscale, float* __restrict__ partials,
+                                unsigned* __restrict__ counters,
                                 int max_chunks, unsigned* status, const FusedQKV f) {
   using C = MmaCfg<D, G>;
   constexpr int S = C::kStages;
@@ -141,6 +142,14 @@ __global__ void __launch_bounds__(128, 3)
   grid_dependency_wait();
 
   int64_t pos = positions[b];
+  // Keys per chunk: the step's plan (q3t_attention_plan: one wave of resident CTAs for this
+  // batch's contexts) when present. Any multiple of 64 >= chunk_min is a valid split of the
+  // grid's chunk range, so a stale plan costs speed only.
+  int chunk = chunk_min;
+  if (plan != nullptr) {
+    const unsigned planned = *plan;
+    if (planned >= unsigned(chunk_min) && planned % 64u == 0u && planned <= unsigned(1 << 30)) chunk = int(planned);
+  }
   const bool pos_ok = pos >= 0 && pos < context;
   if (pos < 0 || pos >= context) {
     if (c == 0 && h == 0 && threadIdx.x == 0) raise_status(status, kStatusBadIndex);
@@ -442,12 +451,40 @@ int launch_mma(const AttentionCall& a, const FusedQKV& f) {
                 dim3(128), size_t(C::kSmem), a.stream, true, "decode_attention_mma", tmk, tmv,
                 static_cast<const __nv_bfloat16*>(a.query), a.positions, static_cast<__nv_bfloat16*>(a.out),
                 int(a.kv_heads), a.capacity, a.context, int(a.window), int(a.rows_per_slot), a.slots, a.chunk,
-                a.scale * kLog2e, a.partials, a.counters, a.max_chunks, a.status, f);
+                a.plan, a.scale * kLog2e, a.partials, a.counters, a.max_chunks, a.status, f);
 }
 
 }  // namespace
 
 namespace q3t {
+
+template <int D, int G, bool FUSED>
+int wave_of() {
+  static int resident[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 0;
+  if (resident[dev] == 0) {
+    using C = MmaCfg<D, G>;
+    if (cudaFuncSetAttribute(decode_attention_mma_kernel<D, G, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::kSmem) != cudaSuccess)
+      return 0;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_attention_mma_kernel<D, G, FUSED>, 128,
+                                                      size_t(C::kSmem)) != cudaSuccess || per_sm < 1)
+      per_sm = 1;
+    resident[dev] = per_sm * sm_count();
+  }
+  return resident[dev];
+}
+
+int attention_wave_ctas(int64_t head_dim, int64_t group, bool fused) {
+  if (head_dim == 128 && group == 2) return fused ? wave_of<128, 2, true>() : wave_of<128, 2, false>();
+  if (head_dim == 128 && group == 1) return fused ? wave_of<128, 1, true>() : wave_of<128, 1, false>();
+  if (head_dim == 64 && group == 2) return fused ? wave_of<64, 2, true>() : wave_of<64, 2, false>();
+  if (head_dim == 64 && group == 1) return fused ? wave_of<64, 1, true>() : wave_of<64, 1, false>();
+  return 0;
+}
 
 bool attention_mma_supported(int64_t head_dim, int64_t group) {
   return (head_dim == 128 || head_dim == 64) && (group == 1 || group == 2);

@@ -385,6 +385,16 @@ def decode_attention(query, keys, values, positions, *, context=None, scale=None
     return out
 
 
+def attention_plan(positions, workspace, *, q_heads, kv_heads, head_dim, context):
+    """Per-step split-KV chunk plan (q3t_attention_plan) for the decode attention calls that use
+    `workspace`: one wave of resident CTAs over this batch's contexts."""
+    _need_cuda(positions, workspace)
+    if positions.dtype != torch.int64 or positions.ndim != 1:
+        raise ValueError("positions must be int64 [rows]")
+    call("q3t_attention_plan", positions.data_ptr(), positions.shape[0], q_heads, kv_heads, head_dim, context,
+         workspace.data_ptr(), workspace.numel() * workspace.element_size(), _stream())
+
+
 def decode_attention_qkv(qkv, q_norm_weight, k_norm_weight, eps, cos_table, sin_table, rotary_positions, keys,
                          values, positions, *, q_heads, kv_heads, head_dim, context=None, scale=None, out=None,
                          workspace: Optional[torch.Tensor] = None, tag: str = "attention"):

@@ -112,6 +112,9 @@ class TalkerStep:
         lw = ops.linear
         res_in = self.inputs
         layers = w["layers"]
+        # split-KV chunks sized once per step for this batch's contexts (all layers share them)
+        ops.attention_plan(self.positions, self.ws_attn, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads,
+                           head_dim=cfg.head_dim, context=self.context)
         # each GEMM pulls the next GEMM's weights into L2 while it runs
         pf = (lambda t: t) if self.prefetch_weights else (lambda t: None)
         for i, layer in enumerate(layers):
@@ -149,7 +152,7 @@ class TalkerStep:
 
     def launches_per_step(self) -> int:
         per_layer = (6 if self.w["layers"][0].folded else 8) - (1 if self.fused_attention else 0)
-        return per_layer * self.cfg.layers + 2
+        return per_layer * self.cfg.layers + 3
 
     # ---------------------------------------------------------------- graph capture / replay
     @torch.inference_mode()

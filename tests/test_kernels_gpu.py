@@ -384,6 +384,39 @@ def test_fused_qkv_attention_equals_separate_kernels(ops, cuda, rows, q_heads, k
     assert_status_clean(ops, cuda)
 
 
+def test_attention_plan_changes_the_split_not_the_result(ops, cuda):
+    """q3t_attention_plan writes a per-batch chunk size (one wave of resident CTAs) into the
+    workspace; the decode attention then splits the keys differently, which only changes the
+    fp32 merge order of the chunk partials (bf16 outputs within one rounding), and writes the
+    same K/V rows."""
+    from qwen3_tts_b200.talker import rope_tables
+    rows, q_heads, kv_heads, head_dim, capacity = 32, 16, 8, 128, 4096
+    gen = torch.Generator().manual_seed(91)
+    width = (q_heads + 2 * kv_heads) * head_dim
+    qkv = torch.randn(rows, width, generator=gen).to(BF16).to(cuda)
+    keys = torch.randn(rows, kv_heads, capacity, head_dim, generator=gen).to(BF16).to(cuda)
+    values = torch.randn(rows, kv_heads, capacity, head_dim, generator=gen).to(BF16).to(cuda)
+    positions = torch.randint(64, 2049, (rows,), generator=gen).to(cuda)
+    qn = (1 + 0.1 * torch.randn(head_dim, generator=gen)).to(BF16).to(cuda)
+    kn = (1 + 0.1 * torch.randn(head_dim, generator=gen)).to(BF16).to(cuda)
+    cos, sin = rope_tables(capacity, head_dim, 1e6, cuda)
+    ws = torch.zeros(ops.decode_attention_workspace_bytes(rows, q_heads, head_dim, capacity), dtype=torch.uint8,
+                     device=cuda)
+    k0, v0 = keys.clone(), values.clone()
+    base = ops.decode_attention_qkv(qkv, qn, kn, 1e-6, cos, sin, positions, k0, v0, positions, q_heads=q_heads,
+                                    kv_heads=kv_heads, head_dim=head_dim, context=capacity, workspace=ws)
+    ops.attention_plan(positions, ws, q_heads=q_heads, kv_heads=kv_heads, head_dim=head_dim, context=capacity)
+    planned = int(ws.view(torch.int32)[65535].item())
+    assert planned >= 512 and planned % 64 == 0 and planned <= 2 * capacity
+    k1, v1 = keys.clone(), values.clone()
+    got = ops.decode_attention_qkv(qkv, qn, kn, 1e-6, cos, sin, positions, k1, v1, positions, q_heads=q_heads,
+                                   kv_heads=kv_heads, head_dim=head_dim, context=capacity, workspace=ws)
+    torch.cuda.synchronize()
+    assert torch.equal(k1, k0) and torch.equal(v1, v0)
+    torch.testing.assert_close(got.float(), base.float(), atol=1e-2, rtol=1e-2)
+    assert_status_clean(ops, cuda)
+
+
 def test_linear_graph_replay_is_deterministic(ops, cuda):
     x = rnd(60, (32, 2048), 1.0, BF16).to(cuda)
     w = rnd(61, (6144, 2048), 0.02, BF16).to(cuda)
