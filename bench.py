@@ -52,10 +52,12 @@ def parse_args():
                    help="step workload: concurrent slots (32 = BASELINE config 2; 64 = the C=64 roofline target)")
     p.add_argument("--op-costs", action="store_true",
                    help="print the in-graph cost of each talker-layer op (28 chained launches per op) and exit")
-    p.add_argument("--workload", choices=["step", "serving"], default="step",
+    p.add_argument("--workload", choices=["step", "serving", "predictor", "codec"], default="step",
                    help="step: BASELINE config 2 (default); serving: BASELINE config 5, end-to-end ContinuousModel")
     p.add_argument("--concurrency", type=int, default=32, help="serving: requests in flight (closed loop)")
     p.add_argument("--requests", type=int, default=128, help="serving: synthetic requests per timed pass")
+    p.add_argument("--batch", type=int, default=64, help="predictor / codec: rows or streams (BASELINE configs 3, 4)")
+    p.add_argument("--frames", type=int, default=200, help="predictor: timed frames (BASELINE config 3)")
     return p.parse_args()
 
 
@@ -173,13 +175,16 @@ def measured_peaks():
 
 
 def profile_traffic(kernel: str):
-    """Per-launch DRAM bytes of `kernel` from the committed ncu summary, if present."""
-    path = ROOT / "profiles" / "traffic.json"
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary (profiles/traffic.md,
+    a `| kernel | bytes | ...` table row), if present."""
+    path = ROOT / "profiles" / "traffic.md"
     if not path.exists():
         return None
-    data = json.loads(path.read_text())
-    entry = data.get(kernel)
-    return None if entry is None else entry.get("dram_bytes_per_launch")
+    for line in path.read_text().splitlines():
+        cells = [c.strip() for c in line.strip().strip("|").split("|")]
+        if len(cells) >= 2 and cells[0] == kernel and cells[1].isdigit():
+            return int(cells[1])
+    return None
 
 
 # ---------------------------------------------------------------------- CPU baseline (oracle)
@@ -562,6 +567,91 @@ def run_serving(args) -> dict:
             "ttfa_p50_ms": pct(0.5) * 1e3, "ttfa_p95_ms": pct(0.95) * 1e3, "rtf": res["rtf"], "slots": slots}
 
 
+# BASELINE config 3 per predictor step: 5 layers (QKV, O, gate/up, down) + input projection +
+# one head, bf16 = 165.7 MB; one frame runs 15 steps.
+PREDICTOR_STEP_BYTES = (5 * (1024 * 4096 + 2048 * 1024 + 3 * 1024 * 3072) + 2048 * 1024 + 1024 * 2048) * 2
+
+
+def timed_region(fn, count: int) -> float:
+    """CUDA-event milliseconds of `count` calls of fn on the current stream; the region is also
+    bracketed by cudaProfilerStart/Stop (no-ops without a profiler) for ncu --profile-from-start off."""
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(count):
+        fn(i)
+    b.record()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    return a.elapsed_time(b)
+
+
+def run_predictor(args) -> dict:
+    """the 15-codebook code predictor for `batch` rows (64), Philox sampling
+    with T 0.9, top-k 50, top-p 0.95, over `frames` frames (200). One frame = PredictorStep.run:
+    the talker hidden state and first code of every row copied in, then one replay of the
+    captured chain (15 steps x 5 layers, heads, sampling, frame embedding). Inputs are
+    device-resident seeded N(0,1) hidden states and uniform first codes."""
+    from qwen3_tts_b200 import ops
+    from qwen3_tts_b200.config import PREDICTOR
+    from qwen3_tts_b200.predictor import PredictorStep
+    from qwen3_tts_b200.weights import decoder_weights, pack_decoder
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    B, F = args.batch, args.frames
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    weights = pack_decoder(decoder_weights(PREDICTOR, args.seed, dev), dev)
+    talker_emb = (torch.randn(3072, PREDICTOR.talker_hidden, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    step = PredictorStep(PREDICTOR, weights, talker_emb, B, dev, temperature=0.9, top_k=50, top_p=0.95,
+                         philox_seed=args.seed)
+    step.capture()
+    total = F + args.warmup
+    hidden = torch.randn(total, B, PREDICTOR.talker_hidden, generator=g, device=dev).to(torch.bfloat16)
+    first = torch.randint(0, 2048, (total, B), generator=g, device=dev)
+    offsets = torch.zeros(B, dtype=torch.long, device=dev)
+
+    def frame(i):
+        offsets.add_(16)  # each frame draws 15 Philox uniforms per row
+        step.run(hidden[i], first[i], offsets=offsets, clone=False)
+
+    for i in range(args.warmup):
+        frame(i)
+    ms = timed_region(lambda i: frame(args.warmup + i), F)
+    status = ops.read_status(dev)
+    step.close()
+    per_frame_bytes = 15 * PREDICTOR_STEP_BYTES
+    fps = B * F / (ms / 1e3)
+    peak, peak_kind = measured_peaks()
+    return {"frames_per_s": fps, "ms_per_frame": ms / F, "status": status,
+            "hbm_fraction": per_frame_bytes * (F / (ms / 1e3)) / (peak * 1e9), "peak_kind": peak_kind}
+
+
+def run_codec(args) -> dict:
+    """incremental codec decode of `batch` streams (64) in 4-frame chunks.
+    One step = CodecSlots.decode of every stream's next 4 frames (codes uniform over 2048,
+    seeded, device-resident): RVQ, pre-conv, 8-layer sliding-window transformer, upsampling,
+    decoder convolutions, PCM16, as one captured graph per (batch, frames)."""
+    from qwen3_tts_b200 import ops
+    from qwen3_tts_b200.codec import CodecSlots, pack_codec
+    from qwen3_tts_b200.codec_weights import random_codec
+    from qwen3_tts_b200.config import CODEC
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    B, T = args.batch, 4
+    codec = CodecSlots(CODEC, pack_codec(random_codec(CODEC, args.seed), dev), B, dev, max_chunk_frames=8)
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    total = args.steps + args.warmup
+    codes = torch.randint(0, CODEC.codebook_size, (total, B, CODEC.codebooks, T), generator=g, device=dev)
+    indices = list(range(B))
+    for i in range(args.warmup):
+        codec.decode(indices, codes[i])
+    ms = timed_region(lambda i: codec.decode(indices, codes[args.warmup + i]), args.steps)
+    status = ops.read_status(dev)
+    codec.close()
+    return {"frames_per_s": B * T * args.steps / (ms / 1e3), "ms_per_step": ms / args.steps, "status": status}
+
+
 def main():
     global SLOTS
     args = parse_args()
@@ -570,6 +660,26 @@ def main():
     SLOTS = args.slots
     if args.op_costs:
         op_costs(args)
+        return
+    if args.workload == "predictor":
+        res = run_predictor(args)
+        print(json.dumps({
+            "metric": f"codec frames/s (code predictor, batch {args.batch})", "value": res["frames_per_s"],
+            "unit": UNIT, "n_gpus": 1, "frames": args.frames, "warmup": args.warmup, "ms_per_frame": res["ms_per_frame"],
+            "higher_is_better": True, "dtype": "bf16", "data": "synthetic (seeded random-init weights, N(0,1) hidden)",
+            "config": {"workload": "BASELINE config 3: 15-codebook predictor, T 0.9, top-k 50, top-p 0.95, Philox",
+                       "batch": args.batch},
+            "hbm_fraction": res["hbm_fraction"], "peak_kind": res["peak_kind"], "status_word": res["status"]}))
+        return
+    if args.workload == "codec":
+        res = run_codec(args)
+        print(json.dumps({
+            "metric": f"codec frames/s (incremental codec decode, {args.batch} streams x 4-frame chunks)",
+            "value": res["frames_per_s"], "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": res["ms_per_step"], "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic (seeded random-init codec, uniform codes)",
+            "config": {"workload": "BASELINE config 4: incremental codec decode", "streams": args.batch,
+                       "chunk_frames": 4}, "status_word": res["status"]}))
         return
     if args.workload == "serving":
         res = run_serving(args)

@@ -23,7 +23,6 @@
 #include "host.cuh"
 
 #include <mutex>
-#include <stdlib.h>
 #include <string.h>
 
 using namespace q3t;
@@ -742,13 +741,6 @@ void choose_splits(Plan& p) {
     if (ctas > target || per_split < 2 || (ctas > 64 && per_split < 4)) break;
     splits = next;
   }
-#ifdef Q3T_TUNING
-  // tuning builds only: force the split count (a power of two <= 8, >= 2 k-blocks per split)
-  if (const char* forced = getenv("Q3T_SPLITS")) {
-    const int s = atoi(forced);
-    if (s >= 1 && s <= 8 && (s & (s - 1)) == 0 && p.kblocks >= 2 * s) splits = s;
-  }
-#endif
   p.splits = splits;
 }
 
