@@ -57,6 +57,8 @@ def parse_args():
     p.add_argument("--concurrency", type=int, default=32, help="serving: requests in flight (closed loop)")
     p.add_argument("--requests", type=int, default=128, help="serving: synthetic requests per timed pass")
     p.add_argument("--batch", type=int, default=64, help="predictor / codec: rows or streams (BASELINE configs 3, 4)")
+    p.add_argument("--codec-streams", type=int, default=1, choices=[1, 2],
+                   help="serving: codec decode lanes (ContinuousModel codec_streams)")
     p.add_argument("--frames", type=int, default=200, help="predictor: timed frames (BASELINE config 3)")
     return p.parse_args()
 
@@ -528,7 +530,8 @@ def run_serving(args) -> dict:
     from qwen3_tts_b200.continuous import ContinuousModel
     dev = torch.device("cuda:0")
     slots = 1 << max(0, (args.concurrency - 1).bit_length())
-    model = ContinuousModel(None, dev, max_slots=slots, initial_capacity=1024, seed=args.seed, codec_batch_size=4)
+    model = ContinuousModel(None, dev, max_slots=slots, initial_capacity=1024, seed=args.seed, codec_batch_size=4,
+                            codec_streams=args.codec_streams)
     requests = serving_requests(args.seed, args.requests)
 
     def one_pass():
@@ -688,7 +691,8 @@ def main():
             "unit": UNIT, "n_gpus": 1, "higher_is_better": True, "dtype": "bf16",
             "data": "synthetic (BASELINE config 5 request recipe, seeded random-init weights)",
             "config": {"workload": "BASELINE config 5: talker -> code predictor -> incremental codec, closed loop",
-                       "concurrency": args.concurrency, "requests": args.requests, "slots": res["slots"]},
+                       "concurrency": args.concurrency, "requests": args.requests, "slots": res["slots"],
+                       "codec_streams": args.codec_streams},
             "ttfa_p50_ms": res["ttfa_p50_ms"], "ttfa_p95_ms": res["ttfa_p95_ms"], "rtf": res["rtf"],
             "frames": res["frames"], "wall_s": res["wall_s"]}))
         return

@@ -175,16 +175,21 @@ int q3t_linear_rownorm(const void* x, int64_t x_stride, int64_t rows, int64_t in
                        int64_t residual_stride, const void* scale, float eps, const void* weight_tiles,
                        unsigned* status, void* stream);
 
-/* q3t_linear (eps == 0) or q3t_linear_rownorm (eps > 0) that also pulls the next
- * kernel's weights into L2 while it runs: [prefetch, prefetch + prefetch_bytes)
- * is split over the CTAs and requested before the dependency wait, so the next
- * GEMM of a decode chain streams its weights from L2 (a hint only: no ordering,
- * no completion). prefetch 16-byte aligned, prefetch_bytes % 16 == 0; NULL or 0 = none. */
-int q3t_linear_prefetch(const void* x, int64_t x_stride, int64_t rows, int64_t in_features,
-                        const void* weight, int64_t out_features, const void* bias, void* out,
-                        int64_t out_stride, int out_dtype, int epilogue, const void* residual,
-                        int64_t residual_stride, const void* scale, float eps, const void* weight_tiles,
-                        const void* prefetch, size_t prefetch_bytes, unsigned* status, void* stream);
+/* Flags of q3t_linear_ex. */
+#define Q3T_LINEAR_KEEP_WEIGHTS 1 /* load the weight tiles evict-last (the chain re-reads them soon) */
+
+/* q3t_linear (eps == 0) or q3t_linear_rownorm (eps > 0) with two cache controls:
+ * - prefetch: [prefetch, prefetch + prefetch_bytes) (the next kernel's weights) is split
+ *   over the CTAs and pulled into L2 before the dependency wait (a hint only: no
+ *   ordering, no completion); 16-byte aligned, prefetch_bytes % 16 == 0; NULL or 0 = none;
+ * - flags: Q3T_LINEAR_KEEP_WEIGHTS loads this GEMM's weight tiles with L2 evict-last
+ *   priority instead of evict-first (the code predictor keeps part of its layers in L2
+ *   across its 15 codebook steps, continuous.py:49-68). */
+int q3t_linear_ex(const void* x, int64_t x_stride, int64_t rows, int64_t in_features,
+                  const void* weight, int64_t out_features, const void* bias, void* out,
+                  int64_t out_stride, int out_dtype, int epilogue, const void* residual,
+                  int64_t residual_stride, const void* scale, float eps, const void* weight_tiles,
+                  const void* prefetch, size_t prefetch_bytes, int flags, unsigned* status, void* stream);
 
 /* Pre-swizzled weight layout for q3t_linear (pass it as weight_tiles, weight may
  * then be NULL): tile (n, k) of 128 rows x 64 columns is the contiguous 16 KB image

@@ -183,6 +183,14 @@ Q3T_DEV void prefetch_l2(const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
                : "memory");
 }
+// Untiled bulk copy global -> shared with an L2 cache policy (createpolicy); same alignment.
+Q3T_DEV void bulk_load_hint(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
 // Untiled bulk copy global -> shared; both addresses 16-byte aligned, bytes % 16 == 0.
 Q3T_DEV void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(

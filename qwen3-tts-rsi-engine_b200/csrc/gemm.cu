@@ -70,6 +70,10 @@ struct GemmArgs {
   // split evenly over this grid's CTAs and requested at kernel start
   const uint8_t* prefetch;
   uint64_t prefetch_bytes;
+  // L2 priority of the weight tiles: 0 = normal (several row tiles read each weight tile),
+  // 1 = evict-first (one row tile: streamed once), 2 = evict-last (Q3T_LINEAR_KEEP_WEIGHTS:
+  // weights a chain re-reads soon, the code predictor's layers once per codebook step).
+  int weight_policy;
   // Implicit causal convolution (conv_taps > 0): the activations are a padded buffer
   // [batch, pad + frames, channels] (3-D tensor map); k-block kb covers tap j = kb / conv_cblocks,
   // channels (kb % conv_cblocks) * 64 + [0, 64), and reads frames t + shift(j) of the stream, with
@@ -189,7 +193,10 @@ Q3T_DEV void load_weights(uint8_t* dst, const CUtensorMap* tmw, const GemmArgs& 
                           uint64_t pol) {
   if (a.tiles != nullptr) {
     const size_t tile = size_t(n0 / kTileN) * size_t(a.kblocks) + size_t(kb);
-    bulk_load(dst, a.tiles + tile * size_t(kABytes), uint32_t(kABytes), bar);
+    if (a.weight_policy != 0)
+      bulk_load_hint(dst, a.tiles + tile * size_t(kABytes), uint32_t(kABytes), bar, pol);
+    else
+      bulk_load(dst, a.tiles + tile * size_t(kABytes), uint32_t(kABytes), bar);
   } else {
     tma_load_2d(dst, tmw, bar, kb * kTileK, n0, pol);
   }
@@ -305,7 +312,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // ---------------- TMA producer: weight tiles of the first ring slots go out before the
       // dependency wait (weights never depend on the previous kernel), activations after it.
-      const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
+      const uint64_t pol_w = a.weight_policy == 2 ? policy_evict_last() : policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
       auto load_act = [&](uint8_t* dst, uint64_t* bar, int kb) {
         if (a.conv_taps) {
           const int j = kb / a.conv_cblocks, cb = kb - j * a.conv_cblocks;
@@ -830,7 +838,7 @@ namespace {
 int linear_impl(const void* x, int64_t x_stride, int64_t rows, int64_t in_features, const void* weight,
                 int64_t out_features, const void* bias, void* out, int64_t out_stride, int out_dtype, int epilogue,
                 const void* residual, int64_t residual_stride, const void* scale, float row_norm_eps,
-                const void* weight_tiles, const void* prefetch, size_t prefetch_bytes, unsigned* status,
+                const void* weight_tiles, const void* prefetch, size_t prefetch_bytes, int flags, unsigned* status,
                 void* stream) {
   if (!x || (!weight && !weight_tiles) || !out) return fail(Q3T_EINVAL, "linear: null pointer");
   if (prefetch != nullptr && (!aligned16(prefetch) || prefetch_bytes % 16))
@@ -885,6 +893,7 @@ int linear_impl(const void* x, int64_t x_stride, int64_t rows, int64_t in_featur
   a.norm_eps = row_norm_eps;
   a.prefetch = prefetch_bytes ? static_cast<const uint8_t*>(prefetch) : nullptr;
   a.prefetch_bytes = prefetch_bytes;
+  a.weight_policy = (flags & Q3T_LINEAR_KEEP_WEIGHTS) ? 2 : p.m_tiles == 1 ? 1 : 0;
   a.tma_out = p.splits == 1 && p.bn >= 64 && epilogue != Q3T_EPI_SWIGLU_PAIRED && out_dtype == Q3T_BF16 &&
               staged_maps(maps, p.bn, out_features, out, out_stride, residual, residual_stride, rows, 1, 0);
   a.status = status;
@@ -908,7 +917,7 @@ extern "C" int q3t_linear(const void* x, int64_t x_stride, int64_t rows, int64_t
   (void)workspace;
   (void)workspace_bytes;
   return linear_impl(x, x_stride, rows, in_features, weight, out_features, bias, out, out_stride, out_dtype, epilogue,
-                     residual, residual_stride, scale, 0.f, weight_tiles, nullptr, 0, status, stream);
+                     residual, residual_stride, scale, 0.f, weight_tiles, nullptr, 0, 0, status, stream);
 }
 
 extern "C" int q3t_linear_rownorm(const void* x, int64_t x_stride, int64_t rows, int64_t in_features,
@@ -918,17 +927,19 @@ extern "C" int q3t_linear_rownorm(const void* x, int64_t x_stride, int64_t rows,
                                   unsigned* status, void* stream) {
   if (!(eps > 0.f)) return fail(Q3T_EINVAL, "linear_rownorm: eps must be positive");
   return linear_impl(x, x_stride, rows, in_features, weight, out_features, bias, out, out_stride, out_dtype, epilogue,
-                     residual, residual_stride, scale, eps, weight_tiles, nullptr, 0, status, stream);
+                     residual, residual_stride, scale, eps, weight_tiles, nullptr, 0, 0, status, stream);
 }
 
-extern "C" int q3t_linear_prefetch(const void* x, int64_t x_stride, int64_t rows, int64_t in_features,
-                                   const void* weight, int64_t out_features, const void* bias, void* out,
-                                   int64_t out_stride, int out_dtype, int epilogue, const void* residual,
-                                   int64_t residual_stride, const void* scale, float eps, const void* weight_tiles,
-                                   const void* prefetch, size_t prefetch_bytes, unsigned* status, void* stream) {
-  if (!(eps >= 0.f)) return fail(Q3T_EINVAL, "linear_prefetch: eps must be >= 0");
+extern "C" int q3t_linear_ex(const void* x, int64_t x_stride, int64_t rows, int64_t in_features, const void* weight,
+                             int64_t out_features, const void* bias, void* out, int64_t out_stride, int out_dtype,
+                             int epilogue, const void* residual, int64_t residual_stride, const void* scale,
+                             float eps, const void* weight_tiles, const void* prefetch, size_t prefetch_bytes,
+                             int flags, unsigned* status, void* stream) {
+  if (!(eps >= 0.f)) return fail(Q3T_EINVAL, "linear_ex: eps must be >= 0");
+  if (flags & ~Q3T_LINEAR_KEEP_WEIGHTS) return fail(Q3T_EINVAL, "linear_ex: unknown flags");
   return linear_impl(x, x_stride, rows, in_features, weight, out_features, bias, out, out_stride, out_dtype, epilogue,
-                     residual, residual_stride, scale, eps, weight_tiles, prefetch, prefetch_bytes, status, stream);
+                     residual, residual_stride, scale, eps, weight_tiles, prefetch, prefetch_bytes, flags, status,
+                     stream);
 }
 
 extern "C" int q3t_conv_linear(const void* xs, int64_t batch, int64_t frames, int64_t pad, int64_t channels,

@@ -15,6 +15,7 @@ LIBRARY_PATH = _HERE / "libq3t_b200.so"
 Q3T_OK, Q3T_EINVAL, Q3T_EUNSUPPORTED, Q3T_ECUDA, Q3T_ESPACE = 0, -1, -2, -3, -4
 Q3T_BF16, Q3T_F32 = 0, 1
 EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU_PAIRED, EPI_RESIDUAL_SCALED, EPI_GELU, EPI_SILU, EPI_SNAKE = 0, 1, 2, 3, 4, 5, 6
+LINEAR_KEEP_WEIGHTS = 1
 NORM_REFERENCE, NORM_NATIVE = 0, 1
 
 _p = ctypes.c_void_p
@@ -48,8 +49,8 @@ SIGNATURES: dict[str, tuple[object, list]] = {
                                   _p, _p]),
     "q3t_linear": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _p, _p, _i64, _i32, _i32, _p, _i64, _p, _p, _p, _sz,
                           _p, _p]),
-    "q3t_linear_prefetch": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _p, _p, _i64, _i32, _i32, _p, _i64, _p, _f32,
-                                   _p, _p, _sz, _p, _p]),
+    "q3t_linear_ex": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _p, _p, _i64, _i32, _i32, _p, _i64, _p, _f32, _p, _p,
+                             _sz, _i32, _p, _p]),
     "q3t_weight_tiles_bytes": (_sz, [_i64, _i64]),
     "q3t_pack_weight_tiles": (_i32, [_p, _i64, _i64, _p, _p]),
     "q3t_qk_norm_rope_kv": (_i32, [_p, _i64, _p, _p, _f32, _p, _p, _i64, _p, _p, _p, _p, _p, _i64, _i64, _p, _i64,

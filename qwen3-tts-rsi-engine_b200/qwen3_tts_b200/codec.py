@@ -386,9 +386,11 @@ class CodecSlots:
     """Slot-indexed incremental codec (codec_slots.py:133-338 surface)."""
 
     def __init__(self, cfg: CodecConfig, packed: dict, slots: int, device, max_chunk_frames: int = 8,
-                 use_graphs: bool = True, max_positions: int = 1 << 14):
+                 use_graphs: bool = True, max_positions: int = 1 << 14, streams: int = 1):
         if slots < 1:
             raise ValueError("Codec slots must be positive")
+        if streams not in (1, 2):
+            raise ValueError("Codec streams must be 1 or 2")
         if not 1 <= max_chunk_frames <= RING - cfg.window:
             raise ValueError("Codec maximum chunk must fit the KV ring")
         self.cfg, self.packed, self.slots = cfg, packed, slots
@@ -397,10 +399,14 @@ class CodecSlots:
         self.state = CodecState(cfg, packed, slots, self.device)
         self.cos, self.sin = rope_tables(max_positions, cfg.head_dim, cfg.theta, self.device)
         self.use_graphs = use_graphs
-        self.graphs: dict[tuple[int, int], CodecStep] = {}
+        self.graphs: dict[tuple, CodecStep] = {}
+        # Two lanes (codec_slots.py:279-305): groups of one call alternate between two streams,
+        # each lane with its own graphs and buffers, fenced before decode_groups returns.
+        self.stream_count = streams
+        self.lanes = [torch.cuda.Stream(device=self.device) for _ in range(streams)] if streams == 2 else []
 
-    def _graph(self, batch: int, length: int) -> CodecStep:
-        key = (batch, length)
+    def _graph(self, batch: int, length: int, lane: int = 0) -> CodecStep:
+        key = (batch, length) if self.stream_count == 1 else (batch, length, lane)
         step = self.graphs.get(key)
         if step is None:
             step = CodecStep(self.cfg, self.packed, self.state, batch, length, self.cos, self.sin)
@@ -421,24 +427,46 @@ class CodecSlots:
             raise ValueError("Codec warmup batch must fit the slot arena")
         for batch in range(1, max_batch + 1):
             for length in range(1, self.max_chunk_frames + 1):
-                self._graph(batch, length)
+                for lane in range(self.stream_count):
+                    self._graph(batch, length, lane)
 
-    def decode(self, indices, codes):
+    def decode(self, indices, codes, lane: int = 0):
         """Decode new codes of the given slots -> (wave fp32 [b, len*1920], pcm16 [b, len*1920])."""
         indices = list(indices)
         self._validate(indices, codes)
-        return self._graph(len(indices), codes.shape[-1]).run(torch.tensor(indices, device=self.device), codes)
+        return self._graph(len(indices), codes.shape[-1], lane).run(torch.tensor(indices, device=self.device), codes)
 
     def decode_groups(self, groups, on_output=None):
-        """Decode several (indices, codes) groups in order (codec_slots.py:241-305 surface).
-
-        Every group is enqueued on the current stream; `on_output(i, output)` is
-        called as each group's (wave, pcm) clone is enqueued. Returns the outputs."""
+        """Decode several (indices, codes) groups (codec_slots.py:241-305 surface); the groups'
+        slots are disjoint. With one stream they are enqueued in order on the current stream;
+        with two, group i runs on lane i % 2 after the current stream's pending work, and the
+        current stream waits for both lanes before this returns (so resets and moves that
+        follow are ordered after the decodes). `on_output(i, output)` gets each (wave, pcm)."""
+        if self.stream_count == 1 or len(groups) < 2:
+            outputs = []
+            for index, (indices, codes) in enumerate(groups):
+                outputs.append(self.decode(indices, codes))
+                if on_output is not None:
+                    on_output(index, outputs[-1])
+            return outputs
+        producer = torch.cuda.current_stream(self.device)
+        for lane in self.lanes:
+            lane.wait_stream(producer)
         outputs = []
-        for index, (indices, codes) in enumerate(groups):
-            outputs.append(self.decode(indices, codes))
+        try:
+            for index, (indices, codes) in enumerate(groups):
+                lane = self.lanes[index % 2]
+                with torch.cuda.stream(lane):
+                    codes.record_stream(lane)
+                    outputs.append(self.decode(indices, codes, lane=index % 2))
+        finally:
+            for lane in self.lanes:
+                producer.wait_stream(lane)
+        for index, (wave, pcm) in enumerate(outputs):
+            wave.record_stream(producer)
+            pcm.record_stream(producer)
             if on_output is not None:
-                on_output(index, outputs[-1])
+                on_output(index, (wave, pcm))
         return outputs
 
     def reset(self, slot: int) -> None:

@@ -220,7 +220,8 @@ class ContinuousModel:
                                   self.device)
         if incremental_codec:
             self.codec = CodecSlots(codec_config, packed_codec, max_slots, self.device,
-                                    max_chunk_frames=codec_chunk_frames, use_graphs=use_graphs)
+                                    max_chunk_frames=codec_chunk_frames, use_graphs=use_graphs,
+                                    streams=codec_streams)
             if prewarm_codec:
                 self.codec.prewarm(min(codec_batch_size, max_slots))
         else:
@@ -397,11 +398,19 @@ class ContinuousModel:
             start = state.emitted if self.incremental_codec else max(0, state.emitted - self.context)
             groups.setdefault(state.frames - start, []).append((state, start, (state.emitted - start) * 1920))
         pending = []
+        lanes = []   # with two codec streams: every group's (indices, codes), decoded on alternating lanes
         for length, entries in groups.items():
             for offset in range(0, len(entries), self.codec_batch_size):
                 group = entries[offset:offset + self.codec_batch_size]
                 indices = [slots[id(entry[0])] for entry in group]
-                pending.append((group, self._decode_group(indices, [entry[1] for entry in group], length)))
+                if self.incremental_codec and getattr(self, "codec_streams", 1) == 2:
+                    lanes.append((group, indices, self.codec_codes.read(indices, [entry[1] for entry in group],
+                                                                        length)))
+                else:
+                    pending.append((group, self._decode_group(indices, [entry[1] for entry in group], length)))
+        if lanes:
+            outputs = self.codec.decode_groups([(indices, codes) for _, indices, codes in lanes])
+            pending += [(group, out[1]) for (group, _, _), out in zip(lanes, outputs)]
         if not pending:
             return
         for (group, _), block in zip(pending, self._to_host([pcm for _, pcm in pending])):

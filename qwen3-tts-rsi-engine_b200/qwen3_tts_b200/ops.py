@@ -288,7 +288,7 @@ def pack_tiles(weight: torch.Tensor) -> TiledWeight:
 
 def linear(x, weight, bias=None, *, out=None, out_dtype=BF16, epilogue: int = _lib.EPI_STORE, residual=None,
            scale=None, row_norm_eps: Optional[float] = None, workspace: Optional[torch.Tensor] = None,
-           prefetch=None, tag: str = "linear"):
+           prefetch=None, keep_weights: bool = False, tag: str = "linear"):
     """out = x @ weight.T (+ bias) with a fused epilogue, on tcgen05 tensor cores.
 
     `weight` is a contiguous bf16 [out, in] tensor or a TiledWeight. With
@@ -296,7 +296,8 @@ def linear(x, weight, bias=None, *, out=None, out_dtype=BF16, epilogue: int = _l
     an RMSNorm of x folded into the GEMM (the norm weight must already be
     multiplied into `weight`, see weights.fold_norm). `prefetch` (a weight
     tensor or TiledWeight, normally the next GEMM's) is pulled into L2 while
-    this GEMM runs (q3t_linear_prefetch)."""
+    this GEMM runs; `keep_weights` loads the weight tiles evict-last so that a
+    chain that re-reads them finds them in L2 (q3t_linear_ex)."""
     tiled = isinstance(weight, TiledWeight)
     _need_cuda(x, weight.tiles if tiled else weight)
     if x.dtype != BF16 or (not tiled and (weight.dtype != BF16 or weight.ndim != 2 or not weight.is_contiguous())):
@@ -316,15 +317,16 @@ def linear(x, weight, bias=None, *, out=None, out_dtype=BF16, epilogue: int = _l
     if residual is not None:
         res2 = residual.reshape(rows, n_out) if residual.is_contiguous() else residual
     odt = _lib.Q3T_BF16 if out.dtype == BF16 else _lib.Q3T_F32
-    if prefetch is not None:
+    if prefetch is not None or keep_weights:
         pre = prefetch.tiles if isinstance(prefetch, TiledWeight) else prefetch
-        _need_cuda(pre)
-        call("q3t_linear_prefetch", x2.data_ptr(), x2.stride(0), rows, in_features,
+        if pre is not None:
+            _need_cuda(pre)
+        call("q3t_linear_ex", x2.data_ptr(), x2.stride(0), rows, in_features,
              None if tiled else weight.data_ptr(), n_rows_w, _ptr(bias), out2.data_ptr(), out2.stride(0), odt,
              epilogue, _ptr(res2), res2.stride(0) if res2 is not None else 0, _ptr(scale),
              float(row_norm_eps) if row_norm_eps is not None else 0.0, weight.tiles.data_ptr() if tiled else None,
-             pre.data_ptr(), (pre.numel() * pre.element_size()) // 16 * 16, status_word(x.device).data_ptr(),
-             _stream())
+             _ptr(pre), (pre.numel() * pre.element_size()) // 16 * 16 if pre is not None else 0,
+             _lib.LINEAR_KEEP_WEIGHTS if keep_weights else 0, status_word(x.device).data_ptr(), _stream())
         return out
     if row_norm_eps is not None:
         call("q3t_linear_rownorm", x2.data_ptr(), x2.stride(0), rows, in_features,

@@ -68,6 +68,9 @@ class PredictorStep:
         self.ws_attn = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
         self.status = ops.status_word(dev)
         self.prefetch_weights = True  # GEMMs pull the next GEMM's weights into L2
+        # The first layers' weights are loaded evict-last so that they stay in L2 across the
+        # 15 codebook steps (3 of the 5 layers: 90 MB of the 126 MB L2).
+        self.keep_layers = 3
         self.graph = None
 
     def _layers(self, rows: int, length: int, positions: torch.Tensor, tail=None) -> None:
@@ -81,11 +84,13 @@ class PredictorStep:
         for i, layer in enumerate(layers):
             keys, values = self.cache[i], self.cache[L + i]
             following = layers[i + 1].qkv if i + 1 < L else tail
+            keep = i < self.keep_layers
             if layer.folded:
-                lw(x, layer.qkv, out=self.qkv[:rows], row_norm_eps=cfg.eps, prefetch=pf(layer.o))
+                lw(x, layer.qkv, out=self.qkv[:rows], row_norm_eps=cfg.eps, prefetch=pf(layer.o), keep_weights=keep)
             else:
                 ops.rms_norm(x, layer.input_norm, cfg.eps, out=self.xn[:rows])
-                lw(self.xn[:rows], layer.qkv, out=self.qkv[:rows], workspace=self.ws_linear, prefetch=pf(layer.o))
+                lw(self.xn[:rows], layer.qkv, out=self.qkv[:rows], workspace=self.ws_linear, prefetch=pf(layer.o),
+                   keep_weights=keep)
             if length == 1:
                 # one query row per slot: q/k norm, RoPE and the K/V write run inside attention
                 ops.decode_attention_qkv(self.qkv[:rows], layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin,
@@ -99,16 +104,16 @@ class PredictorStep:
                 ops.decode_attention(self.q[:rows], keys, values, positions, context=keys.shape[2],
                                      rows_per_slot=length, out=self.attn[:rows], workspace=self.ws_attn)
             lw(self.attn[:rows].view(rows, cfg.q_width), layer.o, out=x, epilogue=_lib.EPI_RESIDUAL, residual=x,
-               workspace=self.ws_linear, prefetch=pf(layer.gate_up))
+               workspace=self.ws_linear, prefetch=pf(layer.gate_up), keep_weights=keep)
             if layer.folded:
                 lw(x, layer.gate_up, out=self.act[:rows], epilogue=_lib.EPI_SWIGLU_PAIRED, row_norm_eps=cfg.eps,
-                   prefetch=pf(layer.down))
+                   prefetch=pf(layer.down), keep_weights=keep)
             else:
                 ops.rms_norm(x, layer.post_norm, cfg.eps, out=self.xn[:rows])
                 lw(self.xn[:rows], layer.gate_up, out=self.act[:rows], epilogue=_lib.EPI_SWIGLU_PAIRED,
-                   workspace=self.ws_linear, prefetch=pf(layer.down))
+                   workspace=self.ws_linear, prefetch=pf(layer.down), keep_weights=keep)
             lw(self.act[:rows], layer.down, out=x, epilogue=_lib.EPI_RESIDUAL, residual=x, workspace=self.ws_linear,
-               prefetch=pf(following) if following is not None else None)
+               prefetch=pf(following) if following is not None else None, keep_weights=keep)
         if not self.w.get("heads_folded", False):
             ops.rms_norm(x, self.w["norm"], self.cfg.eps, out=self.xn[:rows])
 

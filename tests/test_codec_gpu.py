@@ -114,3 +114,30 @@ def test_full_size_codec_chunk_runs_clean(cuda):
     assert wave.shape == (64, 4 * 1920)
     assert torch.isfinite(wave).all()
     engine.close()
+
+
+def test_codec_two_lanes_match_one_lane(cuda):
+    """codec_streams=2 (codec_slots.py:279-305): the groups of one decode_groups call run on two
+    alternating streams with per-lane graphs; the audio and the per-slot state equal the
+    one-stream decode bit for bit, and a reset after the call is ordered after the lanes."""
+    from qwen3_tts_b200.codec import CodecSlots, pack_codec
+    cfg = small_cfg()
+    decoder = OC.randomize(OC.CodecDecoder(cfg), seed=11)
+    packed = pack_codec(decoder, cuda)
+    one = CodecSlots(cfg, packed, 6, cuda, max_chunk_frames=8, streams=1)
+    two = CodecSlots(cfg, packed, 6, cuda, max_chunk_frames=8, streams=2)
+    gen = torch.Generator().manual_seed(5)
+    for chunk in range(3):
+        groups = [([0, 3], 4), ([5], 2), ([1, 2], 4), ([4], 8)]
+        calls = [(idx, torch.randint(0, cfg.codebook_size, (len(idx), cfg.codebooks, n), generator=gen).to(cuda))
+                 for idx, n in groups]
+        out1 = one.decode_groups(calls)
+        out2 = two.decode_groups(calls)
+        for (w1, p1), (w2, p2) in zip(out1, out2):
+            assert torch.equal(w1, w2) and torch.equal(p1, p2)
+    two.reset(5)
+    one.reset(5)
+    for a, b in zip(one.state.buffers, two.state.buffers):
+        assert torch.equal(a, b)
+    one.close()
+    two.close()

@@ -247,7 +247,7 @@ def test_linear_fp32_bias_residual_and_strided_input(ops, cuda):
 @pytest.mark.parametrize("rows,k,n", [(32, 1024, 4096), (5000, 192, 192), (7680, 96, 96)])
 def test_linear_inplace_residual_and_l2_prefetch(ops, cuda, rows, k, n):
     """In-place residual epilogue (out aliases the residual, as the codec's residual units and the
-    decoder's O/down projections run it) against the fp32 reference, and q3t_linear_prefetch
+    decoder's O/down projections run it) against the fp32 reference, and q3t_linear_ex
     (next weights pulled into L2) bit-identical to the plain GEMM, with and without the row norm."""
     from qwen3_tts_b200 import _lib
     x = rnd(60 + rows, (rows, k), 1.0, BF16)
