@@ -733,20 +733,22 @@ bool staged_maps(Maps& m, int bn, int64_t out_features, const void* out, int64_t
 }
 
 
-// K splits: a power of two <= 8 (one thread-block cluster per tile), at most
-// ~1.33 CTAs per SM in total, each split at least two k-blocks, and at least
-// four once the grid exceeds 64 CTAs. (Measured in dependent launch chains of
-// the talker, predictor and codec projections at 8-128 rows: this pick was the
-// fastest split or within 5% of it for every shape; grids beyond ~200 CTAs, or
-// 2-k-block splits on grids of 128+, ran 10-50% slower; 16-CTA and 3- or 9-CTA
-// clusters ran 1.6-2x slower.)
+// K splits: a power of two <= 8 (one thread-block cluster per tile) with at most
+// ~1.33 CTAs per SM in total and at least two k-blocks per split; grids beyond 64
+// CTAs need four k-blocks per split, beyond 128 CTAs sixteen, and 8-CTA clusters
+// (the costliest reduction) six unless the grid has at most 64 CTAs. (Measured in
+// dependent launch chains of every talker, predictor and codec projection at 8-128
+// rows, splits 1-8: this pick is the fastest power of two or within 5% of it;
+// 3-, 5- and 6-CTA clusters were no faster, 16-CTA clusters 1.6-2x slower.)
 void choose_splits(Plan& p) {
   const int base = p.n_tiles * p.m_tiles;
   const int target = sm_count() + sm_count() / 3;
   int splits = 1;
   while (splits < 8) {
     const int next = splits * 2, ctas = base * next, per_split = p.kblocks / next;
-    if (ctas > target || per_split < 2 || (ctas > 64 && per_split < 4)) break;
+    if (ctas > target || per_split < 2 || (ctas > 64 && per_split < 4) || (ctas > 128 && per_split < 16) ||
+        (next == 8 && ctas > 64 && per_split < 6))
+      break;
     splits = next;
   }
   p.splits = splits;

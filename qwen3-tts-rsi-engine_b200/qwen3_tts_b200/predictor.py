@@ -68,9 +68,9 @@ class PredictorStep:
         self.ws_attn = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
         self.status = ops.status_word(dev)
         self.prefetch_weights = True  # GEMMs pull the next GEMM's weights into L2
-        # The first layers' weights are loaded evict-last so that they stay in L2 across the
-        # 15 codebook steps (3 of the 5 layers: 90 MB of the 126 MB L2).
-        self.keep_layers = 3
+        # Layers [0, keep_layers) load their weights evict-last (Q3T_LINEAR_KEEP_WEIGHTS) to keep them
+        # in L2 across the 15 codebook steps; measured no faster (the GEMMs are latency-bound), so off.
+        self.keep_layers = 0
         self.graph = None
 
     def _layers(self, rows: int, length: int, positions: torch.Tensor, tail=None) -> None:
