@@ -73,7 +73,11 @@ class Dist:
         if self.enabled:
             import datetime
             import torch.distributed as dist
-            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+            kwargs = {}
+            if backend == "nccl":  # one GPU per rank, bound before the group forms
+                torch.cuda.set_device(self.local)
+                kwargs["device_id"] = torch.device("cuda", self.local)
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kwargs)
 
     def barrier(self):
         if self.enabled:
