@@ -532,11 +532,19 @@ def run_serving(args) -> dict:
     frames/s = codec frames delivered / wall time; TTFA = submission -> first PCM chunk;
     RTF = mean request latency / mean request audio duration."""
     from qwen3_tts_b200.continuous import ContinuousModel
-    dev = torch.device("cuda:0")
     slots = 1 << max(0, (args.concurrency - 1).bit_length())
-    model = ContinuousModel(None, dev, max_slots=slots, initial_capacity=1024, seed=args.seed, codec_batch_size=4,
-                            codec_streams=args.codec_streams)
-    requests = serving_requests(args.seed, args.requests)
+    engine = dict(max_slots=slots, initial_capacity=1024, seed=args.seed, codec_batch_size=4,
+                  codec_streams=args.codec_streams)
+    gpus = max(1, args.gpus)
+    if gpus > 1:
+        # request-level data parallelism: one engine process per GPU behind the host dispatcher,
+        # `concurrency` requests in flight per GPU
+        from qwen3_tts_b200.dispatcher import Dispatcher
+        model = Dispatcher.start(gpus, engine, per_engine=args.concurrency)
+    else:
+        model = ContinuousModel(None, torch.device("cuda:0"), **engine)
+    concurrency = args.concurrency * gpus
+    requests = serving_requests(args.seed, args.requests * gpus)
 
     def one_pass():
         pending = list(enumerate(requests))
@@ -549,7 +557,7 @@ def run_serving(args) -> dict:
         start = time.perf_counter()
         while pending or in_flight:
             subs = []
-            while pending and in_flight + len(subs) < args.concurrency:
+            while pending and in_flight + len(subs) < concurrency:
                 subs.append(pending.pop(0))
             now = time.perf_counter()
             for identifier, _ in subs:
@@ -571,7 +579,8 @@ def run_serving(args) -> dict:
     ttfa = res["ttfa"]
     pct = lambda q: ttfa[min(len(ttfa) - 1, int(q * len(ttfa)))]
     return {"frames_per_s": res["frames"] / res["wall_s"], "frames": res["frames"], "wall_s": res["wall_s"],
-            "ttfa_p50_ms": pct(0.5) * 1e3, "ttfa_p95_ms": pct(0.95) * 1e3, "rtf": res["rtf"], "slots": slots}
+            "ttfa_p50_ms": pct(0.5) * 1e3, "ttfa_p95_ms": pct(0.95) * 1e3, "rtf": res["rtf"], "slots": slots,
+            "gpus": gpus}
 
 
 # BASELINE config 3 per predictor step: 5 layers (QKV, O, gate/up, down) + input projection +
@@ -689,13 +698,15 @@ def main():
                        "chunk_frames": 4}, "status_word": res["status"]}))
         return
     if args.workload == "serving":
+        if int(os.environ.get("RANK", 0)) != 0:
+            return  # one host process drives every GPU through the dispatcher
         res = run_serving(args)
         print(json.dumps({
-            "metric": f"codec frames/s (end-to-end serving, C={args.concurrency})", "value": res["frames_per_s"],
-            "unit": UNIT, "n_gpus": 1, "higher_is_better": True, "dtype": "bf16",
+            "metric": f"codec frames/s (end-to-end serving, C={args.concurrency} per GPU)", "value": res["frames_per_s"],
+            "unit": UNIT, "n_gpus": res["gpus"], "higher_is_better": True, "dtype": "bf16",
             "data": "synthetic (BASELINE config 5 request recipe, seeded random-init weights)",
             "config": {"workload": "BASELINE config 5: talker -> code predictor -> incremental codec, closed loop",
-                       "concurrency": args.concurrency, "requests": args.requests, "slots": res["slots"],
+                       "concurrency": args.concurrency, "requests": args.requests * res["gpus"], "slots": res["slots"],
                        "codec_streams": args.codec_streams},
             "ttfa_p50_ms": res["ttfa_p50_ms"], "ttfa_p95_ms": res["ttfa_p95_ms"], "rtf": res["rtf"],
             "frames": res["frames"], "wall_s": res["wall_s"]}))
