@@ -7,9 +7,11 @@
 // rows, streams its 128 x K weight slab through a TMA/mbarrier ring into
 // 128-byte-swizzled shared memory and accumulates in TMEM. K is split across
 // the CTAs of a thread-block cluster (1..8 splits) so that ~2 CTAs per SM
-// stream weights; each CTA parks its fp32 tile in shared memory and the
-// cluster reduces the tiles through distributed shared memory in fixed rank
-// order (deterministic, no global scratch) and applies the fused epilogue.
+// stream weights; once every CTA of the cluster is past its MMAs, each pushes
+// its fp32 partials into the shared memory of the CTA that finalises those
+// features (distributed shared memory stores), and every CTA reduces its inbox
+// in fixed rank order (deterministic, no global scratch) and applies the fused
+// epilogue.
 //
 // Roles (256 threads): warp0.lane0 = TMA producer, warp1 = TMEM owner and
 // lane0 = MMA issuer, warps 2-3 = row sums of the folded RMSNorm, all eight
@@ -215,18 +217,8 @@ Q3T_DEV uint32_t map_peer(uint32_t local_smem, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_smem), "r"(rank));
   return remote;
 }
-Q3T_DEV float ld_peer1(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
-}
-Q3T_DEV float4 ld_peer4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
+Q3T_DEV void st_peer1(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 
 // One CTA = 128 weight rows x BN activation rows x one K slice. The CTAs of
@@ -485,9 +477,108 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
-  } else {
-    // Failure path first: outstanding ring loads must land before the ring
-    // is reused as the reduce buffer (bounded waits).
+  } else if (clustered) {
+    // ---------------- split-K reduction across the cluster, push form. After barrier A no
+    // CTA of the cluster reads its ring any more, so each CTA writes its fp32 partials
+    // straight into the shared memory of the CTA that finalises those features (slot =
+    // source rank); after barrier B every CTA reduces its inbox locally, in rank order
+    // (deterministic), and leaves without a further cluster barrier.
+    if (threadIdx.x == 0 && *abort_flag)  // outstanding ring loads land before the ring is an inbox
+      for (int j = *consumed; j < issued; ++j) mbar_wait(&full[j % S], (j / S) & 1, a.status, kStatusTmaTimeout);
+    __syncthreads();
+    cluster_sync();  // A
+    const int cs = a.splits;
+    const int rank = int(cluster_rank());
+    const int W = kTileN / cs;  // features this CTA finalises (cs is a power of two <= 8)
+    const int rs = W + 4;       // inbox row stride in floats; column W holds the partial row sums
+    float* inbox = reinterpret_cast<float*>(smem);  // [cs][BN][rs]
+    const uint32_t inbox_u32 = smem_u32(inbox);
+    int owner, fl;
+    if constexpr (EPI == Q3T_EPI_SWIGLU_PAIRED) {  // tile rows are [64 gate; 64 up]
+      const int hw = W / 2, rr = r < 64 ? r : r - 64;
+      owner = rr / hw;
+      fl = (r < 64 ? 0 : hw) + rr - owner * hw;
+    } else {
+      owner = r / W;
+      fl = r - owner * W;
+    }
+    const uint32_t dst = map_peer(inbox_u32, uint32_t(owner)) + uint32_t(rank * BN * rs + fl) * 4u;
+#pragma unroll 1
+    for (int c0 = 16 * half; c0 < BN; c0 += 32) {
+      float v[16];
+      tmem_ld16(taddr + c0, v);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) st_peer1(dst + uint32_t((c0 + j) * rs) * 4u, ok ? v[j] : 0.f);
+    }
+    if (a.row_norm && (warp == 2 || warp == 3))  // this CTA's partial row sums go to every owner
+#pragma unroll
+      for (int q = 0; q < RPT; ++q) {
+        const int m = threadIdx.x - 64 + 64 * q;
+        if (m < BN)
+          for (int o = 0; o < cs; ++o)
+            st_peer1(map_peer(inbox_u32, uint32_t(o)) + uint32_t((rank * BN + m) * rs + W) * 4u, ss[q]);
+      }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
+    cluster_sync();  // B: every partial has landed in its owner's inbox
+    const int mcount = (m_end - m0) < BN ? (m_end - m0) : BN;
+    auto row_scale = [&](int c) -> float {
+      float total = 0.f;
+      for (int j = 0; j < cs; ++j) total += inbox[(j * BN + c) * rs + W];
+      return 1.0f / sqrtf(total / float(a.in_features) + a.norm_eps);
+    };
+    if constexpr (EPI == Q3T_EPI_SWIGLU_PAIRED) {
+      const int hw = W / 2, nq = hw / 4;
+      const int units = mcount * nq;
+      for (int u = threadIdx.x; u < units; u += blockDim.x) {
+        const int c = u / nq;
+        const int f = (u % nq) * 4;  // local gate feature; its up partner sits at hw + f
+        float4 g = make_float4(0.f, 0.f, 0.f, 0.f), up = g;
+        for (int j = 0; j < cs; ++j) {
+          const float* row = inbox + (j * BN + c) * rs;
+          const float4 gv = *reinterpret_cast<const float4*>(row + f);
+          const float4 uv = *reinterpret_cast<const float4*>(row + hw + f);
+          g.x += gv.x; g.y += gv.y; g.z += gv.z; g.w += gv.w;
+          up.x += uv.x; up.y += uv.y; up.z += uv.z; up.w += uv.w;
+        }
+        if (a.row_norm) {
+          const float rn = row_scale(c);
+          g.x *= rn; g.y *= rn; g.z *= rn; g.w *= rn;
+          up.x *= rn; up.y *= rn; up.z *= rn; up.w *= rn;
+        }
+        const int ft = rank * hw + f;  // gate feature within the tile
+        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + int64_t(m0 + c) * a.out_stride + (n0 / 2 + ft);
+        const float gs[4] = {g.x, g.y, g.z, g.w}, us[4] = {up.x, up.y, up.z, up.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (n0 + 64 + ft + j < a.out_features) o[j] = __float2bfloat16_rn(silu_gate(bf16r(gs[j]), bf16r(us[j])));
+      }
+    } else {
+      const int nq = W / 4;
+      const int units = mcount * nq;
+      for (int u = threadIdx.x; u < units; u += blockDim.x) {
+        const int c = u / nq;
+        const int f = (u % nq) * 4;
+        const int n = n0 + rank * W + f;
+        const Inputs4 in = load_inputs4<EPI>(a, m0 + c, n);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = 0; j < cs; ++j) {
+          const float4 v = *reinterpret_cast<const float4*>(inbox + (j * BN + c) * rs + f);
+          acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+        }
+        float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+        if (a.row_norm) {
+          const float rn = row_scale(c);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) vals[j] *= rn;
+        }
+        store_features4<EPI>(a, m0 + c, n, vals, in);
+      }
+    }
+  } else if constexpr (EPI == Q3T_EPI_SWIGLU_PAIRED) {
+    // ---------------- one CTA per tile, paired SwiGLU: the tile goes through shared memory so
+    // that each thread finalises whole gate/up quad pairs
     if (threadIdx.x == 0 && *abort_flag)
       for (int j = *consumed; j < issued; ++j) mbar_wait(&full[j % S], (j / S) & 1, a.status, kStatusTmaTimeout);
     __syncthreads();
@@ -498,122 +589,34 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int j = 0; j < 16; ++j) red[(c0 + j) * C::kRedStride + r] = ok ? v[j] : 0.f;
     }
-    if (a.row_norm && (warp == 2 || warp == 3))  // this CTA's partial row sums ride in the padding column
+    if (a.row_norm && (warp == 2 || warp == 3))
 #pragma unroll
       for (int q = 0; q < RPT; ++q) {
         const int m = threadIdx.x - 64 + 64 * q;
-        if (m < BN) red[m * C::kRedStride + kTileN] = ss[q];
+        if (m < BN) rnorm[m] = 1.0f / sqrtf(ss[q] / float(a.in_features) + a.norm_eps);
       }
     tc_fence_before();
     __syncthreads();
     if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
-  }
-  if (threadIdx.x == 0 && !clustered && *abort_flag)
-    for (int j = *consumed; j < issued; ++j) mbar_wait(&full[j % S], (j / S) & 1, a.status, kStatusTmaTimeout);
-  if (!clustered && EPI != Q3T_EPI_SWIGLU_PAIRED) return;
-
-  // ---------------- split-K reduction across the cluster through DSMEM
-  if (clustered) cluster_sync();  // every peer's tile is in its shared memory
-  const int cs = a.splits;
-  const uint32_t rank = clustered ? cluster_rank() : 0u;
-  const int mcount = (m_end - m0) < BN ? (m_end - m0) : BN;
-  const uint32_t red_local = smem_u32(red);
-  // Every peer's partial quad (and, with the folded RMSNorm, its partial sum of squares of
-  // the row, kept in the padding column) is requested at once, after the unit's global
-  // epilogue inputs; the partials are then added in rank order, so every CTA of the
-  // cluster computes the same row scale and the result does not depend on timing.
-  constexpr int kMaxSplits = 8;
-  const uint32_t ss_col = uint32_t(kTileN) * 4u;
-  auto scale_of = [&](const float* ss) -> float {
-    float total = 0.f;
-#pragma unroll
-    for (int j = 0; j < kMaxSplits; ++j)
-      if (j < cs) total += ss[j];
-    return 1.0f / sqrtf(total / float(a.in_features) + a.norm_eps);
-  };
-  if constexpr (EPI == Q3T_EPI_SWIGLU_PAIRED) {
-    // this CTA finalises feature quads [q0, q1) of the 16 gate/up quad pairs
-    const int q0 = int(rank) * 16 / cs, nq = (int(rank) + 1) * 16 / cs - q0;
-    const int f0 = q0 * 4;
-    const int units = mcount * nq;
+    const int mcount = (m_end - m0) < BN ? (m_end - m0) : BN;
+    const int units = mcount * 16;
     for (int u = threadIdx.x; u < units; u += blockDim.x) {
-      const int c = u / nq;
-      const int f = f0 + (u % nq) * 4;
-      const uint32_t row = uint32_t(c * C::kRedStride) * 4u;
-      float4 gv[kMaxSplits], uv[kMaxSplits];
-      float ss[kMaxSplits];
-#pragma unroll
-      for (int j = 0; j < kMaxSplits; ++j) {
-        if (j < cs) {
-          if (clustered) {
-            const uint32_t base = map_peer(red_local, uint32_t(j)) + row;
-            gv[j] = ld_peer4(base + uint32_t(f) * 4u);
-            uv[j] = ld_peer4(base + uint32_t(64 + f) * 4u);
-            ss[j] = a.row_norm ? ld_peer1(base + ss_col) : 0.f;
-          } else {
-            gv[j] = *reinterpret_cast<const float4*>(red + c * C::kRedStride + f);
-            uv[j] = *reinterpret_cast<const float4*>(red + c * C::kRedStride + 64 + f);
-            ss[j] = a.row_norm ? red[c * C::kRedStride + kTileN] : 0.f;
-          }
-        }
-      }
-      float4 g = make_float4(0.f, 0.f, 0.f, 0.f), up = g;
-#pragma unroll
-      for (int j = 0; j < kMaxSplits; ++j) {
-        if (j < cs) {
-          g.x += gv[j].x; g.y += gv[j].y; g.z += gv[j].z; g.w += gv[j].w;
-          up.x += uv[j].x; up.y += uv[j].y; up.z += uv[j].z; up.w += uv[j].w;
-        }
-      }
+      const int c = u / 16;
+      const int f = (u % 16) * 4;
+      float4 g = *reinterpret_cast<const float4*>(red + c * C::kRedStride + f);
+      float4 up = *reinterpret_cast<const float4*>(red + c * C::kRedStride + 64 + f);
       if (a.row_norm) {
-        const float rn = scale_of(ss);
+        const float rn = rnorm[c];
         g.x *= rn; g.y *= rn; g.z *= rn; g.w *= rn;
         up.x *= rn; up.y *= rn; up.z *= rn; up.w *= rn;
       }
-      const int m = m0 + c;
-      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + int64_t(m) * a.out_stride + (n0 / 2 + f);
+      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + int64_t(m0 + c) * a.out_stride + (n0 / 2 + f);
       const float gs[4] = {g.x, g.y, g.z, g.w}, us[4] = {up.x, up.y, up.z, up.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         if (n0 + 64 + f + j < a.out_features) o[j] = __float2bfloat16_rn(silu_gate(bf16r(gs[j]), bf16r(us[j])));
     }
-  } else {
-    // this CTA finalises feature quads [q0, q1) of the tile's 32 (clustered only)
-    const int q0 = int(rank) * 32 / cs, nq = (int(rank) + 1) * 32 / cs - q0;
-    const int f0 = q0 * 4;
-    const int units = mcount * nq;
-    for (int u = threadIdx.x; u < units; u += blockDim.x) {
-      const int c = u / nq;
-      const int f = f0 + (u % nq) * 4;
-      const Inputs4 in = load_inputs4<EPI>(a, m0 + c, n0 + f);
-      const uint32_t row = uint32_t(c * C::kRedStride) * 4u;
-      float4 v[kMaxSplits];
-      float ss[kMaxSplits];
-#pragma unroll
-      for (int j = 0; j < kMaxSplits; ++j) {
-        if (j < cs) {
-          const uint32_t base = map_peer(red_local, uint32_t(j)) + row;
-          v[j] = ld_peer4(base + uint32_t(f) * 4u);
-          ss[j] = a.row_norm ? ld_peer1(base + ss_col) : 0.f;
-        }
-      }
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int j = 0; j < kMaxSplits; ++j) {
-        if (j < cs) {
-          acc.x += v[j].x; acc.y += v[j].y; acc.z += v[j].z; acc.w += v[j].w;
-        }
-      }
-      float vals[4] = {acc.x, acc.y, acc.z, acc.w};
-      if (a.row_norm) {
-        const float rn = scale_of(ss);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) vals[j] *= rn;
-      }
-      store_features4<EPI>(a, m0 + c, n0 + f, vals, in);
-    }
   }
-  if (clustered) cluster_sync();  // peers finished reading this CTA's shared memory
 }
 
 // Weight [N, K] row-major -> tiles [ceil(N/128)][ceil(K/64)] of the 128-byte-swizzled
