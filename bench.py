@@ -194,38 +194,43 @@ def profile_traffic(kernel: str):
 
 
 # ---------------------------------------------------------------------- CPU baseline (oracle)
-def cpu_decode_sample(cfg, positions, steps: int, sample_layers: int, seed: int):
+def cpu_decode_sample(cfg, positions, steps: int, sample_layers: int, seed: int, threads=(None,)):
     """Time the oracle's fp32 talker layers on the host cores for `steps` steps.
 
     Bounded sample: `sample_layers` of the 28 layers at full widths and the
     real ragged contexts; the per-step time is scaled by 28 / sample_layers.
+    Runs once per entry of `threads` (None = every host core) and returns
+    [(seconds per step, threads used)] in that order.
     """
     from dataclasses import replace
 
     from oracle import decoder as OD
     from qwen3_tts_b200.weights import decoder_weights
 
-    torch.set_num_threads(os.cpu_count() or 1)
     small = replace(cfg, layers=sample_layers)
     weights = decoder_weights(small, seed, device="cpu", dtype=torch.bfloat16)
     for layer in weights["layers"]:
         for key in list(layer):
             layer[key] = layer[key].float()
     cap = int(positions.max()) + steps + 2
-    cache = OD.new_cache(small, len(positions), cap)
     tables = OD.Tables(cap + 1, cfg.head_dim, cfg.theta)
     h = torch.randn(len(positions), 1, cfg.hidden) * 0.1
-    pos = positions.clone().view(-1, 1)
-    times = []
-    for _ in range(steps):
-        t0 = time.perf_counter()
-        x = h
-        for w, (ck, cv) in zip(weights["layers"], cache):
-            x = OD.layer_forward(small, w, x, pos, ck, cv, pos, tables, "fp32")
-        times.append(time.perf_counter() - t0)
-        pos = pos + 1
-    per_step = float(np.median(times)) * (cfg.layers / sample_layers)
-    return per_step, torch.get_num_threads()
+    results = []
+    for count in threads:
+        torch.set_num_threads(count or os.cpu_count() or 1)
+        cache = OD.new_cache(small, len(positions), cap)
+        pos = positions.clone().view(-1, 1)
+        times = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            x = h
+            for w, (ck, cv) in zip(weights["layers"], cache):
+                x = OD.layer_forward(small, w, x, pos, ck, cv, pos, tables, "fp32")
+            times.append(time.perf_counter() - t0)
+            pos = pos + 1
+        results.append((float(np.median(times)) * (cfg.layers / sample_layers), torch.get_num_threads()))
+    torch.set_num_threads(os.cpu_count() or 1)
+    return results
 
 
 # ---------------------------------------------------------------------- B200 arm
@@ -448,7 +453,7 @@ def run_reference(args, dist: Dist):
     from qwen3_tts_b200.config import TALKER
     work = Workload(args.seed)
     layers = 2
-    per_step, threads = cpu_decode_sample(TALKER, work.positions, args.warmup + args.steps, layers, args.seed)
+    [(per_step, threads)] = cpu_decode_sample(TALKER, work.positions, args.warmup + args.steps, layers, args.seed)
     value = SLOTS / per_step
     return {
         "metric": f"codec frames/s (talker decode step, C={SLOTS})", "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
@@ -793,10 +798,12 @@ def main():
         "clocks": res["clocks"],
     }
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        per_step, threads = cpu_decode_sample(cfg, positions, 3, 2, args.seed)
+        (per_step, threads), (per_step4, _) = cpu_decode_sample(cfg, positions, 3, 2, args.seed, (None, 4))
         line["cpu_baseline"] = {"value": SLOTS / per_step, "unit": UNIT, "cores": threads, "kind": "port",
+                                "value_4_threads": SLOTS / per_step4,
                                 "sample": f"oracle fp32 talker, 2 of 28 layers at full width, {SLOTS} slots, "
-                                          "same contexts, median of 3 steps scaled by 14"}
+                                          "same contexts, median of 3 steps scaled by 14; value_4_threads = the "
+                                          "same at 4 threads (the reference's default torch thread count)"}
     if dist.rank == 0:
         print(json.dumps(line))
     dist.close()

@@ -20,25 +20,34 @@ from .config import CodecConfig
 
 
 class _Draw:
-    def __init__(self, seed: int):
-        self.g = torch.Generator().manual_seed(seed)
+    """Seeded draws; with ``seed=None`` every draw is an uninitialised tensor of the same shape
+    (the tree a checkpoint is read into)."""
+
+    def __init__(self, seed):
+        self.g = None if seed is None else torch.Generator().manual_seed(seed)
+
+    def randn(self, *shape):
+        return torch.empty(shape) if self.g is None else torch.randn(shape, generator=self.g)
+
+    def rand(self, *shape):
+        return torch.empty(shape) if self.g is None else torch.rand(shape, generator=self.g)
 
     def matrix(self, *shape):
         fan_in = math.prod(shape[1:])
-        return torch.randn(shape, generator=self.g) * (0.5 / math.sqrt(fan_in))
+        return self.randn(*shape) * (0.5 / math.sqrt(fan_in))
 
     def bias(self, n):
-        return torch.randn(n, generator=self.g) * 0.02
+        return self.randn(n) * 0.02
 
     def norm(self, n):
-        return 1.0 + 0.02 * torch.randn(n, generator=self.g)
+        return 1.0 + 0.02 * self.randn(n)
 
     def scale(self, n):
-        return 0.1 + 0.02 * torch.randn(n, generator=self.g)
+        return 0.1 + 0.02 * self.randn(n)
 
     def snake(self, channels):
-        alpha = torch.log(0.5 + torch.rand(channels, generator=self.g))
-        return NS(alpha=alpha, beta=torch.randn(channels, generator=self.g) * 0.1, no_div_by_zero=1e-9)
+        alpha = torch.log(0.5 + self.rand(channels))
+        return NS(alpha=alpha, beta=self.randn(channels) * 0.1, no_div_by_zero=1e-9)
 
     def conv(self, c_in, c_out, k, dilation=1, groups=1):
         w = self.matrix(c_out, c_in // groups, k)
@@ -46,7 +55,7 @@ class _Draw:
                   padding=(k - 1) * dilation)
 
     def tconv(self, c_in, c_out, k, stride):
-        w = torch.randn(c_in, c_out, k, generator=self.g) * (0.5 / math.sqrt(c_in))
+        w = self.randn(c_in, c_out, k) * (0.5 / math.sqrt(c_in))
         return NS(conv=NS(weight=w, bias=self.bias(c_out), stride=(stride,)), right_pad=k - stride)
 
     def linear(self, c_in, c_out, bias=True):
@@ -54,11 +63,19 @@ class _Draw:
 
 
 def random_codec(cfg: CodecConfig, seed: int):
-    d = _Draw(seed)
+    return _codec_tree(cfg, _Draw(seed))
+
+
+def codec_template(cfg: CodecConfig):
+    """The codec tree with uninitialised tensors of the right shapes (filled from a checkpoint)."""
+    return _codec_tree(cfg, _Draw(None))
+
+
+def _codec_tree(cfg: CodecConfig, d: _Draw):
 
     def rvq(layers):
-        books = [NS(_codebook=NS(embedding_sum=torch.randn(cfg.codebook_size, cfg.codebook_dim, generator=d.g),
-                                 cluster_usage=0.5 + torch.rand(cfg.codebook_size, generator=d.g), epsilon=1e-5))
+        books = [NS(_codebook=NS(embedding_sum=d.randn(cfg.codebook_size, cfg.codebook_dim),
+                                 cluster_usage=0.5 + d.rand(cfg.codebook_size), epsilon=1e-5))
                  for _ in range(layers)]
         return NS(vq=NS(layers=books), output_proj=NS(weight=d.matrix(cfg.codebook_dim, cfg.codebook_dim, 1)))
 

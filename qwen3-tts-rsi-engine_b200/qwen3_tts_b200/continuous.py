@@ -28,12 +28,13 @@ called for every delivered chunk.
 from __future__ import annotations
 
 import logging
+from pathlib import Path
 from dataclasses import dataclass, field
 
 import numpy as np
 import torch
 
-from . import ops
+from . import checkpoint, ops
 from .batching import context_bucket, decode_batch_size, emission_target
 from .code_buffer import CodecCodeBuffer
 from .codec import CodecGraph, CodecSlots, pack_codec
@@ -158,11 +159,16 @@ class TickGraph:
 class ContinuousModel:
     """Drop-in for the reference ContinuousModel on one CUDA device.
 
-    ``model_path`` must be None: this build serves seeded random-init weights of
-    the 1.7B CustomVoice geometry (``seed``), or caller-provided weight dicts
-    (``weights={"talker", "predictor", "prompt"}``) and a codec decoder module
-    tree (``codec_decoder``). Reference flags that select between NPU kernel
-    variants are accepted and ignored (there is one CUDA path).
+    ``model_path`` is a checkpoint directory (``model.safetensors`` or a sharded
+    index, ``config.json``, and ``speech_tokenizer/model.safetensors`` for the
+    codec; ``checkpoint.load_model`` / ``checkpoint.load_codec``): the
+    geometry and prompt ids come from the checkpoint and override the config
+    arguments. With ``model_path=None`` the engine serves seeded random-init
+    weights of the 1.7B CustomVoice geometry (``seed``), or caller-provided
+    weight dicts (``weights={"talker", "predictor", "prompt"}``) and a codec
+    decoder module tree (``codec_decoder``); a checkpoint without a codec
+    directory gets the seeded codec. Reference flags that select between NPU
+    kernel variants are accepted and ignored (there is one CUDA path).
     """
 
     def __init__(self, model_path=None, device="cuda:0", max_slots=64, initial_capacity=512, *, seed: int = 0,
@@ -173,8 +179,6 @@ class ContinuousModel:
                  prewarm_prefill=False, bucket_prefill=True, max_frames=4096, max_prefill_batch=16, use_graphs=True,
                  temperature=0.9, top_k=50, top_p=1.0, subtalker_temperature=0.9, subtalker_top_k=50,
                  subtalker_top_p=1.0, penalty=1.05, **flags):
-        if model_path is not None:
-            raise ValueError("Checkpoint loading is not part of this build; pass model_path=None with a seed")
         if codec_chunk_frames not in (8, 16) or (codec_chunk_frames != 8 and not incremental_codec):
             raise ValueError("16-frame chunks require the incremental codec")
         if codec_streams not in (1, 2) or (codec_streams == 2 and not incremental_codec):
@@ -185,6 +189,13 @@ class ContinuousModel:
         self.flags = flags
         self.device = torch.device(device)
         torch.cuda.set_device(self.device)
+        if model_path is not None:
+            loaded = checkpoint.load_model(model_path, self.device, prompt_base=prompt_config)
+            talker_config, predictor_config = loaded["talker_config"], loaded["predictor_config"]
+            prompt_config, weights = loaded["prompt_config"], loaded["weights"]
+            codec_dir = Path(model_path) / "speech_tokenizer"
+            if codec_decoder is None and codec_dir.is_dir():
+                codec_decoder = checkpoint.load_codec(codec_dir, codec_config)
         self.max_slots, self.decode_bucket_step = max_slots, decode_bucket_step
         self.talker_config, self.predictor_config = talker_config, predictor_config
         self.codec_config, self.prompt_config = codec_config, prompt_config

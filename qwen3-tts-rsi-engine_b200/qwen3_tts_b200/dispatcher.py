@@ -41,7 +41,7 @@ def engine_main(rank: int, device: str, kwargs: dict, inbox, outbox, factory: st
     try:
         if factory is None:
             from qwen3_tts_b200.continuous import ContinuousModel
-            model = ContinuousModel(None, device, **kwargs)
+            model = ContinuousModel(device=device, **kwargs)
         else:
             model = _load(factory)(device=device, **kwargs)
         outbox.put(("hello", rank, list(model.speakers), list(model.languages)))

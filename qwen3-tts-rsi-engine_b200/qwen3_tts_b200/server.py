@@ -298,20 +298,23 @@ def engine_factory(options):
                   codec_batch_size=options.codec_batch_size, codec_chunk_frames=options.codec_chunk_frames,
                   incremental_codec=True, seed=options.seed, prewarm_codec=options.prewarm_codec,
                   decode_bucket_step=options.decode_bucket_step)
+    if str(options.model) != "random-init":   # a checkpoint directory (checkpoint.load_model)
+        kwargs["model_path"] = str(options.model)
     if options.gpus > 1:
         from .dispatcher import Dispatcher
         return lambda model, device: Dispatcher.start(options.gpus, kwargs, per_engine=options.max_batch_size)
 
     def build(model, device):
         from .continuous import ContinuousModel
-        return ContinuousModel(None, device, **kwargs)
+        return ContinuousModel(device=device, **kwargs)
     return build
 
 
 def main(argv=None) -> None:
     from aiohttp import web
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    parser.add_argument("--model", type=Path, default=Path("random-init"))
+    parser.add_argument("--model", type=Path, default=Path("random-init"),
+                        help="checkpoint directory, or random-init for seeded weights")
     parser.add_argument("--device", default="cuda:0")
     parser.add_argument("--gpus", type=int, default=1, help="engine processes, one per GPU")
     parser.add_argument("--seed", type=int, default=0, help="random-init weight seed")

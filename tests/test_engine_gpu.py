@@ -156,3 +156,39 @@ def test_engine_prompt_matches_oracle(cuda):
         builder.build(dict(PAYLOADS["a"], voice="nobody"))
     with pytest.raises(ValueError):
         builder.build(dict(PAYLOADS["a"], language="klingon"))
+
+
+def test_engine_from_checkpoint_matches_engine_from_weights(cuda, tmp_path):
+    """``ContinuousModel(model_path=...)`` over a safetensors checkpoint (sharded talker/predictor/
+    prompt file, config.json, codec under speech_tokenizer/) reads the geometry and weights the
+    weight-dict engine is given: the same codes, tokens and PCM, bit for bit."""
+    from qwen3_tts_b200 import checkpoint as C
+    from qwen3_tts_b200 import prompt as P
+    from qwen3_tts_b200.codec_weights import random_codec
+    from qwen3_tts_b200.continuous import ContinuousModel
+    from qwen3_tts_b200.weights import decoder_weights
+    tcfg, pcfg, prcfg, ccfg = configs()
+    tw, pw = decoder_weights(tcfg, 31, "cpu"), decoder_weights(pcfg, 32, "cpu")
+    prw, codec = P.prompt_weights(prcfg, 33, "cpu"), random_codec(ccfg, 34)
+    C.save_model(tmp_path, tw, pw, prw, tcfg, pcfg, prcfg, shards=2)
+    C.save_codec(tmp_path / "speech_tokenizer", codec)
+    common = dict(max_slots=4, initial_capacity=64, codec_config=ccfg, prompt_config=prcfg, top_k=1,
+                  subtalker_top_k=1, max_frames=64)
+    sources = [dict(talker_config=tcfg, predictor_config=pcfg, weights={"talker": tw, "predictor": pw, "prompt": prw},
+                    codec_decoder=codec), dict(model_path=str(tmp_path))]
+    runs = []
+    for source in sources:
+        engine = ContinuousModel(device=cuda, **common, **source)
+        assert engine.talker_config == tcfg and engine.predictor_config == pcfg
+        log, chunks, results = defaultdict(list), defaultdict(list), {}
+        engine.on_codes = lambda ident, frame, codes, token: log[ident].append((frame, codes, token))
+        for tick in range(48):
+            submissions = [(name, PAYLOADS[name]) for name in (("a", "c", "d") if tick == 0 else ())]
+            out = engine.tick(submissions, emit=lambda ident, pcm, rate: chunks[ident].append(pcm))
+            results.update(dict(out))
+            if not engine.states and tick > 0:
+                break
+        engine.close()
+        assert set(results) == {"a", "c", "d"}
+        runs.append((dict(log), dict(chunks), results))
+    assert runs[0] == runs[1]
