@@ -565,9 +565,12 @@ def run_serving(args) -> dict:
 
     A first pass over the same request set captures every graph shape (untimed); the
     second pass is timed on the host clock (the engine synchronises once per tick).
-    frames/s = codec frames delivered / wall time; TTFA = submission -> first PCM chunk;
-    RTF = mean request latency / mean request audio duration."""
+    Metrics follow the reference's service benchmark (``metrics.summarize``): frames/s =
+    delivered audio x 12.5 / wall time; TTFA = submission -> first PCM chunk (p50/p95,
+    interpolated); RTF = mean over requests of latency / audio duration. A request ends at
+    its synthetic target length (the max_new_tokens cap stands in for EOS at the target)."""
     from qwen3_tts_b200.continuous import ContinuousModel
+    from qwen3_tts_b200.metrics import summarize
     slots = 1 << max(0, (args.concurrency - 1).bit_length())
     engine = dict(max_slots=slots, initial_capacity=1024, seed=args.seed, codec_batch_size=4,
                   codec_streams=args.codec_streams)
@@ -588,7 +591,8 @@ def run_serving(args) -> dict:
         in_flight = 0
 
         def emit(identifier, pcm, rate):
-            first_audio.setdefault(identifier, time.perf_counter())
+            if len(pcm):
+                first_audio.setdefault(identifier, time.perf_counter())
 
         start = time.perf_counter()
         while pending or in_flight:
@@ -600,23 +604,25 @@ def run_serving(args) -> dict:
                 submitted[identifier] = now
             in_flight += len(subs)
             for identifier, result in model.tick(subs, emit=emit):
-                done[identifier] = time.perf_counter()
+                done[identifier] = (time.perf_counter(), result)
                 frames += result["codec_frames"]
                 in_flight -= 1
         wall = time.perf_counter() - start
-        ttfa = sorted(first_audio[i] - submitted[i] for i in submitted)
-        latency = [done[i] - submitted[i] for i in submitted]
-        audio_s = [(requests[i]["max_new_tokens"] - 1) / 12.5 for i in submitted]
-        return {"frames": frames, "wall_s": wall, "ttfa": ttfa, "rtf": float(np.mean(latency) / np.mean(audio_s))}
+        records = []
+        for i in submitted:
+            finished, result = done[i]
+            records.append({"success": result["finish_reason"] in ("stop", "length") and result["codec_frames"] > 0
+                            and i in first_audio, "audio_seconds": result["codec_frames"] / 12.5,
+                            "elapsed_seconds": finished - submitted[i],
+                            "ttfa_seconds": first_audio.get(i, finished) - submitted[i]})
+        return dict(summarize(records, wall, 12.5), frames=frames)
 
     one_pass()                       # graph capture for every (batch, context) and codec shape met
     res = one_pass()
     model.close()
-    ttfa = res["ttfa"]
-    pct = lambda q: ttfa[min(len(ttfa) - 1, int(q * len(ttfa)))]
-    return {"frames_per_s": res["frames"] / res["wall_s"], "frames": res["frames"], "wall_s": res["wall_s"],
-            "ttfa_p50_ms": pct(0.5) * 1e3, "ttfa_p95_ms": pct(0.95) * 1e3, "rtf": res["rtf"], "slots": slots,
-            "gpus": gpus}
+    return {"frames_per_s": res["throughput_frames_s"], "frames": res["frames"], "wall_s": res["wall_seconds"],
+            "ttfa_p50_ms": res["ttfa_p50_ms"], "ttfa_p95_ms": res["ttfa_p95_ms"], "rtf": res["rtf_mean"],
+            "status": res["status"], "failed_requests": res["failed_requests"], "slots": slots, "gpus": gpus}
 
 
 # BASELINE config 3 per predictor step: 5 layers (QKV, O, gate/up, down) + input projection +
@@ -745,7 +751,8 @@ def main():
                        "concurrency": args.concurrency, "requests": args.requests * res["gpus"], "slots": res["slots"],
                        "codec_streams": args.codec_streams},
             "ttfa_p50_ms": res["ttfa_p50_ms"], "ttfa_p95_ms": res["ttfa_p95_ms"], "rtf": res["rtf"],
-            "frames": res["frames"], "wall_s": res["wall_s"]}))
+            "frames": res["frames"], "wall_s": res["wall_s"], "status": res["status"],
+            "failed_requests": res["failed_requests"]}))
         return
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", 0))

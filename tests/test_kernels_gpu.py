@@ -540,6 +540,21 @@ def test_sample_boundary_cases(ops, cuda):
     assert got == [1, 3, 3]
 
 
+def test_sample_frequencies_and_permutation_equivariance(ops, cuda):
+    """p = (1/4, 3/4) over 10000 table draws: id 1 three times in four, equal to the oracle draw
+    for draw, and permuting rows permutes the tokens."""
+    draws = S.random_table(42, 1000).flatten()[:10000]
+    scores = torch.tensor([[0.0, 1.0986122886681098]]).repeat(len(draws), 1)
+    got = ops.sample(scores.to(cuda), uniforms=draws.to(cuda), temperature=1.0, top_k=2).flatten().cpu()
+    ref = S.categorical(scores, draws, temperature=1.0, top_k=2).flatten()
+    assert abs(got.float().mean().item() - 0.75) < 0.02
+    assert boundary_free(got, ref)
+    order = torch.randperm(len(draws), generator=torch.Generator().manual_seed(123))
+    permuted = ops.sample(scores[order].to(cuda), uniforms=draws[order].to(cuda), temperature=1.0,
+                          top_k=2).flatten().cpu()
+    assert torch.equal(permuted, got[order])
+
+
 def test_semantic_sampling_and_seen_update(ops, cuda):
     vocab, eos = 3072, 2150
     logits = bf16_scores(21, 128, vocab, 2.0).to(BF16)
