@@ -441,7 +441,16 @@ class CodecSlots:
         slots are disjoint. With one stream they are enqueued in order on the current stream;
         with two, group i runs on lane i % 2 after the current stream's pending work, and the
         current stream waits for both lanes before this returns (so resets and moves that
-        follow are ordered after the decodes). `on_output(i, output)` gets each (wave, pcm)."""
+        follow are ordered after the decodes). `on_output(i, output)` gets each (wave, pcm).
+        Every group is checked (slots in range, unique within and across groups, code shape and
+        type) before the first one is submitted, so an invalid later group launches nothing."""
+        groups = [(list(indices), codes) for indices, codes in groups]
+        claimed = set()
+        for indices, codes in groups:
+            self._validate(indices, codes)
+            if claimed.intersection(indices):
+                raise ValueError("Codec groups must use disjoint slots")
+            claimed.update(indices)
         if self.stream_count == 1 or len(groups) < 2:
             outputs = []
             for index, (indices, codes) in enumerate(groups):
