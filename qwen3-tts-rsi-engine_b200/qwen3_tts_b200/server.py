@@ -292,14 +292,120 @@ class SpeechService:
         return response
 
 
-def engine_factory(options):
-    """Model factory for one GPU (``--gpus 1``) or the multi-GPU dispatcher."""
+# Reference flags that choose between its NPU kernel variants or graph modes (server.py:265-309 of
+# the reference). Every one of these paths is the single CUDA path here, so they are accepted, checked
+# for the same combinations the reference rejects, passed to the engine as ignored flags, and do not
+# change the computation.
+VARIANT_FLAGS = ("talker_graph", "pack_qkv", "native_gqa", "text_only_rope", "triton_kv_update",
+                 "triton_talker_rope", "bucket_kv", "valid_length_kv", "graph_embeddings", "fixed_predictor_rope",
+                 "batch_audio_transfer", "reference_single", "graph_sampling", "triton_cdf", "direct_prompt",
+                 "native_rope", "fused_residual", "cache_codec_constants", "codec_code_buffer", "triton_snake",
+                 "cache_codec_codebooks", "pack_mlp", "fused_swiglu", "packed_kv_load", "single_request_views",
+                 "batch_prefill", "graph_prefill", "native_kv_update")
+
+
+def build_parser() -> argparse.ArgumentParser:
+    """The reference's command line (server.py:258-311) plus ``--gpus`` and ``--seed``."""
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    parser.add_argument("--model", type=Path, default=Path("random-init"),
+                        help="checkpoint directory, or random-init for seeded weights")
+    parser.add_argument("--device", default="cuda:0")
+    parser.add_argument("--gpus", type=int, default=1, help="engine processes, one per GPU")
+    parser.add_argument("--seed", type=int, default=0, help="random-init weight seed")
+    parser.add_argument("--host", default="127.0.0.1")
+    parser.add_argument("--port", type=int, default=8097)
+    parser.add_argument("--max-batch-size", type=int, default=1, help="slots per engine (power of two)")
+    parser.add_argument("--queue-size", type=int, default=128)
+    parser.add_argument("--batch-wait-ms", type=float, default=0)
+    parser.add_argument("--predictor-graph", nargs="?", const="step", choices=["step", "whole"])
+    parser.add_argument("--streaming", action="store_true")
+    parser.add_argument("--prewarm-codec", action="store_true")
+    parser.add_argument("--prewarm-prefill", action="store_true")
+    parser.add_argument("--codec-chunk-frames", type=int, choices=[8, 16], default=8)
+    parser.add_argument("--bucket-prefill", action="store_true")
+    parser.add_argument("--decode-bucket-step", type=int, default=0)
+    parser.add_argument("--native-rope-scope", choices=["all", "talker", "predictor"], default="all")
+    parser.add_argument("--rms-norm", choices=["native", "reference-rounding"])
+    parser.add_argument("--codec-left-context", type=int, default=72)
+    parser.add_argument("--codec-batch-size", type=int, choices=[1, 2, 4, 8], default=1)
+    parser.add_argument("--continuous", action="store_true",
+                        help="accepted; the server always runs the continuous engine")
+    parser.add_argument("--incremental-codec", action="store_true")
+    parser.add_argument("--codec-streams", type=int, choices=[1, 2], default=1)
+    parser.add_argument("--prefill-per-tick", type=int, default=4)
+    parser.add_argument("--prefill-interval", type=int, default=1)
+    for flag in VARIANT_FLAGS:
+        parser.add_argument("--" + flag.replace("_", "-"), action="store_true")
+    return parser
+
+
+def _rules(o) -> list:
+    """(rejected, message) for the flag combinations the reference rejects (server.py:313-373)."""
+    incremental = o.incremental_codec
+    needs_incremental = [(o.cache_codec_codebooks, "--cache-codec-codebooks"), (o.triton_snake, "--triton-snake"),
+                         (o.codec_code_buffer, "--codec-code-buffer"),
+                         (o.cache_codec_constants, "--cache-codec-constants"),
+                         (o.codec_streams == 2, "--codec-streams 2"), (o.prewarm_codec, "--prewarm-codec")]
+    return ([(not 1 <= o.prefill_interval <= 64, "--prefill-interval must be 1..64"),
+             (o.native_rope_scope != "all" and not o.native_rope, "--native-rope-scope requires --native-rope")]
+            + [(used and not incremental, f"{name} requires --continuous --incremental-codec")
+               for used, name in needs_incremental]
+            + [(o.fused_residual and o.rms_norm != "native", "--fused-residual requires --rms-norm native"),
+               (o.packed_kv_load and (not o.graph_prefill or o.reference_single),
+                "--packed-kv-load requires --continuous --graph-prefill without --reference-single"),
+               (o.prewarm_prefill and (not o.graph_prefill or o.reference_single),
+                "--prewarm-prefill requires --graph-prefill and excludes --reference-single"),
+               (o.codec_chunk_frames != 8 and (not incremental or o.codec_code_buffer),
+                "--codec-chunk-frames 16 requires continuous incremental codec without --codec-code-buffer"),
+               (o.triton_talker_rope and not o.text_only_rope, "--triton-talker-rope requires --continuous --text-only-rope"),
+               (o.triton_kv_update and not o.native_kv_update,
+                "--triton-kv-update requires --continuous --native-kv-update"),
+               (o.direct_prompt and o.reference_single, "--direct-prompt requires continuous mode without reference-single"),
+               (o.bucket_prefill and not o.graph_prefill, "--bucket-prefill requires --graph-prefill"),
+               (o.valid_length_kv and (not o.native_gqa or o.reference_single),
+                "--valid-length-kv requires continuous native GQA without reference-single"),
+               (min(o.max_batch_size, o.queue_size) <= 0 or o.batch_wait_ms < 0 or o.codec_left_context < 0,
+                "Invalid batch or queue settings"),
+               (o.prefill_per_tick < 1 or o.max_batch_size & (o.max_batch_size - 1),
+                "Continuous slots must be a power of two and prefill budget must be positive"),
+               (o.gpus < 1, "--gpus must be positive")])
+
+
+def parse_options(argv=None):
+    """Parse and cross-check the command line; errors exit through ``parser.error`` as the reference's do."""
+    parser = build_parser()
+    options = parser.parse_args(argv)
+    for rejected, message in _rules(options):
+        if rejected:
+            parser.error(message)
+    if options.decode_bucket_step:
+        from .batching import decode_batch_size
+        try:
+            decode_batch_size(1, options.max_batch_size, options.decode_bucket_step)
+        except ValueError as error:
+            parser.error(str(error))
+    options.continuous = True      # the batch (non-continuous) model path is not part of this build
+    return options
+
+
+def engine_kwargs(options) -> dict:
+    """ContinuousModel keyword arguments for the parsed command line."""
     kwargs = dict(max_slots=options.max_batch_size, codec_left_context=options.codec_left_context,
                   codec_batch_size=options.codec_batch_size, codec_chunk_frames=options.codec_chunk_frames,
-                  incremental_codec=True, seed=options.seed, prewarm_codec=options.prewarm_codec,
-                  decode_bucket_step=options.decode_bucket_step)
+                  incremental_codec=options.incremental_codec, codec_streams=options.codec_streams,
+                  seed=options.seed, prewarm_codec=options.prewarm_codec, prewarm_prefill=options.prewarm_prefill,
+                  bucket_prefill=options.bucket_prefill, decode_bucket_step=options.decode_bucket_step)
+    kwargs.update({flag: getattr(options, flag) for flag in VARIANT_FLAGS if getattr(options, flag, False)})
+    if getattr(options, "rms_norm", None):
+        kwargs["rms_norm"] = options.rms_norm
     if str(options.model) != "random-init":   # a checkpoint directory (checkpoint.load_model)
         kwargs["model_path"] = str(options.model)
+    return kwargs
+
+
+def engine_factory(options):
+    """Model factory for one GPU (``--gpus 1``) or the multi-GPU dispatcher."""
+    kwargs = engine_kwargs(options)
     if options.gpus > 1:
         from .dispatcher import Dispatcher
         return lambda model, device: Dispatcher.start(options.gpus, kwargs, per_engine=options.max_batch_size)
@@ -312,30 +418,7 @@ def engine_factory(options):
 
 def main(argv=None) -> None:
     from aiohttp import web
-    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    parser.add_argument("--model", type=Path, default=Path("random-init"),
-                        help="checkpoint directory, or random-init for seeded weights")
-    parser.add_argument("--device", default="cuda:0")
-    parser.add_argument("--gpus", type=int, default=1, help="engine processes, one per GPU")
-    parser.add_argument("--seed", type=int, default=0, help="random-init weight seed")
-    parser.add_argument("--host", default="127.0.0.1")
-    parser.add_argument("--port", type=int, default=8097)
-    parser.add_argument("--max-batch-size", type=int, default=64, help="slots per engine (power of two)")
-    parser.add_argument("--queue-size", type=int, default=512)
-    parser.add_argument("--streaming", action="store_true")
-    parser.add_argument("--prefill-per-tick", type=int, default=4)
-    parser.add_argument("--prefill-interval", type=int, default=1)
-    parser.add_argument("--codec-left-context", type=int, default=72)
-    parser.add_argument("--codec-batch-size", type=int, choices=[1, 2, 4, 8], default=4)
-    parser.add_argument("--codec-chunk-frames", type=int, choices=[8, 16], default=8)
-    parser.add_argument("--decode-bucket-step", type=int, default=0)
-    parser.add_argument("--prewarm-codec", action="store_true")
-    options = parser.parse_args(argv)
-    options.continuous = True
-    if options.max_batch_size < 1 or options.max_batch_size & (options.max_batch_size - 1):
-        parser.error("Continuous slots must be a power of two")
-    if options.prefill_per_tick < 1 or not 1 <= options.prefill_interval <= 64 or options.queue_size < 1:
-        parser.error("Invalid admission or queue settings")
+    options = parse_options(argv)
     logging.basicConfig(level=logging.INFO)
     factory = engine_factory(options)
     options.max_batch_size *= max(1, options.gpus)   # requests in flight across all engines
