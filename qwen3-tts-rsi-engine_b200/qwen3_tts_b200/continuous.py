@@ -28,6 +28,7 @@ called for every delivered chunk.
 from __future__ import annotations
 
 import logging
+import time
 from pathlib import Path
 from dataclasses import dataclass, field
 
@@ -48,6 +49,23 @@ from .weights import decoder_weights, pack_decoder
 
 BF16 = torch.bfloat16
 SAMPLE_RATE = 24000
+
+
+@dataclass
+class EngineStats:
+    """Per-engine counters, updated on the owner thread once per tick (served by /health)."""
+    ticks: int = 0
+    frames: int = 0           # codec frames decoded (one per active slot per tick)
+    admitted: int = 0
+    finished: int = 0
+    cancelled: int = 0
+    active: int = 0           # slots decoded by the last tick
+    batch: int = 0            # the last tick's decode batch bucket
+    last_tick_ms: float = 0.0
+    tick_seconds: float = 0.0
+
+    def as_dict(self) -> dict:
+        return dict(vars(self))
 
 
 @dataclass
@@ -240,6 +258,7 @@ class ContinuousModel:
                                     use_graphs=use_graphs)
         self.subtalker = dict(temperature=subtalker_temperature, top_k=subtalker_top_k, top_p=subtalker_top_p)
         self.states: list[RequestState] = []
+        self.stats = EngineStats()
         # Optional observer of every decoded frame: on_codes(identifier, frame, codes, next_token)
         # (one extra device->host copy per tick when set; used for auditing and parity checks).
         self.on_codes = None
@@ -489,14 +508,21 @@ class ContinuousModel:
     def tick(self, submissions=(), emit=None, cancelled=()):
         if self.device.type == "cuda":
             torch.cuda.set_device(self.device)
+        started = time.perf_counter()
+        stats = self.stats
         cancelled = set(cancelled)
         for index in reversed(range(len(self.states))):
             if self.states[index].identifier in cancelled:
                 self._remove(index)
+                stats.cancelled += 1
         if submissions:
+            before = len(self.states)
             self.admit_batch(submissions)
+            stats.admitted += len(self.states) - before
         if not self.states:
             return []
+        stats.active = len(self.states)
+        stats.batch = decode_batch_size(stats.active, self.max_slots, self.decode_bucket_step)
         tokens = self._run_tick(len(self.states))
         if self.on_codes is not None:
             self._report_codes(tokens)
@@ -516,6 +542,12 @@ class ContinuousModel:
             results.append((state.identifier, {"pcm": b"".join(state.audio), "sample_rate": SAMPLE_RATE,
                                                "codec_frames": state.frames, "finish_reason": reason}))
             self._remove(index)
+        elapsed = time.perf_counter() - started
+        stats.ticks += 1
+        stats.frames += stats.active
+        stats.finished += len(results)
+        stats.last_tick_ms = elapsed * 1e3
+        stats.tick_seconds += elapsed
         return results
 
     def close(self) -> None:

@@ -238,6 +238,9 @@ class SpeechService:
         state = "failed" if self.failure else "ready" if self.model else "starting"
         body = {"status": state, "queued": self.queue.qsize(), "backend": "b200",
                 "audio_delivery": "codec-windows" if self.streaming else "complete-waveform"}
+        stats = getattr(self.model, "stats", None)
+        if hasattr(stats, "as_dict"):
+            body["engine"] = stats.as_dict()
         return web.json_response(body, status=503 if self.failure else 200)
 
     async def speech(self, incoming):

@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from qwen3_tts_b200.continuous import ContinuousModel, RequestState
+from qwen3_tts_b200.continuous import ContinuousModel, EngineStats, RequestState
 
 EOS = 2150
 
@@ -27,6 +27,7 @@ def fake_engine(tokens_by_id, codec_batch_size=2, incremental=True, context=72):
     model.codec_batch_size = codec_batch_size
     model.context = context
     model.on_codes = None
+    model.stats = EngineStats()
     model.calls = {"decode": [], "move": []}
 
     def admit_batch(submissions):
@@ -118,3 +119,15 @@ def test_windowed_codec_decodes_left_context_and_skips_it():
 def test_tick_without_requests_is_a_no_op():
     model = fake_engine({})
     assert model.tick() == []
+
+
+def test_engine_counters_follow_the_ticks():
+    tokens = {1: [5] * 40, 2: [5, 5, EOS] + [5] * 40, 3: [5] * 40}
+    model = fake_engine(tokens)
+    model.tick([(1, {"max_new_tokens": 30}), (2, {"max_new_tokens": 30}), (3, {"max_new_tokens": 30})])
+    model.tick(cancelled=[3])
+    model.tick()                                  # request 2 draws EOS on its third frame
+    stats = model.stats.as_dict()
+    assert (stats["ticks"], stats["admitted"], stats["cancelled"], stats["finished"]) == (3, 3, 1, 1)
+    assert stats["frames"] == 3 + 2 + 2 and stats["active"] == 2 and stats["batch"] == 2
+    assert stats["tick_seconds"] >= stats["last_tick_ms"] / 1e3 > 0
