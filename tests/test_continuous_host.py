@@ -131,3 +131,27 @@ def test_engine_counters_follow_the_ticks():
     assert (stats["ticks"], stats["admitted"], stats["cancelled"], stats["finished"]) == (3, 3, 1, 1)
     assert stats["frames"] == 3 + 2 + 2 and stats["active"] == 2 and stats["batch"] == 2
     assert stats["tick_seconds"] >= stats["last_tick_ms"] / 1e3 > 0
+
+
+@pytest.mark.parametrize("mode", ["timed", "nvtx"])
+def test_phase_tracing_wraps_and_restores(mode):
+    from qwen3_tts_b200.tracing import instrument
+    tokens = {1: [5] * 40}
+    model = fake_engine(tokens)
+    originals = {name: vars(model).get(name) for name in ("admit_batch", "_run_tick", "_decode_group", "tick")}
+    trace = instrument(model, mode)
+    model.tick([(1, {"max_new_tokens": 30})], emit=lambda *a: None)
+    model.tick(emit=lambda *a: None)
+    assert trace.tick == 2
+    if mode == "timed":
+        phases = [(r["phase"], r["tick"]) for r in trace.records]
+        assert ("admit", 0) in phases and ("tick_graph", 0) in phases and ("tick_graph", 1) in phases
+        assert ("codec", 1) in phases          # the first chunk (2 frames) is due at the second tick
+        summary = trace.summary()
+        assert summary["tick_graph"]["calls"] == 2 and summary["tick_graph"]["seconds"] >= 0
+    else:
+        assert trace.records == []
+    trace.remove()
+    assert {name: vars(model).get(name) for name in originals} == originals
+    with pytest.raises(ValueError):
+        instrument(model, "perf")
