@@ -117,7 +117,8 @@ class Workload:
 
 # ---------------------------------------------------------------------- clocks
 class ClockSampler:
-    """Samples SM clock, power and clock-event reasons every 200 ms through NVML (read-only)."""
+    """Samples SM clock, power and clock-event reasons every 10 ms through NVML (read-only), so that a
+    timed region of a tenth of a second still gets several samples."""
 
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
 
@@ -150,7 +151,7 @@ class ClockSampler:
                     self.samples.append((sm, reasons, power))
                 except Exception:
                     pass
-                self.stop_flag.wait(0.2)
+                self.stop_flag.wait(0.01)
 
         self.thread = threading.Thread(target=loop, daemon=True)
         self.thread.start()
