@@ -5,10 +5,55 @@ The expected history is kept in plain Python lists: frame f of a slot is the
 codes written for it at f, and a read of ``length`` frames from ``start``
 returns them as [codebooks, length] for each requested slot.
 """
+from pathlib import Path
+
+import numpy as np
 import pytest
 import torch
 
 from qwen3_tts_b200.code_buffer import CodecCodeBuffer
+
+FIXTURE = np.load(Path(__file__).resolve().parent / "golden" / "decode_path.npz")["code_buffer_reads"]
+
+
+class ListRing:
+    """CPU restatement of the ring (codec_code_buffer.py:5-31): frame f of slot s is row s * 8 + f % 8."""
+
+    def __init__(self, slots, codebooks):
+        self.rows = [[0] * codebooks for _ in range(slots * 8)]
+
+    def write(self, codes, frames):
+        for i, (row, frame) in enumerate(zip(codes.tolist(), frames.tolist())):
+            self.rows[i * 8 + frame % 8] = row
+
+    def read(self, slots, starts, length):
+        return torch.tensor([[self.rows[s * 8 + (start + k) % 8] for k in range(length)]
+                             for s, start in zip(slots, starts)]).transpose(1, 2)
+
+    def move(self, source, destination):
+        self.rows[destination * 8:destination * 8 + 8] = [list(r) for r in self.rows[source * 8:source * 8 + 8]]
+
+
+def reference_sequence(buffer, to_device):
+    """The write/read/move sequence tests/golden/make_golden.py ran on the reference's buffer."""
+    reads = []
+    for tick in range(19):
+        buffer.write(to_device(torch.arange(48).view(3, 16) + tick * 100), to_device(torch.tensor([tick, tick + 3,
+                                                                                                      tick + 7])))
+        if tick >= 7:
+            reads.append(buffer.read([2, 0], [tick, tick - 7], 8).cpu().numpy())
+    buffer.move(2, 0)
+    reads.append(buffer.read([0], [18], 8).cpu().numpy())
+    return np.stack([r if r.shape[0] == 2 else np.concatenate([r, r]) for r in reads])
+
+
+def test_ring_restatement_matches_the_reference_fixture():
+    assert np.array_equal(reference_sequence(ListRing(4, 16), lambda t: t), FIXTURE)
+
+
+@pytest.mark.gpu
+def test_cuda_ring_matches_the_reference_fixture(cuda):
+    assert np.array_equal(reference_sequence(CodecCodeBuffer(4, 16, cuda), lambda t: t.to(cuda)), FIXTURE)
 
 
 @pytest.mark.parametrize("slots,starts,length", [([], [], 2), ([0], [0], 9), ([4], [0], 2), ([0], [-1], 2),

@@ -110,3 +110,23 @@ def test_module_imports_without_torch():
     out = subprocess.run([sys.executable, "-c", code, rv.__file__], capture_output=True, text=True, timeout=60)
     assert out.returncode == 0, out.stderr
     assert out.stdout.strip() == "single_request_inputs"
+
+
+def test_views_match_the_reference_fixture():
+    """The state tests/golden/make_golden.py gave the reference's single_request_inputs."""
+    from pathlib import Path
+    import json
+    import numpy as np
+    golden = Path(__file__).resolve().parent / "golden"
+    arrays = np.load(golden / "decode_path.npz")
+    meta = json.loads((golden / "decode_path.json").read_text())
+    g = torch.Generator().manual_seed(42)
+    state = SimpleNamespace(token=torch.tensor([[42]]), hidden=torch.randn(1, 1, 12, generator=g),
+                            uniforms=torch.rand(129, 16, generator=g), trailing=torch.randn(1, 3, 12, generator=g),
+                            pad=torch.randn(1, 1, 12, generator=g), seen=torch.zeros(1, 31, dtype=torch.bool),
+                            frames=2, position=165, rope_delta=-13)
+    views = single_request_inputs(state)
+    assert np.array_equal(views.draws.numpy(), arrays["views_draws"])
+    assert np.array_equal(views.text.numpy(), arrays["views_text"])
+    assert np.array_equal(views.uniforms.numpy(), arrays["views_uniforms"])
+    assert [int(views.positions[0]), int(views.rotary[0, 0, 0]), int(views.steps[0])] == meta["views_integers"]
