@@ -120,6 +120,16 @@ class Checkpoint:
     def keys(self) -> set:
         return self._keys
 
+    def close(self) -> None:
+        """Release the open file handles (tensors already read stay valid)."""
+        self._handles.clear()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
     def __contains__(self, key: str) -> bool:
         return key in self._keys
 
@@ -247,7 +257,10 @@ def load_model(path, device="cpu", dtype=BF16, prompt_base: PromptConfig = PROMP
     "predictor", "prompt"}}`` with the weight dicts in the layout of ``weights.decoder_weights``
     and ``prompt.prompt_weights``; all shapes are checked before the first tensor is read.
     """
-    ckpt = path if isinstance(path, Checkpoint) else Checkpoint(path)
+    if not isinstance(path, Checkpoint):
+        with Checkpoint(path) as ckpt:
+            return load_model(ckpt, device, dtype, prompt_base)
+    ckpt = path
     tcfg, pcfg, prcfg = read_configs(ckpt, prompt_base)
     prefix = ckpt.prefix(HEAD_SUFFIX, "talker output head") + "talker."
     pp = prefix + "code_predictor."
@@ -391,7 +404,10 @@ def load_codec(path, cfg: CodecConfig = CODEC):
     """A codec module tree for ``codec.pack_codec`` from a safetensors file or directory
     (``model.safetensors`` there), with every tensor's shape checked against ``cfg``."""
     from .codec_weights import codec_template
-    ckpt = path if isinstance(path, Checkpoint) else Checkpoint(path)
+    if not isinstance(path, Checkpoint):
+        with Checkpoint(path) as ckpt:
+            return load_codec(ckpt, cfg)
+    ckpt = path
     prefix = ckpt.prefix(CODEC_ANCHOR, "codec pre-conv")
     tree = codec_template(cfg)
     for key, parent, name in list(_leaves(tree)):
