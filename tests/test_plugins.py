@@ -91,8 +91,8 @@ def test_packed_weights_follow_the_reference_layout():
 
 
 def test_fake_reference_cache_paths_agree():
-    """The fp32 stand-ins the GPU tests compare against: prefill + decode through either cache equals
-    one pass over the whole sequence."""
+    """The fp32 stand-ins the GPU tests compare against: prefill + decode through the concatenating
+    cache equals one pass over the whole sequence."""
     m = Q.randomize(Q.TinyDecoder(layers=2, talker=False), 5)
     x = torch.randn(2, 6, 256, generator=torch.Generator().manual_seed(6))
     pos = torch.arange(6).repeat(2, 1)
