@@ -246,7 +246,9 @@ int q3t_decode_attention(const void* query, const void* keys, const void* values
  * (row, kv head) pairs (a power of two times the default chunk). Later
  * q3t_decode_attention / _qkv calls on the same workspace (one query row per slot, no
  * window) use it; without a plan, or with a stale one, results are identical and only
- * the split differs. positions: int64 [rows]. */
+ * the split differs. positions: int64 [rows]. Part of the replacement of the talker's
+ * fused attention call (npu_attention.py:11-26), whose NPU operator splits the keys
+ * internally; here the split is planned once per step instead of once per layer. */
 int q3t_attention_plan(const int64_t* positions, int64_t rows, int64_t q_heads, int64_t kv_heads,
                        int64_t head_dim, int64_t context, void* workspace, size_t workspace_bytes,
                        void* stream);
