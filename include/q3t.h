@@ -191,7 +191,9 @@ int q3t_linear_ex(const void* x, int64_t x_stride, int64_t rows, int64_t in_feat
                   int64_t residual_stride, const void* scale, float eps, const void* weight_tiles,
                   const void* prefetch, size_t prefetch_bytes, int flags, unsigned* status, void* stream);
 
-/* Pre-swizzled weight layout for q3t_linear (pass it as weight_tiles, weight may
+/* Weight re-layout done once at load, in place of the reference's packed QKV and gate/up
+ * concatenations (packed_attention.py:17-22, packed_mlp.py:13-14).
+ * Pre-swizzled weight layout for q3t_linear (pass it as weight_tiles, weight may
  * then be NULL): tile (n, k) of 128 rows x 64 columns is the contiguous 16 KB image
  * of the 128-byte-swizzled shared-memory tile, tiles ordered [n][k], zero padded.
  * Each pipeline stage then streams one contiguous 16 KB block from HBM. */
@@ -315,7 +317,9 @@ int q3t_sample(const void* logits, int logits_dtype, int64_t logits_stride, cons
                uint8_t* seen_out, int64_t seen_out_stride, int64_t rows, int64_t width,
                void* stream);
 
-/* Philox4x32-10 uniforms in [0, 1): out[i] = u(key=seed, counter={offset + i/4 lo, hi, 0, 0})[i%4]. */
+/* Device-side uniforms for sampling without a host table (the reference draws its
+ * per-request tables on the host, sampling.py:17-19).
+ * Philox4x32-10 uniforms in [0, 1): out[i] = u(key=seed, counter={offset + i/4 lo, hi, 0, 0})[i%4]. */
 int q3t_philox_uniforms(uint64_t seed, uint64_t offset, float* out, int64_t count, void* stream);
 
 /* ------------------------------------------------------------------ embeddings */
@@ -331,7 +335,9 @@ int q3t_frame_embed(const int64_t* codes, int64_t codes_stride, const void* firs
                     int64_t group_vocab, const void* text, int64_t text_stride, void* out,
                     int64_t batch, int64_t hidden, unsigned* status, void* stream);
 
-/* Row gather out[r] = table[ids[r]] (embedding lookup, bf16 rows of `hidden`). */
+/* Replaces the token embedding lookups of continuous.py:584 (talker.get_input_embeddings())
+ * and custom_voice_prompt.py:38-63 (text embedding).
+ * Row gather out[r] = table[ids[r]] (embedding lookup, bf16 rows of `hidden`). */
 int q3t_embedding(const int64_t* ids, int64_t ids_stride, const void* table, int64_t vocab,
                   void* out, int64_t out_stride, int64_t rows, int64_t hidden, unsigned* status,
                   void* stream);
@@ -378,7 +384,9 @@ int q3t_conv_pad(const void* x, int64_t x_stride, int64_t batch, int64_t frames,
                  const void* history, int64_t history_len, const int64_t* slots, const float* alpha,
                  const float* inverse_beta, void* xs, void* stream);
 
-/* Causal conv (kernel `taps`, `dilation`) as an implicit tcgen05 GEMM over q3t_conv_pad's
+/* Replaces the codec's causal and transposed conv modules as IncrementalCodec.run_module
+ * applies them (incremental_codec.py:53-65).
+ * Causal conv (kernel `taps`, `dilation`) as an implicit tcgen05 GEMM over q3t_conv_pad's
  * buffer xs [batch, pad + frames, channels]: k-block (tap j, 64 channels) streams frames
  * t + j*dilation (or t + (taps-1-j)*dilation with reverse: transposed convs' [x[t] | x[t-1]])
  * of its stream straight from xs through a 3-D TMA map, so no im2col copy is written.
