@@ -762,10 +762,7 @@ def main():
         print(json.dumps(run_reference(args, Dist.__new__(Dist))))
         return
     dist = Dist("nccl")
-    try:
-        res = run_b200(args, dist)
-    finally:
-        pass
+    res = run_b200(args, dist)
     cfg = res["cfg"]
     frames = SLOTS * args.steps * dist.world
     seconds = res["elapsed_ms"] / 1e3

@@ -332,7 +332,13 @@ def model_state_dict(talker: dict, predictor: dict, prompt: dict, prefix: str = 
     tp = prefix + "text_projection."
     out[tp + "linear_fc1.weight"], out[tp + "linear_fc1.bias"] = prompt["fc1"], prompt["fc1_bias"]
     out[tp + "linear_fc2.weight"], out[tp + "linear_fc2.bias"] = prompt["fc2"], prompt["fc2_bias"]
-    return {k: v.detach().to("cpu").contiguous() for k, v in out.items()}
+    return {k: _owned(v) for k, v in out.items()}
+
+
+def _owned(tensor: torch.Tensor) -> torch.Tensor:
+    """A CPU tensor that owns its storage (safetensors refuses tensors that share one)."""
+    t = tensor.detach().to("cpu").contiguous()
+    return t if t.untyped_storage().nbytes() == t.numel() * t.element_size() else t.clone()
 
 
 def model_config_json(talker: TalkerConfig, predictor: PredictorConfig, prompt: PromptConfig) -> dict:
