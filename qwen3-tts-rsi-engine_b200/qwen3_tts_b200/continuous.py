@@ -550,6 +550,24 @@ class ContinuousModel:
         stats.tick_seconds += elapsed
         return results
 
+    def generate(self, payloads, emit=None):
+        """The batch API of the reference's CustomVoiceModel.generate (model.py:58-129): run
+        `payloads` to completion and return one result record per payload, in order;
+        `emit(index, pcm, sample_rate)` streams audio chunks under the payload's index. Served by
+        the continuous tick: at most `max_slots` requests in flight, the rest admitted as slots
+        free up. Raises ValueError while continuous requests are active (one mode at a time)."""
+        if self.states:
+            raise ValueError("generate() needs an idle engine; continuous requests are active")
+        pending = [(("batch", index), payload) for index, payload in enumerate(payloads)]
+        relay = None if emit is None else (lambda ident, pcm, rate: emit(ident[1], pcm, rate))
+        results = {}
+        while pending or self.states:
+            free = self.max_slots - len(self.states)
+            submissions, pending = pending[:free], pending[free:]
+            for ident, record in self.tick(submissions, emit=relay):
+                results[ident[1]] = record
+        return [results[index] for index in range(len(payloads))]
+
     def close(self) -> None:
         logging.getLogger(__name__).info("Captured graph shapes: prefill=%s tick=%s codec=%s", sorted(self.prefills),
                                          sorted(self.graphs), sorted(self.codec.slots.graphs

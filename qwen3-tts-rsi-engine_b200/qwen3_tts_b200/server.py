@@ -332,7 +332,7 @@ def build_parser() -> argparse.ArgumentParser:
     parser.add_argument("--codec-left-context", type=int, default=72)
     parser.add_argument("--codec-batch-size", type=int, choices=[1, 2, 4, 8], default=1)
     parser.add_argument("--continuous", action="store_true",
-                        help="accepted; the server always runs the continuous engine")
+                        help="continuous admission through tick(); without it, micro-batches through generate()")
     parser.add_argument("--incremental-codec", action="store_true")
     parser.add_argument("--codec-streams", type=int, choices=[1, 2], default=1)
     parser.add_argument("--prefill-per-tick", type=int, default=4)
@@ -344,34 +344,46 @@ def build_parser() -> argparse.ArgumentParser:
 
 def _rules(o) -> list:
     """(rejected, message) for the flag combinations the reference rejects (server.py:313-373)."""
-    incremental = o.incremental_codec
+    cont, incremental = o.continuous, o.incremental_codec
     needs_incremental = [(o.cache_codec_codebooks, "--cache-codec-codebooks"), (o.triton_snake, "--triton-snake"),
                          (o.codec_code_buffer, "--codec-code-buffer"),
                          (o.cache_codec_constants, "--cache-codec-constants"),
                          (o.codec_streams == 2, "--codec-streams 2"), (o.prewarm_codec, "--prewarm-codec")]
-    return ([(not 1 <= o.prefill_interval <= 64, "--prefill-interval must be 1..64"),
+    needs_continuous = [(o.single_request_views, "--single-request-views"), (incremental, "--incremental-codec"),
+                        (o.batch_prefill, "--batch-prefill"), (o.graph_prefill, "--graph-prefill"),
+                        (o.triton_cdf, "--triton-cdf"), (o.graph_sampling, "--graph-sampling"),
+                        (o.batch_audio_transfer, "--batch-audio-transfer"),
+                        (bool(o.decode_bucket_step), "--decode-bucket-step"),
+                        (o.fixed_predictor_rope, "--fixed-predictor-rope"), (o.graph_embeddings, "--graph-embeddings"),
+                        (o.bucket_kv, "--bucket-kv"), (o.native_kv_update, "--native-kv-update")]
+    return ([(not 1 <= o.prefill_interval <= 64 or (o.prefill_interval != 1 and not cont),
+              "--prefill-interval must be 1..64 and requires --continuous when not 1"),
              (o.native_rope_scope != "all" and not o.native_rope, "--native-rope-scope requires --native-rope")]
-            + [(used and not incremental, f"{name} requires --continuous --incremental-codec")
+            + [(used and not (cont and incremental), f"{name} requires --continuous --incremental-codec")
                for used, name in needs_incremental]
+            + [(used and not cont, f"{name} requires --continuous") for used, name in needs_continuous]
             + [(o.fused_residual and o.rms_norm != "native", "--fused-residual requires --rms-norm native"),
-               (o.packed_kv_load and (not o.graph_prefill or o.reference_single),
+               (o.packed_kv_load and not (cont and o.graph_prefill and not o.reference_single),
                 "--packed-kv-load requires --continuous --graph-prefill without --reference-single"),
                (o.prewarm_prefill and (not o.graph_prefill or o.reference_single),
                 "--prewarm-prefill requires --graph-prefill and excludes --reference-single"),
-               (o.codec_chunk_frames != 8 and (not incremental or o.codec_code_buffer),
+               (o.codec_chunk_frames != 8 and (not cont or not incremental or o.codec_code_buffer),
                 "--codec-chunk-frames 16 requires continuous incremental codec without --codec-code-buffer"),
-               (o.triton_talker_rope and not o.text_only_rope, "--triton-talker-rope requires --continuous --text-only-rope"),
-               (o.triton_kv_update and not o.native_kv_update,
+               (o.triton_talker_rope and not (cont and o.text_only_rope),
+                "--triton-talker-rope requires --continuous --text-only-rope"),
+               (o.triton_kv_update and not (cont and o.native_kv_update),
                 "--triton-kv-update requires --continuous --native-kv-update"),
-               (o.direct_prompt and o.reference_single, "--direct-prompt requires continuous mode without reference-single"),
+               (o.direct_prompt and (not cont or o.reference_single),
+                "--direct-prompt requires continuous mode without reference-single"),
                (o.bucket_prefill and not o.graph_prefill, "--bucket-prefill requires --graph-prefill"),
-               (o.valid_length_kv and (not o.native_gqa or o.reference_single),
+               (o.valid_length_kv and (not cont or not o.native_gqa or o.reference_single),
                 "--valid-length-kv requires continuous native GQA without reference-single"),
                (min(o.max_batch_size, o.queue_size) <= 0 or o.batch_wait_ms < 0 or o.codec_left_context < 0,
                 "Invalid batch or queue settings"),
-               (o.prefill_per_tick < 1 or o.max_batch_size & (o.max_batch_size - 1),
+               (o.prefill_per_tick < 1 or (cont and o.max_batch_size & (o.max_batch_size - 1)),
                 "Continuous slots must be a power of two and prefill budget must be positive"),
-               (o.gpus < 1, "--gpus must be positive")])
+               (o.gpus < 1, "--gpus must be positive"),
+               (o.gpus > 1 and not cont, "--gpus above 1 requires --continuous")])
 
 
 def parse_options(argv=None):
@@ -387,13 +399,14 @@ def parse_options(argv=None):
             decode_batch_size(1, options.max_batch_size, options.decode_bucket_step)
         except ValueError as error:
             parser.error(str(error))
-    options.continuous = True      # the batch (non-continuous) model path is not part of this build
     return options
 
 
 def engine_kwargs(options) -> dict:
     """ContinuousModel keyword arguments for the parsed command line."""
-    kwargs = dict(max_slots=options.max_batch_size, codec_left_context=options.codec_left_context,
+    # micro-batch mode (no --continuous) serves generate() batches of any size from a power-of-two arena
+    slots = options.max_batch_size if options.continuous else 1 << (options.max_batch_size - 1).bit_length()
+    kwargs = dict(max_slots=slots, codec_left_context=options.codec_left_context,
                   codec_batch_size=options.codec_batch_size, codec_chunk_frames=options.codec_chunk_frames,
                   incremental_codec=options.incremental_codec, codec_streams=options.codec_streams,
                   seed=options.seed, prewarm_codec=options.prewarm_codec, prewarm_prefill=options.prewarm_prefill,

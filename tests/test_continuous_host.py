@@ -43,8 +43,9 @@ def fake_engine(tokens_by_id, codec_batch_size=2, incremental=True, context=72):
         rows = []
         for slot, start in zip(indices, starts):
             ident = model.states[slot].identifier
+            base = ident if isinstance(ident, int) else 20 + ident[1]      # ("batch", i) from generate()
             frames = np.repeat(np.arange(start, start + length), 1920)
-            rows.append(torch.from_numpy((ident * 1000 + frames).astype(np.int16)))
+            rows.append(torch.from_numpy((base * 1000 + frames).astype(np.int16)))
         return torch.stack(rows)
 
     model.admit_batch = admit_batch
@@ -155,3 +156,23 @@ def test_phase_tracing_wraps_and_restores(mode):
     assert {name: vars(model).get(name) for name in originals} == originals
     with pytest.raises(ValueError):
         instrument(model, "perf")
+
+
+def test_batch_generate_runs_every_payload_in_order():
+    """CustomVoiceModel.generate's contract (model.py:58-129) over the continuous tick: results in
+    payload order, chunks emitted under the payload index, more payloads than slots admitted as
+    slots free up."""
+    tokens = {("batch", i): [5] * (3 + 2 * i) + [EOS] + [5] * 40 for i in range(5)}
+    model = fake_engine(tokens)
+    model.max_slots = 2
+    emitted = []
+    payloads = [{"max_new_tokens": 30} for _ in range(5)]
+    results = model.generate(payloads, emit=lambda index, pcm, rate: emitted.append((index, len(pcm) // 3840)))
+    assert [r["finish_reason"] for r in results] == ["stop"] * 5
+    assert [r["codec_frames"] for r in results] == [4, 6, 8, 10, 12]
+    for index in range(5):
+        assert sum(n for i, n in emitted if i == index) == results[index]["codec_frames"]
+    assert not model.states
+    model.states.append(RequestState("live", {}, 10, 0, 30))
+    with pytest.raises(ValueError):
+        model.generate(payloads)

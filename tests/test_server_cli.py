@@ -27,23 +27,33 @@ def test_measured_reference_argv_parses_and_reaches_the_engine():
 
 def test_defaults_and_checkpoint_path():
     options = parse_options([])
+    assert not options.continuous                 # micro-batches through generate(), as the reference
     kwargs = engine_kwargs(options)
     assert kwargs["max_slots"] == 1 and kwargs["codec_batch_size"] == 1 and not kwargs["incremental_codec"]
     assert not any(flag in kwargs for flag in VARIANT_FLAGS)
     assert engine_kwargs(parse_options(["--model", "/models/cv"]))["model_path"] == "/models/cv"
+    # a micro-batch size that is not a power of two runs on the next power-of-two arena
+    assert engine_kwargs(parse_options(["--max-batch-size", "3"]))["max_slots"] == 4
+    assert engine_kwargs(parse_options(["--continuous", "--max-batch-size", "16"]))["max_slots"] == 16
+
+
+C = "--continuous "
 
 
 @pytest.mark.parametrize("argv", [
-    "--prefill-interval 0", "--prefill-interval 65", "--native-rope-scope talker",
-    "--codec-streams 2", "--triton-snake", "--codec-code-buffer", "--cache-codec-constants",
-    "--cache-codec-codebooks", "--prewarm-codec", "--fused-residual", "--fused-residual --rms-norm reference-rounding",
-    "--packed-kv-load", "--packed-kv-load --graph-prefill --reference-single", "--prewarm-prefill",
-    "--codec-chunk-frames 16", "--codec-chunk-frames 16 --incremental-codec --codec-code-buffer",
-    "--triton-talker-rope", "--triton-kv-update", "--direct-prompt --reference-single", "--bucket-prefill",
-    "--valid-length-kv", "--valid-length-kv --native-gqa --reference-single", "--max-batch-size 0",
-    "--queue-size 0", "--batch-wait-ms -1", "--codec-left-context -1", "--prefill-per-tick 0",
-    "--max-batch-size 48", "--max-batch-size 64 --decode-bucket-step 7", "--codec-batch-size 3",
-    "--gpus 0"])
+    "--prefill-interval 0", C + "--prefill-interval 65", "--prefill-interval 4", C + "--native-rope-scope talker",
+    C + "--codec-streams 2", C + "--triton-snake", C + "--codec-code-buffer", C + "--cache-codec-constants",
+    C + "--cache-codec-codebooks", C + "--prewarm-codec", "--incremental-codec --prewarm-codec",
+    "--fused-residual", "--fused-residual --rms-norm reference-rounding",
+    C + "--packed-kv-load", C + "--packed-kv-load --graph-prefill --reference-single", C + "--prewarm-prefill",
+    C + "--codec-chunk-frames 16", C + "--codec-chunk-frames 16 --incremental-codec --codec-code-buffer",
+    C + "--triton-talker-rope", C + "--triton-kv-update", C + "--direct-prompt --reference-single", "--direct-prompt",
+    C + "--bucket-prefill", C + "--valid-length-kv", C + "--valid-length-kv --native-gqa --reference-single",
+    "--max-batch-size 0", "--queue-size 0", "--batch-wait-ms -1", "--codec-left-context -1", "--prefill-per-tick 0",
+    C + "--max-batch-size 48", C + "--max-batch-size 64 --decode-bucket-step 7", "--decode-bucket-step 8",
+    "--codec-batch-size 3", "--gpus 0", "--gpus 2", "--incremental-codec", "--graph-prefill", "--batch-prefill",
+    "--graph-sampling", "--triton-cdf", "--native-kv-update", "--single-request-views", "--bucket-kv",
+    "--graph-embeddings", "--fixed-predictor-rope", "--batch-audio-transfer"])
 def test_rejected_combinations_exit(argv, capsys):
     with pytest.raises(SystemExit) as info:
         parse_options(argv.split())
@@ -51,9 +61,11 @@ def test_rejected_combinations_exit(argv, capsys):
 
 
 @pytest.mark.parametrize("argv", [
-    "--codec-streams 2 --incremental-codec", "--codec-chunk-frames 16 --incremental-codec",
-    "--fused-residual --rms-norm native", "--prewarm-prefill --graph-prefill", "--bucket-prefill --graph-prefill",
-    "--valid-length-kv --native-gqa", "--max-batch-size 64 --decode-bucket-step 8",
-    "--triton-talker-rope --text-only-rope", "--triton-kv-update --native-kv-update"])
+    C + "--codec-streams 2 --incremental-codec", C + "--codec-chunk-frames 16 --incremental-codec",
+    "--fused-residual --rms-norm native", C + "--prewarm-prefill --graph-prefill",
+    C + "--bucket-prefill --graph-prefill", C + "--valid-length-kv --native-gqa",
+    C + "--max-batch-size 64 --decode-bucket-step 8", C + "--triton-talker-rope --text-only-rope",
+    C + "--triton-kv-update --native-kv-update", "--max-batch-size 3 --batch-wait-ms 5",
+    C + "--gpus 2 --max-batch-size 32"])
 def test_accepted_combinations(argv):
     parse_options(argv.split())
