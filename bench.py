@@ -182,8 +182,8 @@ def measured_peaks():
 
 
 def profile_traffic(kernel: str):
-    """Per-launch DRAM bytes of `kernel` from the committed ncu summary (profiles/traffic.md,
-    a `| kernel | bytes | ...` table row), if present."""
+    """Per-launch DRAM bytes of `kernel` from the committed ncu traffic summary under profiles/
+    (a `| kernel | bytes | ...` table row), if present."""
     path = ROOT / "profiles" / "traffic.md"
     if not path.exists():
         return None

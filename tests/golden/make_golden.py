@@ -202,4 +202,6 @@ def codec_fixtures() -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/qwen3-tts-rsi-engine")
+    main(sys.argv[1])
