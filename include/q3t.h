@@ -273,20 +273,27 @@ int q3t_decode_attention_qkv(const void* qkv, int64_t qkv_stride, const void* q_
 /* No counterpart in the reference: an allocation-free form of
  * q3t_decode_attention for callers that cannot allocate device memory (a
  * runtime with a fixed pre-reserved pool, a foreign-language host without a
- * CUDA allocator). Same arguments and results, minus the workspace: the
- * split-KV scratch is a 4 MiB file-scope device array that every GPU loading
- * the library keeps until exit. Limits: rows * kv_heads <= 16384 and the
- * chunk partials must fit the rest of the 4 MiB; larger calls return
- * Q3T_ESPACE before launching. The first call on a device resolves the
- * array's device address (cudaGetSymbolAddress), so make that first call
- * before any stream capture. Calls share the array and keep the last call's
- * contents (each clears its own tickets first); calls that overlap on the GPU
- * race and must be ordered by the caller. No cudaMalloc/cudaFree anywhere. */
+ * CUDA allocator). It takes q3t_decode_attention's arguments without the
+ * workspace and without a slot table or ring: keys/values are linear arenas
+ * [arena_slots, kv_heads, capacity, head_dim] and query row b reads slot
+ * b / rows_per_slot, so arena_slots * rows_per_slot >= rows is required
+ * (Q3T_EINVAL otherwise). Results agree with q3t_decode_attention within the
+ * bf16 attention tolerance (it always runs the CUDA-core attention kernel,
+ * while the workspace entry point may pick the tensor-core one). The split-KV
+ * scratch is a 4 MiB file-scope device array that every GPU loading the
+ * library keeps until exit. Limits: rows * kv_heads <= 16384 and the chunk
+ * partials must fit the rest of the 4 MiB; larger calls return Q3T_ESPACE
+ * before launching. The first call in each CUDA context resolves the array's
+ * device address (cudaGetSymbolAddress), so make that first call before any
+ * stream capture. Calls share the array and keep the last call's contents
+ * (each clears its own tickets first); calls that overlap on the GPU race and
+ * must be ordered by the caller. No cudaMalloc/cudaFree anywhere. */
 int q3t_decode_attention_noalloc(const void* query, const void* keys, const void* values,
                                  const int64_t* positions, void* out, int64_t rows,
                                  int64_t rows_per_slot, int64_t q_heads, int64_t kv_heads,
-                                 int64_t head_dim, int64_t capacity, int64_t context,
-                                 int64_t window, float scale, unsigned* status, void* stream);
+                                 int64_t head_dim, int64_t arena_slots, int64_t capacity,
+                                 int64_t context, int64_t window, float scale, unsigned* status,
+                                 void* stream);
 
 /* ------------------------------------------------------------------ sampling */
 

@@ -354,15 +354,8 @@ int launch_attn(const void* q, const void* k, const void* v, const int64_t* pos,
   const int64_t span = window > 0 && window < context ? window : context;
   const int chunk = pick_chunk(rows, kv_heads, span);
   const int max_chunks = int((span + chunk - 1) / chunk);
-  static bool configured[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(decode_attention_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
-        cudaSuccess)
-      return check_cuda("attention: set smem");
-    configured[dev] = true;
-  }
+  static PerDevice smem_once;
+  if (const int rc = smem_limit(smem_once, decode_attention_kernel<D, G>, C::kSmem, "attention: set smem")) return rc;
   unsigned* counters = static_cast<unsigned*>(ws);
   float* partials = reinterpret_cast<float*>(static_cast<char*>(ws) + kTicketBytes);
   return launch(decode_attention_kernel<D, G>, dim3(max_chunks, unsigned(kv_heads), unsigned(rows)), dim3(128),
@@ -518,8 +511,6 @@ extern "C" int q3t_decode_attention(const void* query, const void* keys, const v
 // runs. Calls whose kernels overlap on the GPU (different streams, no
 // ordering between them) race on the array and must not be issued.
 // ======================================================================
-#include <mutex>
-
 namespace {
 
 constexpr size_t kStaticScratchBytes = size_t(4) << 20;  // 4 MiB
@@ -528,24 +519,62 @@ constexpr size_t kStaticTicketBytes = kStaticTickets * sizeof(unsigned);
 
 __device__ __align__(256) unsigned char g_attention_scratch[kStaticScratchBytes];
 
-std::mutex g_static_mutex;
-void* g_static_address[64] = {nullptr};
+// The array's device address differs per CUDA context, so the resolved address is
+// cached per device together with the unique id of the context it was resolved in
+// (cuCtxGetId; ids are never reused within a process): a caller on a non-primary
+// context, or one that reset the device since, gets the address re-resolved.
+using CtxGetCurrent = CUresult (*)(CUcontext*);
+using CtxGetId = CUresult (*)(CUcontext, unsigned long long*);
 
-// Device address of g_attention_scratch on the current device. The first call
-// on a device resolves it with cudaGetSymbolAddress (that device current).
+struct ScratchAddress {
+  unsigned long long context_id = 0;
+  void* address = nullptr;
+};
+std::mutex g_static_mutex;
+ScratchAddress g_static_address[64];
+
+int current_context_id(unsigned long long* id) {
+  static CtxGetCurrent get_current = nullptr;
+  static CtxGetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrent>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetId>(p);
+  });
+  if (get_current == nullptr || get_id == nullptr)
+    return fail(Q3T_ECUDA, "attention (no-alloc): context queries unavailable");
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr || get_id(ctx, id) != CUDA_SUCCESS)
+    return fail(Q3T_ECUDA, "attention (no-alloc): no current CUDA context");
+  return Q3T_OK;
+}
+
+// Device address of g_attention_scratch in the current context. The first call in a
+// context resolves it with cudaGetSymbolAddress (that device and context current).
 int static_scratch(void** out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return fail(Q3T_ECUDA, "attention (no-alloc): no current CUDA device");
+  unsigned long long id = 0;
+  if (const int rc = current_context_id(&id)) return rc;
   std::lock_guard<std::mutex> lock(g_static_mutex);
-  if (g_static_address[dev] == nullptr) {
+  ScratchAddress& entry = g_static_address[dev];
+  if (entry.address == nullptr || entry.context_id != id) {
     void* p = nullptr;
     const cudaError_t err = cudaGetSymbolAddress(&p, g_attention_scratch);
     if (err != cudaSuccess || p == nullptr)
       return fail(Q3T_ECUDA, "attention (no-alloc): cudaGetSymbolAddress failed: %s", cudaGetErrorString(err));
-    g_static_address[dev] = p;
+    entry.address = p;
+    entry.context_id = id;
   }
-  *out = g_static_address[dev];
+  *out = entry.address;
   return Q3T_OK;
 }
 
@@ -567,15 +596,9 @@ int launch_attn_static(const void* q, const void* k, const void* v, const int64_
   void* base = nullptr;
   int rc = static_scratch(&base);
   if (rc != Q3T_OK) return rc;
-  static bool configured[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(decode_attention_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
-        cudaSuccess)
-      return check_cuda("attention (no-alloc): set smem");
-    configured[dev] = true;
-  }
+  static PerDevice smem_once;
+  rc = smem_limit(smem_once, decode_attention_kernel<D, G>, C::kSmem, "attention (no-alloc): set smem");
+  if (rc != Q3T_OK) return rc;
   if (cudaMemsetAsync(base, 0, tickets * sizeof(unsigned), as_stream(stream)) != cudaSuccess)
     return check_cuda("attention (no-alloc): clear tickets");
   unsigned* counters = static_cast<unsigned*>(base);
@@ -592,13 +615,15 @@ int launch_attn_static(const void* q, const void* k, const void* v, const int64_
 
 extern "C" int q3t_decode_attention_noalloc(const void* query, const void* keys, const void* values,
                                             const int64_t* positions, void* out, int64_t rows, int64_t rows_per_slot,
-                                            int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t capacity,
-                                            int64_t context, int64_t window, float scale, unsigned* status,
-                                            void* stream) {
+                                            int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t arena_slots,
+                                            int64_t capacity, int64_t context, int64_t window, float scale,
+                                            unsigned* status, void* stream) {
   if (!query || !keys || !values || !positions || !out) return fail(Q3T_EINVAL, "attention (no-alloc): null pointer");
   if (rows < 1 || rows > 65535 || rows_per_slot < 1 || rows % rows_per_slot || kv_heads < 1 || kv_heads > 65535 ||
-      q_heads % kv_heads || window < 0)
+      q_heads % kv_heads || window < 0 || arena_slots < 1)
     return fail(Q3T_EINVAL, "attention (no-alloc): invalid row or head geometry");
+  if (arena_slots * rows_per_slot < rows)
+    return fail(Q3T_EINVAL, "attention (no-alloc): more query rows than arena slots");
   if (context < 1 || context > capacity) return fail(Q3T_EINVAL, "Attention context must fit the KV arena");
   if (!aligned16(keys) || !aligned16(values) || !aligned16(query))
     return fail(Q3T_EINVAL, "attention (no-alloc): 16-byte alignment");

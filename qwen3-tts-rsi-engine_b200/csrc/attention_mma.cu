@@ -432,15 +432,9 @@ __global__ void __launch_bounds__(128, 3)
 template <int D, int G, bool FUSED>
 int launch_mma(const AttentionCall& a, const FusedQKV& f) {
   using C = MmaCfg<D, G>;
-  static bool configured[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(decode_attention_mma_kernel<D, G, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             C::kSmem) != cudaSuccess)
-      return check_cuda("attention: set smem");
-    configured[dev] = true;
-  }
+  static PerDevice smem_once;
+  if (const int rc = smem_limit(smem_once, decode_attention_mma_kernel<D, G, FUSED>, C::kSmem, "attention: set smem"))
+    return rc;
   const int64_t arena_rows = a.arena_slots * a.kv_heads * a.capacity;
   CUtensorMap tmk, tmv;
   int rc = make_map_bf16(&tmk, a.keys, arena_rows, D, D, 64, C::kTile);
@@ -460,22 +454,25 @@ namespace q3t {
 
 template <int D, int G, bool FUSED>
 int wave_of() {
-  static int resident[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return 0;
-  if (resident[dev] == 0) {
-    using C = MmaCfg<D, G>;
-    if (cudaFuncSetAttribute(decode_attention_mma_kernel<D, G, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             C::kSmem) != cudaSuccess)
-      return 0;
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_attention_mma_kernel<D, G, FUSED>, 128,
-                                                      size_t(C::kSmem)) != cudaSuccess || per_sm < 1)
-      per_sm = 1;
-    resident[dev] = per_sm * sm_count();
-  }
-  return resident[dev];
+  static PerDevice once;
+  static std::atomic<int> resident[64];
+  const int rc = once.run(
+      [&](int dev) {
+        using C = MmaCfg<D, G>;
+        if (cudaFuncSetAttribute(decode_attention_mma_kernel<D, G, FUSED>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
+          return check_cuda("attention: set smem");
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_attention_mma_kernel<D, G, FUSED>, 128,
+                                                          size_t(C::kSmem)) != cudaSuccess || per_sm < 1)
+          per_sm = 1;
+        resident[dev].store(per_sm * sm_count(), std::memory_order_relaxed);
+        return int(Q3T_OK);
+      },
+      "attention: wave size");
+  int dev = -1;
+  if (rc != Q3T_OK || cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  return resident[dev].load(std::memory_order_relaxed);
 }
 
 int attention_wave_ctas(int64_t head_dim, int64_t group, bool fused) {

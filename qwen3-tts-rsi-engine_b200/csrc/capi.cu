@@ -10,7 +10,7 @@ namespace q3t {
 namespace {
 thread_local char g_error[512] = "";
 std::atomic<uint64_t> g_launches{0};
-int g_sms[64] = {0};
+std::atomic<int> g_sms[64];
 }  // namespace
 
 int fail(int code, const char* fmt, ...) {
@@ -32,12 +32,12 @@ void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 int sm_count() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (g_sms[dev] == 0) {
-    int n = 0;
+  int n = g_sms[dev].load(std::memory_order_relaxed);
+  if (n == 0) {  // the same value from every thread: a racing first query is harmless
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    g_sms[dev] = n;
+    g_sms[dev].store(n, std::memory_order_relaxed);
   }
-  return g_sms[dev];
+  return n;
 }
 
 namespace {

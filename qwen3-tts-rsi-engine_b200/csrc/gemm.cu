@@ -770,15 +770,8 @@ Plan plan(int64_t rows, int64_t in_features, int64_t out_features) {
 template <int BN, int EPI>
 int launch_linear(const Plan& p, const Maps& m, const GemmArgs& args, void* stream) {
   using C = Cfg<BN>;
-  static bool configured[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(linear_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
-        cudaSuccess)
-      return check_cuda("linear: set smem");
-    configured[dev] = true;
-  }
+  static PerDevice smem_once;
+  if (const int rc = smem_limit(smem_once, linear_kernel<BN, EPI>, C::kSmem, "linear: set smem")) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.n_tiles, p.splits, p.m_tiles);
   cfg.blockDim = dim3(kThreads);

@@ -8,6 +8,9 @@
 #include <stdarg.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "q3t.h"
 
 namespace q3t {
@@ -25,6 +28,43 @@ int sm_count();
 // elements, box {box_cols, box_rows}, 128-byte swizzle (box_cols * 2 <= 128).
 int make_map_bf16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t stride_elems,
                   int box_cols, int box_rows);
+
+// A per-device one-time set-up (a kernel attribute, a cached query): `run(init)`
+// calls init() for the current device until it first succeeds, under a mutex, so
+// host threads that make their first calls concurrently neither race on the flag
+// nor skip the set-up.
+class PerDevice {
+ public:
+  template <typename Init>
+  int run(Init&& init, const char* what) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+      return fail(Q3T_ECUDA, "%s: no current CUDA device", what);
+    if (done_[dev].load(std::memory_order_acquire)) return Q3T_OK;
+    std::lock_guard<std::mutex> lock(mutex_);
+    if (done_[dev].load(std::memory_order_relaxed)) return Q3T_OK;
+    const int rc = init(dev);
+    if (rc == Q3T_OK) done_[dev].store(true, std::memory_order_release);
+    return rc;
+  }
+
+ private:
+  static constexpr int kMaxDevices = 64;
+  std::mutex mutex_;
+  std::atomic<bool> done_[kMaxDevices] = {};
+};
+
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` once per device.
+template <typename Kernel>
+int smem_limit(PerDevice& once, Kernel* kernel, int bytes, const char* what) {
+  return once.run(
+      [&](int) {
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+          return check_cuda(what);
+        return int(Q3T_OK);
+      },
+      what);
+}
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
