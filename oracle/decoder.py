@@ -6,7 +6,12 @@ q_norm/k_norm, rotate-half RoPE, cache update and GQA attention
 (packed_attention.py:42-85), residual add, post-attention RMSNorm, SwiGLU MLP
 (packed_mlp.py:19-27), final norm and LM head (continuous.py:188-198, 613).
 Layer internals belong to qwen-tts==0.1.1 (absent here), so they are restated
-from those call sites: this part of the oracle is unpinned.
+from those call sites. Pinned: the fp32 mode reproduces, to fp32 accuracy
+(tests/test_oracle_decoder_pinned.py), the reference's own PackedAttention and
+PackedMLP forwards run inside its SlotGraph decode step, its PrefillGraph and
+the predictor's position/mask pattern (tests/golden/make_golden.py), with the
+four qwen-tts functions PackedAttention imports (rotate-half RoPE, repeat-KV
+attention) restated in tests/qwen_tts_fakes.py.
 
 Three precisions:
   mode="fp32"  every op in fp32 from the bf16 weights (the parity truth);

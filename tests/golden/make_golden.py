@@ -6,9 +6,14 @@ Run in a container where the reference checkout is available:
 
 It imports the reference's own CPU-runnable modules (``qwen3_tts_engine``:
 batching, sampling, continuous.SlotCache / ContinuousModel.semantic,
-packed_kv, codec_code_buffer, request_views) and records their outputs on
-seeded inputs. The fixtures pin the CPU oracle in ``oracle/``; nothing at test
-or bench time reads the reference checkout.
+packed_kv, codec_code_buffer, request_views, codec_slots) and records their
+outputs on seeded inputs. For the decoder it runs the reference's own
+PackedAttention / PackedMLP (installed by the reference's install functions)
+inside its SlotArena / SlotGraph decode step and its PrefillGraph, over small
+stand-in decoder layers (``tests/qwen_tts_fakes.py``, which also stands in for
+the four qwen-tts functions PackedAttention imports). The fixtures pin the CPU
+oracle in ``oracle/``; nothing at test or bench time reads the reference
+checkout.
 """
 from __future__ import annotations
 
@@ -147,6 +152,7 @@ def main(reference: str) -> None:
     (HERE / "decode_path.json").write_text(json.dumps(out, indent=1) + "\n")
     print("wrote", HERE / "decode_path.npz", HERE / "decode_path.json")
     codec_fixtures()
+    decoder_fixtures()
 
 
 TINY_CODEC = dict(codebooks=4, codebook_size=32, codebook_dim=8, semantic_codebooks=1, latent=12, hidden=8,
@@ -199,6 +205,88 @@ def codec_fixtures() -> None:
     arrays["codec_frames"] = slots.frames.numpy()
     np.savez_compressed(HERE / "codec.npz", **arrays)
     print("wrote", HERE / "codec.npz")
+
+
+def decoder_fixtures() -> None:
+    """The talker decode step (SlotGraph.compute + codec_head, continuous.py:172-198, 612-613) and the
+    padded batch prefill (PrefillGraph.compute, prefill_graph.py:31-50) run by the reference over
+    fp32 stand-in layers with its PackedAttention (text-only RoPE, packed_attention.py:37-85) and
+    PackedMLP (packed_mlp.py:19-27) installed."""
+    from tests import qwen_tts_fakes as fakes
+    from tests.golden import decoder_case as case
+    fakes.install_modeling_stub()
+    from qwen3_tts_engine.continuous import SlotArena, SlotGraph
+    from qwen3_tts_engine.packed_attention import install_packed_attention
+    from qwen3_tts_engine.packed_mlp import install_packed_mlp
+    from qwen3_tts_engine.prefill_graph import PrefillGraph
+
+    weights = case.weights()
+    model = fakes.TalkerModel(case.LAYERS, case.HIDDEN, case.Q_HEADS, case.KV_HEADS, case.HEAD_DIM, case.FFN,
+                              case.THETA)
+    talker = fakes.Talker(model, case.VOCAB)
+    fakes.load_oracle_weights(talker, weights)
+    for layer in model.layers:
+        layer.input_layernorm.variance_epsilon = case.EPS
+        layer.post_attention_layernorm.variance_epsilon = case.EPS
+        layer.self_attn.q_norm.variance_epsilon = case.EPS
+        layer.self_attn.k_norm.variance_epsilon = case.EPS
+    model.norm.variance_epsilon = case.EPS
+    assert len(install_packed_attention(model, text_only_rope=True)) == case.LAYERS
+    assert len(install_packed_mlp(model)) == case.LAYERS
+    arrays = {}
+    with torch.inference_mode():
+        arena = SlotArena(model, case.SLOTS, case.CAPACITY)
+        for layer in range(case.LAYERS):
+            k, v = case.history(layer)
+            arena.keys[layer].copy_(k)
+            arena.values[layer].copy_(v)
+        graph = SlotGraph(arena, case.SLOTS, case.CAPACITY)
+        positions = torch.tensor(case.POSITIONS)
+        deltas = torch.tensor(case.ROPE_DELTAS)
+        for step in range(2):
+            graph.inputs.copy_(case.step_inputs(step)[:, None])
+            graph.positions.copy_(positions + step)
+            graph.rotary.copy_((positions + step + deltas).view(1, -1, 1).expand(3, -1, 1))
+            hidden = graph.compute()
+            arrays[f"decode_hidden_{step}"] = case.as_numpy(hidden[:, 0])
+            arrays[f"decode_logits_{step}"] = case.as_numpy(talker.codec_head(hidden[:, -1]).float())
+        arrays["decode_keys"] = np.stack([case.as_numpy(k) for k in arena.keys])
+        arrays["decode_values"] = np.stack([case.as_numpy(v) for v in arena.values])
+        prefill = PrefillGraph(talker, case.PREFILL_BATCH, case.PREFILL_LEN)
+        prefill.inputs.copy_(case.prefill_inputs())
+        prefill.mask.copy_(case.prefill_mask())
+        hidden, logits, cache = prefill.compute()
+        arrays["prefill_hidden"] = case.as_numpy(hidden[:, 0])
+        arrays["prefill_logits"] = case.as_numpy(logits)
+        arrays["prefill_keys"] = np.stack([case.as_numpy(layer.keys) for layer in cache.layers])
+        arrays["prefill_values"] = np.stack([case.as_numpy(layer.values) for layer in cache.layers])
+        # the code predictor's layer stack over its 15-step position and mask pattern, with the
+        # reference's PackedAttention on single-axis RoPE (continuous.py:37-61)
+        from transformers.cache_utils import DynamicCache
+        predictor = fakes.TalkerModel(case.LAYERS, case.HIDDEN, case.Q_HEADS, case.KV_HEADS, case.HEAD_DIM,
+                                      case.FFN, case.THETA, talker=False)
+        fakes.load_oracle_weights(fakes.Talker(predictor, case.VOCAB), weights)
+        for layer in predictor.layers:
+            for norm in (layer.input_layernorm, layer.post_attention_layernorm, layer.self_attn.q_norm,
+                         layer.self_attn.k_norm):
+                norm.variance_epsilon = case.EPS
+        predictor.norm.variance_epsilon = case.EPS
+        assert len(install_packed_attention(predictor)) == case.LAYERS
+        assert len(install_packed_mlp(predictor)) == case.LAYERS
+        cache = DynamicCache()
+        mask = torch.zeros(1, 1, 2, 2)
+        mask[..., 0, 1] = torch.finfo(torch.float32).min
+        for step in range(case.PREDICTOR_STEPS):
+            hidden = case.predictor_inputs(step)
+            positions = torch.arange(2) if step == 0 else torch.tensor([step + 1])
+            rotary = predictor.rotary_emb(hidden, positions[None].expand(hidden.shape[0], -1))
+            for layer in predictor.layers:
+                hidden = layer(hidden, attention_mask=mask if step == 0 else None, position_ids=positions[None],
+                               past_key_values=cache, use_cache=True, cache_position=positions,
+                               position_embeddings=rotary)[0]
+            arrays[f"predictor_hidden_{step}"] = case.as_numpy(predictor.norm(hidden))
+    np.savez_compressed(HERE / "decoder.npz", **arrays)
+    print("wrote", HERE / "decoder.npz")
 
 
 if __name__ == "__main__":

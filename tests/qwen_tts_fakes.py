@@ -189,3 +189,116 @@ class SlotCache:
         self.arena_keys[layer_idx][rows, :, self.positions] = key[:, :, 0].to(self.arena_keys[layer_idx].dtype)
         self.arena_values[layer_idx][rows, :, self.positions] = value[:, :, 0].to(self.arena_values[layer_idx].dtype)
         return self.arena_keys[layer_idx], self.arena_values[layer_idx]
+
+
+# ---------------------------------------------------------------------------------------------
+# The qwen-tts functions the reference's PackedAttention imports at module level
+# (packed_attention.py:5-8), restated from the Qwen3 decoder they come from (transformers'
+# rotate-half RoPE with cos/sin broadcast over heads, repeat-KV GQA attention returning
+# [batch, seq, heads, dim]). Registered under `qwen_tts.core.models.modeling_qwen3_tts` so that
+# the reference module imports and its own forward runs on the CPU.
+
+def _apply_rotary_pos_emb(q, k, cos, sin, position_ids=None, unsqueeze_dim=1):
+    cos, sin = cos.unsqueeze(unsqueeze_dim), sin.unsqueeze(unsqueeze_dim)
+    return q * cos + rotate_half(q) * sin, k * cos + rotate_half(k) * sin
+
+
+def _apply_multimodal_rotary_pos_emb(*args, **kwargs):
+    raise NotImplementedError("the fixtures run the talker with text_only_rope=True")
+
+
+def _repeat_kv(x, groups):
+    if groups == 1:
+        return x
+    b, h, s, d = x.shape
+    return x[:, :, None].expand(b, h, groups, s, d).reshape(b, h * groups, s, d)
+
+
+def _eager_attention_forward(module, query, key, value, attention_mask, scaling, dropout=0.0, **kwargs):
+    groups = query.shape[1] // key.shape[1]
+    key, value = _repeat_kv(key, groups), _repeat_kv(value, groups)
+    scores = torch.matmul(query, key.transpose(2, 3)) * scaling
+    if attention_mask is not None:
+        scores = scores + attention_mask[:, :, :, :key.shape[-2]]
+    weights = torch.softmax(scores.float(), dim=-1).to(query.dtype)
+    out = torch.matmul(weights, value).transpose(1, 2).contiguous()
+    return out, weights
+
+
+def _sdpa_attention_forward(module, query, key, value, attention_mask, dropout=0.0, scaling=None, **kwargs):
+    groups = query.shape[1] // key.shape[1]
+    key, value = _repeat_kv(key, groups), _repeat_kv(value, groups)
+    mask = None if attention_mask is None else attention_mask[:, :, :, :key.shape[-2]]
+    out = F.scaled_dot_product_attention(query, key, value, attn_mask=mask, dropout_p=dropout, scale=scaling)
+    return out.transpose(1, 2).contiguous(), None
+
+
+def install_modeling_stub():
+    """Register the stand-in `qwen_tts.core.models.modeling_qwen3_tts` module (idempotent)."""
+    import sys
+    import types
+    name = "qwen_tts.core.models.modeling_qwen3_tts"
+    if name in sys.modules:
+        return sys.modules[name]
+    parts = name.split(".")
+    for i in range(1, len(parts)):
+        sys.modules.setdefault(".".join(parts[:i]), types.ModuleType(".".join(parts[:i])))
+    module = types.ModuleType(name)
+    module.apply_rotary_pos_emb = _apply_rotary_pos_emb
+    module.apply_multimodal_rotary_pos_emb = _apply_multimodal_rotary_pos_emb
+    module.eager_attention_forward = _eager_attention_forward
+    module.ALL_ATTENTION_FUNCTIONS = {"sdpa": _sdpa_attention_forward, "eager": _eager_attention_forward}
+    sys.modules[name] = module
+    return module
+
+
+class TalkerModel(torch.nn.Module):
+    """The talker's inner model as the reference's graphs drive it: `layers`, `norm` and
+    `rotary_emb(hidden, position_ids [3, B, S]) -> (cos, sin) [3, B, S, D]` (identical axes).
+    With talker=False the layers are the code predictor's (single-axis RoPE: position_ids
+    [B, S] -> (cos, sin) [B, S, D])."""
+
+    def __init__(self, layers, hidden, q_heads, kv_heads, head_dim, ffn, theta, talker=True):
+        super().__init__()
+        layer = Qwen3TTSTalkerDecoderLayer if talker else Qwen3TTSDecoderLayer
+        self.layers = torch.nn.ModuleList([layer(hidden, q_heads, kv_heads, head_dim, ffn, layer_idx=i)
+                                           for i in range(layers)])
+        self.norm = Qwen3TTSRMSNorm(hidden)
+        self.head_dim, self.theta = head_dim, theta
+        self.config = SimpleNamespace(hidden_size=hidden, num_key_value_heads=kv_heads, head_dim=head_dim)
+
+    def rotary_emb(self, hidden, position_ids):
+        inv = 1.0 / self.theta ** (torch.arange(0, self.head_dim, 2, dtype=torch.int64).float() / self.head_dim)
+        angles = position_ids.float()[..., None] * inv
+        emb = torch.cat((angles, angles), dim=-1)
+        return emb.cos().to(hidden.dtype), emb.sin().to(hidden.dtype)
+
+
+class Talker(torch.nn.Module):
+    """`model` plus the codec head, with the attributes PrefillGraph reads (prefill_graph.py:18-50)."""
+
+    def __init__(self, model, vocab):
+        super().__init__()
+        self.model = model
+        self.codec_head = torch.nn.Linear(model.config.hidden_size, vocab, bias=False)
+        self.config = model.config
+
+
+def load_oracle_weights(talker, weights):
+    """Copy oracle-format weights (oracle/decoder.py) into a Talker's modules."""
+    with torch.no_grad():
+        for layer, w in zip(talker.model.layers, weights["layers"]):
+            attn = layer.self_attn
+            layer.input_layernorm.weight.copy_(w["input_norm"])
+            layer.post_attention_layernorm.weight.copy_(w["post_norm"])
+            attn.q_proj.weight.copy_(w["q"])
+            attn.k_proj.weight.copy_(w["k"])
+            attn.v_proj.weight.copy_(w["v"])
+            attn.o_proj.weight.copy_(w["o"])
+            attn.q_norm.weight.copy_(w["q_norm"])
+            attn.k_norm.weight.copy_(w["k_norm"])
+            layer.mlp.gate_proj.weight.copy_(w["gate"])
+            layer.mlp.up_proj.weight.copy_(w["up"])
+            layer.mlp.down_proj.weight.copy_(w["down"])
+        talker.model.norm.weight.copy_(weights["norm"])
+        talker.codec_head.weight.copy_(weights["head"])
