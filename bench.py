@@ -1,18 +1,31 @@
 #!/usr/bin/env python
-"""Benchmark of the B200 Qwen3-TTS decode path (BASELINE config 2).
+"""Benchmark of the B200 Qwen3-TTS decode path.
 
-One "step" is one talker decode step for a continuous batch of 32 slots:
-the 28-layer Qwen3 talker (hidden 2048, 16q/8kv x 128, FFN 6144, vocab 3072,
-random-init N(0, 0.02) weights from a seed) on the slot-table KV arena with
-ragged contexts U[64, 2048], greedy next-token selection, and the next
-step's input embedding, replayed as one CUDA graph. Every 16 steps a few
-slots are evicted and re-admitted with new seeded contexts. Each step emits
-one codec frame per slot, so throughput is reported as frames/s.
+Default (the contract line): BASELINE config 5, end-to-end serving of the full
+talker -> code predictor -> incremental codec pipeline at concurrency 64 per
+GPU, random-init weights of the 1.7B geometry, synthetic requests from a seed
+(text ids U[0, 151936) of length U[20, 200], one of two speakers, U[50, 400]
+target frames). BASELINE's corpus (Seed-TTS transcripts) is not used.
+
+* ``value``: device pipeline throughput in codec frames/s. One step = one
+  steady-state engine tick for 64 active slots, all device-resident: the tick
+  graph (frame embedding -> 15-codebook predictor -> 28-layer talker -> semantic
+  sampling -> commit) plus the incremental codec decode of 64 frames of audio
+  (8 streams x 8-frame chunks, rotating over the slots) and PCM16. W untimed
+  steps, then exactly K steps between CUDA events.
+* ``e2e``: the same metric through the public API, ``ContinuousModel.tick``, in
+  a closed loop over the request set (admission and prefill, host token reads,
+  PCM16 copied to the host every tick), timed with CUDA events; TTFA p50/p95
+  and RTF follow the reference's service benchmark (benchmark.py:17-34).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-N > 1 runs one independent engine replica per GPU (request-level data
-parallelism: no collective on the data path); rank 0 prints one JSON line.
+N > 1 (torchrun, one rank per GPU) runs one engine per GPU over its own shard of
+requests (request-level data parallelism: no collective on the data path); the
+timed regions are bracketed by barriers and the max over ranks is reported.
+Other workloads: ``--workload step`` (config 2, the talker decode step),
+``predictor`` (config 3), ``codec`` (config 4), ``dispatch`` (closed-loop
+serving through the host dispatcher over several GPUs from one process).
 """
 from __future__ import annotations
 
@@ -31,8 +44,10 @@ sys.path.insert(0, str(ROOT))
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-METRIC = "codec frames/s (talker decode step, C=32)"
 UNIT = "frames/s"
+SERVING_SLOTS = 64          # BASELINE config 5 at C=64 per GPU
+SERVING_CODEC_BATCH = 8     # streams per codec call (the reference's largest --codec-batch-size)
+SERVING_CHUNK = 8           # frames per steady-state codec chunk
 SLOTS = 32
 CAPACITY = 4096
 ADMIT_EVERY = 16
@@ -42,23 +57,22 @@ ADMIT_SLOTS = 4
 def parse_args():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=40)
+    p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--layers", type=int, default=28, help="talker depth (28 = the benchmarked model)")
+    p.add_argument("--workload", choices=["serving", "step", "predictor", "codec", "dispatch"], default="serving",
+                   help="serving: BASELINE config 5 (default); step: config 2; predictor: config 3; codec: config 4; "
+                        "dispatch: closed-loop serving through the host dispatcher")
+    p.add_argument("--layers", type=int, default=28, help="step: talker depth (28 = the benchmarked model)")
     p.add_argument("--slots", type=int, default=SLOTS,
-                   help="step workload: concurrent slots (32 = BASELINE config 2; 64 = the C=64 roofline target)")
-    p.add_argument("--op-costs", action="store_true",
-                   help="print the in-graph cost of each talker-layer op (28 chained launches per op) and exit")
-    p.add_argument("--workload", choices=["step", "serving", "predictor", "codec"], default="step",
-                   help="step: BASELINE config 2 (default); serving: BASELINE config 5, end-to-end ContinuousModel")
-    p.add_argument("--concurrency", type=int, default=32, help="serving: requests in flight (closed loop)")
-    p.add_argument("--requests", type=int, default=128, help="serving: synthetic requests per timed pass")
+                   help="step: concurrent slots (32 = BASELINE config 2; 64 = the C=64 roofline target)")
+    p.add_argument("--concurrency", type=int, default=SERVING_SLOTS, help="serving/dispatch: requests in flight")
+    p.add_argument("--requests", type=int, default=128, help="serving/dispatch: synthetic requests per GPU")
     p.add_argument("--batch", type=int, default=64, help="predictor / codec: rows or streams (BASELINE configs 3, 4)")
-    p.add_argument("--codec-streams", type=int, default=1, choices=[1, 2],
-                   help="serving: codec decode lanes (ContinuousModel codec_streams)")
+    p.add_argument("--codec-streams", type=int, default=2, choices=[1, 2],
+                   help="serving/dispatch: codec decode lanes (ContinuousModel codec_streams)")
     p.add_argument("--frames", type=int, default=200, help="predictor: timed frames (BASELINE config 3)")
     return p.parse_args()
 
@@ -91,6 +105,15 @@ class Dist:
         t = torch.tensor([value], dtype=torch.float64,
                          device="cuda" if dist.get_backend() == "nccl" else "cpu")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, value: float) -> float:
+        if not self.enabled:
+            return value
+        import torch.distributed as dist
+        t = torch.tensor([value], dtype=torch.float64,
+                         device="cuda" if dist.get_backend() == "nccl" else "cpu")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
         return float(t.item())
 
     def close(self):
@@ -181,17 +204,17 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def profile_traffic(kernel: str):
-    """Per-launch DRAM bytes of `kernel` from the committed ncu traffic summary under profiles/
-    (a `| kernel | bytes | ...` table row), if present."""
-    path = ROOT / "profiles" / "traffic.md"
-    if not path.exists():
-        return None
-    for line in path.read_text().splitlines():
-        cells = [c.strip() for c in line.strip().strip("|").split("|")]
-        if len(cells) >= 2 and cells[0] == kernel and cells[1].isdigit():
-            return int(cells[1])
-    return None
+# DRAM bytes per launch of a kernel, from one ncu capture each (dram__bytes_read.sum +
+# dram__bytes_write.sum), with the capture it came from; None where no capture exists.
+TRAFFIC = {
+    "decode_attention": (146493952, "ncu, 2 launches of the 32-slot decode attention, ctx U[64,2048] "
+                                    "(bench.py --workload step --layers 2)"),
+}
+
+
+def traffic(kernel: str):
+    entry = TRAFFIC.get(kernel)
+    return (entry[0], entry[1]) if entry else (None, None)
 
 
 # ---------------------------------------------------------------------- CPU baseline (oracle)
@@ -357,16 +380,6 @@ def run_b200(args, dist: Dist):
     e2e_ms = dist.max(e0.elapsed_time(e1))
     h2d = host_in.numel() * 2 + host_pos.numel() * 8 * 2
     d2h = host_tok.numel() * 8
-    if os.environ.get("Q3T_BENCH_DIAG"):
-        for name, g in (("tick_graph", graph), ("step_graph", e2e_graph)):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            for _ in range(args.steps):
-                g.replay()
-            b.record()
-            torch.cuda.synchronize()
-            print(json.dumps({"diag": name, "ms_per_replay": a.elapsed_time(b) / args.steps}), file=sys.stderr)
-
     # ---- roofline of the dominant kernels, timed alone with L2 flushed between launches
     kernels = kernel_rooflines(cfg, engine, step, positions_at_start, dev)
     result = {
@@ -450,101 +463,33 @@ def kernel_rooflines(cfg, engine, step, positions, dev):
 
 
 # ---------------------------------------------------------------------- reference (CPU) arm
+def step_config(cfg, slots: int, world: int) -> dict:
+    """The `config` of the step workload, shared by both arms."""
+    return {"workload": f"BASELINE config 2: talker decode step, {slots} slots, ctx U[64,2048], "
+                        "greedy, evict/admit 4 slots every 16 steps",
+            "model": f"qwen3-tts talker {cfg.layers}L h{cfg.hidden} (random init)", "layers": cfg.layers,
+            "global_batch": slots * world, "slots_per_gpu": slots,
+            "parallelism": f"replicas x{world} (request-level data parallel)"}
+
+
 def run_reference(args, dist: Dist):
+    """The reference arm of the step workload: the CPU port of the talker step."""
     from qwen3_tts_b200.config import TALKER
-    work = Workload(args.seed)
+    work = Workload(args.seed, SLOTS)
     layers = 2
     [(per_step, threads)] = cpu_decode_sample(TALKER, work.positions, args.warmup + args.steps, layers, args.seed)
     value = SLOTS / per_step
     return {
-        "metric": f"codec frames/s (talker decode step, C={SLOTS})", "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"BASELINE config 2: talker decode step, {SLOTS} slots, ctx U[64,2048]",
-                   "model": "qwen3-tts talker 28L h2048 (random init)", "global_batch": SLOTS,
-                   "parallelism": "cpu"},
+        "metric": f"codec frames/s (talker decode step, C={SLOTS})", "value": value, "unit": UNIT,
+        "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded random-init weights)",
+        "config": step_config(TALKER, SLOTS, args.gpus),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"oracle fp32 talker, {layers} of 28 layers at full width, 32 slots, "
+                         "sample": f"oracle fp32 talker, {layers} of 28 layers at full width, {SLOTS} slots, "
                                    f"ragged ctx; median step time scaled by 28/{layers}"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-
-
-def op_costs(args) -> None:
-    """In-graph cost of each op of a talker layer: one CUDA graph of 28 back-to-back launches
-    of the same op cycling through the 28 layers' weights and KV (nothing stays in L2), timed
-    with CUDA events; one JSON line per op (us per launch, achieved GB/s)."""
-    from qwen3_tts_b200 import _lib, ops
-    from qwen3_tts_b200.config import TALKER
-    from qwen3_tts_b200.talker import TalkerDecoder
-    from qwen3_tts_b200.weights import decoder_weights
-
-    dev = torch.device("cuda:0")
-    cfg, L = TALKER, TALKER.layers
-    work = Workload(args.seed)
-    positions = work.positions.to(dev)
-    engine = TalkerDecoder(cfg, decoder_weights(cfg, args.seed, dev), SLOTS, CAPACITY, dev, use_graphs=False)
-    step = engine.step_for(SLOTS, CAPACITY)
-    for plane in engine.arena.keys + engine.arena.values:
-        plane.normal_()
-    W = engine.weights["layers"]
-    eps = cfg.eps if W[0].folded else None
-    # the step's split-KV plan, as TalkerStep.compute makes it once per step
-    ops.attention_plan(positions, step.ws_attn, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
-                       context=CAPACITY)
-
-    def graph_us(fn, replays=10):
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            for i in range(L):
-                fn(i)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=side):
-            for i in range(L):
-                fn(i)
-        graph.replay()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for _ in range(replays):
-            graph.replay()
-        b.record()
-        torch.cuda.synchronize()
-        return a.elapsed_time(b) * 1e3 / (L * replays)
-
-    kv = int(((work.positions + 1).sum()).item()) * cfg.kv_heads * cfg.head_dim * 2 * 2
-    B = SLOTS
-    costs = {
-        "linear_qkv": (lambda i: ops.linear(step.h, W[i].qkv, out=step.qkv, row_norm_eps=eps), W[0].qkv.numel() * 2),
-        "qk_norm_rope_kv": (lambda i: ops.qk_norm_rope_kv(
-            step.qkv, W[i].q_norm, W[i].k_norm, cfg.eps, engine.cos, engine.sin, positions, positions,
-            engine.arena.keys[i], engine.arena.values[i], q_heads=cfg.q_heads, kv_heads=cfg.kv_heads,
-            head_dim=cfg.head_dim, query_out=step.q), B * cfg.qkv_width * 2 * 2),
-        "decode_attention": (lambda i: ops.decode_attention(
-            step.q, engine.arena.keys[i], engine.arena.values[i], positions, context=CAPACITY, out=step.attn,
-            workspace=step.ws_attn), kv),
-        "decode_attention_qkv (fused q/k norm, RoPE, KV write)": (lambda i: ops.decode_attention_qkv(
-            step.qkv, W[i].q_norm, W[i].k_norm, cfg.eps, engine.cos, engine.sin, positions, engine.arena.keys[i],
-            engine.arena.values[i], positions, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
-            context=CAPACITY, out=step.attn, workspace=step.ws_attn), kv),
-        "linear_o": (lambda i: ops.linear(step.attn.view(B, -1), W[i].o, out=step.h, epilogue=_lib.EPI_RESIDUAL,
-                                          residual=step.h), W[0].o.numel() * 2),
-        "linear_gate_up": (lambda i: ops.linear(step.h, W[i].gate_up, out=step.act, epilogue=_lib.EPI_SWIGLU_PAIRED,
-                                                row_norm_eps=eps), W[0].gate_up.numel() * 2),
-        "linear_down": (lambda i: ops.linear(step.act, W[i].down, out=step.h, epilogue=_lib.EPI_RESIDUAL,
-                                             residual=step.h), W[0].down.numel() * 2),
-    }
-    total = 0.0
-    step_ops = {"linear_qkv", "decode_attention_qkv (fused q/k norm, RoPE, KV write)", "linear_o", "linear_gate_up",
-                "linear_down"}
-    for name, (fn, nbytes) in costs.items():
-        us = graph_us(fn)
-        total += us if name in step_ops else 0.0
-        print(json.dumps({"op": name, "us_per_launch": round(us, 2), "GBps": round(nbytes / us / 1e3, 1)}))
-    print(json.dumps({"layer_us (ops of the decode step)": round(total, 1), "step_ms_28_layers": round(total * L / 1e3, 3),
-                      "status": ops.read_status(dev)}))
 
 
 def serving_requests(seed: int, count: int):
@@ -561,69 +506,252 @@ def serving_requests(seed: int, count: int):
     return out
 
 
-def run_serving(args) -> dict:
-    """Closed-loop serving through ContinuousModel.tick at `concurrency` requests in flight.
-
-    A first pass over the same request set captures every graph shape (untimed); the
-    second pass is timed on the host clock (the engine synchronises once per tick).
-    Metrics follow the reference's service benchmark (``metrics.summarize``): frames/s =
-    delivered audio x 12.5 / wall time; TTFA = submission -> first PCM chunk (p50/p95,
-    interpolated); RTF = mean over requests of latency / audio duration. A request ends at
-    its synthetic target length (the max_new_tokens cap stands in for EOS at the target)."""
-    from qwen3_tts_b200.continuous import ContinuousModel
+def closed_loop(model, requests, concurrency: int, timed: bool = False) -> dict:
+    """Serve `requests` through model.tick with at most `concurrency` in flight (closed loop:
+    a finished request is replaced by the next one). Metrics follow the reference's service
+    benchmark (``metrics.summarize``, benchmark.py:17-34): frames/s = delivered audio x 12.5 /
+    wall time; TTFA = submission -> first PCM chunk (p50/p95, interpolated); RTF = mean over
+    requests of latency / audio duration. A request ends at its synthetic target length (the
+    max_new_tokens cap stands in for EOS at the target). With `timed`, the pass is also timed
+    with CUDA events on the engine's stream, and the host<->device bytes are counted: per
+    request the prompt ids and the uniform table going in, per tick the token ids and status
+    word coming out, and every PCM16 chunk delivered."""
     from qwen3_tts_b200.metrics import summarize
+    pending = list(enumerate(requests))
+    submitted, first_audio, done = {}, {}, {}
+    counts = {"frames": 0, "ticks": 0, "pcm_bytes": 0, "token_bytes": 0, "h2d": 0}
+    in_flight = 0
+
+    def emit(identifier, pcm, rate):
+        counts["pcm_bytes"] += len(pcm)
+        if len(pcm):
+            first_audio.setdefault(identifier, time.perf_counter())
+
+    table_rows = getattr(getattr(model, "state", None), "table_rows", 0)
+    events = None
+    if timed:
+        torch.cuda.synchronize()
+        events = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        events[0].record()
+    start = time.perf_counter()
+    while pending or in_flight:
+        subs = []
+        while pending and in_flight + len(subs) < concurrency:
+            subs.append(pending.pop(0))
+        now = time.perf_counter()
+        for identifier, payload in subs:
+            submitted[identifier] = now
+            counts["h2d"] += len(payload["input_ids"]) * 8 + table_rows * 16 * 4 + 64
+        in_flight += len(subs)
+        counts["token_bytes"] += in_flight * 8 + 4
+        counts["ticks"] += 1
+        for identifier, result in model.tick(subs, emit=emit):
+            done[identifier] = (time.perf_counter(), result)
+            counts["frames"] += result["codec_frames"]
+            in_flight -= 1
+    wall = time.perf_counter() - start
+    device_ms = None
+    if timed:
+        events[1].record()
+        torch.cuda.synchronize()
+        device_ms = events[0].elapsed_time(events[1])
+    records = []
+    for i in submitted:
+        finished, result = done[i]
+        records.append({"success": result["finish_reason"] in ("stop", "length") and result["codec_frames"] > 0
+                        and i in first_audio, "audio_seconds": result["codec_frames"] / 12.5,
+                        "elapsed_seconds": finished - submitted[i],
+                        "ttfa_seconds": first_audio.get(i, finished) - submitted[i]})
+    return dict(summarize(records, wall, 12.5), device_ms=device_ms, **counts)
+
+
+def serving_engine(args, device):
+    from qwen3_tts_b200.continuous import ContinuousModel
     slots = 1 << max(0, (args.concurrency - 1).bit_length())
-    engine = dict(max_slots=slots, initial_capacity=1024, seed=args.seed, codec_batch_size=4,
+    return ContinuousModel(None, device, max_slots=slots, initial_capacity=1024, seed=args.seed,
+                           codec_batch_size=SERVING_CODEC_BATCH, codec_streams=args.codec_streams)
+
+
+def steady_state(model, requests, steps: int, warmup: int, seed: int, dist) -> dict:
+    """Device pipeline throughput at full concurrency: the engine holds `max_slots` active
+    requests in mid-stream (positions = prompt length + U[0, target) frames already decoded);
+    one step = one replay of the (batch, context) tick graph plus the codec decode of
+    SERVING_CHUNK-frame chunks for max_slots / SERVING_CHUNK streams (rotating over the slots:
+    every slot's audio is decoded once per SERVING_CHUNK steps, as in steady-state serving),
+    PCM16 on the device. Nothing is copied to the host and the host never waits inside the
+    timed region. Returns frames/s (max_slots frames per step) and the timing."""
+    from qwen3_tts_b200.batching import context_bucket
+    slots = model.max_slots
+    subs = [(("steady", i), dict(req, max_new_tokens=4000)) for i, req in enumerate(requests[:slots])]
+    model.tick(subs)                                   # admission: batched prefill + first frame
+    states, S = model.states, model.state
+    advance = torch.tensor(steady_advance(requests[:slots], seed), dtype=torch.long)
+    S.positions[:slots] += advance.to(S.positions.device)
+    S.rotary[:slots] += advance.to(S.rotary.device)
+    for state, extra in zip(states, advance.tolist()):
+        state.position += extra
+    priming = SERVING_CHUNK
+    top = max(state.position for state in states) + priming + warmup + steps + 1
+    model.ensure_capacity(top)
+    graph = model._tick_graph(slots, context_bucket(top + 1, model.arena.capacity))
+    model._set_active(slots)
+    groups = slots // SERVING_CHUNK
+
+    def tick_only():
+        graph.run()
+        for state in states:
+            state.frames += 1
+
+    def step(i):
+        tick_only()
+        due = states[(i % groups) * SERVING_CHUNK:(i % groups + 1) * SERVING_CHUNK] if groups else states
+        for state in due:
+            state.emitted = state.frames - SERVING_CHUNK
+        model.decode_chunks(due)
+
+    for _ in range(priming):                            # fill every slot's code ring
+        tick_only()
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    from qwen3_tts_b200 import _lib
+    codec_graphs = list(model.codec.graphs.values())
+    replays = [c.replays for c in codec_graphs]
+    ticks, host = graph.replays, _lib.launch_count()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(steps):
+        step(warmup + i)
+    b.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    elapsed_ms = dist.max(a.elapsed_time(b))
+    # this library's kernels in the timed region: graph replays x kernels captured per replay,
+    # plus the kernels launched directly (code ring reads)
+    launches = (graph.replays - ticks) * graph.launches + (_lib.launch_count() - host)
+    launches += sum((c.replays - r) * c.launches for c, r in zip(codec_graphs, replays))
+    context = graph.context
+    mean_position = sum(state.position for state in states) / len(states)
+    model.states.clear()
+    model._set_active(0)
+    return {"elapsed_ms": elapsed_ms, "frames": slots * steps, "context": context, "mean_position": mean_position,
+            "launches": launches, "tick_launches": graph.launches}
+
+
+def gemm_roofline(model, peak: float) -> dict:
+    """The dominant kernel of a serving step: the projection GEMM (tcgen05 linear kernel), which
+    carries the code predictor's and the talker's weight streams. Timed as the predictor runs it
+    at 64 rows: one CUDA graph with one codebook step's projections (5 layers x QKV, O, gate/up,
+    down, then the head) launched back to back, replayed, CUDA events on the replay stream.
+    achieved = weight + activation bytes per launch / mean launch time."""
+    from qwen3_tts_b200 import _lib, ops
+    cfg, w = model.predictor_config, model.predictor_weights
+    dev = model.device
+    rows = model.max_slots
+    x = torch.zeros(rows, cfg.hidden, dtype=torch.bfloat16, device=dev)
+    qkv = torch.zeros(rows, cfg.qkv_width, dtype=torch.bfloat16, device=dev)
+    attn = torch.zeros(rows, cfg.q_width, dtype=torch.bfloat16, device=dev)
+    act = torch.zeros(rows, cfg.ffn, dtype=torch.bfloat16, device=dev)
+    logits = torch.zeros(rows, cfg.vocab, dtype=torch.float32, device=dev)
+    calls, nbytes = [], 0
+
+    def add(fn, weight, x_bytes, out_bytes):
+        nonlocal nbytes
+        calls.append(fn)
+        nbytes += weight.numel() * 2 + x_bytes + out_bytes
+
+    for layer in w["layers"]:
+        add(lambda l=layer: ops.linear(x, l.qkv, out=qkv, row_norm_eps=cfg.eps), layer.qkv, x.numel() * 2,
+            qkv.numel() * 2)
+        add(lambda l=layer: ops.linear(attn, l.o, out=x, epilogue=_lib.EPI_RESIDUAL, residual=x), layer.o,
+            attn.numel() * 2, 2 * x.numel() * 2)
+        add(lambda l=layer: ops.linear(x, l.gate_up, out=act, epilogue=_lib.EPI_SWIGLU_PAIRED, row_norm_eps=cfg.eps),
+            layer.gate_up, x.numel() * 2, act.numel() * 2)
+        add(lambda l=layer: ops.linear(act, l.down, out=x, epilogue=_lib.EPI_RESIDUAL, residual=x), layer.down,
+            act.numel() * 2, 2 * x.numel() * 2)
+    head = w["heads"][0]
+    add(lambda: ops.linear(x, head, out=logits, out_dtype=torch.float32, row_norm_eps=cfg.eps), head, x.numel() * 2,
+        logits.numel() * 4)
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for fn in calls:
+            fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        for fn in calls:
+            fn()
+    replays = 20
+    with torch.cuda.stream(side):
+        graph.replay()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(side)
+        for _ in range(replays):
+            graph.replay()
+        b.record(side)
+    torch.cuda.synchronize()
+    graph.reset()
+    seconds = a.elapsed_time(b) / 1e3 / (replays * len(calls))
+    per_launch = nbytes / len(calls)
+    achieved = per_launch / seconds / 1e9
+    return {"bound": "hbm", "kernel": "linear_kernel (tcgen05 projection GEMM, 64 rows)", "achieved": achieved,
+            "peak": peak, "unit": "GB/s", "frac": achieved / peak, "launch_us": seconds * 1e6,
+            "bytes_per_launch": per_launch,
+            "method": "in graph: one predictor codebook step's 21 projections back to back, CUDA events"}
+
+
+def serving_contract(args, dist) -> dict:
+    """BASELINE config 5 at C=64 per GPU on this rank's GPU (see the module docstring)."""
+    from qwen3_tts_b200 import ops
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    model = serving_engine(args, dev)
+    requests = serving_requests(args.seed + 7919 * dist.rank, args.requests)
+    closed_loop(model, requests, args.concurrency)     # captures every graph shape the pass meets
+    dist.barrier()
+    e2e = closed_loop(model, requests, args.concurrency, timed=True)
+    dist.barrier()
+    e2e_ms = dist.max(e2e["device_ms"])
+    frames_all = dist.sum(e2e["frames"])
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    steady = steady_state(model, serving_requests(args.seed + 104729 + dist.rank, SERVING_SLOTS), args.steps,
+                          args.warmup, args.seed + dist.rank, dist)
+    clock_info = clocks.stop()
+    status = ops.read_status(dev)
+    peak, peak_kind = measured_peaks()
+    roofline = gemm_roofline(model, peak)
+    roofline["peak_kind"] = peak_kind
+    roofline["traffic"], roofline["traffic_source"] = traffic("linear_kernel")
+    model.close()
+    return {"steady": steady, "e2e": e2e, "e2e_ms": e2e_ms, "e2e_frames_all": frames_all, "clocks": clock_info,
+            "status": status, "roofline": roofline}
+
+
+def run_dispatch(args) -> dict:
+    """Closed-loop serving through the host dispatcher: one engine process per GPU (--gpus N),
+    `concurrency` requests in flight per GPU, from this single process. A first pass over the
+    same requests captures the graph shapes; the second is timed on the host clock."""
+    from qwen3_tts_b200.continuous import ContinuousModel
+    slots = 1 << max(0, (args.concurrency - 1).bit_length())
+    engine = dict(max_slots=slots, initial_capacity=1024, seed=args.seed, codec_batch_size=SERVING_CODEC_BATCH,
                   codec_streams=args.codec_streams)
     gpus = max(1, args.gpus)
     if gpus > 1:
-        # request-level data parallelism: one engine process per GPU behind the host dispatcher,
-        # `concurrency` requests in flight per GPU
         from qwen3_tts_b200.dispatcher import Dispatcher
         model = Dispatcher.start(gpus, engine, per_engine=args.concurrency)
     else:
         model = ContinuousModel(None, torch.device("cuda:0"), **engine)
-    concurrency = args.concurrency * gpus
     requests = serving_requests(args.seed, args.requests * gpus)
-
-    def one_pass():
-        pending = list(enumerate(requests))
-        submitted, first_audio, done, frames = {}, {}, {}, 0
-        in_flight = 0
-
-        def emit(identifier, pcm, rate):
-            if len(pcm):
-                first_audio.setdefault(identifier, time.perf_counter())
-
-        start = time.perf_counter()
-        while pending or in_flight:
-            subs = []
-            while pending and in_flight + len(subs) < concurrency:
-                subs.append(pending.pop(0))
-            now = time.perf_counter()
-            for identifier, _ in subs:
-                submitted[identifier] = now
-            in_flight += len(subs)
-            for identifier, result in model.tick(subs, emit=emit):
-                done[identifier] = (time.perf_counter(), result)
-                frames += result["codec_frames"]
-                in_flight -= 1
-        wall = time.perf_counter() - start
-        records = []
-        for i in submitted:
-            finished, result = done[i]
-            records.append({"success": result["finish_reason"] in ("stop", "length") and result["codec_frames"] > 0
-                            and i in first_audio, "audio_seconds": result["codec_frames"] / 12.5,
-                            "elapsed_seconds": finished - submitted[i],
-                            "ttfa_seconds": first_audio.get(i, finished) - submitted[i]})
-        return dict(summarize(records, wall, 12.5), frames=frames)
-
-    one_pass()                       # graph capture for every (batch, context) and codec shape met
-    res = one_pass()
+    closed_loop(model, requests, args.concurrency * gpus)
+    res = closed_loop(model, requests, args.concurrency * gpus)
     model.close()
     return {"frames_per_s": res["throughput_frames_s"], "frames": res["frames"], "wall_s": res["wall_seconds"],
             "ttfa_p50_ms": res["ttfa_p50_ms"], "ttfa_p95_ms": res["ttfa_p95_ms"], "rtf": res["rtf_mean"],
-            "status": res["status"], "failed_requests": res["failed_requests"], "slots": slots, "gpus": gpus}
+            "status": res["status"], "failed_requests": res["failed_requests"], "gpus": gpus}
 
 
 # BASELINE config 3 per predictor step: 5 layers (QKV, O, gate/up, down) + input projection +
@@ -711,14 +839,143 @@ def run_codec(args) -> dict:
     return {"frames_per_s": B * T * args.steps / (ms / 1e3), "ms_per_step": ms / args.steps, "status": status}
 
 
+# ---------------------------------------------------------------------- CPU tick (serving arms)
+PROMPT_PREFIX = 9   # CustomVoice prompt rows around the text ids (role, speaker, language, codec tags)
+
+
+def steady_advance(requests, seed: int) -> list:
+    """Frames already decoded per slot in the steady state (U[0, target)), shared by both arms."""
+    g = torch.Generator().manual_seed(seed + 17)
+    return [int(torch.randint(0, max(1, r["max_new_tokens"] - 1), (1,), generator=g)) for r in requests]
+
+
+class CpuTick:
+    """One steady-state serving tick of the CPU port (the oracle, fp32) for `slots` active
+    requests, in bounded samples: the talker step as one of its 28 layers at full width over
+    the slots' contexts (scaled by 28) plus the LM head; the whole code-predictor frame (5
+    layers, 15 codebooks, heads and top-k sampling) for every slot; the incremental codec
+    decode of one stream's 8-frame chunk, scaled by the slots / 8 streams a tick decodes."""
+
+    def __init__(self, slots: int, positions, seed: int, steps: int):
+        from dataclasses import replace
+
+        from oracle import codec as OC
+        from oracle import decoder as OD
+        from qwen3_tts_b200.config import CODEC, PREDICTOR, TALKER
+        from qwen3_tts_b200.weights import decoder_weights
+
+        def fp32(weights):
+            for layer in weights["layers"]:
+                for key in list(layer):
+                    layer[key] = layer[key].float()
+            for key in list(weights):
+                if isinstance(weights[key], torch.Tensor):
+                    weights[key] = weights[key].float()
+            return weights
+
+        self.OD, self.slots = OD, slots
+        self.talker_cfg = replace(TALKER, layers=1)
+        self.talker = fp32(decoder_weights(self.talker_cfg, seed, dtype=torch.bfloat16))
+        self.positions = torch.tensor(positions, dtype=torch.long).view(-1, 1)
+        cap = int(self.positions.max()) + steps + 2
+        self.tables = OD.Tables(cap + 1, TALKER.head_dim, TALKER.theta)
+        self.cache = OD.new_cache(self.talker_cfg, slots, cap)
+        self.predictor_cfg = PREDICTOR
+        self.predictor = fp32(decoder_weights(PREDICTOR, seed + 1, dtype=torch.bfloat16))
+        self.ptables = OD.Tables(PREDICTOR.groups + 1, PREDICTOR.head_dim, PREDICTOR.theta)
+        g = torch.Generator().manual_seed(seed + 2)
+        self.h = torch.randn(slots, 1, TALKER.hidden, generator=g) * 0.1
+        self.first = torch.randn(slots, PREDICTOR.talker_hidden, generator=g) * 0.02
+        self.draws = torch.rand(slots, 16, generator=g)
+        self.codec = OC.IncrementalOracle(OC.randomize(OC.CodecDecoder(CODEC), seed + 3))
+        self.codec_state = self.codec.new_state()
+        self.codes = torch.randint(0, CODEC.codebook_size, (1, CODEC.codebooks, SERVING_CHUNK), generator=g)
+        self.streams = max(1, slots // SERVING_CHUNK)
+
+    def step(self) -> float:
+        """Seconds of one tick (sampled parts scaled)."""
+        OD = self.OD
+        t0 = time.perf_counter()
+        x = OD.layer_forward(self.talker_cfg, self.talker["layers"][0], self.h, self.positions, *self.cache[0],
+                             self.positions, self.tables, "fp32")
+        t1 = time.perf_counter()
+        hidden = OD._rms(x, self.talker["norm"], self.talker_cfg.eps, "fp32")
+        torch.argmax(hidden[:, 0] @ self.talker["head"].T, dim=-1)
+        t2 = time.perf_counter()
+        OD.predictor_frame(self.predictor_cfg, self.predictor, self.h[:, 0].float(), self.first, self.draws,
+                           self.ptables, "fp32")
+        t3 = time.perf_counter()
+        self.codec.decode(self.codes, self.codec_state)
+        t4 = time.perf_counter()
+        self.positions += 1
+        return (t1 - t0) * 28 + (t2 - t1) + (t3 - t2) + (t4 - t3) * self.streams
+
+
+def cpu_serving_sample(args, steps: int):
+    """Seconds per CPU tick (median of `steps`) and the thread count, on the serving workload's
+    steady state (same requests and contexts as the GPU arm's)."""
+    requests = serving_requests(args.seed + 104729, SERVING_SLOTS)
+    advance = steady_advance(requests, args.seed)
+    positions = [len(r["input_ids"]) + PROMPT_PREFIX + a for r, a in zip(requests, advance)]
+    torch.set_num_threads(os.cpu_count() or 1)
+    tick = CpuTick(SERVING_SLOTS, positions, args.seed, steps)
+    times = [tick.step() for _ in range(steps)]
+    return float(np.median(times)), torch.get_num_threads()
+
+
+CPU_SERVING_SAMPLE = ("oracle fp32 serving tick at 64 slots (steady state, same requests and contexts): talker 1 of "
+                      "28 layers at full width x 28 + LM head, the full 15-codebook predictor frame, one of 8 "
+                      "streams' 8-frame codec chunks x 8; median tick time")
+
+
+def serving_config(args, world: int) -> dict:
+    """The `config` of the serving workload, shared by both arms."""
+    return {"workload": "BASELINE config 5: talker -> code predictor -> incremental codec, C=64 per GPU; value: "
+                        "steady-state tick (64 slots, 8 streams x 8-frame codec chunks per step); e2e: closed loop "
+                        "through ContinuousModel.tick",
+            "model": "qwen3-tts 1.7B CustomVoice geometry (talker 28L h2048, predictor 5L h1024, codec 8L h512 / "
+                     "1536-ch decoder), random init",
+            "concurrency": args.concurrency, "requests_per_gpu": args.requests, "global_batch": SERVING_SLOTS * world,
+            "codec_batch": SERVING_CODEC_BATCH, "codec_streams": args.codec_streams,
+            "parallelism": f"replicas x{world} (request-level data parallel, one engine per GPU)",
+            "l2": "inputs > L2 (talker 2.8 GB + predictor 2.5 GB of weights streamed per step)"}
+
+
+SERVING_METRIC = "codec frames/s (end-to-end serving, C=64 per GPU)"
+
+
+def run_reference_serving(args) -> dict:
+    per_tick, threads = cpu_serving_sample(args, args.warmup + args.steps)
+    value = SERVING_SLOTS / per_tick
+    return {
+        "metric": SERVING_METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_tick * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (BASELINE config 5 request recipe, seeded random-init weights)",
+        "config": serving_config(args, args.gpus),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": CPU_SERVING_SAMPLE},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
 def main():
     global SLOTS
     args = parse_args()
     if args.slots < 1 or args.slots > 64:
         raise SystemExit("--slots must be within 1..64")
+    if args.concurrency != SERVING_SLOTS and args.workload == "serving":
+        raise SystemExit("the serving contract runs at C=64 per GPU (use --workload dispatch for other C)")
     SLOTS = args.slots
-    if args.op_costs:
-        op_costs(args)
+    rank = int(os.environ.get("RANK", 0))
+    if args.impl == "reference":
+        if rank != 0:
+            return            # the CPU arm runs on rank 0 alone
+        if args.workload == "serving":
+            print(json.dumps(run_reference_serving(args)))
+        elif args.workload == "step":
+            print(json.dumps(run_reference(args, Dist.__new__(Dist))))
+        else:
+            print(json.dumps({"impl": "reference", "unavailable": f"no CPU arm for --workload {args.workload}"}))
         return
     if args.workload == "predictor":
         res = run_predictor(args)
@@ -740,28 +997,67 @@ def main():
             "config": {"workload": "BASELINE config 4: incremental codec decode", "streams": args.batch,
                        "chunk_frames": 4}, "status_word": res["status"]}))
         return
-    if args.workload == "serving":
-        if int(os.environ.get("RANK", 0)) != 0:
+    if args.workload == "dispatch":
+        if rank != 0:
             return  # one host process drives every GPU through the dispatcher
-        res = run_serving(args)
+        res = run_dispatch(args)
         print(json.dumps({
-            "metric": f"codec frames/s (end-to-end serving, C={args.concurrency} per GPU)", "value": res["frames_per_s"],
-            "unit": UNIT, "n_gpus": res["gpus"], "higher_is_better": True, "dtype": "bf16",
-            "data": "synthetic (BASELINE config 5 request recipe, seeded random-init weights)",
+            "metric": f"codec frames/s (end-to-end serving through the dispatcher, C={args.concurrency} per GPU)",
+            "value": res["frames_per_s"], "unit": UNIT, "n_gpus": res["gpus"], "higher_is_better": True,
+            "dtype": "bf16", "data": "synthetic (BASELINE config 5 request recipe, seeded random-init weights)",
             "config": {"workload": "BASELINE config 5: talker -> code predictor -> incremental codec, closed loop",
-                       "concurrency": args.concurrency, "requests": args.requests * res["gpus"], "slots": res["slots"],
+                       "concurrency": args.concurrency, "requests": args.requests * res["gpus"],
                        "codec_streams": args.codec_streams},
             "ttfa_p50_ms": res["ttfa_p50_ms"], "ttfa_p95_ms": res["ttfa_p95_ms"], "rtf": res["rtf"],
             "frames": res["frames"], "wall_s": res["wall_s"], "status": res["status"],
             "failed_requests": res["failed_requests"]}))
         return
-    if args.impl == "reference":
-        rank = int(os.environ.get("RANK", 0))
-        if rank != 0:
-            return
-        print(json.dumps(run_reference(args, Dist.__new__(Dist))))
-        return
     dist = Dist("nccl")
+    if args.workload == "serving":
+        line = serving_line(args, dist)
+    else:
+        line = step_line(args, dist)
+    if dist.rank == 0:
+        print(json.dumps(line))
+    dist.close()
+
+
+def serving_line(args, dist) -> dict:
+    res = serving_contract(args, dist)
+    steady, e2e = res["steady"], res["e2e"]
+    seconds = steady["elapsed_ms"] / 1e3
+    value = steady["frames"] * dist.world / seconds
+    e2e_value = res["e2e_frames_all"] / (res["e2e_ms"] / 1e3)
+    ticks = max(1, e2e["ticks"])
+    line = {
+        "metric": SERVING_METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": steady["elapsed_ms"] / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": value / REFERENCE_C64_FRAMES, "dtype": "bf16",
+        "data": "synthetic (BASELINE config 5 request recipe, seeded random-init weights)",
+        "config": dict(serving_config(args, dist.world), steady_context=steady["context"],
+                       steady_mean_position=steady["mean_position"]),
+        "roofline": res["roofline"],
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": e2e["h2d"] / ticks,
+                "d2h_bytes_per_step": (e2e["pcm_bytes"] + e2e["token_bytes"]) / ticks, "ticks": e2e["ticks"],
+                "frames": e2e["frames"], "ms": res["e2e_ms"], "method": "CUDA events around the closed-loop pass"},
+        "ttfa_p50_ms": e2e["ttfa_p50_ms"], "ttfa_p95_ms": e2e["ttfa_p95_ms"], "rtf": e2e["rtf_mean"],
+        "failed_requests": e2e["failed_requests"],
+        "gpu_launches": steady["launches"], "tick_graph_kernels": steady["tick_launches"],
+        "status_word": res["status"],
+        "clocks": res["clocks"],
+    }
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        per_tick, threads = cpu_serving_sample(args, 3)
+        line["cpu_baseline"] = {"value": SERVING_SLOTS / per_tick, "unit": UNIT, "cores": threads, "kind": "port",
+                                "sample": CPU_SERVING_SAMPLE + " of 3 ticks"}
+    return line
+
+
+# the reference's published throughput at C=64 (1x Ascend 910B1, bf16, mean of 3 runs)
+REFERENCE_C64_FRAMES = 549.39
+
+
+def step_line(args, dist) -> dict:
     res = run_b200(args, dist)
     cfg = res["cfg"]
     frames = SLOTS * args.steps * dist.world
@@ -778,20 +1074,19 @@ def main():
     kv_step = int(((positions + 1).sum()).item()) * cfg.kv_heads * cfg.head_dim * 2 * 2 * cfg.layers
     step_bytes = cfg.weight_bytes() + kv_step
     e2e_value = SLOTS * res["e2e_steps"] * dist.world / (res["e2e_ms"] / 1e3)
+    dom_traffic, dom_source = traffic(dom_name) if SLOTS == 32 else (None, None)
     line = {
-        "metric": f"codec frames/s (talker decode step, C={SLOTS})", "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": res["elapsed_ms"] / args.steps, "higher_is_better": True,
+        "metric": f"codec frames/s (talker decode step, C={SLOTS})", "value": value, "unit": UNIT,
+        "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": res["elapsed_ms"] / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights)",
-        "config": {"workload": f"BASELINE config 2: talker decode step, {SLOTS} slots, ctx U[64,2048], "
-                               "greedy, evict/admit 4 slots every 16 steps",
-                   "layers": cfg.layers, "global_batch": SLOTS * dist.world, "slots_per_gpu": SLOTS,
-                   "parallelism": f"replicas x{dist.world} (request-level data parallel)",
-                   "l2": f"inputs > L2 ({step_bytes / 1e9:.1f} GB streamed per step)",
-                   "hbm_fraction_step": step_bytes / (res["elapsed_ms"] / args.steps / 1e3) / (peak * 1e9),
-                   "bytes_per_step": step_bytes},
+        "config": dict(step_config(cfg, SLOTS, dist.world),
+                       l2=f"inputs > L2 ({step_bytes / 1e9:.1f} GB streamed per step)",
+                       hbm_fraction_step=step_bytes / (res["elapsed_ms"] / args.steps / 1e3) / (peak * 1e9),
+                       bytes_per_step=step_bytes),
         "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "peak_kind": peak_kind,
-                     "traffic": profile_traffic(dom_name),
+                     "frac": achieved / peak, "peak_kind": peak_kind, "traffic": dom_traffic,
+                     "traffic_source": dom_source,
                      "method": ("in graph: the step's back-to-back launches over every layer's K/V, CUDA events"
                                 if in_graph else "alone, L2 flushed between launches, CUDA events"),
                      "achieved_alone": dom["bytes"] / dom["seconds"] / 1e9},
@@ -809,9 +1104,7 @@ def main():
                                 "sample": f"oracle fp32 talker, 2 of 28 layers at full width, {SLOTS} slots, "
                                           "same contexts, median of 3 steps scaled by 14; value_4_threads = the "
                                           "same at 4 threads (the reference's default torch thread count)"}
-    if dist.rank == 0:
-        print(json.dumps(line))
-    dist.close()
+    return line
 
 
 if __name__ == "__main__":

@@ -191,6 +191,44 @@ int q3t_linear_ex(const void* x, int64_t x_stride, int64_t rows, int64_t in_feat
                   int64_t residual_stride, const void* scale, float eps, const void* weight_tiles,
                   const void* prefetch, size_t prefetch_bytes, int flags, unsigned* status, void* stream);
 
+/* A chain of dependent projections in one persistent launch: the projections a decode
+ * layer runs between two attentions (PackedAttention's o_proj, packed_attention.py:85,
+ * then PackedMLP's gate/up and down, packed_mlp.py:19-27, then the next layer's packed
+ * QKV, packed_attention.py:42, with the RMSNorms of operators.py:16-23 folded in as in
+ * q3t_linear_rownorm), or the last layer's projections followed by a codebook head.
+ * Stage s computes out_s = epilogue(x_s @ W_s^T) exactly as q3t_linear(_rownorm) would
+ * (W_s given as q3t_pack_weight_tiles tiles), but no stage waits for a kernel boundary:
+ * every SM streams its even share of all the stages' weight tiles without a break, and
+ * only the activation tiles of stage s wait until stage `depends` has stored all its
+ * outputs (depends = -1: stage s reads only what earlier kernels wrote). Split-K partials
+ * are reduced in a fixed order (deterministic). */
+#define Q3T_CHAIN_MAX_STAGES 8
+typedef struct {
+  const void* x;              /* bf16 [rows, in_features], row stride x_stride */
+  int64_t x_stride;
+  const void* weight_tiles;   /* q3t_pack_weight_tiles of the bf16 [out_features, in_features] weight */
+  int64_t in_features, out_features;
+  void* out;                  /* bf16, or fp32 with Q3T_EPI_STORE; row stride out_stride */
+  int64_t out_stride;
+  int out_dtype;              /* Q3T_BF16 or Q3T_F32 */
+  int epilogue;               /* Q3T_EPI_STORE, Q3T_EPI_RESIDUAL or Q3T_EPI_SWIGLU_PAIRED */
+  const void* residual;       /* bf16, Q3T_EPI_RESIDUAL (may alias out) */
+  int64_t residual_stride;
+  const void* bias;           /* bf16 [out_features] or NULL */
+  float row_norm_eps;         /* > 0: folded RMSNorm of x (see q3t_linear_rownorm); 0: none */
+  int depends;                /* earlier stage whose output x (or the residual) reads; -1: none */
+} q3t_chain_stage;
+
+/* Workspace of q3t_linear_chain for `rows` activation rows (1..64): a counter block and the
+ * split-K partials. Zero it once before the first call; every call leaves the counters zero. */
+size_t q3t_linear_chain_workspace_bytes(int64_t rows);
+
+/* Runs `count` (1..Q3T_CHAIN_MAX_STAGES) stages on `rows` (1..64) activation rows. Every stage
+ * needs at least as many weight tiles x k-blocks as the device has SMs. One workspace per
+ * stream: two chains sharing a workspace must not overlap on the GPU. */
+int q3t_linear_chain(const q3t_chain_stage* stages, int count, int64_t rows, void* workspace,
+                     size_t workspace_bytes, unsigned* status, void* stream);
+
 /* Weight re-layout done once at load, in place of the reference's packed QKV and gate/up
  * concatenations (packed_attention.py:17-22, packed_mlp.py:13-14).
  * Pre-swizzled weight layout for q3t_linear (pass it as weight_tiles, weight may

@@ -25,6 +25,18 @@ _f32 = ctypes.c_float
 _u64 = ctypes.c_uint64
 _sz = ctypes.c_size_t
 
+CHAIN_MAX_STAGES = 8
+
+
+class ChainStage(ctypes.Structure):
+    """q3t_chain_stage (include/q3t.h): one projection of a q3t_linear_chain."""
+    _fields_ = [("x", ctypes.c_void_p), ("x_stride", ctypes.c_int64), ("weight_tiles", ctypes.c_void_p),
+                ("in_features", ctypes.c_int64), ("out_features", ctypes.c_int64), ("out", ctypes.c_void_p),
+                ("out_stride", ctypes.c_int64), ("out_dtype", ctypes.c_int), ("epilogue", ctypes.c_int),
+                ("residual", ctypes.c_void_p), ("residual_stride", ctypes.c_int64), ("bias", ctypes.c_void_p),
+                ("row_norm_eps", ctypes.c_float), ("depends", ctypes.c_int)]
+
+
 # name -> (restype, argtypes); mirrors include/q3t.h exactly.
 SIGNATURES: dict[str, tuple[object, list]] = {
     "q3t_abi_version": (_i32, []),
@@ -81,6 +93,8 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "q3t_tick_commit": (_i32, [_p, _p, _i64, _i64, _p, _p, _p, _i64, _p, _p, _p, _i64, _i64, _p]),
     "q3t_code_ring_write": (_i32, [_p, _i64, _p, _p, _i64, _i64, _i64, _p]),
     "q3t_code_ring_read": (_i32, [_p, _i64, _i64, _i64, _p, _p, _i64, _i64, _p, _p, _p]),
+    "q3t_linear_chain_workspace_bytes": (_sz, [_i64]),
+    "q3t_linear_chain": (_i32, [_p, _i32, _i64, _p, _sz, _p, _p]),
 }
 
 _lock = threading.Lock()

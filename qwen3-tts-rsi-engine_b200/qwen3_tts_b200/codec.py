@@ -215,6 +215,8 @@ class CodecStep:
         self.status = ops.status_word(dev)
         self.ws_attn = None
         self.graph = None
+        self.launches = 0          # this library's kernels per replay (counted at capture)
+        self.replays = 0
         self._allocate(dev)
 
     def _b(self, name, rows, cols):
@@ -359,8 +361,10 @@ class CodecStep:
         torch.cuda.current_stream().wait_stream(stream)
         torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
+        before = _lib.launch_count()
         with torch.cuda.graph(self.graph, stream=stream):
             self.compute()
+        self.launches = _lib.launch_count() - before     # this library's kernels per replay
         torch.cuda.synchronize()
         for buf, original in zip(self.state.buffers, saved):
             buf.index_copy_(0 if buf is not self.state.kv else 1, self.indices, original)
@@ -373,6 +377,7 @@ class CodecStep:
             self.compute()
         else:
             self.graph.replay()
+            self.replays += 1
         return (self.wave.clone(), self.pcm.clone()) if clone else (self.wave, self.pcm)
 
     def close(self) -> None:

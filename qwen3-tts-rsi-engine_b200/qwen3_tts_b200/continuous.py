@@ -35,7 +35,7 @@ from dataclasses import dataclass, field
 import numpy as np
 import torch
 
-from . import checkpoint, ops
+from . import _lib, checkpoint, ops
 from .batching import context_bucket, decode_batch_size, emission_target
 from .code_buffer import CodecCodeBuffer
 from .codec import CodecGraph, CodecSlots, pack_codec
@@ -122,6 +122,8 @@ class TickGraph:
         self.talk.positions, self.talk.rotary = shared["positions"], shared["rotary"]
         self.uniform, self.steps = shared["uniform"], shared["steps"]
         self.graph = None
+        self.launches = 0          # this library's kernels per replay (counted at capture)
+        self.replays = 0
 
     def compute(self) -> None:
         e, S, B, p, t = self.engine, self.engine.state, self.batch, self.pred, self.talk
@@ -153,8 +155,10 @@ class TickGraph:
         torch.cuda.current_stream().wait_stream(stream)
         torch.cuda.synchronize(e.device)
         self.graph = torch.cuda.CUDAGraph()
+        before = _lib.launch_count()
         with torch.cuda.graph(self.graph, stream=stream):
             self.compute()
+        self.launches = _lib.launch_count() - before     # this library's kernels per replay
         torch.cuda.synchronize(e.device)
         e.arena.packed[:, :B, :, 0].copy_(saved_kv)
         S.tokens[:B].copy_(saved[0])
@@ -166,6 +170,7 @@ class TickGraph:
             self.compute()
         else:
             self.graph.replay()
+            self.replays += 1
 
     def close(self) -> None:
         if self.graph is not None:
@@ -420,6 +425,22 @@ class ContinuousModel:
     def emit_audio(self, selected, emit) -> None:
         """Decode due chunks grouped by length (<= codec_batch_size streams per call), convert
         to PCM16 on the device and deliver after one host copy (continuous.py:475-539)."""
+        pending = self.decode_chunks(selected)
+        if not pending:
+            return
+        for (group, _), block in zip(pending, self._to_host([pcm for _, pcm in pending])):
+            for row, (state, _, skip) in enumerate(group):
+                data = block[row, skip:].astype("<i2").tobytes()
+                state.audio.append(data)
+                state.emitted = state.frames
+                if emit is not None:
+                    emit(state.identifier, data, SAMPLE_RATE)
+
+    def decode_chunks(self, selected) -> list:
+        """The device half of emit_audio: decode every pending chunk of `selected` (frames
+        state.emitted .. state.frames, or the windowed span with its left context) and return
+        [(group, pcm16 device block)], group = [(state, start frame, samples to skip)]. Nothing
+        is copied to the host and no request state changes."""
         slots = {id(state): index for index, state in enumerate(self.states)}
         groups: dict[int, list] = {}
         for state in selected:
@@ -441,15 +462,7 @@ class ContinuousModel:
         if lanes:
             outputs = self.codec.decode_groups([(indices, codes) for _, indices, codes in lanes])
             pending += [(group, out[1]) for (group, _, _), out in zip(lanes, outputs)]
-        if not pending:
-            return
-        for (group, _), block in zip(pending, self._to_host([pcm for _, pcm in pending])):
-            for row, (state, _, skip) in enumerate(group):
-                data = block[row, skip:].astype("<i2").tobytes()
-                state.audio.append(data)
-                state.emitted = state.frames
-                if emit is not None:
-                    emit(state.identifier, data, SAMPLE_RATE)
+        return pending
 
     def _decode_group(self, indices, starts, length):
         """PCM16 [len(indices), length * 1920] (device) of frames starts[i] .. + length of each slot."""

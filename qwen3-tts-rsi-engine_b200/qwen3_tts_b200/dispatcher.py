@@ -9,7 +9,9 @@ independent ``ContinuousModel`` replicas with no collective on the data path.
 * each new request goes to the live engine with the fewest requests in flight
   (ties: lowest rank), never above ``per_engine``;
 * each engine process (``engine_main``) runs its own tick loop on its GPU and
-  streams ``delta`` / ``done`` events back over one shared queue;
+  streams ``delta`` / ``done`` events back over one shared queue; a request's PCM
+  crosses the process boundary once, as its deltas (``done`` carries the record
+  without the audio, which the dispatcher reassembles from the deltas it relayed);
 * cancellations go to the engine that owns the request;
 * failure detection is on the host: an engine that raises or whose process
   exits is marked dead, its in-flight requests complete with
@@ -77,7 +79,8 @@ def engine_main(rank: int, device: str, kwargs: dict, inbox, outbox, factory: st
 
             for identifier, output in model.tick(submissions, emit, cancelled):
                 active.discard(identifier)
-                outbox.put(("done", rank, identifier, output))
+                # the audio already crossed as deltas: the record travels without its PCM
+                outbox.put(("done", rank, identifier, {k: v for k, v in output.items() if k != "pcm"}))
     except Exception as error:
         LOGGER.exception("engine %d failed", rank)
         outbox.put(("failed", rank, repr(error)))
@@ -213,9 +216,10 @@ class Dispatcher:
                         emit(identifier, event[3], event[4])
             elif kind == "done":
                 identifier = event[2]
-                if engine.requests.pop(identifier, None) is not None:
+                delivered = engine.requests.pop(identifier, None)
+                if delivered is not None:
                     self.owner.pop(identifier, None)
-                    outputs.append((identifier, event[3]))
+                    outputs.append((identifier, dict(event[3], pcm=b"".join(delivered))))
             elif kind == "failed":
                 self._fail_engine(engine, event[2], outputs)
             elif kind == "hello":

@@ -7,6 +7,7 @@ written, as the reference wrappers do.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 from typing import Optional
 
@@ -340,6 +341,58 @@ def linear(x, weight, bias=None, *, out=None, out_dtype=BF16, epilogue: int = _l
          _ptr(workspace), workspace.numel() if workspace is not None else 0, status_word(x.device).data_ptr(),
          _stream())
     return out
+
+
+def linear_chain_workspace(rows: int, device) -> torch.Tensor:
+    """Zeroed workspace of q3t_linear_chain for `rows` activation rows (one per stream of chains)."""
+    nbytes = int(_lib.load().q3t_linear_chain_workspace_bytes(rows))
+    if nbytes == 0:
+        raise ValueError("linear_chain: rows must be within 1..64")
+    return torch.zeros(nbytes, dtype=torch.uint8, device=device)
+
+
+def linear_chain(stages, workspace: torch.Tensor) -> None:
+    """A chain of dependent projections in one persistent launch (q3t_linear_chain).
+
+    Each stage is a dict: x (bf16 [rows, in], unit inner stride), weight (TiledWeight), out
+    (bf16 or fp32 [rows, out or out/2 for SwiGLU]), and optionally epilogue (EPI_STORE,
+    EPI_RESIDUAL, EPI_SWIGLU_PAIRED), residual, bias, row_norm_eps (folded RMSNorm), depends
+    (the earlier stage whose output this stage reads; default: the previous stage, -1 for
+    the first). Stage s computes what ops.linear(x, weight, ...) would, with every SM
+    streaming weights across the whole chain."""
+    if not 1 <= len(stages) <= _lib.CHAIN_MAX_STAGES:
+        raise ValueError(f"linear_chain: 1..{_lib.CHAIN_MAX_STAGES} stages")
+    rows = None
+    table = (_lib.ChainStage * len(stages))()
+    for i, st in enumerate(stages):
+        x, w, out = st["x"], st["weight"], st["out"]
+        if not isinstance(w, TiledWeight):
+            raise ValueError("linear_chain: weights must be TiledWeight (ops.pack_tiles)")
+        _need_cuda(x, w.tiles, out)
+        if x.dtype != BF16 or x.ndim != 2 or x.stride(1) != 1 or x.shape[1] != w.in_features:
+            raise ValueError("linear_chain: x must be BF16 [rows, in_features] with unit inner stride")
+        if rows is None:
+            rows = x.shape[0]
+        epi = st.get("epilogue", _lib.EPI_STORE)
+        n_out = w.out_features // 2 if epi == _lib.EPI_SWIGLU_PAIRED else w.out_features
+        if x.shape[0] != rows or out.ndim != 2 or out.shape != (rows, n_out) or out.stride(1) != 1:
+            raise ValueError("linear_chain: every stage has the same rows; out must be [rows, out_features]")
+        res, bias = st.get("residual"), st.get("bias")
+        if res is not None and (res.shape != out.shape or res.stride(1) != 1 or res.dtype != BF16):
+            raise ValueError("linear_chain: residual must be BF16 shaped like out")
+        eps = st.get("row_norm_eps")
+        e = table[i]
+        e.x, e.x_stride, e.weight_tiles = x.data_ptr(), x.stride(0), w.tiles.data_ptr()
+        e.in_features, e.out_features = w.in_features, w.out_features
+        e.out, e.out_stride = out.data_ptr(), out.stride(0)
+        e.out_dtype = _lib.Q3T_BF16 if out.dtype == BF16 else _lib.Q3T_F32
+        e.epilogue = epi
+        e.residual, e.residual_stride = _ptr(res), res.stride(0) if res is not None else 0
+        e.bias = _ptr(bias)
+        e.row_norm_eps = float(eps) if eps is not None else 0.0
+        e.depends = int(st.get("depends", i - 1))
+    call("q3t_linear_chain", ctypes.cast(table, ctypes.c_void_p), len(stages), rows, workspace.data_ptr(),
+         workspace.numel(), status_word(workspace.device).data_ptr(), _stream())
 
 
 # ------------------------------------------------------------------ attention

@@ -23,7 +23,8 @@ import torch
 
 from . import _lib, ops
 from .config import PredictorConfig
-from .talker import rope_tables
+from . import talker
+from .talker import mlp_stages, qkv_stage, rope_tables
 from .weights import pack_decoder
 
 BF16 = torch.bfloat16
@@ -68,6 +69,11 @@ class PredictorStep:
         self.ws_attn = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
         self.status = ops.status_word(dev)
         self.prefetch_weights = True  # GEMMs pull the next GEMM's weights into L2
+        # steps >= 1 (one row per slot, <= 64 rows): each layer's O, gate/up, down and the next
+        # layer's QKV (or the codebook head after the last layer) run as one q3t_linear_chain launch
+        self.use_chain = (talker.CHAIN_PROJECTIONS and B <= 64 and weights["layers"][0].folded and weights.get("heads_folded", False)
+                          and isinstance(weights["layers"][0].qkv, ops.TiledWeight))
+        self.ws_chain = ops.linear_chain_workspace(B, dev) if self.use_chain else None
         # Layers [0, keep_layers) load their weights evict-last (Q3T_LINEAR_KEEP_WEIGHTS) to keep them
         # in L2 across the 15 codebook steps; measured no faster (the GEMMs are latency-bound), so off.
         self.keep_layers = 0
@@ -117,6 +123,29 @@ class PredictorStep:
         if not self.w.get("heads_folded", False):
             ops.rms_norm(x, self.w["norm"], self.cfg.eps, out=self.xn[:rows])
 
+    def _chained_step(self, step: int) -> None:
+        """Steps >= 1 with the projections as chains: QKV of layer 0, then per layer the fused
+        attention and one chain (O, gate/up, down, next QKV; the last layer's chain ends with
+        codebook head `step`, final norm folded in, fp32 logits)."""
+        cfg, B = self.cfg, self.batch
+        x = self.x[:B]
+        layers = self.w["layers"]
+        positions = self.pos[step - 1]
+        ops.linear_chain([qkv_stage(x, layers[0], self.qkv[:B], cfg.eps, depends=-1)], self.ws_chain)
+        for i, layer in enumerate(layers):
+            keys, values = self.cache[i], self.cache[cfg.layers + i]
+            ops.decode_attention_qkv(self.qkv[:B], layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin,
+                                     positions, keys, values, positions, q_heads=cfg.q_heads,
+                                     kv_heads=cfg.kv_heads, head_dim=cfg.head_dim, context=keys.shape[2],
+                                     out=self.attn[:B], workspace=self.ws_attn)
+            stages = mlp_stages(self.attn[:B].view(B, cfg.q_width), x, layer, x, self.act[:B], cfg.eps)
+            if i + 1 < len(layers):
+                stages.append(qkv_stage(x, layers[i + 1], self.qkv[:B], cfg.eps, depends=2))
+            else:
+                stages.append({"x": x, "weight": self.w["heads"][step], "out": self._logits(step),
+                               "row_norm_eps": cfg.eps, "depends": 2})
+            ops.linear_chain(stages, self.ws_chain)
+
     def _head(self, step: int, last: slice) -> None:
         """Codebook head `step` on the last decoder row of every slot (`last` picks those rows of
         x / xn). With folded heads the final RMSNorm weight is inside the head matrix and the GEMM
@@ -156,8 +185,11 @@ class PredictorStep:
             else:
                 ops.embedding(self.codes[:, step], w["embeddings"][step - 1], out=self.e)
                 lw(self.e, w["proj"], w["proj_bias"], out=self.x[:B], workspace=self.ws_linear)
-            self._layers(B, 1, self.pos[step - 1], tail=w["heads"][step])
-            self._head(step, slice(0, B))
+            if self.use_chain:
+                self._chained_step(step)
+            else:
+                self._layers(B, 1, self.pos[step - 1], tail=w["heads"][step])
+                self._head(step, slice(0, B))
             self._sample(step)
         ops.frame_embed(self.codes, self.talker_embedding, w["embeddings"], self.text, out=self.embeds)
 

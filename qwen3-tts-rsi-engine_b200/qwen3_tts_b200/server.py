@@ -105,12 +105,113 @@ def delta(pcm: bytes, sample_rate: int) -> dict:
             "channels": 1}
 
 
+def settle(future, channel, output) -> None:
+    """Complete a request's future from the engine's result record (a failed audio channel wins)."""
+    if future.done():
+        return
+    if channel.error is not None:
+        future.set_exception(channel.error)
+    else:
+        future.set_result(output)
+
+
+class OwnerThread:
+    """The single thread that owns the model and does all device work (the engine is not
+    thread-safe and CUDA graphs are replayed from one host thread)."""
+
+    def __init__(self):
+        self._pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="model-owner")
+
+    async def call(self, fn, *args, **kwargs):
+        return await asyncio.get_running_loop().run_in_executor(self._pool, partial(fn, *args, **kwargs))
+
+    def shutdown(self) -> None:
+        self._pool.shutdown(wait=True, cancel_futures=True)
+
+
+class RequestBook:
+    """Requests admitted to a continuous model, keyed by the integer identifier the engine
+    sees (0, 1, 2, ... in admission order). Every entry taken from the service queue is
+    matched by exactly one ``task_done`` - when it is found cancelled before admission, when
+    its cancellation is passed to the engine, when the engine returns its result, or when the
+    engine fails - so ``queue.join()`` tracks requests still in flight."""
+
+    def __init__(self, queue: asyncio.Queue, slots: int, budget: int, interval: int):
+        self.queue, self.slots, self.budget, self.interval = queue, slots, budget, interval
+        self.entries: dict = {}          # identifier -> (payload, future, channel)
+        self.issued = 0                  # identifiers handed out
+        self.ticks = 0
+
+    def _admit(self, entry, into: list) -> None:
+        payload, future, _ = entry
+        if future.cancelled():           # the client left while the request was queued
+            self.queue.task_done()
+            return
+        self.entries[self.issued] = entry
+        into.append((self.issued, payload))
+        self.issued += 1
+
+    def withdraw_cancelled(self) -> list:
+        """Identifiers whose clients went away; the engine drops them on the next tick."""
+        gone = [ident for ident, (_, future, _) in self.entries.items() if future.cancelled()]
+        for ident in gone:
+            del self.entries[ident]
+            self.queue.task_done()
+        return gone
+
+    async def next_admissions(self, withdrawn: list) -> list:
+        """New requests for this tick: with nothing in flight, wait for one; then take queued
+        requests up to the slot count and the per-tick budget, every `interval` ticks (at once
+        when the engine is idle)."""
+        fresh: list = []
+        idle = not self.entries
+        if idle and not withdrawn:
+            self._admit(await self.queue.get(), fresh)
+            if not fresh:
+                return None              # it was cancelled while queued: look again
+        if idle or fresh or self.ticks % self.interval == 0:
+            while len(self.entries) < self.slots and len(fresh) < self.budget and not self.queue.empty():
+                self._admit(self.queue.get_nowait(), fresh)
+        return fresh
+
+    def relay(self, streaming: bool):
+        """The engine's emit callback: chunks go to the request's audio channel when streaming."""
+        def emit(ident, pcm, rate):
+            entry = self.entries.get(ident)
+            if entry is not None and streaming:
+                entry[2].emit(pcm, rate)
+        return emit
+
+    def finish(self, results) -> None:
+        self.ticks += 1
+        for ident, output in results:
+            _, future, channel = self.entries.pop(ident)
+            settle(future, channel, output)
+            self.queue.task_done()
+
+    def fail(self, error: Exception) -> None:
+        for _, future, _ in self.entries.values():
+            if not future.done():
+                future.set_exception(error)
+            self.queue.task_done()
+        self.entries.clear()
+
+    def abandon(self) -> None:
+        for _, future, channel in self.entries.values():
+            channel.close()
+            future.cancel()
+
+
 class SpeechService:
+    """The HTTP/SSE service: handlers validate and queue requests; one worker task feeds
+    them to the model on the owner thread, either as micro-batches (``generate``) or through
+    the continuous ``tick`` loop (``--continuous``)."""
+
     def __init__(self, options, model_factory):
         self.options = options
         self.model_factory = model_factory
         self.queue: asyncio.Queue = asyncio.Queue(maxsize=options.queue_size)
-        self.executor = ThreadPoolExecutor(max_workers=1, thread_name_prefix="model-owner")
+        self.owner = OwnerThread()
         self.model = None
         self.worker = None
         self.failure = None
@@ -120,117 +221,82 @@ class SpeechService:
         return bool(getattr(self.options, "streaming", False))
 
     async def start(self, app) -> None:
-        loop = asyncio.get_running_loop()
-        self.model = await loop.run_in_executor(self.executor, self.model_factory, str(self.options.model),
-                                                self.options.device)
-        loop_fn = self.run_continuous if getattr(self.options, "continuous", False) else self.run
-        self.worker = asyncio.create_task(loop_fn())
+        self.model = await self.owner.call(self.model_factory, str(self.options.model), self.options.device)
+        continuous = getattr(self.options, "continuous", False)
+        self.worker = asyncio.create_task(self.run_continuous() if continuous else self.run())
 
     async def stop(self, app) -> None:
         if self.worker is not None:
             self.worker.cancel()
             await asyncio.gather(self.worker, return_exceptions=True)
         if self.model is not None:
-            await asyncio.get_running_loop().run_in_executor(self.executor, self.model.close)
-        self.executor.shutdown(wait=True, cancel_futures=True)
+            await self.owner.call(self.model.close)
+        self.owner.shutdown()
 
     # ------------------------------------------------------------------ micro-batch mode
+    async def _collect_batch(self) -> list:
+        batch = [await self.queue.get()]
+        wait_ms = getattr(self.options, "batch_wait_ms", 0)
+        if wait_ms:
+            await asyncio.sleep(wait_ms / 1000)
+        while len(batch) < self.options.max_batch_size and not self.queue.empty():
+            batch.append(self.queue.get_nowait())
+        return batch
+
+    async def _generate(self, group: list) -> None:
+        """One generate() call for requests sharing (seed, max_new_tokens); results in order."""
+        emit = None
+        if self.streaming:
+            def emit(index, pcm, rate):
+                group[index][2].emit(pcm, rate)
+        try:
+            outputs = await self.owner.call(self.model.generate, [payload for payload, _, _ in group],
+                                            **({"emit": emit} if emit else {}))
+            if len(outputs) != len(group):
+                raise RuntimeError("Model batch output count mismatch")
+        except Exception as error:
+            LOGGER.exception("Model batch failed")
+            for _, future, _ in group:
+                if not future.done():
+                    future.set_exception(error)
+            return
+        for (_, future, channel), output in zip(group, outputs):
+            settle(future, channel, output)
+
     async def run(self) -> None:
-        loop = asyncio.get_running_loop()
         while True:
-            batch = [await self.queue.get()]
-            if getattr(self.options, "batch_wait_ms", 0):
-                await asyncio.sleep(self.options.batch_wait_ms / 1000)
-            while len(batch) < self.options.max_batch_size and not self.queue.empty():
-                batch.append(self.queue.get_nowait())
+            batch = await self._collect_batch()
             groups: dict = {}
             for entry in batch:
                 if not entry[1].cancelled():
                     groups.setdefault((entry[0]["seed"], entry[0]["max_new_tokens"]), []).append(entry)
             for group in groups.values():
-                operation = self.model.generate
-                if self.streaming:
-                    operation = partial(operation, emit=lambda i, pcm, rate, g=group: g[i][2].emit(pcm, rate))
-                try:
-                    outputs = await loop.run_in_executor(self.executor, operation, [p for p, _, _ in group])
-                    if len(outputs) != len(group):
-                        raise RuntimeError("Model batch output count mismatch")
-                    for (_, future, channel), output in zip(group, outputs):
-                        self._resolve(future, channel, output)
-                except Exception as error:
-                    LOGGER.exception("Model batch failed")
-                    for _, future, _ in group:
-                        if not future.done():
-                            future.set_exception(error)
+                await self._generate(group)
             for _ in batch:
                 self.queue.task_done()
 
-    @staticmethod
-    def _resolve(future, channel, output) -> None:
-        if future.done():
-            return
-        if channel.error is not None:
-            future.set_exception(channel.error)
-        else:
-            future.set_result(output)
-
     # ------------------------------------------------------------------ continuous mode
     async def run_continuous(self) -> None:
-        loop = asyncio.get_running_loop()
-        pending: dict = {}
-        next_id, ticks = 0, 0
-        interval = getattr(self.options, "prefill_interval", 1)
-        budget = getattr(self.options, "prefill_per_tick", 4)
-        while True:
-            cancelled = [i for i, (_, future, _) in pending.items() if future.cancelled()]
-            for identifier in cancelled:
-                del pending[identifier]
-                self.queue.task_done()
-            submissions = []
-
-            def admit(entry):
-                nonlocal next_id
-                if entry[1].cancelled():
-                    self.queue.task_done()
-                    return
-                pending[next_id] = entry
-                submissions.append((next_id, entry[0]))
-                next_id += 1
-
-            if not pending and not cancelled:
-                admit(await self.queue.get())   # idle: block for the next request
-                if not submissions:
+        book = RequestBook(self.queue, self.options.max_batch_size, getattr(self.options, "prefill_per_tick", 4),
+                           getattr(self.options, "prefill_interval", 1))
+        emit = book.relay(self.streaming)
+        try:
+            while True:
+                withdrawn = book.withdraw_cancelled()
+                fresh = await book.next_admissions(withdrawn)
+                if fresh is None:
                     continue
-            if not pending or ticks % interval == 0 or submissions:
-                while (len(pending) < self.options.max_batch_size and len(submissions) < budget
-                       and not self.queue.empty()):
-                    admit(self.queue.get_nowait())
-
-            def emit(identifier, pcm, rate):
-                entry = pending.get(identifier)
-                if entry is not None and self.streaming:
-                    entry[2].emit(pcm, rate)
-
-            try:
-                outputs = await loop.run_in_executor(self.executor, self.model.tick, submissions, emit, cancelled)
-            except asyncio.CancelledError:
-                for _, future, channel in pending.values():
-                    channel.close()
-                    future.cancel()
-                raise
-            except Exception as error:
-                LOGGER.exception("Continuous model failed")
-                self.failure = error
-                for _, future, _ in pending.values():
-                    if not future.done():
-                        future.set_exception(error)
-                    self.queue.task_done()
-                return
-            ticks += 1
-            for identifier, output in outputs:
-                _, future, channel = pending.pop(identifier)
-                self._resolve(future, channel, output)
-                self.queue.task_done()
+                try:
+                    results = await self.owner.call(self.model.tick, fresh, emit, withdrawn)
+                except Exception as error:     # the engine is unusable: fail everything in flight
+                    LOGGER.exception("Continuous model failed")
+                    self.failure = error
+                    book.fail(error)
+                    return
+                book.finish(results)
+        except asyncio.CancelledError:
+            book.abandon()
+            raise
 
     # ------------------------------------------------------------------ HTTP
     async def health(self, incoming):
@@ -243,6 +309,29 @@ class SpeechService:
             body["engine"] = stats.as_dict()
         return web.json_response(body, status=503 if self.failure else 200)
 
+    async def _events(self, future, channel):
+        """The SSE events of one request: streamed chunks while the request runs, then the
+        tail of the final waveform the stream has not carried, then the done record."""
+        sent = 0
+        while self.streaming and not future.done():
+            chunk = asyncio.ensure_future(channel.queue.get())
+            try:
+                await asyncio.wait((future, chunk), return_when=asyncio.FIRST_COMPLETED)
+            finally:
+                if not chunk.done():
+                    chunk.cancel()
+                    await asyncio.gather(chunk, return_exceptions=True)
+            if chunk.done() and not chunk.cancelled():
+                pcm, rate = chunk.result()
+                sent += len(pcm)
+                yield delta(pcm, rate)
+        output = await future
+        if sent > len(output["pcm"]):
+            raise RuntimeError("Streaming output exceeded final waveform length")
+        yield delta(output["pcm"][sent:], output["sample_rate"])
+        yield {"type": "speech.audio.done", "finish_reason": output["finish_reason"],
+               "codec_frames": output["codec_frames"]}
+
     async def speech(self, incoming):
         from aiohttp import web
         if self.failure is not None:
@@ -252,8 +341,7 @@ class SpeechService:
         except (ValueError, TypeError) as error:
             return web.json_response({"error": str(error)}, status=400)
         loop = asyncio.get_running_loop()
-        future = loop.create_future()
-        channel = AudioChannel(loop)
+        future, channel = loop.create_future(), AudioChannel(loop)
         try:
             self.queue.put_nowait((request, future, channel))
         except asyncio.QueueFull:
@@ -261,26 +349,8 @@ class SpeechService:
         response = web.StreamResponse(headers={"Content-Type": "text/event-stream"})
         try:
             await response.prepare(incoming)
-            sent = 0
-            while self.streaming:
-                chunk = asyncio.ensure_future(channel.queue.get())
-                try:
-                    done, _ = await asyncio.wait((future, chunk), return_when=asyncio.FIRST_COMPLETED)
-                finally:
-                    if not chunk.done():
-                        chunk.cancel()
-                        await asyncio.gather(chunk, return_exceptions=True)
-                if chunk not in done:
-                    break
-                pcm, rate = chunk.result()
-                await response.write(sse(delta(pcm, rate)))
-                sent += len(pcm)
-            output = await future
-            if sent > len(output["pcm"]):
-                raise RuntimeError("Streaming output exceeded final waveform length")
-            await response.write(sse(delta(output["pcm"][sent:], output["sample_rate"])))
-            await response.write(sse({"type": "speech.audio.done", "finish_reason": output["finish_reason"],
-                                      "codec_frames": output["codec_frames"]}))
+            async for event in self._events(future, channel):
+                await response.write(sse(event))
         except asyncio.CancelledError:
             future.cancel()
             raise
@@ -432,18 +502,30 @@ def engine_factory(options):
     return build
 
 
+ROUTES = (("GET", "/health", "health"), ("POST", "/v1/audio/speech", "speech"))
+
+
+def build_app(options):
+    """The aiohttp application: the service's routes, model start-up and shutdown. The engine
+    factory sees `max_batch_size` per engine; the service admits that many per GPU."""
+    from aiohttp import web
+    factory = engine_factory(argparse.Namespace(**vars(options)))
+    options = argparse.Namespace(**vars(options))
+    options.max_batch_size *= max(1, options.gpus)
+    service = SpeechService(options, factory)
+    app = web.Application(client_max_size=1024 * 1024)
+    for method, path, handler in ROUTES:
+        app.router.add_route(method, path, getattr(service, handler))
+    app.on_startup.append(service.start)
+    app.on_cleanup.append(service.stop)
+    return app
+
+
 def main(argv=None) -> None:
     from aiohttp import web
     options = parse_options(argv)
     logging.basicConfig(level=logging.INFO)
-    factory = engine_factory(options)
-    options.max_batch_size *= max(1, options.gpus)   # requests in flight across all engines
-    service = SpeechService(options, factory)
-    app = web.Application(client_max_size=1024 * 1024)
-    app.router.add_get("/health", service.health)
-    app.router.add_post("/v1/audio/speech", service.speech)
-    app.on_startup.append(service.start)
-    app.on_cleanup.append(service.stop)
+    app = build_app(options)
     web.run_app(app, host=options.host, port=options.port, handler_cancellation=True)
 
 

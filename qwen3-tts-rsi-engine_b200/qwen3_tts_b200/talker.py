@@ -22,6 +22,8 @@ from .config import DecoderConfig
 from .weights import pack_decoder
 
 BF16 = torch.bfloat16
+# Run each layer's projections as one persistent q3t_linear_chain launch where the shape allows.
+CHAIN_PROJECTIONS = False
 
 
 def rope_tables(positions: int, dim: int, theta: float, device) -> tuple[torch.Tensor, torch.Tensor]:
@@ -30,6 +32,22 @@ def rope_tables(positions: int, dim: int, theta: float, device) -> tuple[torch.T
     freqs = torch.arange(positions, dtype=torch.float32)[:, None] * inv_freq[None, :]
     emb = torch.cat([freqs, freqs], dim=-1)
     return emb.cos().to(BF16).to(device), emb.sin().to(BF16).to(device)
+
+
+def qkv_stage(x, layer, out, eps, depends):
+    """Chain stage: the packed QKV projection with the input RMSNorm folded in."""
+    return {"x": x, "weight": layer.qkv, "out": out, "row_norm_eps": eps, "depends": depends}
+
+
+def mlp_stages(attn, residual, layer, h, act, eps):
+    """Chain stages after an attention: h = residual + O(attn); act = SwiGLU(gate/up(norm(h)));
+    h = h + down(act) (PackedAttention.o_proj, packed_attention.py:85; PackedMLP, packed_mlp.py:19-27)."""
+    return [
+        {"x": attn, "weight": layer.o, "out": h, "epilogue": _lib.EPI_RESIDUAL, "residual": residual, "depends": -1},
+        {"x": h, "weight": layer.gate_up, "out": act, "epilogue": _lib.EPI_SWIGLU_PAIRED, "row_norm_eps": eps,
+         "depends": 0},
+        {"x": act, "weight": layer.down, "out": h, "epilogue": _lib.EPI_RESIDUAL, "residual": h, "depends": 1},
+    ]
 
 
 class SlotArena:
@@ -103,11 +121,19 @@ class TalkerStep:
         need = ops.decode_attention_workspace_bytes(B, cfg.q_heads, cfg.head_dim, context)
         self.ws_attn = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
         self.status = ops.status_word(dev)
+        # Projections between two attentions run as one persistent chain launch (q3t_linear_chain):
+        # needs folded norms, tiled weights and at most 64 rows
+        self.use_chain = (CHAIN_PROJECTIONS and B <= 64 and fused_attention and weights["layers"][0].folded
+                          and isinstance(weights["layers"][0].qkv, ops.TiledWeight))
+        self.ws_chain = ops.linear_chain_workspace(B, dev) if self.use_chain else None
         self.graph = None
         self.output = (self.hidden, self.logits)
 
     # ---------------------------------------------------------------- one eager pass
     def compute(self) -> None:
+        if self.use_chain:
+            self._compute_chained()
+            return
         cfg, w, B = self.cfg, self.w, self.batch
         lw = ops.linear
         res_in = self.inputs
@@ -150,7 +176,32 @@ class TalkerStep:
         ops.rms_norm(res_in, w["norm"], cfg.eps, self.norm_mode, out=self.hidden)
         lw(self.hidden, w["head"], out=self.logits, workspace=self.ws_linear)
 
+    def _compute_chained(self) -> None:
+        """The step with each layer's O, gate/up, down and the next layer's QKV as one
+        q3t_linear_chain launch: per layer one attention kernel and one chain kernel."""
+        cfg, w, B = self.cfg, self.w, self.batch
+        layers = w["layers"]
+        ops.attention_plan(self.positions, self.ws_attn, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads,
+                           head_dim=cfg.head_dim, context=self.context)
+        ops.linear_chain([qkv_stage(self.inputs, layers[0], self.qkv, cfg.eps, depends=-1)], self.ws_chain)
+        res_in = self.inputs
+        for i, layer in enumerate(layers):
+            ops.decode_attention_qkv(self.qkv, layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin,
+                                     self.rotary, self.arena.keys[i], self.arena.values[i], self.positions,
+                                     q_heads=cfg.q_heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
+                                     context=self.context, out=self.attn, workspace=self.ws_attn)
+            stages = mlp_stages(self.attn.view(B, cfg.q_width), res_in, layer, self.h, self.act, cfg.eps)
+            if i + 1 < len(layers):
+                stages.append(qkv_stage(self.h, layers[i + 1], self.qkv, cfg.eps, depends=2))
+            ops.linear_chain(stages, self.ws_chain)
+            res_in = self.h
+        ops.rms_norm(res_in, w["norm"], cfg.eps, self.norm_mode, out=self.hidden)
+        ops.linear(self.hidden, w["head"], out=self.logits, workspace=self.ws_linear)
+
     def launches_per_step(self) -> int:
+        if self.use_chain:
+            return 2 * self.cfg.layers + 4
+
         per_layer = (6 if self.w["layers"][0].folded else 8) - (1 if self.fused_attention else 0)
         return per_layer * self.cfg.layers + 3
 

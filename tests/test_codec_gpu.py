@@ -99,23 +99,6 @@ def test_codec_move_reset_and_pcm16(cuda):
     engine.close()
 
 
-def test_full_size_codec_chunk_runs_clean(cuda):
-    """BASELINE config 4 geometry (16x2048 RVQ, dim 512, 8 layers x 512 / 8 heads, window 72,
-    1920 samples per frame), 64 streams x 4-frame chunks, random-init weights."""
-    from qwen3_tts_b200 import ops
-    from qwen3_tts_b200.config import CODEC
-    decoder, engine = build(CODEC, cuda, slots=64, seed=3)
-    g = torch.Generator().manual_seed(0)
-    for _ in range(2):
-        codes = torch.randint(0, 2048, (64, 16, 4), generator=g).to(cuda)
-        wave, pcm = engine.decode(list(range(64)), codes)
-    torch.cuda.synchronize()
-    assert ops.read_status(cuda) == 0
-    assert wave.shape == (64, 4 * 1920)
-    assert torch.isfinite(wave).all()
-    engine.close()
-
-
 def test_codec_two_lanes_match_one_lane(cuda):
     """codec_streams=2 (codec_slots.py:279-305): the groups of one decode_groups call run on two
     alternating streams with per-lane graphs; the audio and the per-slot state equal the

@@ -55,10 +55,9 @@ def test_tiny_talker_step_matches_oracle(cuda, use_graph):
     h_ref, l_ref = OD.talker_decode_step(cfg, weights, embeds, pos, delta, cache_b, tables, mode="bf16f")
     torch.testing.assert_close(hidden.float(), h_ref, atol=3e-2, rtol=3e-2)
     torch.testing.assert_close(logits, l_ref, atol=2e-2, rtol=2e-2)
-    # fp32 truth: logits within 1e-2 relative of the logit scale
+    # fp32 truth: logits within 1e-2 relative (normwise)
     h32, l32 = OD.talker_decode_step(cfg, weights, embeds, pos, delta, cache, tables, mode="fp32")
-    scale = l32.abs().max()
-    assert (logits - l32).abs().max() <= 1e-2 * scale * 4
+    assert float((logits - l32).norm() / l32.norm()) <= 1e-2
     # greedy ids bit-exact wherever the fp32 top-1/top-2 margin exceeds the logit error bound
     top2 = l32.topk(2, dim=-1).values
     margin = top2[:, 0] - top2[:, 1]
