@@ -164,3 +164,83 @@ def test_codec_shape_mismatch_raises(tmp_path):
     safetensors.save_file({k: v.contiguous() for k, v in tensors.items()}, str(tmp_path / "model.safetensors"))
     with pytest.raises(ValueError, match="pre_transformer.layers.1.q_proj.weight"):
         C.load_codec(tmp_path, ccfg)
+
+
+# ------------------------------------------------------------------ names from the module tree
+class _Bag(torch.nn.Module):
+    def __init__(self, **children):
+        super().__init__()
+        for name, child in children.items():
+            setattr(self, name, child)
+
+
+def _model_tree(tcfg, pcfg, prcfg):
+    """A stand-in for the qwen-tts CustomVoice model as the reference drives it
+    (model.py:18-34 ``wrapper.model.talker``): ``talker.model.layers`` / ``.norm`` (prefill_graph.py:34-44),
+    ``talker.get_input_embeddings()`` and ``talker.code_predictor.get_input_embeddings()[i]``
+    (continuous.py:584-590), ``talker.codec_head`` (continuous.py:458, 613), ``talker.text_projection`` over
+    ``talker.get_text_embeddings()`` (custom_voice_prompt.py:38-63), decoder layers with the attribute names
+    the reference's PackedAttention / PackedMLP / FusedResidualDecoder read (q_proj, k_proj, v_proj,
+    o_proj, q_norm, k_norm, gate_proj, up_proj, down_proj, input_layernorm, post_attention_layernorm).
+    Names the reference never spells out (text_projection.linear_fc1/2, code_predictor.lm_head,
+    small_to_mtp_projection) are qwen-tts's own."""
+    from tests.qwen_tts_fakes import Qwen3TTSDecoderLayer, Qwen3TTSRMSNorm, Qwen3TTSTalkerDecoderLayer, randomize
+    from torch import nn
+
+    def layers(kind, cfg):
+        return nn.ModuleList([kind(cfg.hidden, cfg.q_heads, cfg.kv_heads, cfg.head_dim, cfg.ffn, layer_idx=i)
+                              for i in range(cfg.layers)])
+
+    predictor = _Bag(model=_Bag(layers=layers(Qwen3TTSDecoderLayer, pcfg), norm=Qwen3TTSRMSNorm(pcfg.hidden),
+                                codec_embedding=nn.ModuleList([nn.Embedding(pcfg.vocab, tcfg.hidden)
+                                                               for _ in range(pcfg.groups)])),
+                     lm_head=nn.ModuleList([nn.Linear(pcfg.hidden, pcfg.vocab, bias=False)
+                                            for _ in range(pcfg.groups)]),
+                     small_to_mtp_projection=nn.Linear(tcfg.hidden, pcfg.hidden))
+    predictor.get_input_embeddings = lambda: predictor.model.codec_embedding
+    talker = _Bag(model=_Bag(layers=layers(Qwen3TTSTalkerDecoderLayer, tcfg), norm=Qwen3TTSRMSNorm(tcfg.hidden),
+                             codec_embedding=nn.Embedding(tcfg.vocab, tcfg.hidden),
+                             text_embedding=nn.Embedding(prcfg.text_vocab, prcfg.text_hidden)),
+                  text_projection=_Bag(linear_fc1=nn.Linear(prcfg.text_hidden, prcfg.text_hidden),
+                                       linear_fc2=nn.Linear(prcfg.text_hidden, prcfg.hidden)),
+                  codec_head=nn.Linear(tcfg.hidden, tcfg.vocab, bias=False), code_predictor=predictor)
+    talker.get_input_embeddings = lambda: talker.model.codec_embedding
+    talker.get_text_embeddings = lambda: talker.model.text_embedding
+    model = _Bag(talker=talker)
+    randomize(model, seed=9)
+    return model
+
+
+def test_checkpoint_named_by_the_reference_module_tree_loads(tmp_path):
+    """A checkpoint whose keys are the state_dict of the module tree the reference walks (not this
+    module's own writer) loads, and every logical tensor is the module parameter it names."""
+    tcfg, pcfg, prcfg, *_ = model(dialect=False)
+    tree = _model_tree(tcfg, pcfg, prcfg)
+    state = {k: v.detach().to(torch.bfloat16).contiguous() for k, v in tree.state_dict().items()}
+    assert sum(k.endswith("talker.codec_head.weight") for k in state) == 1    # the probe's lookup
+    safetensors.save_file(state, str(tmp_path / "model.safetensors"))
+    (tmp_path / "config.json").write_text(json.dumps(C.model_config_json(tcfg, pcfg, prcfg)))
+    loaded = C.load_model(tmp_path, prompt_base=tiny_prompt(256))
+    assert loaded["talker_config"] == tcfg and loaded["predictor_config"] == pcfg
+    talker, code_predictor = tree.talker, tree.talker.code_predictor
+    w = loaded["weights"]
+    bf = lambda p: p.detach().to(torch.bfloat16)     # noqa: E731
+    for logical, tree_layers in ((w["talker"]["layers"], talker.model.layers),
+                                 (w["predictor"]["layers"], code_predictor.model.layers)):
+        for got, layer in zip(logical, tree_layers):
+            attn, mlp = layer.self_attn, layer.mlp
+            pairs = {"q": attn.q_proj, "k": attn.k_proj, "v": attn.v_proj, "o": attn.o_proj, "q_norm": attn.q_norm,
+                     "k_norm": attn.k_norm, "input_norm": layer.input_layernorm,
+                     "post_norm": layer.post_attention_layernorm, "gate": mlp.gate_proj, "up": mlp.up_proj,
+                     "down": mlp.down_proj}
+            for key, module in pairs.items():
+                assert torch.equal(got[key], bf(module.weight)), key
+    assert torch.equal(w["talker"]["head"], bf(talker.codec_head.weight))
+    assert torch.equal(w["talker"]["embedding"], bf(talker.get_input_embeddings().weight))
+    assert torch.equal(w["talker"]["norm"], bf(talker.model.norm.weight))
+    for j in range(pcfg.groups):
+        assert torch.equal(w["predictor"]["embeddings"][j], bf(code_predictor.get_input_embeddings()[j].weight))
+        assert torch.equal(w["predictor"]["heads"][j], bf(code_predictor.lm_head[j].weight))
+    assert torch.equal(w["predictor"]["proj"], bf(code_predictor.small_to_mtp_projection.weight))
+    assert torch.equal(w["prompt"]["text_embedding"], bf(talker.get_text_embeddings().weight))
+    assert torch.equal(w["prompt"]["fc2_bias"], bf(talker.text_projection.linear_fc2.bias))
