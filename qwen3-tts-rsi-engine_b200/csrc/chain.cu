@@ -44,6 +44,14 @@ constexpr int kMaxStages = Q3T_CHAIN_MAX_STAGES;
 constexpr int kSyncExit = 0, kSyncAbort = 1, kSyncStage = 4, kSyncTiles = 16;
 constexpr int kSyncWords = 2048;  // room for kSyncTiles + every stage's tile counters
 constexpr int kMaxPieces = 4;     // tiles one CTA may touch in one stage (scratch slots per CTA)
+// A stage runs on at most units / kMinUnits CTAs, so that no tile is cut into more than about
+// kblocks / kMinUnits + 1 pieces: the reduction of a tile reads every piece, so a stage of few
+// weight tiles is better served by fewer, longer pieces than by every SM.
+constexpr int kMinUnits = 4;
+constexpr int kMaxGrid = 256;     // contributor slots of one tile (shared memory)
+// Weight tiles the producer pulls into L2 ahead of the ring: the HBM stream keeps going while a
+// stage waits for its input (16 x 16 KB per CTA, ~38 MB in flight over 148 SMs).
+constexpr int kPrefetchAhead = 16;
 
 template <int BN>
 struct ChainCfg {
@@ -51,7 +59,9 @@ struct ChainCfg {
   static constexpr int kSlotBytes = kABytes + kBBytes;   // a multiple of 1024 (swizzle atoms)
   static constexpr int kSlots = (200 * 1024) / kSlotBytes;
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
-  static constexpr int kSmem = kSlots * kSlotBytes + 1024 + 1024;   // ring + barriers + alignment slack
+  // ring, then 512 bytes of barriers and flags, the contributor slots of the tile being reduced,
+  // and 1 KB of alignment slack
+  static constexpr int kSmem = kSlots * kSlotBytes + 512 + kMaxGrid * 4 + 1024;
 };
 
 struct Stage {
@@ -64,6 +74,7 @@ struct Stage {
   int epilogue, out_f32, row_norm;
   float norm_eps;
   int segments;                       // (CTA, tile) pieces: stored slices per launch
+  int ctas;                           // CTAs [0, ctas) split this stage's units
   int tile_base;                      // first tile counter of this stage in the sync block
   int depends;                        // stage whose completion gates this stage's activations (-1: none)
 };
@@ -118,11 +129,11 @@ Q3T_DEV void epilogue_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 Q3T_DEV bool wait_count(const unsigned* p, unsigned target, unsigned* sync, unsigned* status) {
   if (ld_acquire(p) >= target) return true;
   const uint64_t start = global_ns();
-  while (true) {
+  for (int spin = 0;; ++spin) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i) {
       if (ld_acquire(p) >= target) return true;
-      __nanosleep(64);
+      if (spin >= 64) __nanosleep(64);   // tight polling first: the wait is normally short
     }
     if (ld_volatile(sync + kSyncAbort)) return false;
     if (global_ns() - start > kWaitLimitNs) {
@@ -148,13 +159,15 @@ struct Items {
     next_stage();
   }
   Q3T_DEV void next_stage() {
-    if (++s >= p->stages) {
-      done = true;
-      return;
-    }
+    do {   // skip the stages this CTA takes no part in
+      if (++s >= p->stages) {
+        done = true;
+        return;
+      }
+    } while (c >= p->st[s].ctas);
     const Stage& st = p->st[s];
-    u0 = range_start(c, st.units, grid);
-    u1 = range_start(c + 1, st.units, grid);
+    u0 = range_start(c, st.units, st.ctas);
+    u1 = range_start(c + 1, st.units, st.ctas);
     t = u0 / st.kblocks;
     t_last = (u1 - 1) / st.kblocks;
     set_tile();
@@ -195,6 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
   volatile int* issued_a = consumed + 1;
   volatile int* issued_b = issued_a + 1;
   volatile int* last_flag = issued_b + 1;
+  int* tile_slots = reinterpret_cast<int*>(smem + S * C::kSlotBytes + 512);   // [kMaxGrid]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = blockIdx.x, grid = gridDim.x;
@@ -233,20 +247,34 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
       // ---------------- producer: weights as far ahead as the ring allows (the first S before the
       // dependency wait), activations once their stage's input is complete
       const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
-      Items A, B;
+      Items A, B, P;
       A.start(&a, c, grid);
       B.start(&a, c, grid);
+      P.start(&a, c, grid);
+      auto tile_of = [&](const Items& it) {
+        const Stage& st = a.st[it.s];
+        return st.tiles + (size_t(it.t) * size_t(st.kblocks) + size_t(it.kb)) * size_t(kABytes);
+      };
+      auto prefetch_ahead = [&]() {   // L2 prefetch of the weight tiles after the ring's
+        bool any = false;
+        while (!P.done && P.i < A.i + S + kPrefetchAhead) {
+          if (P.i >= A.i + S) prefetch_l2(tile_of(P), uint32_t(kABytes));
+          P.advance();
+          any = true;
+        }
+        return any;
+      };
       auto issue_a = [&]() {
         const int slot = A.i % S;
         const Stage& st = a.st[A.s];
+        (void)st;
         mbar_expect_tx(&full_a[slot], uint32_t(kABytes));
-        bulk_load_hint(smem + slot * C::kSlotBytes,
-                       st.tiles + (size_t(A.t) * size_t(st.kblocks) + size_t(A.kb)) * size_t(kABytes),
-                       uint32_t(kABytes), &full_a[slot], pol_w);
+        bulk_load_hint(smem + slot * C::kSlotBytes, tile_of(A), uint32_t(kABytes), &full_a[slot], pol_w);
         A.advance();
         *issued_a = A.i;
       };
       while (!A.done && A.i < S) issue_a();
+      prefetch_ahead();
       grid_dependency_wait();
       int ready_stage = 0;   // stages [0, ready_stage) may load activations
       bool ok = true;
@@ -277,6 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
             progress = true;
           }
         }
+        if (prefetch_ahead()) progress = true;
         if (progress) {
           idle_since = 0;
         } else {
@@ -369,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
       if (lane == 0) mbar_arrive(&empty[slot]);
       if (it.advance()) {   // piece complete: its row sums go to the piece's scratch slot
         if (st.row_norm && m < BN)
-          __stcg(a.sumsq + size_t(piece_slot(st, c, t_now, grid, a.pieces)) * BN + m, ss);
+          __stcg(a.sumsq + size_t(piece_slot(st, c, t_now, st.ctas, a.pieces)) * BN + m, ss);
         (void)s_now;
         ss = 0.f;
         __threadfence();
@@ -389,8 +418,9 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
     bool ok = true;
     for (int s = 0; s < a.stages && ok; ++s) {
       const Stage& st = a.st[s];
-      const int K = st.kblocks;
-      const int u0 = range_start(c, st.units, grid), u1 = range_start(c + 1, st.units, grid);
+      if (c >= st.ctas) continue;
+      const int K = st.kblocks, G = st.ctas;
+      const int u0 = range_start(c, st.units, G), u1 = range_start(c + 1, st.units, G);
       const int t0 = u0 / K, t1 = (u1 - 1) / K;
       // (1) drain every piece of this stage into its scratch slot and count it at its tile
       for (int t = t0; t <= t1 && ok; ++t, ++seg) {
@@ -400,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
           break;
         }
         tc_fence_after();
-        float* part = a.partials + size_t(piece_slot(st, c, t, grid, a.pieces)) * BN * kTileN;
+        float* part = a.partials + size_t(piece_slot(st, c, t, G, a.pieces)) * BN * kTileN;
         const uint32_t taddr = tmem + (uint32_t(quad * 32) << 16) + uint32_t(buf * BN);
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 16) {
@@ -410,7 +440,6 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
           for (int j = 0; j < 16; ++j)
             if (c0 + j < R) __stcg(part + (c0 + j) * kTileN + r, v[j]);
         }
-        __threadfence();   // this thread's partials reach L2 before the piece is counted
         tc_fence_before();
         epilogue_sync();
         if (leader) {
@@ -431,66 +460,140 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
       if (!ok) break;
       // (2) reduce this CTA's row slice of every tile it touched, once all its pieces are in
       for (int t = t0; t <= t1 && ok; ++t) {
-        const int c_lo = owner_of(t * K, st.units, grid), c_hi = owner_of((t + 1) * K - 1, st.units, grid);
+        const int c_lo = owner_of(t * K, st.units, G), c_hi = owner_of((t + 1) * K - 1, st.units, G);
         const int nc = c_hi - c_lo + 1, j = c - c_lo;
+        for (int k = r; k < nc; k += kTileN) tile_slots[k] = piece_slot(st, c_lo + k, t, G, a.pieces);
         if (leader && !wait_count(sync + kSyncTiles + st.tile_base + t, unsigned(nc), sync, a.status))
           atomicExch(sync + kSyncAbort, 1u);
-        epilogue_sync();
+        epilogue_sync();   // the tile's pieces are in; tile_slots is visible to every thread
         if (ld_volatile(sync + kSyncAbort)) {
           ok = false;
           break;
         }
         const int m0 = int((int64_t(j) * R) / nc), m1 = int((int64_t(j + 1) * R) / nc);
         const int n0 = t * kTileN;
+        // Every piece of the tile is summed in contributor order (deterministic). A thread owns
+        // four consecutive features (one float4 of each partial row) and a fixed set of rows; the
+        // loads of up to eight contributors x its rows are issued together, so a slice costs about
+        // one L2 round trip.
         if (st.epilogue == Q3T_EPI_SWIGLU_PAIRED) {
-          // tile rows are [64 gate; 64 up] of features n0/2 .. n0/2 + 63
-          const int f = r & 63;
-          for (int m = m0 + (r >> 6); m < m1; m += 2) {
-            float g = 0.f, u = 0.f, ssum = 0.f;
-            for (int k = 0; k < nc; ++k) {
-              const int slot = piece_slot(st, c_lo + k, t, grid, a.pieces);
-              const float* pp = a.partials + (size_t(slot) * BN + m) * kTileN;
-              g += __ldcg(pp + f);
-              u += __ldcg(pp + 64 + f);
-              if (st.row_norm) ssum += __ldcg(a.sumsq + size_t(slot) * BN + m);
+          // tile rows are [64 gate; 64 up] of features n0/2 .. n0/2 + 63: thread = 4 gate features
+          // (f4) x every 8th row of the slice
+          const int f4 = r & 15, sub = r >> 4;
+          for (int mb = m0 + sub; mb < m1; mb += 16) {
+            float4 g[2], u[2];
+            float ssum[2] = {0.f, 0.f};
+#pragma unroll
+            for (int q = 0; q < 2; ++q) g[q] = u[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int k0 = 0; k0 < nc; k0 += 8) {
+              float4 gv[8][2], uv[8][2];
+              float sv[8][2];
+#pragma unroll
+              for (int kk = 0; kk < 8; ++kk) {
+                const bool kin = k0 + kk < nc;
+                const int slot = kin ? tile_slots[k0 + kk] : 0;
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                  const int m = mb + 8 * q;
+                  const bool in = kin && m < m1;
+                  const float4* pp = reinterpret_cast<const float4*>(a.partials + (size_t(slot) * BN + (in ? m : 0)) * kTileN);
+                  gv[kk][q] = in ? __ldcg(pp + f4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                  uv[kk][q] = in ? __ldcg(pp + 16 + f4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                  sv[kk][q] = in && st.row_norm ? __ldcg(a.sumsq + size_t(slot) * BN + m) : 0.f;
+                }
+              }
+#pragma unroll
+              for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                  g[q].x += gv[kk][q].x; g[q].y += gv[kk][q].y; g[q].z += gv[kk][q].z; g[q].w += gv[kk][q].w;
+                  u[q].x += uv[kk][q].x; u[q].y += uv[kk][q].y; u[q].z += uv[kk][q].z; u[q].w += uv[kk][q].w;
+                  ssum[q] += sv[kk][q];
+                }
             }
-            if (st.row_norm) {
-              const float rs = 1.0f / sqrtf(ssum / float(st.in_features) + st.norm_eps);
-              g *= rs;
-              u *= rs;
-            }
-            if (n0 + 64 + f < st.out_features) {
-              const float gr = bf16r(g), ur = bf16r(u);
-              const float v = bf16r(bf16r(gr / (1.0f + expf(-gr))) * ur);
-              static_cast<__nv_bfloat16*>(st.out)[int64_t(m) * st.out_stride + n0 / 2 + f] = __float2bfloat16_rn(v);
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              const int m = mb + 8 * q;
+              if (m >= m1) continue;
+              const float rs = st.row_norm ? 1.0f / sqrtf(ssum[q] / float(st.in_features) + st.norm_eps) : 1.f;
+              const float gs[4] = {g[q].x, g[q].y, g[q].z, g[q].w}, us[4] = {u[q].x, u[q].y, u[q].z, u[q].w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int f = 4 * f4 + e;
+                if (n0 + 64 + f >= st.out_features) continue;
+                const float gr = bf16r(st.row_norm ? gs[e] * rs : gs[e]), ur = bf16r(st.row_norm ? us[e] * rs : us[e]);
+                const float v = bf16r(bf16r(gr / (1.0f + expf(-gr))) * ur);
+                static_cast<__nv_bfloat16*>(st.out)[int64_t(m) * st.out_stride + n0 / 2 + f] = __float2bfloat16_rn(v);
+              }
             }
           }
         } else {
-          const int n = n0 + r;
-          const bool live = n < st.out_features;
-          const float bias = (live && st.bias != nullptr) ? __bfloat162float(st.bias[n]) : 0.f;
-          for (int m = m0; m < m1; ++m) {
-            float acc = 0.f, ssum = 0.f;
-            for (int k = 0; k < nc; ++k) {
-              const int slot = piece_slot(st, c_lo + k, t, grid, a.pieces);
-              acc += __ldcg(a.partials + (size_t(slot) * BN + m) * kTileN + r);
-              if (st.row_norm) ssum += __ldcg(a.sumsq + size_t(slot) * BN + m);
+          // thread = 4 features (n4) x every 4th row of the slice
+          const int n4 = r & 31, sub = r >> 5;
+          const int nb = n0 + 4 * n4;
+          float bias[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            bias[e] = (nb + e < st.out_features && st.bias != nullptr) ? __bfloat162float(st.bias[nb + e]) : 0.f;
+          for (int mb = m0 + sub; mb < m1; mb += 8) {
+            float4 acc[2];
+            float ssum[2] = {0.f, 0.f};
+            acc[0] = acc[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int k0 = 0; k0 < nc; k0 += 8) {
+              float4 v[8][2];
+              float sv[8][2];
+#pragma unroll
+              for (int kk = 0; kk < 8; ++kk) {
+                const bool kin = k0 + kk < nc;
+                const int slot = kin ? tile_slots[k0 + kk] : 0;
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                  const int m = mb + 4 * q;
+                  const bool in = kin && m < m1;
+                  v[kk][q] = in ? __ldcg(reinterpret_cast<const float4*>(a.partials + (size_t(slot) * BN + m) * kTileN) + n4)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+                  sv[kk][q] = in && st.row_norm ? __ldcg(a.sumsq + size_t(slot) * BN + m) : 0.f;
+                }
+              }
+#pragma unroll
+              for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                  acc[q].x += v[kk][q].x; acc[q].y += v[kk][q].y; acc[q].z += v[kk][q].z; acc[q].w += v[kk][q].w;
+                  ssum[q] += sv[kk][q];
+                }
             }
-            if (st.row_norm) acc *= 1.0f / sqrtf(ssum / float(st.in_features) + st.norm_eps);
-            acc += bias;
-            if (!live) continue;
-            if (st.epilogue == Q3T_EPI_RESIDUAL) {
-              const float res = __bfloat162float(__ldcg(st.residual + int64_t(m) * st.res_stride + n));
-              static_cast<__nv_bfloat16*>(st.out)[int64_t(m) * st.out_stride + n] = __float2bfloat16_rn(res + bf16r(acc));
-            } else if (st.out_f32) {
-              static_cast<float*>(st.out)[int64_t(m) * st.out_stride + n] = bf16r(acc);
-            } else {
-              static_cast<__nv_bfloat16*>(st.out)[int64_t(m) * st.out_stride + n] = __float2bfloat16_rn(acc);
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              const int m = mb + 4 * q;
+              if (m >= m1) continue;
+              const float rs = st.row_norm ? 1.0f / sqrtf(ssum[q] / float(st.in_features) + st.norm_eps) : 1.f;
+              const float vals[4] = {acc[q].x, acc[q].y, acc[q].z, acc[q].w};
+              float res[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                res[e] = (st.epilogue == Q3T_EPI_RESIDUAL && nb + e < st.out_features)
+                             ? __bfloat162float(__ldcg(st.residual + int64_t(m) * st.res_stride + nb + e))
+                             : 0.f;
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int n = nb + e;
+                if (n >= st.out_features) continue;
+                float val = st.row_norm ? vals[e] * rs : vals[e];
+                val += bias[e];
+                if (st.epilogue == Q3T_EPI_RESIDUAL) {
+                  static_cast<__nv_bfloat16*>(st.out)[int64_t(m) * st.out_stride + n] =
+                      __float2bfloat16_rn(res[e] + bf16r(val));
+                } else if (st.out_f32) {
+                  static_cast<float*>(st.out)[int64_t(m) * st.out_stride + n] = bf16r(val);
+                } else {
+                  static_cast<__nv_bfloat16*>(st.out)[int64_t(m) * st.out_stride + n] = __float2bfloat16_rn(val);
+                }
+              }
             }
           }
         }
-        __threadfence();   // this thread's outputs are visible before the slice is counted
-        epilogue_sync();
+        epilogue_sync();   // every output of the slice is stored (and tile_slots may be rewritten)
         if (leader) {
           __threadfence();
           atomicAdd(sync + kSyncStage + s, 1u);
@@ -611,19 +714,25 @@ extern "C" int q3t_linear_chain(const q3t_chain_stage* stages, int count, int64_
     st.tile_base = tile_base;
     st.depends = q.depends;
     tile_base += st.n_tiles;
-    if (st.units < grid) grid = st.units;
+    st.ctas = st.units / kMinUnits < grid ? st.units / kMinUnits : grid;
+    if (st.ctas < 1) st.ctas = 1;
     const int rc = make_map_bf16(&p.x[s], q.x, rows, q.in_features, q.x_stride, kTileK, bn);
     if (rc) return rc;
   }
   if (kSyncTiles + tile_base > kSyncWords) return fail(Q3T_EUNSUPPORTED, "linear_chain: too many output tiles");
-  if (grid < 1) return fail(Q3T_EINVAL, "linear_chain: empty chain");
+  {
+    int widest = 1;
+    for (int s = 0; s < count; ++s) widest = p.st[s].ctas > widest ? p.st[s].ctas : widest;
+    grid = widest;   // every CTA works in at least one stage
+  }
+  if (grid > kMaxGrid) return fail(Q3T_EUNSUPPORTED, "linear_chain: more than %d SMs", kMaxGrid);
   // pieces per stage: every CTA touches tiles [u0 / K, (u1 - 1) / K]
   int per_cta = 1;
   for (int s = 0; s < count; ++s) {
     Stage& st = p.st[s];
     int pieces = 0;
-    for (int c = 0; c < grid; ++c) {
-      const int u0 = int((int64_t(c) * st.units) / grid), u1 = int((int64_t(c + 1) * st.units) / grid);
+    for (int c = 0; c < st.ctas; ++c) {
+      const int u0 = int((int64_t(c) * st.units) / st.ctas), u1 = int((int64_t(c + 1) * st.units) / st.ctas);
       const int touched = (u1 - 1) / st.kblocks - u0 / st.kblocks + 1;
       pieces += touched;
       if (touched > per_cta) per_cta = touched;
