@@ -62,9 +62,11 @@ def parse_args():
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", choices=["serving", "step", "predictor", "codec", "dispatch"], default="serving",
+    p.add_argument("--workload", choices=["serving", "step", "predictor", "codec", "dispatch", "chain"],
+                   default="serving",
                    help="serving: BASELINE config 5 (default); step: config 2; predictor: config 3; codec: config 4; "
-                        "dispatch: closed-loop serving through the host dispatcher")
+                        "dispatch: closed-loop serving through the host dispatcher; chain: one layer's "
+                        "projections as q3t_linear_chain against four linear launches")
     p.add_argument("--layers", type=int, default=28, help="step: talker depth (28 = the benchmarked model)")
     p.add_argument("--slots", type=int, default=SLOTS,
                    help="step: concurrent slots (32 = BASELINE config 2; 64 = the C=64 roofline target)")
@@ -839,6 +841,66 @@ def run_codec(args) -> dict:
     return {"frames_per_s": B * T * args.steps / (ms / 1e3), "ms_per_step": ms / args.steps, "status": status}
 
 
+def run_chain(args) -> list:
+    """One decode layer's projections after its attention (O + residual, gate/up with the folded
+    RMSNorm and SwiGLU, down + residual, the next layer's QKV with the folded RMSNorm) at the
+    predictor's and the talker's widths, as one q3t_linear_chain launch and as four q3t_linear
+    launches, each form captured in a CUDA graph and replayed (CUDA events, mean of 20)."""
+    from qwen3_tts_b200 import _lib, ops
+    from qwen3_tts_b200.talker import mlp_stages, qkv_stage
+    from qwen3_tts_b200.weights import PackedLayer
+    dev = torch.device("cuda:0")
+    bf = torch.bfloat16
+
+    def tiles(o, i, g):
+        return ops.pack_tiles((torch.randn(o, i, generator=g) * i ** -0.5).to(bf).to(dev))
+
+    def graph_us(fn, n=20):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n):
+            graph.replay()
+        b.record()
+        torch.cuda.synchronize()
+        graph.reset()
+        return a.elapsed_time(b) * 1e3 / n
+
+    out = []
+    for name, hidden, ffn, rows in (("predictor", 1024, 3072, 64), ("talker", 2048, 6144, 32),
+                                    ("talker", 2048, 6144, 64)):
+        g = torch.Generator().manual_seed(args.seed + 1)
+        layer = PackedLayer(input_norm=None, qkv=tiles(4096, hidden, g), q_norm=None, k_norm=None,
+                            o=tiles(hidden, 2048, g), post_norm=None, gate_up=tiles(2 * ffn, hidden, g),
+                            down=tiles(hidden, ffn, g), folded=True)
+        attn = torch.randn(rows, 2048, generator=g).to(bf).to(dev)
+        x = torch.randn(rows, hidden, generator=g).to(bf).to(dev)
+        h, act = torch.empty_like(x), torch.empty(rows, ffn, dtype=bf, device=dev)
+        qkv = torch.empty(rows, 4096, dtype=bf, device=dev)
+        ws = ops.linear_chain_workspace(rows, dev)
+        stages = mlp_stages(attn, x, layer, h, act, 1e-6) + [qkv_stage(h, layer, qkv, 1e-6, depends=2)]
+
+        def separate():
+            ops.linear(attn, layer.o, out=h, epilogue=_lib.EPI_RESIDUAL, residual=x)
+            ops.linear(h, layer.gate_up, out=act, epilogue=_lib.EPI_SWIGLU_PAIRED, row_norm_eps=1e-6)
+            ops.linear(act, layer.down, out=h, epilogue=_lib.EPI_RESIDUAL, residual=h)
+            ops.linear(h, layer.qkv, out=qkv, row_norm_eps=1e-6)
+        weights = sum(t.tiles.numel() for t in (layer.qkv, layer.o, layer.gate_up, layer.down))
+        out.append({"layer": name, "rows": rows, "weight_bytes": weights,
+                    "chain_us": graph_us(lambda: ops.linear_chain(stages, ws)), "linear_x4_us": graph_us(separate),
+                    "status_word": ops.read_status(dev)})
+    return out
+
+
 # ---------------------------------------------------------------------- CPU tick (serving arms)
 PROMPT_PREFIX = 9   # CustomVoice prompt rows around the text ids (role, speaker, language, codec tags)
 
@@ -996,6 +1058,10 @@ def main():
             "data": "synthetic (seeded random-init codec, uniform codes)",
             "config": {"workload": "BASELINE config 4: incremental codec decode", "streams": args.batch,
                        "chunk_frames": 4}, "status_word": res["status"]}))
+        return
+    if args.workload == "chain":
+        for row in run_chain(args):
+            print(json.dumps(row))
         return
     if args.workload == "dispatch":
         if rank != 0:
