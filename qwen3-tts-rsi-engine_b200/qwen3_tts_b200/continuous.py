@@ -79,6 +79,19 @@ class RequestState:
     frames: int = 0
     emitted: int = 0
     audio: list = field(default_factory=list)
+    codec_slot: int = -1      # the request's row of the incremental codec's state (fixed for its life)
+    cancelled: bool = False
+
+
+@dataclass
+class AudioInFlight:
+    """One tick's audio on the codec lanes (pipeline_audio): per group the (state, frames decoded
+    up to) pairs and the pinned PCM16 block, the requests that ended with this tick, and the
+    event after the last copy."""
+    finished: list
+    blocks: list = field(default_factory=list)
+    status: object = None
+    done: object = None
 
 
 class SlotState:
@@ -201,7 +214,7 @@ class ContinuousModel:
                  codec_chunk_frames=8, codec_streams=1, decode_bucket_step=0, prewarm_codec=False,
                  prewarm_prefill=False, bucket_prefill=True, max_frames=4096, max_prefill_batch=16, use_graphs=True,
                  temperature=0.9, top_k=50, top_p=1.0, subtalker_temperature=0.9, subtalker_top_k=50,
-                 subtalker_top_p=1.0, penalty=1.05, **flags):
+                 subtalker_top_p=1.0, penalty=1.05, pipeline_audio=False, **flags):
         if codec_chunk_frames not in (8, 16) or (codec_chunk_frames != 8 and not incremental_codec):
             raise ValueError("16-frame chunks require the incremental codec")
         if codec_streams not in (1, 2) or (codec_streams == 2 and not incremental_codec):
@@ -262,6 +275,18 @@ class ContinuousModel:
             self.codec = CodecGraph(codec_config, packed_codec, self.device, max_batch=codec_batch_size,
                                     use_graphs=use_graphs)
         self.subtalker = dict(temperature=subtalker_temperature, top_k=subtalker_top_k, top_p=subtalker_top_p)
+        # Every request owns one row of the incremental codec's state from admission to its end
+        # (compaction moves only the talker-side slot rows). With pipeline_audio the chunks a tick
+        # makes due are decoded on the codec lanes while the next tick's graph runs, and are
+        # delivered (emit, finished results) by that next tick; a finished request's codec row is
+        # reused only after its last chunk has been delivered.
+        self.pipeline_audio = bool(pipeline_audio) and incremental_codec
+        self._codec_free = list(range(max_slots)) if incremental_codec else []
+        self._codec_held: list = []          # rows whose last chunk is still being decoded
+        self._inflight = None                # the previous tick's audio in flight (pipeline_audio)
+        if self.pipeline_audio:
+            self._audio_lanes = (self.codec.lanes if self.codec.lanes
+                                 else [torch.cuda.Stream(device=self.device)])
         self.states: list[RequestState] = []
         self.stats = EngineStats()
         # Optional observer of every decoded frame: on_codes(identifier, frame, codes, next_token)
@@ -402,20 +427,36 @@ class ContinuousModel:
                    steps=self._zeros[:n], eos=self.eos, min_steps=2, penalty=self.penalty,
                    temperature=self.temperature, top_k=self.top_k, top_p=self.top_p, seen_out=S.seen[count:count + n],
                    tokens=S.tokens[count:count + n].view(n, 1))
-        if self.incremental_codec:
-            self.codec.reset_range(count, n)
-        for (identifier, payload), prompt, length in zip(submissions, prompts, lengths):
-            self.states.append(RequestState(identifier, payload, length, 0, prompt["max_new_tokens"]))
+        rows = self._take_codec_rows(n) if self.incremental_codec else [-1] * n
+        for ((identifier, payload), prompt, length), row in zip(zip(submissions, prompts, lengths), rows):
+            self.states.append(RequestState(identifier, payload, length, 0, prompt["max_new_tokens"], codec_slot=row))
+
+    def _take_codec_rows(self, n: int) -> list:
+        """The n lowest free codec rows, cleared for a fresh stream (contiguous runs in one call each)."""
+        self._codec_free.sort()
+        rows, self._codec_free = self._codec_free[:n], self._codec_free[n:]
+        start = 0
+        for i in range(1, n + 1):
+            if i == n or rows[i] != rows[i - 1] + 1:
+                self.codec.reset_range(rows[start], i - start)
+                start = i
+        return rows
+
+    def _release_codec_row(self, state) -> None:
+        if state.codec_slot < 0:
+            return
+        (self._codec_held if self._inflight is not None else self._codec_free).append(state.codec_slot)
+        state.codec_slot = -1
 
     # ------------------------------------------------------------------ compaction
     def _move_slot(self, source: int, destination: int) -> None:
         self.arena.move(source, destination)
         self.state.move(source, destination)
-        if self.incremental_codec:
-            self.codec.move(source, destination)
 
     def _remove(self, index: int) -> None:
         last = len(self.states) - 1
+        if self.incremental_codec:
+            self._release_codec_row(self.states[index])
         self._move_slot(last, index)
         if index != last:
             self.states[index] = self.states[last]
@@ -453,22 +494,90 @@ class ContinuousModel:
         for length, entries in groups.items():
             for offset in range(0, len(entries), self.codec_batch_size):
                 group = entries[offset:offset + self.codec_batch_size]
-                indices = [slots[id(entry[0])] for entry in group]
+                indices = [slots[id(entry[0])] for entry in group]          # code ring rows (talker slots)
                 if self.incremental_codec and getattr(self, "codec_streams", 1) == 2:
-                    lanes.append((group, indices, self.codec_codes.read(indices, [entry[1] for entry in group],
-                                                                        length)))
+                    lanes.append((group, [entry[0].codec_slot for entry in group],
+                                  self.codec_codes.read(indices, [entry[1] for entry in group], length)))
                 else:
-                    pending.append((group, self._decode_group(indices, [entry[1] for entry in group], length)))
+                    pending.append((group, self._decode_group(indices, [entry[1] for entry in group], length,
+                                                              [entry[0].codec_slot for entry in group])))
         if lanes:
             outputs = self.codec.decode_groups([(indices, codes) for _, indices, codes in lanes])
             pending += [(group, out[1]) for (group, _, _), out in zip(lanes, outputs)]
         return pending
 
-    def _decode_group(self, indices, starts, length):
-        """PCM16 [len(indices), length * 1920] (device) of frames starts[i] .. + length of each slot."""
+    # ------------------------------------------------------------------ pipelined audio
+    def _launch_audio(self, due, finished) -> "AudioInFlight":
+        """Decode the chunks of `due` on the codec lanes without waiting: the code rows are read on
+        the engine stream (ordered after this tick's graph and before any later compaction), each
+        lane waits for that, decodes its groups and copies their PCM16 into pinned host buffers.
+        The next tick's graph runs on the engine stream meanwhile."""
+        slots = {id(state): index for index, state in enumerate(self.states)}
+        groups: dict[int, list] = {}
+        for state in due:
+            if state.frames > state.emitted:
+                groups.setdefault(state.frames - state.emitted, []).append(state)
+        reads = []
+        for length, states in groups.items():
+            for offset in range(0, len(states), self.codec_batch_size):
+                group = states[offset:offset + self.codec_batch_size]
+                codes = self.codec_codes.read([slots[id(st)] for st in group], [st.emitted for st in group], length)
+                reads.append(([(st, st.frames) for st in group], [st.codec_slot for st in group], codes))
+        flight = AudioInFlight(finished=list(finished))
+        if not reads:
+            return flight
+        producer = torch.cuda.current_stream(self.device)
+        lanes = self._audio_lanes
+        for lane in lanes:
+            lane.wait_stream(producer)
+        for index, (group, rows, codes) in enumerate(reads):
+            k = index % len(lanes)
+            with torch.cuda.stream(lanes[k]):
+                codes.record_stream(lanes[k])
+                _, pcm = self.codec.decode(rows, codes, lane=k if self.codec.stream_count == 2 else 0)
+                host = torch.empty(pcm.shape, dtype=torch.int16, pin_memory=True)
+                host.copy_(pcm, non_blocking=True)
+            flight.blocks.append((group, host))
+        with torch.cuda.stream(lanes[-1]):
+            for lane in lanes[:-1]:
+                lanes[-1].wait_stream(lane)
+            flight.status = torch.empty(1, dtype=torch.int32, pin_memory=True)
+            flight.status.copy_(self.status[:1], non_blocking=True)
+            flight.done = torch.cuda.Event()
+            flight.done.record(lanes[-1])
+        return flight
+
+    def _deliver(self, flight, emit) -> list:
+        """Wait for a launched tick's audio, hand its chunks to `emit` and return the results of
+        the requests that ended with it; their codec rows become free again."""
+        if flight is None:
+            return []
+        if flight.done is not None:
+            flight.done.synchronize()
+            if int(flight.status[0]) & ops.STATUS_NONFINITE:
+                self.status.zero_()
+                raise ValueError("Native codec emitted nonfinite audio")
+        for group, host in flight.blocks:
+            block = host.numpy()
+            for row, (state, upto) in enumerate(group):
+                data = block[row].astype("<i2").tobytes()
+                state.audio.append(data)
+                state.emitted = upto
+                if emit is not None and not state.cancelled:
+                    emit(state.identifier, data, SAMPLE_RATE)
+        results = [(state.identifier, {"pcm": b"".join(state.audio), "sample_rate": SAMPLE_RATE,
+                                       "codec_frames": state.frames, "finish_reason": reason})
+                   for state, reason in flight.finished if not state.cancelled]
+        self._codec_free.extend(self._codec_held)
+        self._codec_held = []
+        return results
+
+    def _decode_group(self, indices, starts, length, rows=None):
+        """PCM16 [len(indices), length * 1920] (device) of frames starts[i] .. + length of talker
+        slots `indices`, decoded in codec rows `rows` (incremental codec)."""
         codes = self.codec_codes.read(indices, starts, length)
         if self.incremental_codec:
-            return self.codec.decode(indices, codes)[1]
+            return self.codec.decode(rows, codes)[1]
         return self.codec.decode(codes)[1]
 
     def _to_host(self, blocks):
@@ -526,14 +635,20 @@ class ContinuousModel:
         cancelled = set(cancelled)
         for index in reversed(range(len(self.states))):
             if self.states[index].identifier in cancelled:
+                self.states[index].cancelled = True
                 self._remove(index)
                 stats.cancelled += 1
+        if self._inflight is not None:   # requests that ended last tick, awaiting their last chunk
+            for state, _ in self._inflight.finished:
+                if state.identifier in cancelled:
+                    state.cancelled = True
         if submissions:
             before = len(self.states)
             self.admit_batch(submissions)
             stats.admitted += len(self.states) - before
         if not self.states:
-            return []
+            flight, self._inflight = self._inflight, None
+            return self._deliver(flight, emit)
         stats.active = len(self.states)
         stats.batch = decode_batch_size(stats.active, self.max_slots, self.decode_bucket_step)
         tokens = self._run_tick(len(self.states))
@@ -549,12 +664,21 @@ class ContinuousModel:
                 due.append(state)
             if stopped or limited:
                 finished.append((index, state, "stop" if stopped else "length"))
-        self.emit_audio(due, emit)
         results = []
-        for index, state, reason in reversed(finished):
-            results.append((state.identifier, {"pcm": b"".join(state.audio), "sample_rate": SAMPLE_RATE,
-                                               "codec_frames": state.frames, "finish_reason": reason}))
-            self._remove(index)
+        if self.pipeline_audio:
+            # the previous tick's chunks were decoded while this tick's graph ran: deliver them,
+            # then launch this tick's and let them overlap the next tick
+            flight, self._inflight = self._inflight, None
+            results += self._deliver(flight, emit)
+            self._inflight = self._launch_audio(due, [(state, reason) for _, state, reason in finished])
+            for index, _, _ in reversed(finished):
+                self._remove(index)
+        else:
+            self.emit_audio(due, emit)
+            for index, state, reason in reversed(finished):
+                results.append((state.identifier, {"pcm": b"".join(state.audio), "sample_rate": SAMPLE_RATE,
+                                                   "codec_frames": state.frames, "finish_reason": reason}))
+                self._remove(index)
         elapsed = time.perf_counter() - started
         stats.ticks += 1
         stats.frames += stats.active
@@ -574,7 +698,7 @@ class ContinuousModel:
         pending = [(("batch", index), payload) for index, payload in enumerate(payloads)]
         relay = None if emit is None else (lambda ident, pcm, rate: emit(ident[1], pcm, rate))
         results = {}
-        while pending or self.states:
+        while pending or self.states or self._inflight is not None:
             free = self.max_slots - len(self.states)
             submissions, pending = pending[:free], pending[free:]
             for ident, record in self.tick(submissions, emit=relay):
@@ -582,6 +706,9 @@ class ContinuousModel:
         return [results[index] for index in range(len(payloads))]
 
     def close(self) -> None:
+        if self._inflight is not None and self._inflight.done is not None:
+            self._inflight.done.synchronize()
+        self._inflight = None
         logging.getLogger(__name__).info("Captured graph shapes: prefill=%s tick=%s codec=%s", sorted(self.prefills),
                                          sorted(self.graphs), sorted(self.codec.slots.graphs
                                                                      if isinstance(self.codec, CodecGraph)

@@ -407,6 +407,8 @@ def build_parser() -> argparse.ArgumentParser:
     parser.add_argument("--codec-streams", type=int, choices=[1, 2], default=1)
     parser.add_argument("--prefill-per-tick", type=int, default=4)
     parser.add_argument("--prefill-interval", type=int, default=1)
+    parser.add_argument("--pipeline-audio", action="store_true",
+                        help="decode each tick's audio on the codec lanes while the next tick runs")
     for flag in VARIANT_FLAGS:
         parser.add_argument("--" + flag.replace("_", "-"), action="store_true")
     return parser
@@ -453,7 +455,9 @@ def _rules(o) -> list:
                (o.prefill_per_tick < 1 or (cont and o.max_batch_size & (o.max_batch_size - 1)),
                 "Continuous slots must be a power of two and prefill budget must be positive"),
                (o.gpus < 1, "--gpus must be positive"),
-               (o.gpus > 1 and not cont, "--gpus above 1 requires --continuous")])
+               (o.gpus > 1 and not cont, "--gpus above 1 requires --continuous"),
+               (o.pipeline_audio and not (cont and incremental),
+                "--pipeline-audio requires --continuous --incremental-codec")])
 
 
 def parse_options(argv=None):
@@ -480,7 +484,8 @@ def engine_kwargs(options) -> dict:
                   codec_batch_size=options.codec_batch_size, codec_chunk_frames=options.codec_chunk_frames,
                   incremental_codec=options.incremental_codec, codec_streams=options.codec_streams,
                   seed=options.seed, prewarm_codec=options.prewarm_codec, prewarm_prefill=options.prewarm_prefill,
-                  bucket_prefill=options.bucket_prefill, decode_bucket_step=options.decode_bucket_step)
+                  bucket_prefill=options.bucket_prefill, decode_bucket_step=options.decode_bucket_step,
+                  pipeline_audio=getattr(options, "pipeline_audio", False))
     kwargs.update({flag: getattr(options, flag) for flag in VARIANT_FLAGS if getattr(options, flag, False)})
     if getattr(options, "rms_norm", None):
         kwargs["rms_norm"] = options.rms_norm

@@ -29,6 +29,9 @@ def fake_engine(tokens_by_id, codec_batch_size=2, incremental=True, context=72):
     model.on_codes = None
     model.stats = EngineStats()
     model.calls = {"decode": [], "move": []}
+    model.pipeline_audio = False
+    model._inflight = None
+    model._codec_free, model._codec_held = [], []
 
     def admit_batch(submissions):
         for identifier, payload in submissions:
@@ -38,7 +41,7 @@ def fake_engine(tokens_by_id, codec_batch_size=2, incremental=True, context=72):
         assert count == len(model.states)
         return [tokens_by_id[s.identifier][s.frames] for s in model.states]
 
-    def decode_group(indices, starts, length):
+    def decode_group(indices, starts, length, rows=None):
         model.calls["decode"].append((list(indices), list(starts), length))
         rows = []
         for slot, start in zip(indices, starts):
