@@ -626,6 +626,10 @@ def steady_state(model, requests, steps: int, warmup: int, seed: int, dist) -> d
         for lane in getattr(model, "_audio_lanes", []):
             main.wait_stream(lane)
 
+    engine_stream = getattr(model, "_engine_stream", None) if model.pipeline_audio else None
+    if engine_stream is not None:   # the engine's high-priority stream, as its ticks use it
+        engine_stream.wait_stream(torch.cuda.current_stream())
+        torch.cuda.set_stream(engine_stream)
     for _ in range(priming):                            # fill every slot's code ring
         tick_only()
     for i in range(warmup):
@@ -646,6 +650,8 @@ def steady_state(model, requests, steps: int, warmup: int, seed: int, dist) -> d
     b.record()
     torch.cuda.synchronize()
     flights.clear()
+    if engine_stream is not None:
+        torch.cuda.set_stream(torch.cuda.default_stream())
     dist.barrier()
     elapsed_ms = dist.max(a.elapsed_time(b))
     # this library's kernels in the timed region: graph replays x kernels captured per replay,

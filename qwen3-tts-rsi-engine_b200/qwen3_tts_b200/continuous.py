@@ -287,6 +287,7 @@ class ContinuousModel:
         if self.pipeline_audio:
             self._audio_lanes = (self.codec.lanes if self.codec.lanes
                                  else [torch.cuda.Stream(device=self.device)])
+            self._engine_stream = torch.cuda.Stream(device=self.device, priority=-16)
         self.states: list[RequestState] = []
         self.stats = EngineStats()
         # Optional observer of every decoded frame: on_codes(identifier, frame, codes, next_token)
@@ -630,6 +631,15 @@ class ContinuousModel:
     def tick(self, submissions=(), emit=None, cancelled=()):
         if self.device.type == "cuda":
             torch.cuda.set_device(self.device)
+        if self.pipeline_audio:
+            # the tick's own work runs on a high-priority stream, so that the codec lanes decoding the
+            # previous tick's audio take only the SMs its dependent kernels leave free
+            self._engine_stream.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(self._engine_stream):
+                return self._tick(submissions, emit, cancelled)
+        return self._tick(submissions, emit, cancelled)
+
+    def _tick(self, submissions, emit, cancelled):
         started = time.perf_counter()
         stats = self.stats
         cancelled = set(cancelled)
@@ -654,6 +664,12 @@ class ContinuousModel:
         tokens = self._run_tick(len(self.states))
         if self.on_codes is not None:
             self._report_codes(tokens)
+        results = []
+        if self.pipeline_audio:
+            # the previous tick's chunks decoded while this tick's graph ran: deliver them before
+            # this tick's emission schedule is evaluated
+            flight, self._inflight = self._inflight, None
+            results += self._deliver(flight, emit)
         due, finished = [], []
         for index, state in enumerate(self.states):
             state.frames += 1
@@ -664,12 +680,8 @@ class ContinuousModel:
                 due.append(state)
             if stopped or limited:
                 finished.append((index, state, "stop" if stopped else "length"))
-        results = []
         if self.pipeline_audio:
-            # the previous tick's chunks were decoded while this tick's graph ran: deliver them,
-            # then launch this tick's and let them overlap the next tick
-            flight, self._inflight = self._inflight, None
-            results += self._deliver(flight, emit)
+            # this tick's chunks decode on the codec lanes while the next tick's graph runs
             self._inflight = self._launch_audio(due, [(state, reason) for _, state, reason in finished])
             for index, _, _ in reversed(finished):
                 self._remove(index)
