@@ -643,12 +643,15 @@ def steady_state(model, requests, steps: int, warmup: int, seed: int, dist) -> d
     ticks, host = graph.replays, _lib.launch_count()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     join_lanes()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()   # cudaProfilerStart/Stop: no-ops unless a profiler is attached
     a.record()
     for i in range(steps):
         step(warmup + i)
     join_lanes()
     b.record()
     torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
     flights.clear()
     if engine_stream is not None:
         torch.cuda.set_stream(torch.cuda.default_stream())
