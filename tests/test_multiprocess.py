@@ -25,9 +25,10 @@ def _rank(rank, world, port, out):
     dist.barrier()
     value = dist.max(1.5 + rank)          # per-rank timing; the job's time is the slowest rank
     total = dist.max(float(rank * 10))
+    frames = dist.sum(float(64 * (rank + 1)))   # every rank's frames count toward the job's value
     dist.barrier()
     dist.close()
-    out.put((rank, value, total))
+    out.put((rank, value, total, frames))
 
 
 def test_gloo_world_size_two_takes_max_over_ranks():
@@ -41,4 +42,4 @@ def test_gloo_world_size_two_takes_max_over_ranks():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    assert results == [(0, 2.5, 10.0), (1, 2.5, 10.0)]
+    assert results == [(0, 2.5, 10.0, 192.0), (1, 2.5, 10.0, 192.0)]
