@@ -62,7 +62,7 @@ def parse_args():
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", choices=["serving", "step", "predictor", "codec", "dispatch", "chain"],
+    p.add_argument("--workload", choices=["serving", "step", "predictor", "codec", "dispatch", "chain", "prefill"],
                    default="serving",
                    help="serving: BASELINE config 5 (default); step: config 2; predictor: config 3; codec: config 4; "
                         "dispatch: closed-loop serving through the host dispatcher; chain: one layer's "
@@ -868,6 +868,62 @@ def run_codec(args) -> dict:
     return {"frames_per_s": B * T * args.steps / (ms / 1e3), "ms_per_step": ms / args.steps, "status": status}
 
 
+def run_prefill(args) -> list:
+    """Admission prefill of the talker (PrefillGraph, prefill_graph.py:31-50): the 28-layer causal
+    stack over a group of prompts, K/V written into arena slots, last-token hidden state and
+    logits. Two groups: 16 prompts of 256 tokens (no padding either way: the GEMM and attention
+    rate at 4,096 rows) and the first 16 prompts of the serving recipe (
+    lengths 29-209 with the CustomVoice prefix), each as the padded graph (power-of-two length,
+    the reference's shape) and the packed graph (prompts end to end, 512-row buckets). Each
+    line: mean CUDA-event ms over `steps` graph replays after `warmup`, and the projection
+    GEMMs' FLOP/s over the real prompt rows (2 x rows x projection weights x 28 layers)."""
+    from qwen3_tts_b200.batching import packed_rows, packed_tables
+    from qwen3_tts_b200.config import TALKER
+    from qwen3_tts_b200.talker import PackedPrefill, SlotArena, TalkerPrefill, rope_tables
+    from qwen3_tts_b200.weights import decoder_weights, pack_decoder
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    cfg = TALKER
+    weights = pack_decoder(decoder_weights(cfg, args.seed, dev), dev)
+    arena = SlotArena(cfg, 16, 256, dev)
+    cos, sin = rope_tables(4096, cfg.head_dim, cfg.theta, dev)
+    per_row = 2 * cfg.layers * (cfg.hidden * cfg.qkv_width + cfg.q_width * cfg.hidden + cfg.hidden * 2 * cfg.ffn
+                                + cfg.ffn * cfg.hidden)
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    recipe = [len(r["input_ids"]) + PROMPT_PREFIX for r in serving_requests(args.seed, 16)]
+    out = []
+    for name, lengths in (("16x256", [256] * 16), ("serving recipe, 16 prompts", recipe)):
+        total = sum(lengths)
+        x = (torch.randn(total, cfg.hidden, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+        padded_len = 1 << (max(lengths) - 1).bit_length()
+        graphs = {}
+        padded = TalkerPrefill(cfg, weights, arena, 16, padded_len, cos, sin)
+        padded.capture()
+        embeds = torch.zeros(16, padded_len, cfg.hidden, dtype=torch.bfloat16, device=dev)
+        offset = 0
+        for b, n in enumerate(lengths):
+            embeds[b, :n] = x[offset:offset + n]
+            offset += n
+        lens = torch.tensor(lengths, device=dev)
+        slots = torch.arange(16, device=dev)
+        graphs["padded"] = (padded, lambda i: padded.run(embeds, lens, slots), 16 * padded_len)
+        rows = packed_rows(total)
+        packed = PackedPrefill(cfg, weights, arena, rows, 16, cos, sin)
+        packed.capture()
+        px = torch.cat([x, x[-1:].expand(rows - total, -1)])
+        tables = [t.to(dev) for t in packed_tables(lengths, 0, rows, 16)]
+        graphs["packed"] = (packed, lambda i: packed.run(px, *tables), rows)
+        for form, (graph, call, graph_rows) in graphs.items():
+            for i in range(args.warmup):
+                call(i)
+            ms = timed_region(call, args.steps) / args.steps
+            out.append({"workload": "prefill", "group": name, "form": form, "prompts": 16, "real_rows": total,
+                        "graph_rows": graph_rows, "ms": ms, "ttfa_share_ms_per_prompt": ms / 16,
+                        "projection_tflops_real_rows": per_row * total / (ms / 1e3) / 1e12})
+            graph.close()
+    return out
+
+
 def run_chain(args) -> list:
     """One decode layer's projections after its attention (O + residual, gate/up with the folded
     RMSNorm and SwiGLU, down + residual, the next layer's QKV with the folded RMSNorm) at the
@@ -1086,6 +1142,10 @@ def main():
             "data": "synthetic (seeded random-init codec, uniform codes)",
             "config": {"workload": "BASELINE config 4: incremental codec decode", "streams": args.batch,
                        "chunk_frames": 4}, "status_word": res["status"]}))
+        return
+    if args.workload == "prefill":
+        for row in run_prefill(args):
+            print(json.dumps(row))
         return
     if args.workload == "chain":
         for row in run_chain(args):

@@ -29,3 +29,52 @@ def emission_target(emitted: int, chunk_frames: int = 8) -> int:
     if emitted == 0:
         return 2
     return emitted * 2 if emitted < 8 else emitted + chunk_frames
+
+
+# Packed prefill: the attention's split plan counts rows x KV heads (8) below 65,536, and the
+# 512-row buckets keep a packed group within 7,680 rows.
+MAX_PACKED_ROWS = 7680
+
+
+def packed_rows(total: int) -> int:
+    """Row bucket of a packed prefill of `total` prompt rows: powers of two from 64 up to 512,
+    then multiples of 512 (one captured graph per bucket, at most ~25% padding above 512)."""
+    if total < 1:
+        raise ValueError("A packed prefill needs at least one row")
+    if total <= 512:
+        return max(64, 1 << (total - 1).bit_length())
+    return (total + 511) // 512 * 512
+
+
+def packed_groups(lengths, max_rows: int) -> list:
+    """Consecutive [start, end) groups of prompts whose lengths sum to at most `max_rows` (a
+    longer prompt forms a group of its own)."""
+    groups, start, rows = [], 0, 0
+    for i, length in enumerate(lengths):
+        if i > start and rows + length > max_rows:
+            groups.append((start, i))
+            start, rows = i, 0
+        rows += length
+    if lengths:
+        groups.append((start, len(lengths)))
+    return groups
+
+
+def packed_tables(lengths, first_slot: int, rows: int, requests: int):
+    """Row tables of a packed prefill (CPU int64): the arena slot and position of every packed
+    row (prompt i occupies slot first_slot + i, positions 0..lengths[i]-1; rows past the real
+    ones repeat the last real row) and the row index of each prompt's last token (entries past
+    the prompts repeat the last one)."""
+    import torch
+    n, total = len(lengths), sum(lengths)
+    if not 1 <= n <= requests or total > rows:
+        raise ValueError("Packed prompts exceed the prefill's rows or requests")
+    counts = torch.tensor(lengths, dtype=torch.long)
+    row_slots = torch.repeat_interleave(torch.arange(first_slot, first_slot + n), counts)
+    row_pos = torch.cat([torch.arange(length) for length in lengths])
+    last = torch.cumsum(counts, 0) - 1
+    pad = rows - total
+    row_slots = torch.cat([row_slots, row_slots[-1:].expand(pad)])
+    row_pos = torch.cat([row_pos, row_pos[-1:].expand(pad)])
+    last = torch.cat([last, last[-1:].expand(requests - n)])
+    return row_slots, row_pos, last

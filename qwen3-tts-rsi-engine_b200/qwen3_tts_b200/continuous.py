@@ -14,8 +14,8 @@ CUDA graph per (batch bucket, context bucket):
 
 followed by one device->host copy of the new tokens (the reference's
 ``.tolist()`` sync, continuous.py:623) for the host's stop/emit decisions.
-Admission is a batched padded prefill graph that writes K/V straight into the
-arena slots (no intermediate cache copy) and samples each first token on the
+Admission is a batched prefill graph over the prompts packed end to end (no
+padding to the longest) that writes K/V straight into the arena slots (no intermediate cache copy) and samples each first token on the
 device. Audio chunks are decoded by the slot-indexed incremental codec from
 the device code ring, converted to PCM16 on the device and copied to the host
 in one transfer per tick.
@@ -36,7 +36,8 @@ import numpy as np
 import torch
 
 from . import _lib, checkpoint, ops
-from .batching import context_bucket, decode_batch_size, emission_target
+from .batching import (MAX_PACKED_ROWS, context_bucket, decode_batch_size, emission_target, packed_groups,
+                       packed_rows, packed_tables)
 from .code_buffer import CodecCodeBuffer
 from .codec import CodecGraph, CodecSlots, pack_codec
 from .codec_weights import random_codec
@@ -44,7 +45,7 @@ from .config import CODEC, PREDICTOR, PROMPT, TALKER, CodecConfig, PredictorConf
 from .predictor import PredictorStep
 from .prompt import SUPPORTED_SAMPLING, CustomVoicePrompt, prompt_weights
 from .sampling import random_table
-from .talker import SlotArena, TalkerPrefill, TalkerStep, rope_tables
+from .talker import PackedPrefill, SlotArena, TalkerPrefill, TalkerStep, rope_tables
 from .weights import decoder_weights, pack_decoder
 
 BF16 = torch.bfloat16
@@ -214,7 +215,8 @@ class ContinuousModel:
                  codec_chunk_frames=8, codec_streams=1, decode_bucket_step=0, prewarm_codec=False,
                  prewarm_prefill=False, bucket_prefill=True, max_frames=4096, max_prefill_batch=16, use_graphs=True,
                  temperature=0.9, top_k=50, top_p=1.0, subtalker_temperature=0.9, subtalker_top_k=50,
-                 subtalker_top_p=1.0, penalty=1.05, pipeline_audio=False, **flags):
+                 subtalker_top_p=1.0, penalty=1.05, pipeline_audio=False, packed_prefill=True,
+                 max_prefill_rows=4096, **flags):
         if codec_chunk_frames not in (8, 16) or (codec_chunk_frames != 8 and not incremental_codec):
             raise ValueError("16-frame chunks require the incremental codec")
         if codec_streams not in (1, 2) or (codec_streams == 2 and not incremental_codec):
@@ -239,6 +241,9 @@ class ContinuousModel:
         self.codec_streams, self.codec_batch_size = codec_streams, codec_batch_size
         self.context = codec_left_context
         self.bucket_prefill, self.max_prefill_batch = bucket_prefill, max_prefill_batch
+        if not 1 <= max_prefill_rows <= MAX_PACKED_ROWS:
+            raise ValueError(f"max_prefill_rows must be within 1..{MAX_PACKED_ROWS}")
+        self.packed_prefill, self.max_prefill_rows = packed_prefill, max_prefill_rows
         self.use_graphs = use_graphs
         self.temperature, self.top_k, self.top_p, self.penalty = temperature, top_k, top_p, penalty
         self.max_frames = max_frames
@@ -295,6 +300,7 @@ class ContinuousModel:
         self.on_codes = None
         self.graphs: dict[tuple[int, int], TickGraph] = {}
         self.prefills: dict[tuple[int, int], TalkerPrefill] = {}
+        self.packed: dict[int, PackedPrefill] = {}
         self._predictors: dict[int, PredictorStep] = {}
         self._buffers: dict[int, dict] = {}
         self._active = 0
@@ -349,11 +355,22 @@ class ContinuousModel:
             self.prefills[key] = graph
         return graph
 
+    def _packed_prefill(self, rows: int) -> PackedPrefill:
+        graph = self.packed.get(rows)
+        if graph is None:
+            graph = PackedPrefill(self.talker_config, self.talker_weights, self.arena, rows, self.max_slots, self.cos,
+                                  self.sin)
+            if self.use_graphs:
+                graph.capture()
+            self.packed[rows] = graph
+        return graph
+
     def _drop_graphs(self) -> None:
-        for graph in list(self.graphs.values()) + list(self.prefills.values()):
+        for graph in list(self.graphs.values()) + list(self.prefills.values()) + list(self.packed.values()):
             graph.close()
         self.graphs.clear()
         self.prefills.clear()
+        self.packed.clear()
 
     def ensure_capacity(self, required: int) -> None:
         """Double the KV arena when `required` does not fit (continuous.py:353-363); every
@@ -381,21 +398,27 @@ class ContinuousModel:
 
     @torch.inference_mode()
     def admit_batch(self, submissions) -> None:
-        """Batched padded prefill into slots len(states).. (continuous.py:424-473)."""
+        """Batched prefill into slots len(states).. (continuous.py:424-473): prompts packed end to
+        end in groups of at most `max_prefill_rows` rows, or (packed_prefill=False) padded to a
+        power-of-two length in groups of `max_prefill_batch` as the reference pads them."""
         submissions = list(submissions)
         if len(self.states) + len(submissions) > self.max_slots:
             raise ValueError("Insufficient continuous request slots")
-        for offset in range(0, len(submissions), self.max_prefill_batch):
-            self._admit_group(submissions[offset:offset + self.max_prefill_batch])
-
-    def _admit_group(self, submissions) -> None:
+        if not self.packed_prefill:
+            for offset in range(0, len(submissions), self.max_prefill_batch):
+                self._admit_group(submissions[offset:offset + self.max_prefill_batch])
+            return
         prompts = [self.prepare_prompt(payload) for _, payload in submissions]
         lengths = [p["inputs_embeds"].shape[1] for p in prompts]
-        count, n = len(self.states), len(submissions)
+        for start, end in packed_groups(lengths, self.max_prefill_rows):
+            self._admit_group(submissions[start:end], prompts[start:end])
+
+    def _prefill_padded(self, prompts, lengths, count):
+        n = len(prompts)
         padded = 1 << (max(lengths) - 1).bit_length()
         batch = 1 << (n - 1).bit_length() if self.bucket_prefill else n
         self.ensure_capacity(padded - 1)
-        S, H = self.state, self.talker_config.hidden
+        H = self.talker_config.hidden
         embeds = torch.zeros(batch, padded, H, dtype=BF16, device=self.device)
         for row, (prompt, length) in enumerate(zip(prompts, lengths)):
             embeds[row, :length] = prompt["inputs_embeds"][0]
@@ -406,7 +429,32 @@ class ContinuousModel:
                             dtype=torch.long).pin_memory()
         table = host.to(self.device, non_blocking=True)
         slots, lens = table[:batch], table[batch:]
-        hidden, logits = self._prefill(batch, padded).run(embeds, lens, slots)
+        return self._prefill(batch, padded).run(embeds, lens, slots)
+
+    def _prefill_packed(self, prompts, lengths, count):
+        n, total = len(prompts), sum(lengths)
+        rows = packed_rows(total)
+        self.ensure_capacity(max(lengths) - 1)
+        graph = self._packed_prefill(rows)
+        embeds = torch.cat([p["inputs_embeds"][0] for p in prompts])
+        packed = torch.empty(rows, self.talker_config.hidden, dtype=BF16, device=self.device)
+        packed[:total] = embeds
+        packed[total:] = embeds[-1]
+        row_slots, row_pos, last = packed_tables(lengths, count, rows, self.max_slots)
+        host = torch.cat([row_slots, row_pos, last]).pin_memory()
+        table = host.to(self.device, non_blocking=True)
+        return graph.run(packed, table[:rows], table[rows:2 * rows], table[2 * rows:])
+
+    def _admit_group(self, submissions, prompts=None) -> None:
+        if prompts is None:
+            prompts = [self.prepare_prompt(payload) for _, payload in submissions]
+        lengths = [p["inputs_embeds"].shape[1] for p in prompts]
+        count, n = len(self.states), len(submissions)
+        S = self.state
+        if self.packed_prefill:
+            hidden, logits = self._prefill_packed(prompts, lengths, count)
+        else:
+            hidden, logits = self._prefill_padded(prompts, lengths, count)
         # per-slot state of the new requests
         tables = torch.full((n, S.table_rows, 16), 0.5, dtype=torch.float32)
         for row, ((_, payload), prompt) in enumerate(zip(submissions, prompts)):

@@ -354,6 +354,117 @@ class TalkerPrefill:
             self.graph = None
 
 
+class PackedPrefill:
+    """Batched prefill of several prompts packed end to end, without padding to the longest
+    (PrefillGraph, prefill_graph.py:18-78, computes the same causal stack over padded rows).
+
+    Row r of the `rows` packed rows belongs to arena slot ``row_slots[r]`` at position
+    ``row_pos[r]`` (0 .. its prompt length - 1): it writes its K/V there and attends keys
+    0..row_pos[r] of that slot, so every prompt sees only itself. Rows past the real ones
+    repeat the last real row (same slot, position and input: identical K/V writes). Returns
+    the final-norm hidden state and fp32 logits of each prompt's last token (``last`` holds
+    their row indices; up to `requests` prompts)."""
+
+    def __init__(self, cfg: DecoderConfig, weights: dict, arena: SlotArena, rows: int, requests: int, cos, sin,
+                 norm_mode: int = _lib.NORM_REFERENCE):
+        if rows > arena.capacity * arena.slots:
+            raise ValueError("Packed prefill longer than the KV arena")
+        self.cfg, self.w, self.arena = cfg, weights, arena
+        self.rows, self.requests = rows, requests
+        self.context = min(arena.capacity, rows)
+        self.cos, self.sin, self.norm_mode = cos, sin, norm_mode
+        dev = arena.device
+        R, H = rows, cfg.hidden
+        self.inputs = torch.zeros(R, H, dtype=BF16, device=dev)
+        self.row_slots = torch.zeros(R, dtype=torch.long, device=dev)
+        self.row_pos = torch.zeros(R, dtype=torch.long, device=dev)
+        self.last = torch.zeros(requests, dtype=torch.long, device=dev)
+        self.h = torch.zeros(R, H, dtype=BF16, device=dev)
+        self.xn = torch.zeros(R, H, dtype=BF16, device=dev)
+        self.qkv = torch.zeros(R, cfg.qkv_width, dtype=BF16, device=dev)
+        self.q = torch.zeros(R, cfg.q_heads, cfg.head_dim, dtype=BF16, device=dev)
+        self.attn = torch.zeros(R, cfg.q_heads, cfg.head_dim, dtype=BF16, device=dev)
+        self.act = torch.zeros(R, cfg.ffn, dtype=BF16, device=dev)
+        self.gathered = torch.zeros(requests, H, dtype=BF16, device=dev)
+        self.hidden = torch.zeros(requests, H, dtype=BF16, device=dev)
+        self.logits = torch.zeros(requests, cfg.vocab, dtype=torch.float32, device=dev)
+        need = ops.decode_attention_workspace_bytes(R, cfg.q_heads, cfg.head_dim, self.context)
+        self.ws_attn = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
+        self.status = ops.status_word(dev)
+        self.graph = None
+
+    def compute(self) -> None:
+        cfg, w, R = self.cfg, self.w, self.rows
+        res_in = self.inputs
+        ops.attention_plan(self.row_pos, self.ws_attn, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads,
+                           head_dim=cfg.head_dim, context=self.context)
+        for i, layer in enumerate(w["layers"]):
+            if layer.folded:
+                ops.linear(res_in, layer.qkv, out=self.qkv, row_norm_eps=cfg.eps)
+            else:
+                ops.rms_norm(res_in, layer.input_norm, cfg.eps, self.norm_mode, out=self.xn)
+                ops.linear(self.xn, layer.qkv, out=self.qkv)
+            ops.qk_norm_rope_kv(self.qkv, layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin, self.row_pos,
+                                self.row_pos, self.arena.keys[i], self.arena.values[i], q_heads=cfg.q_heads,
+                                kv_heads=cfg.kv_heads, head_dim=cfg.head_dim, length=1, query_out=self.q,
+                                slots=self.row_slots)
+            ops.decode_attention(self.q, self.arena.keys[i], self.arena.values[i], self.row_pos, context=self.context,
+                                 rows_per_slot=1, slots=self.row_slots, out=self.attn, workspace=self.ws_attn)
+            ops.linear(self.attn.view(R, cfg.q_width), layer.o, out=self.h, epilogue=_lib.EPI_RESIDUAL,
+                       residual=res_in)
+            if layer.folded:
+                ops.linear(self.h, layer.gate_up, out=self.act, epilogue=_lib.EPI_SWIGLU_PAIRED, row_norm_eps=cfg.eps)
+            else:
+                ops.rms_norm(self.h, layer.post_norm, cfg.eps, self.norm_mode, out=self.xn)
+                ops.linear(self.xn, layer.gate_up, out=self.act, epilogue=_lib.EPI_SWIGLU_PAIRED)
+            ops.linear(self.act, layer.down, out=self.h, epilogue=_lib.EPI_RESIDUAL, residual=self.h)
+            res_in = self.h
+        ops.embedding(self.last, self.h, out=self.gathered)       # last row of each prompt
+        ops.rms_norm(self.gathered, w["norm"], cfg.eps, self.norm_mode, out=self.hidden)
+        ops.linear(self.hidden, w["head"], out=self.logits)
+
+    @torch.inference_mode()
+    def capture(self, warmup: int = 2) -> None:
+        """Capture after warm-up; warm-up runs every row as position 0 of slot 0, whose first
+        position is saved and restored."""
+        saved = self.arena.packed[:, :1, :, :1].clone()
+        self.row_slots.zero_()
+        self.row_pos.zero_()
+        self.last.zero_()
+        stream = torch.cuda.Stream(device=self.inputs.device)
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                self.compute()
+        torch.cuda.current_stream().wait_stream(stream)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=stream):
+            self.compute()
+        torch.cuda.synchronize()
+        self.arena.packed[:, :1, :, :1].copy_(saved)
+
+    @torch.inference_mode()
+    def run(self, packed, row_slots, row_pos, last):
+        """packed [rows, H] (padding rows repeat the last real row), row_slots / row_pos [rows],
+        last [requests] -> (hidden, logits) of the `requests` prompts."""
+        self.inputs.copy_(packed)
+        self.row_slots.copy_(row_slots)
+        self.row_pos.copy_(row_pos)
+        self.last.copy_(last)
+        if self.graph is None:
+            self.compute()
+        else:
+            self.graph.replay()
+        return self.hidden.clone(), self.logits.clone()
+
+    def close(self) -> None:
+        if self.graph is not None:
+            torch.cuda.synchronize()
+            self.graph.reset()
+            self.graph = None
+
+
 class TalkerDecoder:
     """Talker weights, arena and per-bucket step graphs."""
 

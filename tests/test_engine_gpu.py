@@ -57,7 +57,8 @@ PAYLOADS = {
 }
 
 
-def test_engine_ticks_match_teacher_forced_oracle(cuda):
+@pytest.mark.parametrize("packed", [True, False])
+def test_engine_ticks_match_teacher_forced_oracle(cuda, packed):
     from qwen3_tts_b200 import prompt as P
     from qwen3_tts_b200.continuous import ContinuousModel
     from qwen3_tts_b200.weights import decoder_weights
@@ -69,7 +70,7 @@ def test_engine_ticks_match_teacher_forced_oracle(cuda):
     engine = ContinuousModel(None, cuda, max_slots=4, initial_capacity=64, talker_config=tcfg,
                              predictor_config=pcfg, codec_config=ccfg, prompt_config=prcfg,
                              weights={"talker": tw, "predictor": pw, "prompt": prw}, codec_decoder=decoder,
-                             top_k=1, subtalker_top_k=1, max_frames=64)
+                             top_k=1, subtalker_top_k=1, max_frames=64, packed_prefill=packed)
     log = defaultdict(list)
     engine.on_codes = lambda ident, frame, codes, token: log[ident].append((frame, codes, token))
     chunks = defaultdict(list)

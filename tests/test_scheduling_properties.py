@@ -6,7 +6,8 @@ from hypothesis import given, settings
 from hypothesis import strategies as st
 
 from oracle import scheduling as OS
-from qwen3_tts_b200.batching import context_bucket, decode_batch_size, emission_target
+from qwen3_tts_b200.batching import (MAX_PACKED_ROWS, context_bucket, decode_batch_size, emission_target,
+                                    packed_groups, packed_rows, packed_tables)
 
 POW2 = st.sampled_from([1, 2, 4, 8, 16, 32, 64, 128])
 
@@ -50,3 +51,34 @@ def test_context_bucket_covers_the_keys(capacity, data):
     assert bucket == OS.context_bucket(required, capacity)
     assert required <= bucket <= capacity and bucket >= min(64, capacity)
     assert bucket == capacity or bucket & (bucket - 1) == 0
+
+
+@settings(max_examples=300, deadline=None)
+@given(lengths=st.lists(st.integers(1, 600), min_size=1, max_size=64), max_rows=st.integers(256, MAX_PACKED_ROWS))
+def test_packed_prefill_groups_and_tables_cover_every_prompt_once(lengths, max_rows):
+    """Packed admission: consecutive groups within the row budget (a longer prompt alone), a
+    row bucket that holds the group, and row tables that give every prompt's tokens their own
+    slot and positions 0..n-1 with padding rows repeating the last real row."""
+    groups = packed_groups(lengths, max_rows)
+    assert groups[0][0] == 0 and groups[-1][1] == len(lengths)
+    assert all(a[1] == b[0] for a, b in zip(groups, groups[1:]))
+    first_slot = 3
+    for start, end in groups:
+        part = lengths[start:end]
+        total = sum(part)
+        assert total <= max_rows or end - start == 1
+        if end < len(lengths):
+            assert total + lengths[end] > max_rows             # greedy: the next prompt did not fit
+        rows = packed_rows(total)
+        assert total <= rows and (rows & (rows - 1) == 0 if rows <= 512 else rows % 512 == 0)
+        assert rows <= max(64, 2 * total - 1) if total <= 512 else rows - total < 512
+        slots, pos, last = packed_tables(part, first_slot, rows, 64)
+        assert slots.shape == pos.shape == (rows,) and last.shape == (64,)
+        offset = 0
+        for i, n in enumerate(part):
+            assert slots[offset:offset + n].tolist() == [first_slot + i] * n
+            assert pos[offset:offset + n].tolist() == list(range(n))
+            assert last[i] == offset + n - 1
+            offset += n
+        assert (slots[total:] == slots[total - 1]).all() and (pos[total:] == pos[total - 1]).all()
+        assert (last[end - start:] == total - 1).all()
