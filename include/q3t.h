@@ -177,6 +177,7 @@ int q3t_linear_rownorm(const void* x, int64_t x_stride, int64_t rows, int64_t in
 
 /* Flags of q3t_linear_ex. */
 #define Q3T_LINEAR_KEEP_WEIGHTS 1 /* load the weight tiles evict-last (the chain re-reads them soon) */
+#define Q3T_LINEAR_NARROW 2       /* keep the split-K kernel at prefill-sized row counts (see below) */
 
 /* q3t_linear (eps == 0) or q3t_linear_rownorm (eps > 0) with two cache controls:
  * - prefetch: [prefetch, prefetch + prefetch_bytes) (the next kernel's weights) is split
@@ -184,7 +185,11 @@ int q3t_linear_rownorm(const void* x, int64_t x_stride, int64_t rows, int64_t in
  *   ordering, no completion); 16-byte aligned, prefetch_bytes % 16 == 0; NULL or 0 = none;
  * - flags: Q3T_LINEAR_KEEP_WEIGHTS loads this GEMM's weight tiles with L2 evict-last
  *   priority instead of evict-first (the code predictor keeps part of its layers in L2
- *   across its 15 codebook steps, continuous.py:49-68). */
+ *   across its 15 codebook steps, continuous.py:49-68).
+ * Row counts in the thousands (a packed prefill; PrefillGraph's projections,
+ * prefill_graph.py:31-50) with pre-tiled weights, a bf16 output, eps == 0, no prefetch and
+ * no flags run a persistent kernel of 128-feature x 256-row tiles instead of the split-K
+ * kernel; Q3T_LINEAR_NARROW keeps the split-K kernel (results agree to bf16 rounding). */
 int q3t_linear_ex(const void* x, int64_t x_stride, int64_t rows, int64_t in_features,
                   const void* weight, int64_t out_features, const void* bias, void* out,
                   int64_t out_stride, int out_dtype, int epilogue, const void* residual,

@@ -619,6 +619,278 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------- wide tiles
+// Row counts in the thousands (a packed prefill's prompt rows) make the projections
+// tensor-bound rather than weight-streaming. linear_wide_kernel is persistent, one CTA per SM:
+// CTA c walks tiles c, c + grid, ... of 128 output features x 256 rows over the whole K (no
+// split), with one k-block ring across its tiles and TWO TMEM accumulators of 256 columns, so
+// the epilogue of tile j (TMEM -> registers -> bf16 staging -> TMA store, in 64-row chunks)
+// runs while the MMAs of tile j + 1 fill the other accumulator. Tiles are numbered
+// feature-block-major (consecutive CTAs share a weight tile; every operand stays in L2).
+// Roles (320 threads): warp 0 lane 0 = TMA producer, warp 1 = TMEM owner, lane 0 the MMA
+// issuer, warps 2-9 = epilogue (warp w reads TMEM lanes 32(w%4)..+31 = output features, and
+// the first (w < 6) or second 32 rows of each 64-row chunk).
+// Epilogue decisions that follow a bounded wait are taken together (barrier reduction), so a
+// timeout never splits the epilogue warps across barriers.
+constexpr int kWideRows = 256;                            // activation rows per tile (UMMA N)
+constexpr int kWideStages = 4;
+constexpr int kWideStageBytes = kABytes + kWideRows * kTileK * 2;  // 16 KB weights + 32 KB rows
+constexpr int kWideRing = kWideStages * kWideStageBytes;
+constexpr int kWideChunk = 64;                            // rows per staged output chunk
+constexpr int kWideStaging = kWideChunk * kTileN * 2;     // 16 KB
+constexpr int kWideThreads = 320;
+constexpr int kWideEpiThreads = kWideThreads - 64;
+constexpr int kWideSmem = kWideRing + kWideStaging + 256 + 1024;
+static_assert(kWideSmem <= 232448, "wide GEMM shared memory");
+
+struct WideArgs {
+  int rows, out_features, kblocks, n_tiles, m_tiles;
+  const uint8_t* tiles;        // pre-swizzled weight tiles (Q3T_WEIGHTS_TILED layout)
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* scale;  // per-feature scale of Q3T_EPI_RESIDUAL_SCALED
+  unsigned* status;
+};
+
+Q3T_DEV void epi_bar_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// Barrier of the 256 epilogue threads that also ANDs `pred` over them.
+Q3T_DEV bool epi_bar_and(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.cta.red.and.pred q, 1, 256, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(uint32_t(pred))
+      : "memory");
+  return r != 0;
+}
+// 16 TMEM columns of this warp's lanes without the completion wait (tmem_wait_ld follows).
+Q3T_DEV void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+Q3T_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+template <int EPI>
+__global__ void __launch_bounds__(kWideThreads, 1)
+    linear_wide_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmo,
+                       const __grid_constant__ CUtensorMap tmr, WideArgs a) {
+  constexpr int S = kWideStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* staging = smem + kWideRing;
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + kWideStaging);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;    // [2] accumulator b complete
+  uint64_t* tempty = tfull + 2;   // [2] accumulator b read out by the 8 epilogue warps
+  uint64_t* res_bar = tempty + 2; // residual chunk landed in the staging buffer
+  uint64_t* mma_done = res_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles = a.n_tiles * a.m_tiles;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kWideEpiThreads / 32);
+    }
+    mbar_init(res_bar, 1);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmx);
+    prefetch_tmap(&tmo);
+    if (has_residual(EPI)) prefetch_tmap(&tmr);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * kWideRows);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  grid_dependency_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      const uint64_t pol_x = policy_evict_last();
+      int it = 0;
+      for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x) {
+        const int nt = t / a.m_tiles, mt = t - nt * a.m_tiles;
+        for (int kb = 0; kb < a.kblocks; ++kb) {
+          const int s = it % S;
+          if (*abort_flag || !mbar_wait(&empty[s], ((it / S) & 1) ^ 1, a.status, kStatusMmaTimeout)) {
+            *abort_flag = 1;
+            break;
+          }
+          uint8_t* dst = smem + s * kWideStageBytes;
+          mbar_expect_tx(&full[s], kWideStageBytes);
+          bulk_load(dst, a.tiles + (size_t(nt) * size_t(a.kblocks) + size_t(kb)) * size_t(kABytes), kABytes,
+                    &full[s]);
+          tma_load_2d(dst + kABytes, &tmx, &full[s], kb * kTileK, mt * kWideRows, pol_x);
+          ++it;
+        }
+      }
+      // loads still in flight land before the CTA can exit (the last load of each slot)
+      if (*abort_flag)
+        for (int i = it > S ? it - S : 0; i < it; ++i) mbar_wait(&full[i % S], (i / S) & 1, a.status, kStatusTmaTimeout);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      constexpr uint32_t idesc = umma_idesc_bf16(kTileN, kWideRows);
+      int it = 0, j = 0;
+      for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x, ++j) {
+        const int b = j & 1;
+        if (!mbar_wait(&tempty[b], ((j >> 1) & 1) ^ 1, a.status, kStatusMmaTimeout)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + uint32_t(b * kWideRows);
+        bool ok = true;
+        for (int kb = 0; kb < a.kblocks; ++kb, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(&full[s], (it / S) & 1, a.status, kStatusTmaTimeout)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = umma_desc_sw128(smem_u32(smem + s * kWideStageBytes));
+          const uint64_t bd = umma_desc_sw128(smem_u32(smem + s * kWideStageBytes + kABytes));
+#pragma unroll
+          for (int k = 0; k < kTileK / 16; ++k) umma_bf16(d, ad + 2 * k, bd + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (!ok) {
+          *abort_flag = 1;
+          break;
+        }
+        umma_commit(&tfull[b]);
+      }
+      // every MMA of this CTA has completed before TMEM is released
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, a.status, kStatusMmaTimeout);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue: warps 2-9
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;      // rows 32*half .. +31 of each chunk
+    const int r = quad * 32 + lane;        // tile row = output feature n0 + r
+    const int et = threadIdx.x - 64;       // 0 .. 255
+    const bool leader = et == 0;
+    __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(staging);
+    int j = 0, chunks = 0;
+    bool res_pending = false;  // leader: a residual load whose landing nobody saw
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
+      const int b = j & 1;
+      const int nt = t / a.m_tiles, mt = t - nt * a.m_tiles;
+      const int n0 = nt * kTileN, m0 = mt * kWideRows;
+      const bool ready = mbar_wait(&tfull[b], (j >> 1) & 1, a.status, kStatusMmaTimeout);
+      if (!epi_bar_and(ready && !*abort_flag)) {
+        if (leader) *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t tbase = tmem + (uint32_t(quad * 32) << 16) + uint32_t(b * kWideRows + 32 * half);
+      const int n = n0 + r;
+      const bool live = n < a.out_features;
+      const float bias = (a.bias != nullptr && live) ? __bfloat162float(a.bias[n]) : 0.f;
+      const float g = (EPI == Q3T_EPI_RESIDUAL_SCALED && live) ? __bfloat162float(a.scale[n]) : 0.f;
+      bool ok = true;
+      for (int h = 0; h < kWideRows / kWideChunk && ok; ++h) {
+        const int mc = m0 + h * kWideChunk;
+        if (mc >= a.rows) break;
+        // the staging buffer is free once the previous chunk's store has read it
+        if (leader) {
+          bulk_wait_read0();
+          if constexpr (has_residual(EPI)) {
+            mbar_expect_tx(res_bar, uint32_t(kWideStaging));
+            tma_load_2d(stage, &tmr, res_bar, n0, mc, policy_evict_first());
+            res_pending = true;
+          }
+        }
+        if constexpr (has_residual(EPI)) {
+          const bool landed = mbar_wait(res_bar, uint32_t(chunks & 1), a.status, kStatusTmaTimeout);
+          if (leader && landed) res_pending = false;
+          ok = epi_bar_and(landed);
+          if (!ok) {
+            if (leader) *abort_flag = 1;
+            break;
+          }
+        } else {
+          epi_bar_sync();
+        }
+        ++chunks;
+        uint32_t raw[2][16];
+        tmem_ld16_async(tbase + uint32_t(h * kWideChunk), raw[0]);
+        tmem_ld16_async(tbase + uint32_t(h * kWideChunk + 16), raw[1]);
+        tmem_wait_ld();
+        int store_col = n0;
+        if constexpr (EPI == Q3T_EPI_SWIGLU_PAIRED) {
+          // tile rows are [64 gate; 64 up] of output features n0/2 .. n0/2 + 63. The chunk goes
+          // through shared memory as bf16 (silu_gate rounds both inputs to bf16 first), then every
+          // epilogue thread finalises 16 rows of one feature.
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            stage[(32 * half + i) * kTileN + r] = __float2bfloat16_rn(__uint_as_float(raw[i >> 4][i & 15]));
+          epi_bar_sync();
+          const int f = et & 63, r0 = (et >> 6) * 16;
+          float o[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            o[i] = silu_gate(__bfloat162float(stage[(r0 + i) * kTileN + f]),
+                             __bfloat162float(stage[(r0 + i) * kTileN + 64 + f]));
+          epi_bar_sync();  // every gate/up value is read before the outputs overwrite them
+#pragma unroll
+          for (int i = 0; i < 16; ++i) stage[(r0 + i) * 64 + f] = __float2bfloat16_rn(o[i]);
+          store_col = n0 / 2;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            __nv_bfloat16* slot = stage + (32 * half + i) * kTileN + r;
+            const float rr = has_residual(EPI) ? __bfloat162float(*slot) : 0.f;
+            *slot = __float2bfloat16_rn(epilogue_value<EPI>(__uint_as_float(raw[i >> 4][i & 15]) + bias, rr, g));
+          }
+        }
+        fence_async_shared();  // generic-proxy writes of the chunk, before the TMA store reads them
+        epi_bar_sync();
+        if (leader) {
+          tma_store_2d(&tmo, stage, store_col, mc);
+          bulk_commit_group();
+        }
+      }
+      // accumulator b is read out (every tcgen05.ld above has completed)
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
+      if (!ok) break;
+    }
+    if (leader) {
+      bulk_wait_read0();  // the staging buffer stays until the last store has read it
+      if (res_pending) mbar_wait(res_bar, uint32_t(chunks & 1), a.status, kStatusTmaTimeout);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 2 * kWideRows);
+}
+
 // Weight [N, K] row-major -> tiles [ceil(N/128)][ceil(K/64)] of the 128-byte-swizzled
 // shared-memory image (row r, 16-byte chunk j stored at chunk j ^ (r % 8)); padding is zero.
 __global__ void pack_tiles_kernel(const __nv_bfloat16* __restrict__ w, int64_t n, int64_t k, int64_t kblocks,
@@ -792,6 +1064,70 @@ int launch_linear(const Plan& p, const Maps& m, const GemmArgs& args, void* stre
   return Q3T_OK;
 }
 
+// 2-D bf16 map of an output (or residual) matrix {features, rows} with a {box_cols, 64}
+// box and no swizzle: one staged chunk of the wide kernel.
+bool chunk_map(CUtensorMap* map, const void* base, int64_t rows, int64_t features, int64_t stride, int box_cols) {
+  EncodeTiled enc = encoder();
+  if (enc == nullptr || !aligned16(base) || stride % 8 || stride < features) return false;
+  cuuint64_t dims[2] = {cuuint64_t(features), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(stride) * 2};
+  cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(kWideChunk)};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The wide kernel pays once the 256-row tiles fill every SM (measured on the talker prefill
+// projections: the split-K kernel's 128-row tiles are faster below that).
+bool wide_pays(int64_t rows, int64_t out_features) {
+  const int64_t tiles = ((rows + kWideRows - 1) / kWideRows) * ((out_features + kTileN - 1) / kTileN);
+  return rows >= 1024 && tiles >= sm_count();
+}
+
+template <int EPI>
+int launch_wide(const CUtensorMap& x, const CUtensorMap& o, const CUtensorMap& r, const WideArgs& a, void* stream) {
+  static PerDevice smem_once;
+  if (const int rc = smem_limit(smem_once, linear_wide_kernel<EPI>, kWideSmem, "linear_wide: set smem")) return rc;
+  const int tiles = a.n_tiles * a.m_tiles;
+  return launch(linear_wide_kernel<EPI>, dim3(unsigned(tiles < sm_count() ? tiles : sm_count())), dim3(kWideThreads),
+                size_t(kWideSmem), stream, true, "linear_wide", x, o, r, a);
+}
+
+// Returns Q3T_OK / an error code (negative), or kNotWide when the maps cannot be encoded
+// (the caller then runs the split-K kernel).
+constexpr int kNotWide = 1;
+int linear_wide(const void* x, int64_t x_stride, int64_t rows, int64_t in_features, const void* tiles,
+                int64_t out_features, const void* bias, void* out, int64_t out_stride, int epilogue,
+                const void* residual, int64_t residual_stride, const void* scale, unsigned* status, void* stream) {
+  CUtensorMap mx, mo, mr;
+  memset(&mr, 0, sizeof(mr));
+  const bool paired = epilogue == Q3T_EPI_SWIGLU_PAIRED;
+  if (make_map(&mx, x, rows, in_features, x_stride, kWideRows) != Q3T_OK) return kNotWide;
+  if (!chunk_map(&mo, out, rows, paired ? out_features / 2 : out_features, out_stride, paired ? 64 : kTileN))
+    return kNotWide;
+  if (has_residual(epilogue) && !chunk_map(&mr, residual, rows, out_features, residual_stride, kTileN))
+    return kNotWide;
+  WideArgs a = {};
+  a.rows = int(rows);
+  a.out_features = int(out_features);
+  a.kblocks = int((in_features + kTileK - 1) / kTileK);
+  a.n_tiles = int((out_features + kTileN - 1) / kTileN);
+  a.m_tiles = int((rows + kWideRows - 1) / kWideRows);
+  a.tiles = static_cast<const uint8_t*>(tiles);
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.scale = static_cast<const __nv_bfloat16*>(scale);
+  a.status = status;
+  switch (epilogue) {
+    case Q3T_EPI_STORE: return launch_wide<Q3T_EPI_STORE>(mx, mo, mr, a, stream);
+    case Q3T_EPI_RESIDUAL: return launch_wide<Q3T_EPI_RESIDUAL>(mx, mo, mr, a, stream);
+    case Q3T_EPI_RESIDUAL_SCALED: return launch_wide<Q3T_EPI_RESIDUAL_SCALED>(mx, mo, mr, a, stream);
+    case Q3T_EPI_GELU: return launch_wide<Q3T_EPI_GELU>(mx, mo, mr, a, stream);
+    case Q3T_EPI_SILU: return launch_wide<Q3T_EPI_SILU>(mx, mo, mr, a, stream);
+    default: return launch_wide<Q3T_EPI_SWIGLU_PAIRED>(mx, mo, mr, a, stream);
+  }
+}
+
 template <int EPI>
 int dispatch_bn(const Plan& p, const Maps& m, const GemmArgs& args, void* stream) {
   switch (p.bn) {
@@ -862,6 +1198,12 @@ int linear_impl(const void* x, int64_t x_stride, int64_t rows, int64_t in_featur
     return fail(Q3T_EINVAL, "linear: paired SwiGLU needs out_features %% 128 == 0, bf16 output, no bias");
   if (epilogue < Q3T_EPI_STORE || epilogue > Q3T_EPI_SILU)
     return fail(Q3T_EINVAL, "linear: epilogue (the Snake epilogue needs q3t_conv_linear)");
+  if (weight_tiles != nullptr && row_norm_eps == 0.f && out_dtype == Q3T_BF16 && prefetch == nullptr && flags == 0 &&
+      wide_pays(rows, out_features)) {
+    const int rc = linear_wide(x, x_stride, rows, in_features, weight_tiles, out_features, bias, out, out_stride,
+                               epilogue, residual, residual_stride, scale, status, stream);
+    if (rc != kNotWide) return rc;
+  }
   const Plan p = plan(rows, in_features, out_features);
   if (p.m_tiles > 65535) return fail(Q3T_EINVAL, "linear: too many rows (%lld)", (long long)rows);
   Maps maps;
@@ -934,7 +1276,7 @@ extern "C" int q3t_linear_ex(const void* x, int64_t x_stride, int64_t rows, int6
                              float eps, const void* weight_tiles, const void* prefetch, size_t prefetch_bytes,
                              int flags, unsigned* status, void* stream) {
   if (!(eps >= 0.f)) return fail(Q3T_EINVAL, "linear_ex: eps must be >= 0");
-  if (flags & ~Q3T_LINEAR_KEEP_WEIGHTS) return fail(Q3T_EINVAL, "linear_ex: unknown flags");
+  if (flags & ~(Q3T_LINEAR_KEEP_WEIGHTS | Q3T_LINEAR_NARROW)) return fail(Q3T_EINVAL, "linear_ex: unknown flags");
   return linear_impl(x, x_stride, rows, in_features, weight, out_features, bias, out, out_stride, out_dtype, epilogue,
                      residual, residual_stride, scale, eps, weight_tiles, prefetch, prefetch_bytes, flags, status,
                      stream);

@@ -16,6 +16,7 @@ Q3T_OK, Q3T_EINVAL, Q3T_EUNSUPPORTED, Q3T_ECUDA, Q3T_ESPACE = 0, -1, -2, -3, -4
 Q3T_BF16, Q3T_F32 = 0, 1
 EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU_PAIRED, EPI_RESIDUAL_SCALED, EPI_GELU, EPI_SILU, EPI_SNAKE = 0, 1, 2, 3, 4, 5, 6
 LINEAR_KEEP_WEIGHTS = 1
+LINEAR_NARROW = 2
 NORM_REFERENCE, NORM_NATIVE = 0, 1
 
 _p = ctypes.c_void_p

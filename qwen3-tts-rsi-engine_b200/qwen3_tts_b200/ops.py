@@ -289,7 +289,7 @@ def pack_tiles(weight: torch.Tensor) -> TiledWeight:
 
 def linear(x, weight, bias=None, *, out=None, out_dtype=BF16, epilogue: int = _lib.EPI_STORE, residual=None,
            scale=None, row_norm_eps: Optional[float] = None, workspace: Optional[torch.Tensor] = None,
-           prefetch=None, keep_weights: bool = False, tag: str = "linear"):
+           prefetch=None, keep_weights: bool = False, narrow: bool = False, tag: str = "linear"):
     """out = x @ weight.T (+ bias) with a fused epilogue, on tcgen05 tensor cores.
 
     `weight` is a contiguous bf16 [out, in] tensor or a TiledWeight. With
@@ -298,7 +298,8 @@ def linear(x, weight, bias=None, *, out=None, out_dtype=BF16, epilogue: int = _l
     multiplied into `weight`, see weights.fold_norm). `prefetch` (a weight
     tensor or TiledWeight, normally the next GEMM's) is pulled into L2 while
     this GEMM runs; `keep_weights` loads the weight tiles evict-last so that a
-    chain that re-reads them finds them in L2 (q3t_linear_ex)."""
+    chain that re-reads them finds them in L2 (q3t_linear_ex). Row counts in the thousands run
+    the persistent wide-tile kernel unless `narrow` keeps the split-K kernel."""
     tiled = isinstance(weight, TiledWeight)
     _need_cuda(x, weight.tiles if tiled else weight)
     if x.dtype != BF16 or (not tiled and (weight.dtype != BF16 or weight.ndim != 2 or not weight.is_contiguous())):
@@ -318,7 +319,7 @@ def linear(x, weight, bias=None, *, out=None, out_dtype=BF16, epilogue: int = _l
     if residual is not None:
         res2 = residual.reshape(rows, n_out) if residual.is_contiguous() else residual
     odt = _lib.Q3T_BF16 if out.dtype == BF16 else _lib.Q3T_F32
-    if prefetch is not None or keep_weights:
+    if prefetch is not None or keep_weights or narrow:
         pre = prefetch.tiles if isinstance(prefetch, TiledWeight) else prefetch
         if pre is not None:
             _need_cuda(pre)
@@ -327,7 +328,8 @@ def linear(x, weight, bias=None, *, out=None, out_dtype=BF16, epilogue: int = _l
              epilogue, _ptr(res2), res2.stride(0) if res2 is not None else 0, _ptr(scale),
              float(row_norm_eps) if row_norm_eps is not None else 0.0, weight.tiles.data_ptr() if tiled else None,
              _ptr(pre), (pre.numel() * pre.element_size()) // 16 * 16 if pre is not None else 0,
-             _lib.LINEAR_KEEP_WEIGHTS if keep_weights else 0, status_word(x.device).data_ptr(), _stream())
+             (_lib.LINEAR_KEEP_WEIGHTS if keep_weights else 0) | (_lib.LINEAR_NARROW if narrow else 0),
+             status_word(x.device).data_ptr(), _stream())
         return out
     if row_norm_eps is not None:
         call("q3t_linear_rownorm", x2.data_ptr(), x2.stride(0), rows, in_features,

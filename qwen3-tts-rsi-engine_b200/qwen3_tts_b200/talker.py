@@ -391,7 +391,23 @@ class PackedPrefill:
         need = ops.decode_attention_workspace_bytes(R, cfg.q_heads, cfg.head_dim, self.context)
         self.ws_attn = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
         self.status = ops.status_word(dev)
+        # From a thousand rows on, the projections run the wide-tile kernel, which takes no folded
+        # RMSNorm: the norm runs as its own pass with a unit weight (the norm weight stays
+        # folded into the projection weights), x -> bf16(x * rsqrt(mean(x^2) + eps)).
+        self.unit = torch.ones(H, dtype=BF16, device=dev) if rows >= 1024 else None
         self.graph = None
+
+    def _norm_linear(self, x, layer, weight, out, **kw) -> None:
+        cfg = self.cfg
+        if not layer.folded:
+            ops.rms_norm(x, layer.input_norm if weight is layer.qkv else layer.post_norm, cfg.eps, self.norm_mode,
+                         out=self.xn)
+            ops.linear(self.xn, weight, out=out, **kw)
+        elif self.unit is not None:
+            ops.rms_norm(x, self.unit, cfg.eps, self.norm_mode, out=self.xn)
+            ops.linear(self.xn, weight, out=out, **kw)
+        else:
+            ops.linear(x, weight, out=out, row_norm_eps=cfg.eps, **kw)
 
     def compute(self) -> None:
         cfg, w, R = self.cfg, self.w, self.rows
@@ -399,11 +415,7 @@ class PackedPrefill:
         ops.attention_plan(self.row_pos, self.ws_attn, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads,
                            head_dim=cfg.head_dim, context=self.context)
         for i, layer in enumerate(w["layers"]):
-            if layer.folded:
-                ops.linear(res_in, layer.qkv, out=self.qkv, row_norm_eps=cfg.eps)
-            else:
-                ops.rms_norm(res_in, layer.input_norm, cfg.eps, self.norm_mode, out=self.xn)
-                ops.linear(self.xn, layer.qkv, out=self.qkv)
+            self._norm_linear(res_in, layer, layer.qkv, self.qkv)
             ops.qk_norm_rope_kv(self.qkv, layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin, self.row_pos,
                                 self.row_pos, self.arena.keys[i], self.arena.values[i], q_heads=cfg.q_heads,
                                 kv_heads=cfg.kv_heads, head_dim=cfg.head_dim, length=1, query_out=self.q,
@@ -412,11 +424,7 @@ class PackedPrefill:
                                  rows_per_slot=1, slots=self.row_slots, out=self.attn, workspace=self.ws_attn)
             ops.linear(self.attn.view(R, cfg.q_width), layer.o, out=self.h, epilogue=_lib.EPI_RESIDUAL,
                        residual=res_in)
-            if layer.folded:
-                ops.linear(self.h, layer.gate_up, out=self.act, epilogue=_lib.EPI_SWIGLU_PAIRED, row_norm_eps=cfg.eps)
-            else:
-                ops.rms_norm(self.h, layer.post_norm, cfg.eps, self.norm_mode, out=self.xn)
-                ops.linear(self.xn, layer.gate_up, out=self.act, epilogue=_lib.EPI_SWIGLU_PAIRED)
+            self._norm_linear(self.h, layer, layer.gate_up, self.act, epilogue=_lib.EPI_SWIGLU_PAIRED)
             ops.linear(self.act, layer.down, out=self.h, epilogue=_lib.EPI_RESIDUAL, residual=self.h)
             res_in = self.h
         ops.embedding(self.last, self.h, out=self.gathered)       # last row of each prompt

@@ -320,6 +320,69 @@ def test_linear_paired_swiglu(ops, cuda, rows):
     torch.testing.assert_close(out.cpu().float(), ref.float(), atol=1e-2, rtol=2e-2)
 
 
+def _kernels_launched(fn):
+    """Names of the CUDA kernels `fn` launches (torch profiler, CUPTI)."""
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return {e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA}
+
+
+@pytest.mark.parametrize("rows,k,n,epi", [(2085, 2048, 4096, "store"), (4096, 2048, 2048, "residual"),
+                                          (1500, 2048, 12288, "swiglu"), (3000, 1000, 2000, "bias"),
+                                          (2560, 6144, 2048, "scaled")])
+def test_linear_wide_tiles_match_fp32_and_the_split_k_kernel(ops, cuda, rows, k, n, epi):
+    """Prefill-sized row counts run the persistent 128 x 256 wide-tile kernel (two TMEM
+    accumulators, 64-row TMA-stored chunks): ragged last row tile, K and N off the tile grid
+    (zero-filled loads, clipped stores), an in-place residual, paired SwiGLU, bias and the
+    scaled residual, against the fp32 reference and the split-K kernel (Q3T_LINEAR_NARROW)."""
+    from qwen3_tts_b200 import _lib
+    from qwen3_tts_b200.weights import interleave_gate_up
+    x = rnd(90 + rows, (rows, k), 1.0, BF16)
+    bias = scale = residual = None
+    epilogue = _lib.EPI_STORE
+    if epi == "swiglu":
+        gate, up = rnd(91, (n // 2, k), 0.02, BF16), rnd(92, (n // 2, k), 0.02, BF16)
+        w = interleave_gate_up(gate, up)
+        ref = E.swiglu(torch.cat([torch_linear(x, gate).to(BF16), torch_linear(x, up).to(BF16)], dim=-1)).float()
+        epilogue = _lib.EPI_SWIGLU_PAIRED
+    else:
+        w = rnd(93, (n, k), 0.02, BF16)
+        acc = torch_linear(x, w)
+        if epi == "bias":
+            bias = rnd(94, (n,), 0.5, BF16)
+            acc = acc + bias.float()
+        ref = acc.to(BF16).float()
+        if epi in ("residual", "scaled"):
+            residual = rnd(95, (rows, n), 1.0, BF16)
+            epilogue = _lib.EPI_RESIDUAL
+            if epi == "scaled":
+                scale = rnd(96, (n,), 0.5, BF16)
+                ref = (scale.float() * ref).to(BF16).float()
+                epilogue = _lib.EPI_RESIDUAL_SCALED
+            ref = (residual.float() + ref).to(BF16).float()
+    tiles = ops.pack_tiles(w.to(cuda))
+    dev = lambda t: None if t is None else t.to(cuda)
+
+    def run(narrow):
+        # the residual epilogue runs in place (out aliases the residual), as the decoder layers do
+        out = residual.clone().to(cuda) if epi == "residual" else None
+        res = out if epi == "residual" else dev(residual)
+        return ops.linear(x.to(cuda), tiles, dev(bias), out=out, epilogue=epilogue, residual=res, scale=dev(scale),
+                          narrow=narrow)
+
+    names = _kernels_launched(lambda: run(False))
+    assert any("linear_wide_kernel" in name for name in names), names
+    wide = run(False)
+    narrow = run(True)
+    torch.testing.assert_close(wide.cpu().float(), ref, atol=2e-2, rtol=2e-2)
+    # same bf16 operands and fp32 accumulation; the two kernels differ at most by one rounding
+    torch.testing.assert_close(wide.float(), narrow.float(), atol=1e-2, rtol=1e-2)
+    assert_status_clean(ops, cuda)
+
+
 @pytest.mark.parametrize("rows,k,n", [(1, 2048, 4096), (32, 2048, 4096), (32, 2048, 12288), (64, 1024, 2048),
                                       (100, 2048, 640), (300, 256, 1024)])
 def test_linear_rownorm_equals_rmsnorm_then_linear(ops, cuda, rows, k, n):
