@@ -877,7 +877,7 @@ def run_prefill(args) -> list:
     the reference's shape) and the packed graph (prompts end to end, 512-row buckets). Each
     line: mean CUDA-event ms over `steps` graph replays after `warmup`, and the projection
     GEMMs' FLOP/s over the real prompt rows (2 x rows x projection weights x 28 layers)."""
-    from qwen3_tts_b200.batching import packed_rows, packed_tables
+    from qwen3_tts_b200.batching import packed_rows, packed_tables, packed_units
     from qwen3_tts_b200.config import TALKER
     from qwen3_tts_b200.talker import PackedPrefill, SlotArena, TalkerPrefill, rope_tables
     from qwen3_tts_b200.weights import decoder_weights, pack_decoder
@@ -911,7 +911,7 @@ def run_prefill(args) -> list:
         packed = PackedPrefill(cfg, weights, arena, rows, 16, cos, sin)
         packed.capture()
         px = torch.cat([x, x[-1:].expand(rows - total, -1)])
-        tables = [t.to(dev) for t in packed_tables(lengths, 0, rows, 16)]
+        tables = [t.to(dev) for t in packed_tables(lengths, 0, rows, 16)] + [packed_units(lengths, 0, rows, 16).to(dev)]
         graphs["packed"] = (packed, lambda i: packed.run(px, *tables), rows)
         for form, (graph, call, graph_rows) in graphs.items():
             for i in range(args.warmup):

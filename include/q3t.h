@@ -262,6 +262,24 @@ int q3t_qk_norm_rope_kv(const void* qkv, int64_t qkv_stride, const void* q_norm_
                         int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t capacity,
                         unsigned* status, void* stream);
 
+/* Causal prefill attention over packed prompts: the prefill call of
+ * npu_fused_infer_attention_score (qwen3_tts_engine/npu_attention.py:21, query length L with
+ * the causal mask PrefillGraph builds, prefill_graph.py:31-50), on tcgen05 tensor cores.
+ * query [rows, q_heads, head_dim] bf16 (post q-norm and RoPE); keys/values the arena layer
+ * [arena_slots, kv_heads, capacity, head_dim] bf16 holding every row's K/V already;
+ * positions[r] the position of packed row r. units: int32 [unit_count][4] =
+ * {first_row, count, keys, slot}: rows first_row .. first_row + count - 1 (count <= 64)
+ * are positions of arena slot `slot`, each attending keys 0 .. positions[r] of that slot
+ * (keys = 1 + the largest such position); count 0 = an unused entry. out [rows, q_heads,
+ * head_dim] bf16; rows that no unit covers are not written. head_dim 128 with 2 query heads
+ * per KV head. A unit whose fields do not fit raises the status word's bad-index bit and is
+ * skipped. No workspace. */
+int q3t_prefill_attention(const void* query, const void* keys, const void* values,
+                          const int64_t* positions, const int32_t* units, int64_t unit_count, void* out,
+                          int64_t rows, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                          int64_t arena_slots, int64_t capacity, float scale, unsigned* status,
+                          void* stream);
+
 /* Replaces torch_npu.npu_fused_infer_attention_score at qwen3_tts_engine/npu_attention.py:21
  * (and SDPA over SlotCache, continuous.py:188-198; the predictor's causal
  * 2-token first step, continuous.py:37-40; the codec's sliding window,

@@ -73,6 +73,21 @@ int make_map_bf16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols
   return Q3T_OK;
 }
 
+int make_map_bf16_3d(CUtensorMap* map, const void* base, int64_t d0, int64_t d1, int64_t d2, int box0, int box1,
+                     int box2) {
+  EncodeTiled enc = tiled_encoder();
+  if (enc == nullptr) return fail(Q3T_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {cuuint64_t(d0), cuuint64_t(d1), cuuint64_t(d2)};
+  cuuint64_t strides[2] = {cuuint64_t(d0) * 2, cuuint64_t(d0) * cuuint64_t(d1) * 2};
+  cuuint32_t box[3] = {cuuint32_t(box0), cuuint32_t(box1), cuuint32_t(box2)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(Q3T_EINVAL, "tensor map encode failed (%d)", int(r));
+  return Q3T_OK;
+}
+
 }  // namespace q3t
 
 extern "C" int q3t_abi_version(void) { return 1; }

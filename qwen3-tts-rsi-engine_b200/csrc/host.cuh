@@ -28,6 +28,9 @@ int sm_count();
 // elements, box {box_cols, box_rows}, 128-byte swizzle (box_cols * 2 <= 128).
 int make_map_bf16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t stride_elems,
                   int box_cols, int box_rows);
+// 3-D bf16 tensor map over a dense [d2][d1][d0] array: box {box0, box1, box2}, 128-byte swizzle.
+int make_map_bf16_3d(CUtensorMap* map, const void* base, int64_t d0, int64_t d1, int64_t d2, int box0, int box1,
+                     int box2);
 
 // A per-device one-time set-up (a kernel attribute, a cached query): `run(init)`
 // calls init() for the current device until it first succeeds, under a mutex, so

@@ -73,6 +73,8 @@ SIGNATURES: dict[str, tuple[object, list]] = {
                                     _i64, _f32, _p, _sz, _p, _p]),
     "q3t_decode_attention_noalloc": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                             _i64, _f32, _p, _p]),
+    "q3t_prefill_attention": (_i32, [_p, _p, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p,
+                                     _p]),
     "q3t_cdf_select": (_i32, [_p, _p, _p, _i64, _i64, _p]),
     "q3t_sample": (_i32, [_p, _i32, _i64, _p, _i64, _p, _p, _i64, _i64, _f32, _f32, _i64, _f32, _p, _i64, _u64,
                           _p, _i64, _p, _i64, _p, _i64, _i64, _i64, _p]),

@@ -78,3 +78,39 @@ def packed_tables(lengths, first_slot: int, rows: int, requests: int):
     row_pos = torch.cat([row_pos, row_pos[-1:].expand(pad)])
     last = torch.cat([last, last[-1:].expand(requests - n)])
     return row_slots, row_pos, last
+
+
+PREFILL_UNIT_ROWS = 64
+
+
+def packed_unit_capacity(rows: int, requests: int) -> int:
+    """Entries of the unit table of a packed prefill of `rows` rows and up to `requests`
+    prompts: every prompt adds at most one partial 64-row unit, the padding rows one more."""
+    return (rows + PREFILL_UNIT_ROWS - 1) // PREFILL_UNIT_ROWS + requests + 1
+
+
+def packed_units(lengths, first_slot: int, rows: int, requests: int):
+    """Unit table (CPU int32 [packed_unit_capacity(rows, requests), 4]) of the causal prefill
+    attention: {first_row, count, keys, slot} per block of up to 64 consecutive rows of one
+    prompt, keys = 1 + the block's last position; the padding rows past the prompts (copies
+    of the last prompt's last row, packed_tables) form units of their own over that row's
+    keys, so they compute exactly what it does. Units are ordered by decreasing key count
+    (the longest causal spans start first); unused entries are zero."""
+    import torch
+    units, row = [], 0
+    for i, length in enumerate(lengths):
+        for start in range(0, length, PREFILL_UNIT_ROWS):
+            count = min(PREFILL_UNIT_ROWS, length - start)
+            units.append((row + start, count, start + count, first_slot + i))
+        row += length
+    total = row
+    for start in range(total, rows, PREFILL_UNIT_ROWS):
+        units.append((start, min(PREFILL_UNIT_ROWS, rows - start), lengths[-1], first_slot + len(lengths) - 1))
+    capacity = packed_unit_capacity(rows, requests)
+    if len(units) > capacity:
+        raise ValueError("Packed prompts exceed the prefill's unit table")
+    units.sort(key=lambda u: -u[2])
+    table = torch.zeros(capacity, 4, dtype=torch.int32)
+    if units:
+        table[:len(units)] = torch.tensor(units, dtype=torch.int32)
+    return table

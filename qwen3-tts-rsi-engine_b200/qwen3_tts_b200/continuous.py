@@ -37,7 +37,7 @@ import torch
 
 from . import _lib, checkpoint, ops
 from .batching import (MAX_PACKED_ROWS, context_bucket, decode_batch_size, emission_target, packed_groups,
-                       packed_rows, packed_tables)
+                       packed_rows, packed_tables, packed_units)
 from .code_buffer import CodecCodeBuffer
 from .codec import CodecGraph, CodecSlots, pack_codec
 from .codec_weights import random_codec
@@ -441,9 +441,12 @@ class ContinuousModel:
         packed[:total] = embeds
         packed[total:] = embeds[-1]
         row_slots, row_pos, last = packed_tables(lengths, count, rows, self.max_slots)
-        host = torch.cat([row_slots, row_pos, last]).pin_memory()
+        units = packed_units(lengths, count, rows, self.max_slots)
+        host = torch.cat([row_slots, row_pos, last, units.view(torch.int64).view(-1)]).pin_memory()
         table = host.to(self.device, non_blocking=True)
-        return graph.run(packed, table[:rows], table[rows:2 * rows], table[2 * rows:])
+        end = 2 * rows + self.max_slots
+        return graph.run(packed, table[:rows], table[rows:2 * rows], table[2 * rows:end],
+                         table[end:].view(torch.int32).view(-1, 4))
 
     def _admit_group(self, submissions, prompts=None) -> None:
         if prompts is None:

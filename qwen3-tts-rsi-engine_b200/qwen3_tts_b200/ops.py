@@ -442,6 +442,26 @@ def decode_attention(query, keys, values, positions, *, context=None, scale=None
     return out
 
 
+def prefill_attention(query, keys, values, positions, units, *, out, scale=None):
+    """Causal attention of packed prompt rows over their own slot's keys (q3t_prefill_attention):
+    `units` int32 [n, 4] = {first_row, count, keys, slot} from batching.packed_units; rows no
+    unit covers are left as they are in `out`."""
+    _need_cuda(query, keys, values, positions, units, out)
+    rows, q_heads, head_dim = query.shape
+    n_slots, kv_heads, capacity, width = keys.shape
+    if (width != head_dim or values.shape != keys.shape or not keys.is_contiguous() or not values.is_contiguous()
+            or not query.is_contiguous() or not out.is_contiguous() or out.shape != query.shape
+            or query.dtype != BF16 or keys.dtype != BF16 or values.dtype != BF16 or out.dtype != BF16
+            or positions.dtype != torch.int64 or units.dtype != torch.int32 or units.ndim != 2
+            or units.shape[1] != 4 or not units.is_contiguous()):
+        raise ValueError("Expected BF16 query/out [rows,Hq,D], a contiguous BF16 KV arena and int32 units [n, 4]")
+    scale = head_dim ** -0.5 if scale is None else scale
+    call("q3t_prefill_attention", query.data_ptr(), keys.data_ptr(), values.data_ptr(), positions.data_ptr(),
+         units.data_ptr(), units.shape[0], out.data_ptr(), rows, q_heads, kv_heads, head_dim, n_slots, capacity,
+         float(scale), status_word(query.device).data_ptr(), _stream())
+    return out
+
+
 def attention_plan(positions, workspace, *, q_heads, kv_heads, head_dim, context):
     """Per-step split-KV chunk plan (q3t_attention_plan) for the decode attention calls that use
     `workspace`: one wave of resident CTAs over this batch's contexts."""
@@ -660,6 +680,7 @@ def codec_positions(frames_by_slot, slots, batch: int, frames: int, ring: int, r
          cache.data_ptr(), int(advance), _stream())
 
 
+STATUS_BAD_INDEX = 1 << 3
 STATUS_NONFINITE = 1 << 4
 
 

@@ -18,6 +18,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib, ops
+from .batching import packed_unit_capacity
 from .config import DecoderConfig
 from .weights import pack_decoder
 
@@ -360,9 +361,11 @@ class PackedPrefill:
 
     Row r of the `rows` packed rows belongs to arena slot ``row_slots[r]`` at position
     ``row_pos[r]`` (0 .. its prompt length - 1): it writes its K/V there and attends keys
-    0..row_pos[r] of that slot, so every prompt sees only itself. Rows past the real ones
-    repeat the last real row (same slot, position and input: identical K/V writes). Returns
-    the final-norm hidden state and fp32 logits of each prompt's last token (``last`` holds
+    0..row_pos[r] of that slot, so every prompt sees only itself. The attention runs as
+    causal 64-row query tiles on the tensor cores (ops.prefill_attention over the unit table
+    of batching.packed_units). Rows past the real ones repeat the last real row (same slot,
+    position and input, and units of their own: identical K/V writes). Returns the
+    final-norm hidden state and fp32 logits of each prompt's last token (``last`` holds
     their row indices; up to `requests` prompts)."""
 
     def __init__(self, cfg: DecoderConfig, weights: dict, arena: SlotArena, rows: int, requests: int, cos, sin,
@@ -371,7 +374,6 @@ class PackedPrefill:
             raise ValueError("Packed prefill longer than the KV arena")
         self.cfg, self.w, self.arena = cfg, weights, arena
         self.rows, self.requests = rows, requests
-        self.context = min(arena.capacity, rows)
         self.cos, self.sin, self.norm_mode = cos, sin, norm_mode
         dev = arena.device
         R, H = rows, cfg.hidden
@@ -379,6 +381,7 @@ class PackedPrefill:
         self.row_slots = torch.zeros(R, dtype=torch.long, device=dev)
         self.row_pos = torch.zeros(R, dtype=torch.long, device=dev)
         self.last = torch.zeros(requests, dtype=torch.long, device=dev)
+        self.units = torch.zeros(packed_unit_capacity(rows, requests), 4, dtype=torch.int32, device=dev)
         self.h = torch.zeros(R, H, dtype=BF16, device=dev)
         self.xn = torch.zeros(R, H, dtype=BF16, device=dev)
         self.qkv = torch.zeros(R, cfg.qkv_width, dtype=BF16, device=dev)
@@ -388,8 +391,6 @@ class PackedPrefill:
         self.gathered = torch.zeros(requests, H, dtype=BF16, device=dev)
         self.hidden = torch.zeros(requests, H, dtype=BF16, device=dev)
         self.logits = torch.zeros(requests, cfg.vocab, dtype=torch.float32, device=dev)
-        need = ops.decode_attention_workspace_bytes(R, cfg.q_heads, cfg.head_dim, self.context)
-        self.ws_attn = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
         self.status = ops.status_word(dev)
         # From a thousand rows on, the projections run the wide-tile kernel, which takes no folded
         # RMSNorm: the norm runs as its own pass with a unit weight (the norm weight stays
@@ -412,16 +413,14 @@ class PackedPrefill:
     def compute(self) -> None:
         cfg, w, R = self.cfg, self.w, self.rows
         res_in = self.inputs
-        ops.attention_plan(self.row_pos, self.ws_attn, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads,
-                           head_dim=cfg.head_dim, context=self.context)
         for i, layer in enumerate(w["layers"]):
             self._norm_linear(res_in, layer, layer.qkv, self.qkv)
             ops.qk_norm_rope_kv(self.qkv, layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin, self.row_pos,
                                 self.row_pos, self.arena.keys[i], self.arena.values[i], q_heads=cfg.q_heads,
                                 kv_heads=cfg.kv_heads, head_dim=cfg.head_dim, length=1, query_out=self.q,
                                 slots=self.row_slots)
-            ops.decode_attention(self.q, self.arena.keys[i], self.arena.values[i], self.row_pos, context=self.context,
-                                 rows_per_slot=1, slots=self.row_slots, out=self.attn, workspace=self.ws_attn)
+            ops.prefill_attention(self.q, self.arena.keys[i], self.arena.values[i], self.row_pos, self.units,
+                                  out=self.attn)
             ops.linear(self.attn.view(R, cfg.q_width), layer.o, out=self.h, epilogue=_lib.EPI_RESIDUAL,
                        residual=res_in)
             self._norm_linear(self.h, layer, layer.gate_up, self.act, epilogue=_lib.EPI_SWIGLU_PAIRED)
@@ -439,6 +438,10 @@ class PackedPrefill:
         self.row_slots.zero_()
         self.row_pos.zero_()
         self.last.zero_()
+        self.units.zero_()
+        starts = torch.arange(0, self.rows, 64, dtype=torch.int32)
+        self.units[:len(starts)] = torch.stack([starts, (self.rows - starts).clamp(max=64), torch.ones_like(starts),
+                                                torch.zeros_like(starts)], 1).to(self.units.device)
         stream = torch.cuda.Stream(device=self.inputs.device)
         stream.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(stream):
@@ -453,13 +456,15 @@ class PackedPrefill:
         self.arena.packed[:, :1, :, :1].copy_(saved)
 
     @torch.inference_mode()
-    def run(self, packed, row_slots, row_pos, last):
+    def run(self, packed, row_slots, row_pos, last, units):
         """packed [rows, H] (padding rows repeat the last real row), row_slots / row_pos [rows],
-        last [requests] -> (hidden, logits) of the `requests` prompts."""
+        last [requests], units (batching.packed_units) -> (hidden, logits) of the `requests`
+        prompts."""
         self.inputs.copy_(packed)
         self.row_slots.copy_(row_slots)
         self.row_pos.copy_(row_pos)
         self.last.copy_(last)
+        self.units.copy_(units)
         if self.graph is None:
             self.compute()
         else:

@@ -320,6 +320,62 @@ def test_linear_paired_swiglu(ops, cuda, rows):
     torch.testing.assert_close(out.cpu().float(), ref.float(), atol=1e-2, rtol=2e-2)
 
 
+def _prefill_reference(q, k, v, positions, units, scale):
+    """fp32 causal attention of every row a unit covers over keys 0..positions[r] of its slot."""
+    out = {}
+    qf, kf, vf = q.float(), k.float(), v.float()
+    group = q.shape[1] // k.shape[1]
+    for first, count, keys, slot in units.tolist():
+        for r in range(first, first + count):
+            p = int(positions[r])
+            kk = kf[slot, :, :p + 1].repeat_interleave(group, 0)      # [Hq, p+1, D]
+            vv = vf[slot, :, :p + 1].repeat_interleave(group, 0)
+            w = torch.softmax((kk @ qf[r].unsqueeze(-1)).squeeze(-1) * scale, -1)
+            out[r] = (w.unsqueeze(-1) * vv).sum(1)
+    return out
+
+
+@pytest.mark.parametrize("lengths", [[1], [5, 64, 65, 200], [129, 3, 300, 17]])
+def test_prefill_attention_matches_fp32_causal_reference(ops, cuda, lengths):
+    """The tcgen05 causal prefill attention (64-row query tiles x 64-key blocks, S and PV in
+    TMEM, online softmax, MN-major V operand) over a packed unit table: ragged prompts in
+    scattered slots, a single-token prompt, spans across 1..5 key blocks, and padding rows that
+    repeat the last row."""
+    from qwen3_tts_b200.batching import packed_rows, packed_tables, packed_units
+    slots, kvh, cap, D = 6, 8, 320, 128
+    total = sum(lengths)
+    rows = packed_rows(total)
+    k = rnd(300, (slots, kvh, cap, D), 1.0, BF16)
+    v = rnd(301, (slots, kvh, cap, D), 1.0, BF16)
+    q = rnd(302, (rows, 2 * kvh, D), 1.0, BF16)
+    first_slot = 1
+    _, positions, _ = packed_tables(lengths, first_slot, rows, 8)
+    units = packed_units(lengths, first_slot, rows, 8)
+    out = torch.full((rows, 2 * kvh, D), float("nan"), dtype=BF16, device=cuda)
+    ops.prefill_attention(q.to(cuda), k.to(cuda), v.to(cuda), positions.to(cuda), units.to(cuda), out=out)
+    got = out.cpu().float()
+    ref = _prefill_reference(q, k, v, positions, units, D ** -0.5)
+    assert sorted(ref) == list(range(rows))           # every packed row, padding included
+    want = torch.stack([ref[r] for r in range(rows)])
+    torch.testing.assert_close(got, want, atol=2e-2, rtol=2e-2)
+    assert_status_clean(ops, cuda)
+
+
+def test_prefill_attention_skips_units_out_of_range(ops, cuda):
+    """A unit whose slot lies outside the arena is skipped with the bad-index status bit; the
+    valid units of the same call still run."""
+    k = rnd(310, (2, 8, 64, 128), 1.0, BF16).to(cuda)
+    q = rnd(311, (64, 16, 128), 1.0, BF16).to(cuda)
+    positions = torch.arange(64, dtype=torch.long, device=cuda) % 32
+    units = torch.tensor([[0, 32, 32, 0], [32, 32, 32, 7], [0, 0, 0, 0]], dtype=torch.int32, device=cuda)
+    out = torch.zeros(64, 16, 128, dtype=BF16, device=cuda)
+    ops.read_status(cuda, clear=True)
+    ops.prefill_attention(q, k, k, positions, units, out=out)
+    status = ops.read_status(cuda, clear=True)
+    assert status & ops.STATUS_BAD_INDEX
+    assert out[:32].abs().sum() > 0 and not out[32:].any()
+
+
 def _kernels_launched(fn):
     """Names of the CUDA kernels `fn` launches (torch profiler, CUPTI)."""
     from torch.profiler import ProfilerActivity, profile

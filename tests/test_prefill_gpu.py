@@ -32,7 +32,7 @@ def _prompts(cfg, lengths, seed):
 
 
 def _run_packed(cuda, cfg, packed_w, arena, cos, sin, prompts, first_slot, requests, use_graph):
-    from qwen3_tts_b200.batching import packed_rows, packed_tables
+    from qwen3_tts_b200.batching import packed_rows, packed_tables, packed_units
     from qwen3_tts_b200.talker import PackedPrefill
     lengths = [p.shape[0] for p in prompts]
     rows = packed_rows(sum(lengths))
@@ -42,7 +42,8 @@ def _run_packed(cuda, cfg, packed_w, arena, cos, sin, prompts, first_slot, reque
     x = torch.cat(prompts)
     x = torch.cat([x, x[-1:].expand(rows - x.shape[0], -1)])
     row_slots, row_pos, last = packed_tables(lengths, first_slot, rows, requests)
-    hidden, logits = graph.run(x.to(cuda), row_slots.to(cuda), row_pos.to(cuda), last.to(cuda))
+    units = packed_units(lengths, first_slot, rows, requests)
+    hidden, logits = graph.run(x.to(cuda), row_slots.to(cuda), row_pos.to(cuda), last.to(cuda), units.to(cuda))
     torch.cuda.synchronize()
     graph.close()
     return hidden[:len(prompts)].float().cpu(), logits[:len(prompts)].cpu()

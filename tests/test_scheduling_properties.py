@@ -7,7 +7,8 @@ from hypothesis import strategies as st
 
 from oracle import scheduling as OS
 from qwen3_tts_b200.batching import (MAX_PACKED_ROWS, context_bucket, decode_batch_size, emission_target,
-                                    packed_groups, packed_rows, packed_tables)
+                                    packed_groups, packed_rows, packed_tables, packed_unit_capacity,
+                                    packed_units)
 
 POW2 = st.sampled_from([1, 2, 4, 8, 16, 32, 64, 128])
 
@@ -82,3 +83,27 @@ def test_packed_prefill_groups_and_tables_cover_every_prompt_once(lengths, max_r
             offset += n
         assert (slots[total:] == slots[total - 1]).all() and (pos[total:] == pos[total - 1]).all()
         assert (last[end - start:] == total - 1).all()
+
+
+@settings(max_examples=300, deadline=None)
+@given(lengths=st.lists(st.integers(1, 600), min_size=1, max_size=64))
+def test_packed_prefill_units_cover_every_row_once(lengths):
+    """Unit table of the causal prefill attention: every packed row (padding included) in
+    exactly one unit of at most 64 consecutive rows of one slot, keys = 1 + the unit's last
+    position, longest spans first, within the fixed table size."""
+    rows = packed_rows(sum(lengths))
+    first_slot = 2
+    slots, pos, _ = packed_tables(lengths, first_slot, rows, 64)
+    units = packed_units(lengths, first_slot, rows, 64)
+    assert units.shape == (packed_unit_capacity(rows, 64), 4)
+    used = units[units[:, 1] > 0]
+    assert (units[len(used):] == 0).all()
+    covered = []
+    for first, count, keys, slot in used.tolist():
+        assert 1 <= count <= 64
+        span = range(first, first + count)
+        assert all(int(slots[r]) == slot for r in span)
+        assert keys == max(int(pos[r]) for r in span) + 1
+        covered.extend(span)
+    assert sorted(covered) == list(range(rows))
+    assert used[:, 2].tolist() == sorted(used[:, 2].tolist(), reverse=True)
