@@ -206,6 +206,11 @@ class ContinuousModel:
     decoder module tree (``codec_decoder``); a checkpoint without a codec
     directory gets the seeded codec. Reference flags that select between NPU
     kernel variants are accepted and ignored (there is one CUDA path).
+
+    Admission packs the prompts end to end (``packed_prefill``, groups of at most
+    ``max_prefill_rows`` rows: wide-tile projection GEMMs and the causal tcgen05
+    prefill attention); ``packed_prefill=False`` keeps the reference's padded
+    power-of-two prefill graphs in groups of ``max_prefill_batch``.
     """
 
     def __init__(self, model_path=None, device="cuda:0", max_slots=64, initial_capacity=512, *, seed: int = 0,
@@ -216,7 +221,7 @@ class ContinuousModel:
                  prewarm_prefill=False, bucket_prefill=True, max_frames=4096, max_prefill_batch=16, use_graphs=True,
                  temperature=0.9, top_k=50, top_p=1.0, subtalker_temperature=0.9, subtalker_top_k=50,
                  subtalker_top_p=1.0, penalty=1.05, pipeline_audio=False, packed_prefill=True,
-                 max_prefill_rows=4096, **flags):
+                 max_prefill_rows=MAX_PACKED_ROWS, **flags):
         if codec_chunk_frames not in (8, 16) or (codec_chunk_frames != 8 and not incremental_codec):
             raise ValueError("16-frame chunks require the incremental codec")
         if codec_streams not in (1, 2) or (codec_streams == 2 and not incremental_codec):
@@ -396,6 +401,18 @@ class ContinuousModel:
             raise ValueError(f"max_new_tokens must be within 1..{self.max_frames}")
         return prompt
 
+    def prepare_prompts(self, payloads) -> tuple:
+        """prepare_prompt for several payloads with one text projection (CustomVoicePrompt
+        .build_many): the prompts' rows packed end to end and the per-request prompt dicts."""
+        packed, prompts = self.prompt_builder.build_many(payloads)
+        for prompt in prompts:
+            for key, value in SUPPORTED_SAMPLING.items():
+                if prompt.get(key) != value:
+                    raise ValueError(f"Unsupported native sampling setting: {key}={prompt.get(key)}")
+            if not 1 <= prompt["max_new_tokens"] <= self.max_frames:
+                raise ValueError(f"max_new_tokens must be within 1..{self.max_frames}")
+        return packed, prompts
+
     @torch.inference_mode()
     def admit_batch(self, submissions) -> None:
         """Batched prefill into slots len(states).. (continuous.py:424-473): prompts packed end to
@@ -408,10 +425,11 @@ class ContinuousModel:
             for offset in range(0, len(submissions), self.max_prefill_batch):
                 self._admit_group(submissions[offset:offset + self.max_prefill_batch])
             return
-        prompts = [self.prepare_prompt(payload) for _, payload in submissions]
+        packed, prompts = self.prepare_prompts([payload for _, payload in submissions])
         lengths = [p["inputs_embeds"].shape[1] for p in prompts]
+        offsets = np.cumsum([0] + lengths).tolist()
         for start, end in packed_groups(lengths, self.max_prefill_rows):
-            self._admit_group(submissions[start:end], prompts[start:end])
+            self._admit_group(submissions[start:end], prompts[start:end], packed[offsets[start]:offsets[end]])
 
     def _prefill_padded(self, prompts, lengths, count):
         n = len(prompts)
@@ -431,12 +449,13 @@ class ContinuousModel:
         slots, lens = table[:batch], table[batch:]
         return self._prefill(batch, padded).run(embeds, lens, slots)
 
-    def _prefill_packed(self, prompts, lengths, count):
+    def _prefill_packed(self, prompts, lengths, count, embeds=None):
         n, total = len(prompts), sum(lengths)
         rows = packed_rows(total)
         self.ensure_capacity(max(lengths) - 1)
         graph = self._packed_prefill(rows)
-        embeds = torch.cat([p["inputs_embeds"][0] for p in prompts])
+        if embeds is None:
+            embeds = torch.cat([p["inputs_embeds"][0] for p in prompts])
         packed = torch.empty(rows, self.talker_config.hidden, dtype=BF16, device=self.device)
         packed[:total] = embeds
         packed[total:] = embeds[-1]
@@ -448,22 +467,27 @@ class ContinuousModel:
         return graph.run(packed, table[:rows], table[rows:2 * rows], table[2 * rows:end],
                          table[end:].view(torch.int32).view(-1, 4))
 
-    def _admit_group(self, submissions, prompts=None) -> None:
+    def _admit_group(self, submissions, prompts=None, embeds=None) -> None:
         if prompts is None:
             prompts = [self.prepare_prompt(payload) for _, payload in submissions]
         lengths = [p["inputs_embeds"].shape[1] for p in prompts]
         count, n = len(self.states), len(submissions)
         S = self.state
         if self.packed_prefill:
-            hidden, logits = self._prefill_packed(prompts, lengths, count)
+            hidden, logits = self._prefill_packed(prompts, lengths, count, embeds)
         else:
             hidden, logits = self._prefill_padded(prompts, lengths, count)
         # per-slot state of the new requests
-        tables = torch.full((n, S.table_rows, 16), 0.5, dtype=torch.float32)
+        # uniform tables: only the rows the requests can reach cross the bus; the rest of each
+        # slot's table is reset on the device
+        used = max(p["max_new_tokens"] for p in prompts) + 1
+        tables = torch.full((n, used, 16), 0.5, dtype=torch.float32)
         for row, ((_, payload), prompt) in enumerate(zip(submissions, prompts)):
             table = random_table(int(payload.get("seed", 0)), prompt["max_new_tokens"])
             tables[row, :table.shape[0]] = table
-        S.tables[count:count + n].copy_(tables.pin_memory(), non_blocking=True)
+        S.tables[count:count + n, :used].copy_(tables.pin_memory(), non_blocking=True)
+        if used < S.table_rows:
+            S.tables[count:count + n, used:].fill_(0.5)
         ints = torch.tensor([lengths, lengths, [0] * n, [1] * n], dtype=torch.long).pin_memory()
         ints = ints.to(self.device, non_blocking=True)
         S.positions[count:count + n].copy_(ints[0])
@@ -471,9 +495,8 @@ class ContinuousModel:
         S.frames[count:count + n].copy_(ints[2])
         S.trailing_len[count:count + n].copy_(ints[3])
         S.hidden[count:count + n].copy_(hidden[:n])
-        for row, prompt in enumerate(prompts):
-            S.trailing[count + row, 0].copy_(prompt["trailing_text_hidden"][0, 0])
-            S.pad[count + row].copy_(prompt["tts_pad_embed"][0, 0])
+        S.trailing[count:count + n, 0].copy_(torch.cat([p["trailing_text_hidden"][0, :1] for p in prompts]))
+        S.pad[count:count + n].copy_(torch.cat([p["tts_pad_embed"][0, :1] for p in prompts]))
         # first semantic token: table[0, 0], no seen tokens, EOS blocked (continuous.py:409-422)
         ops.sample(logits[:n], uniforms=S.tables[count:count + n, 0, 0], seen=None, allowed=self.allowed,
                    steps=self._zeros[:n], eos=self.eos, min_steps=2, penalty=self.penalty,

@@ -103,6 +103,12 @@ class CustomVoicePrompt:
         h = ops.linear(x, self.fc1, self.fc1_bias, epilogue=_lib.EPI_SILU)
         return ops.linear(h, self.fc2, self.fc2_bias)
 
+    def _ones(self, length: int) -> torch.Tensor:
+        """[1, length] int64 ones (a view of one cached device row)."""
+        if getattr(self, "_mask", None) is None or self._mask.shape[1] < length:
+            self._mask = torch.ones(1, max(length, 4096), dtype=torch.long, device=self.device)
+        return self._mask[:, :length]
+
     def codec(self, ids: list) -> torch.Tensor:
         index = torch.tensor(ids, dtype=torch.long).to(self.device, non_blocking=True)
         return ops.embedding(index, self.codec_embedding)
@@ -142,3 +148,48 @@ class CustomVoicePrompt:
                       attention_mask=torch.ones(inputs.shape[:2], dtype=torch.long, device=self.device),
                       trailing_text_hidden=pad.clone().unsqueeze(0), tts_pad_embed=pad.clone().unsqueeze(0))
         return result
+
+    @torch.inference_mode()
+    def build_many(self, payloads) -> tuple:
+        """build() for several requests with ONE text projection (one gather, two GEMMs) over
+        every request's ids and one concatenation: returns the prompts' rows packed end to end
+        [sum of lengths, hidden] bf16 and, per request, build()'s dict whose ``inputs_embeds``
+        is a view of its rows. The codec pad row added to the text rows is the same embedding
+        for every request (the last two codec tags are always codec_pad, codec_bos)."""
+        cfg = self.cfg
+        if self.special is None:
+            self.special = self.project([cfg.tts_bos, cfg.tts_eos, cfg.tts_pad]).split(1, 0)
+        _bos, eos, pad = self.special
+        plans, ids_all = [], []
+        for payload in payloads:
+            prefix, codec_pad, final_bos = self._prefix(payload["voice"], payload["language"])
+            ids = assistant_ids(cfg, text_ids(cfg, payload))
+            instruction = payload.get("instructions") or payload.get("instruction_ids")
+            inst = instruct_ids(cfg, text_ids(cfg, payload, "instructions", "instruction_ids")) if instruction else []
+            plans.append((len(ids_all), len(inst), len(ids), prefix, codec_pad, final_bos))
+            ids_all.extend(inst)
+            ids_all.extend(ids)
+        projected = self.project(ids_all)
+        codec_pad = plans[0][4]
+        shifted = projected + codec_pad                    # text rows + codec pad, bf16 adds
+        eos_pad = eos + codec_pad
+        parts, lengths = [], []
+        for start, n_inst, n_ids, prefix, _pad, final_bos in plans:
+            t0 = start + n_inst
+            rows = [projected[start:t0]] if n_inst else []
+            rows += [projected[t0:t0 + 3], prefix, shifted[t0 + 3:t0 + n_ids - 5], eos_pad, final_bos]
+            parts.extend(rows)
+            lengths.append(sum(r.shape[0] for r in rows))
+        packed = torch.cat(parts, 0)
+        prompts, offset = [], 0
+        trailing = pad.unsqueeze(0)
+        for payload, length in zip(payloads, lengths):
+            result = dict(SUPPORTED_SAMPLING)
+            result.update(max_new_tokens=int(payload["max_new_tokens"]),
+                          inputs_embeds=packed[offset:offset + length].unsqueeze(0),
+                          attention_mask=self._ones(length), trailing_text_hidden=trailing,
+                          tts_pad_embed=trailing)
+            prompts.append(result)
+            offset += length
+        return packed, prompts
+

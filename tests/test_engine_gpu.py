@@ -157,6 +157,22 @@ def test_engine_prompt_matches_oracle(cuda):
         builder.build(dict(PAYLOADS["a"], voice="nobody"))
     with pytest.raises(ValueError):
         builder.build(dict(PAYLOADS["a"], language="klingon"))
+    # the batched builder (one projection for every request): same rows, packed end to end
+    payloads = [dict(p, **extra) for p in PAYLOADS.values() for extra in ({}, {"instruction_ids": [11, 12, 13, 14]})]
+    packed, prompts = builder.build_many(payloads)
+    offset = 0
+    for payload, prompt in zip(payloads, prompts):
+        single = builder.build(payload)["inputs_embeds"][0]
+        inputs = prompt["inputs_embeds"][0]
+        assert inputs.shape == single.shape and prompt["max_new_tokens"] == payload["max_new_tokens"]
+        assert inputs.data_ptr() == packed[offset].data_ptr()
+        offset += inputs.shape[0]
+        ids = P.text_ids(prcfg, payload)
+        tags = P.codec_tags(prcfg, payload["voice"], payload["language"])
+        ref = OP.build(prcfg, prw, tw["embedding"].float(), ids, tags, instruction_ids=payload.get("instruction_ids"))
+        torch.testing.assert_close(inputs.float().cpu(), ref["inputs_embeds"], atol=2e-2, rtol=2e-2)
+        torch.testing.assert_close(inputs.float(), single.float(), atol=1e-2, rtol=1e-2)
+    assert offset == packed.shape[0]
 
 
 def test_engine_from_checkpoint_matches_engine_from_weights(cuda, tmp_path):
