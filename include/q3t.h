@@ -331,6 +331,23 @@ int q3t_decode_attention_qkv(const void* qkv, int64_t qkv_stride, const void* q_
                              int64_t capacity, int64_t context, float scale, void* workspace,
                              size_t workspace_bytes, unsigned* status, void* stream);
 
+/* q3t_decode_attention_qkv with an L2 prefetch hint (the same replacement of
+ * PackedAttention.forward's norm / RoPE / cache update / attention,
+ * packed_attention.py:42-74): while the keys stream, the kernel's CTAs pull up
+ * to two byte ranges (prefetchN, prefetchN_bytes; null / 0 = none; 16-byte
+ * aligned, sizes multiples of 16) into L2 - in a decode step the weights of the
+ * projections that follow the attention, so that those latency-bound GEMMs read
+ * them from L2. The hint changes no result. */
+int q3t_decode_attention_qkv_ex(const void* qkv, int64_t qkv_stride, const void* q_norm_weight,
+                                const void* k_norm_weight, float eps, const void* cos_table,
+                                const void* sin_table, int64_t table_len, const int64_t* rotary_positions,
+                                void* keys, void* values, const int64_t* positions, void* out, int64_t rows,
+                                int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t arena_slots,
+                                int64_t capacity, int64_t context, float scale, void* workspace,
+                                size_t workspace_bytes, const void* prefetch0, size_t prefetch0_bytes,
+                                const void* prefetch1, size_t prefetch1_bytes, unsigned* status,
+                                void* stream);
+
 /* No counterpart in the reference: an allocation-free form of
  * q3t_decode_attention for callers that cannot allocate device memory (a
  * runtime with a fixed pre-reserved pool, a foreign-language host without a

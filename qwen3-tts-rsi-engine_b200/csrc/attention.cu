@@ -388,6 +388,25 @@ extern "C" int q3t_decode_attention_qkv(const void* qkv, int64_t qkv_stride, con
                                         int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t arena_slots,
                                         int64_t capacity, int64_t context, float scale, void* workspace,
                                         size_t workspace_bytes, unsigned* status, void* stream) {
+  return q3t_decode_attention_qkv_ex(qkv, qkv_stride, q_norm_weight, k_norm_weight, eps, cos_table, sin_table,
+                                     table_len, rotary_positions, keys, values, positions, out, rows, q_heads,
+                                     kv_heads, head_dim, arena_slots, capacity, context, scale, workspace,
+                                     workspace_bytes, nullptr, 0, nullptr, 0, status, stream);
+}
+
+extern "C" int q3t_decode_attention_qkv_ex(const void* qkv, int64_t qkv_stride, const void* q_norm_weight,
+                                           const void* k_norm_weight, float eps, const void* cos_table,
+                                           const void* sin_table, int64_t table_len,
+                                           const int64_t* rotary_positions, void* keys, void* values,
+                                           const int64_t* positions, void* out, int64_t rows, int64_t q_heads,
+                                           int64_t kv_heads, int64_t head_dim, int64_t arena_slots,
+                                           int64_t capacity, int64_t context, float scale, void* workspace,
+                                           size_t workspace_bytes, const void* prefetch0, size_t prefetch0_bytes,
+                                           const void* prefetch1, size_t prefetch1_bytes, unsigned* status,
+                                           void* stream) {
+  if ((prefetch0_bytes && (!prefetch0 || !aligned16(prefetch0) || prefetch0_bytes % 16)) ||
+      (prefetch1_bytes && (!prefetch1 || !aligned16(prefetch1) || prefetch1_bytes % 16)))
+    return fail(Q3T_EINVAL, "attention_qkv: prefetch ranges need 16-byte alignment and size");
   if (!qkv || !cos_table || !sin_table || !rotary_positions || !keys || !values || !positions || !out)
     return fail(Q3T_EINVAL, "attention_qkv: null pointer");
   if (rows < 1 || rows > 65535 || kv_heads < 1 || q_heads % kv_heads || arena_slots < rows || table_len < 1)
@@ -428,6 +447,10 @@ extern "C" int q3t_decode_attention_qkv(const void* qkv, int64_t qkv_stride, con
   call.plan = call.counters + kPlanSlot;
   call.status = status;
   call.stream = stream;
+  call.prefetch[0] = prefetch0;
+  call.prefetch_bytes[0] = prefetch0_bytes;
+  call.prefetch[1] = prefetch1;
+  call.prefetch_bytes[1] = prefetch1_bytes;
   return launch_attention_fused(call, qkv, qkv_stride, q_norm_weight, k_norm_weight, eps, cos_table, sin_table,
                                 table_len, rotary_positions);
 }

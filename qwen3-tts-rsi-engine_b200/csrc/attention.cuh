@@ -22,6 +22,11 @@ struct AttentionCall {
   const unsigned* plan;  // keys per chunk planned for this batch (q3t_attention_plan), or null
   unsigned* status;
   void* stream;
+  // L2 prefetch hint (fused kernel): up to two byte ranges (normally the weights of the
+  // projections that follow this attention) pulled into L2 while the keys stream; each CTA
+  // requests its share once. Null / 0 = none.
+  const void* prefetch[2];
+  uint64_t prefetch_bytes[2];
 };
 
 // Tensor-core (mma.sync) kernel for linear arenas: head_dim 64/128, 1 or 2 query heads per kv head.

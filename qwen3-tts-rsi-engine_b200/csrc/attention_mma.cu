@@ -85,6 +85,10 @@ struct FusedQKV {
   const int64_t* rot_pos;       // [rows]
   __nv_bfloat16* keys;          // arena [slots, kv_heads, capacity, D] (row b = slot b)
   __nv_bfloat16* values;
+  // L2 prefetch of up to two ranges (the next projections' weights): the key stream leaves
+  // HBM bandwidth unused, and weights already in L2 shorten the latency-bound GEMMs that follow
+  const uint8_t* pf[2];
+  uint64_t pf_bytes[2];
 };
 
 // Per-head RMSNorm (optional weight) and rotate-half RoPE of D values, one warp,
@@ -140,6 +144,15 @@ __global__ void __launch_bounds__(128, 3)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
   grid_dependency_wait();
+  if constexpr (FUSED) {
+    if (threadIdx.x == 32) {  // this CTA's share of the prefetch ranges, requested once
+      const uint64_t ctas = uint64_t(gridDim.x) * gridDim.y * gridDim.z;
+      const uint64_t id = blockIdx.x + uint64_t(gridDim.x) * (blockIdx.y + uint64_t(gridDim.y) * blockIdx.z);
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+        if (f.pf[r] != nullptr) prefetch_l2_share(f.pf[r], f.pf_bytes[r], id, ctas);
+    }
+  }
 
   int64_t pos = positions[b];
   // Keys per chunk: the step's plan (q3t_attention_plan: one wave of resident CTAs for this
@@ -512,6 +525,10 @@ int launch_attention_fused(const AttentionCall& a, const void* qkv, int64_t qkv_
   f.rot_pos = rot_pos;
   f.keys = static_cast<__nv_bfloat16*>(const_cast<void*>(a.keys));
   f.values = static_cast<__nv_bfloat16*>(const_cast<void*>(a.values));
+  for (int r = 0; r < 2; ++r) {
+    f.pf[r] = a.prefetch_bytes[r] ? static_cast<const uint8_t*>(a.prefetch[r]) : nullptr;
+    f.pf_bytes[r] = a.prefetch_bytes[r];
+  }
   const int64_t g = a.q_heads / a.kv_heads;
   if (a.head_dim == 128 && g == 2) return launch_mma<128, 2, true>(a, f);
   if (a.head_dim == 128 && g == 1) return launch_mma<128, 1, true>(a, f);

@@ -183,6 +183,16 @@ Q3T_DEV void prefetch_l2(const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
                : "memory");
 }
+// Share `id` of `parts` equal shares of a byte range (16-byte units), pulled into L2 in
+// requests of at most 32 KB; no completion, no effect on results.
+Q3T_DEV void prefetch_l2_share(const uint8_t* base, uint64_t bytes, uint64_t id, uint64_t parts) {
+  const uint64_t units = bytes / 16, per = (units + parts - 1) / parts;
+  const uint64_t u0 = id * per, u1 = u0 + per < units ? u0 + per : units;
+  for (uint64_t u = u0; u < u1; u += 2048) {
+    const uint64_t n = u1 - u < 2048 ? u1 - u : 2048;
+    prefetch_l2(base + u * 16, uint32_t(n * 16));
+  }
+}
 // Untiled bulk copy global -> shared with an L2 cache policy (createpolicy); same alignment.
 Q3T_DEV void bulk_load_hint(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {
   asm volatile(

@@ -49,6 +49,13 @@ struct Cfg {
   static constexpr int kRedStride = kTileN + 4;
   static constexpr int kRedBytes = BN * kRedStride * 4;
   static constexpr int kMain = kRing > kRedBytes ? kRing : kRedBytes;
+  // Split-K exchange by bulk copies: a CTA's partials grouped by owner (staging) and the peers'
+  // partials of its own features (inbox), cs slices each of [BN][W] partials + [BN] row sums +
+  // 16 floats of padding, inside the idle ring; larger tiles keep the store-based exchange.
+  static constexpr int kNormRows = (BN + 5) / 6;          // activation rows per norm warp (warps 2-7)
+  static constexpr int kNormGroups = (kNormRows + 3) / 4;  // four rows per warp load
+  static constexpr int kExchangeFloats = 2 * (BN * kTileN + 8 * (BN + 16));
+  static constexpr bool kBulkExchange = kExchangeFloats * 4 <= kRing;
   // main area + barriers (2 per stage + done) + tmem slot + flags, row scales [BN] of the
   // folded RMSNorm, plus 1 KB alignment slack
   static constexpr int kSmem = kMain + 256 + 1024 + 1024;
@@ -220,6 +227,17 @@ Q3T_DEV uint32_t map_peer(uint32_t local_smem, uint32_t rank) {
 Q3T_DEV void st_peer1(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
+// Bulk copy of `bytes` from this CTA's shared memory to a cluster peer's (dst and the peer's
+// mbarrier are shared::cluster addresses from map_peer); completion is counted on that
+// mbarrier (complete_tx). Both addresses 16-byte aligned, bytes a multiple of 16.
+Q3T_DEV void bulk_copy_peer(uint32_t dst, const void* src, uint32_t bytes, uint32_t peer_bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst),
+               "r"(smem_u32(src)), "r"(bytes), "r"(peer_bar)
+               : "memory");
+}
+Q3T_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory"); }
+Q3T_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
 
 // One CTA = 128 weight rows x BN activation rows x one K slice. The CTAs of
 // the K slices of one tile form a thread-block cluster (gridDim.y = splits,
@@ -240,11 +258,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + S;
   uint64_t* done = empty + S;
   uint64_t* epi_bar = done + 1;  // residual tile of the staged epilogue
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_bar + 1);
+  uint64_t* inbox_bar = epi_bar + 1;  // split-K partials of this CTA's features have landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(inbox_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* consumed = abort_flag + 1;  // ring slots the MMA issuer has taken
   float* red = reinterpret_cast<float*>(smem);
-  float* rnorm = reinterpret_cast<float*>(smem + C::kMain + 256);  // [BN] row scales (row_norm)
+  // folded RMSNorm: per activation row its sum of squares over this CTA's K slice, later turned
+  // into the row scale in place
+  float* rnorm = reinterpret_cast<float*>(smem + C::kMain + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kTileN;
@@ -264,11 +285,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      // a slot is free once the MMAs read it and, with row_norm, warps 2 and 3 summed its rows
-      mbar_init(&empty[s], a.row_norm ? 3 : 1);
+      // a slot is free once the MMAs read it and, with row_norm, each of the six norm warps summed it
+      mbar_init(&empty[s], a.row_norm ? 7 : 1);
     }
     mbar_init(done, 1);
     mbar_init(epi_bar, 1);
+    mbar_init(inbox_bar, 1);
     *abort_flag = 0;
     *consumed = 0;
     fence_mbar_init();
@@ -292,12 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // this CTA's share of the next kernel's weights, in 16-byte units, pulled into L2
     const uint64_t ctas = uint64_t(gridDim.x) * gridDim.y * gridDim.z;
     const uint64_t id = blockIdx.x + uint64_t(gridDim.x) * (blockIdx.y + uint64_t(gridDim.y) * blockIdx.z);
-    const uint64_t units = a.prefetch_bytes / 16, per = (units + ctas - 1) / ctas;
-    const uint64_t u0 = id * per, u1 = u0 + per < units ? u0 + per : units;
-    for (uint64_t u = u0; u < u1; u += 2048) {  // 32 KB requests
-      const uint64_t n = u1 - u < 2048 ? u1 - u : 2048;
-      prefetch_l2(a.prefetch + u * 16, uint32_t(n * 16));
-    }
+    prefetch_l2_share(a.prefetch, a.prefetch_bytes, id, ctas);
   }
 
   if (warp == 0) {
@@ -360,14 +377,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   }
 
-  // ---------------- folded RMSNorm: warps 2 and 3 (idle during the main loop) sum the
-  // squares of every activation row from the ring slots as they land, over this CTA's K slice
-  constexpr int RPT = BN > 64 ? BN / 64 : 1;  // activation rows per thread
-  float ss[RPT];
+  // ---------------- folded RMSNorm: warps 2-7 (idle during the main loop) sum the squares of
+  // every activation row from the ring slots as they land, over this CTA's K slice. Warp w owns
+  // rows [(w - 2) R, (w - 1) R) (R = ceil(BN / 6)); in each stage lane l reads 16-byte chunk
+  // l % 8 of row l / 8 of a group of four rows (one conflict-free 512-byte wavefront set), so a
+  // stage costs each warp a few loads and a slot is released (empty barrier: MMA commit + one
+  // arrival per norm warp) right after it lands. The eight chunk lanes of a row are added by a
+  // fixed butterfly at the end, and rnorm[m] holds the row's sum over this K slice.
+  if (a.row_norm && warp >= 2) {
+    const int nw = warp - 2;
+    const int row_lo = nw * C::kNormRows;
+    const int chunk = lane & 7, sub = lane >> 3;
+    float acc[C::kNormGroups];
 #pragma unroll
-  for (int q = 0; q < RPT; ++q) ss[q] = 0.f;
-  if (a.row_norm && (warp == 2 || warp == 3)) {
-    const int t2 = threadIdx.x - 64;
+    for (int j = 0; j < C::kNormGroups; ++j) acc[j] = 0.f;
     for (int i = 0; i < nk; ++i) {
       const int s = i % S;
       if (!mbar_wait(&full[s], (i / S) & 1, a.status, kStatusTmaTimeout)) {
@@ -376,24 +399,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const uint8_t* xb = smem + s * C::kStageBytes + kABytes;
 #pragma unroll
-      for (int q = 0; q < RPT; ++q) {
-        const int m = t2 + 64 * q;
-        if (m < BN) {
-          const uint4* row = reinterpret_cast<const uint4*>(xb + m * 128);  // the 64 k of row m, chunk-permuted
+      for (int j = 0; j < C::kNormGroups; ++j) {
+        const int m = row_lo + 4 * j + sub;
+        if (4 * j + sub < C::kNormRows && m < BN) {
+          const uint4 v = *reinterpret_cast<const uint4*>(xb + m * 128 + chunk * 16);
+          const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const uint4 v = row[c];
-            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float lo = __uint_as_float(w4[e] << 16), hi = __uint_as_float(w4[e] & 0xFFFF0000u);
-              ss[q] += lo * lo + hi * hi;
-            }
+          for (int e = 0; e < 4; ++e) {
+            const float lo = __uint_as_float(w4[e] << 16), hi = __uint_as_float(w4[e] & 0xFFFF0000u);
+            acc[j] += lo * lo + hi * hi;
           }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
+    }
+#pragma unroll
+    for (int j = 0; j < C::kNormGroups; ++j) {
+      float v = acc[j];
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      const int m = row_lo + 4 * j + sub;
+      if (chunk == 0 && 4 * j + sub < C::kNormRows && m < BN) rnorm[m] = v;
     }
   }
   grid_dependency_wait();
@@ -407,12 +435,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (!clustered && EPI != Q3T_EPI_SWIGLU_PAIRED) {
     const int n = n0 + r;
     if (a.row_norm) {
-      if (warp == 2 || warp == 3)
-#pragma unroll
-        for (int q = 0; q < RPT; ++q) {
-          const int m = threadIdx.x - 64 + 64 * q;
-          if (m < BN) rnorm[m] = 1.0f / sqrtf(ss[q] / float(a.in_features) + a.norm_eps);
-        }
+      __syncthreads();  // every row's sum is in rnorm
+      if (threadIdx.x < BN) rnorm[threadIdx.x] = 1.0f / sqrtf(rnorm[threadIdx.x] / float(a.in_features) + a.norm_eps);
       __syncthreads();
     }
     // block-uniform: every thread saw the accumulator complete and no load was abandoned
@@ -478,21 +502,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
   } else if (clustered) {
-    // ---------------- split-K reduction across the cluster, push form. After barrier A no
-    // CTA of the cluster reads its ring any more, so each CTA writes its fp32 partials
-    // straight into the shared memory of the CTA that finalises those features (slot =
-    // source rank); after barrier B every CTA reduces its inbox locally, in rank order
-    // (deterministic), and leaves without a further cluster barrier.
-    if (threadIdx.x == 0 && *abort_flag)  // outstanding ring loads land before the ring is an inbox
+    // ---------------- split-K reduction across the cluster. The CTA that finalises a feature
+    // (its owner) receives every peer's fp32 partials of it and sums them in rank order
+    // (deterministic). Bulk form (tiles of <= 64 rows): each CTA writes its partials, grouped by
+    // owner, into its own idle ring; after one cluster barrier (every CTA past its MMAs, so every
+    // ring is free and every inbox barrier armed) one thread copies each owner's slice into that
+    // owner's inbox with a bulk shared::cluster copy counted on the owner's inbox barrier; the
+    // owner reduces as soon as its inbox is complete. A split arrive/wait cluster barrier keeps
+    // every CTA resident until all copies of the cluster have landed. Store form (larger tiles):
+    // each thread stores its partials into the owner's shared memory, then a second cluster
+    // barrier.
+    if (threadIdx.x == 0 && *abort_flag)  // outstanding ring loads land before the ring is reused
       for (int j = *consumed; j < issued; ++j) mbar_wait(&full[j % S], (j / S) & 1, a.status, kStatusTmaTimeout);
     __syncthreads();
-    cluster_sync();  // A
     const int cs = a.splits;
     const int rank = int(cluster_rank());
     const int W = kTileN / cs;  // features this CTA finalises (cs is a power of two <= 8)
-    const int rs = W + 4;       // inbox row stride in floats; column W holds the partial row sums
-    float* inbox = reinterpret_cast<float*>(smem);  // [cs][BN][rs]
-    const uint32_t inbox_u32 = smem_u32(inbox);
     int owner, fl;
     if constexpr (EPI == Q3T_EPI_SWIGLU_PAIRED) {  // tile rows are [64 gate; 64 up]
       const int hw = W / 2, rr = r < 64 ? r : r - 64;
@@ -502,33 +527,92 @@ __global__ void __launch_bounds__(kThreads, 1)
       owner = r / W;
       fl = r - owner * W;
     }
-    const uint32_t dst = map_peer(inbox_u32, uint32_t(owner)) + uint32_t(rank * BN * rs + fl) * 4u;
-#pragma unroll 1
-    for (int c0 = 16 * half; c0 < BN; c0 += 32) {
-      float v[16];
-      tmem_ld16(taddr + c0, v);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) st_peer1(dst + uint32_t((c0 + j) * rs) * 4u, ok ? v[j] : 0.f);
-    }
-    if (a.row_norm && (warp == 2 || warp == 3))  // this CTA's partial row sums go to every owner
-#pragma unroll
-      for (int q = 0; q < RPT; ++q) {
-        const int m = threadIdx.x - 64 + 64 * q;
-        if (m < BN)
-          for (int o = 0; o < cs; ++o)
-            st_peer1(map_peer(inbox_u32, uint32_t(o)) + uint32_t((rank * BN + m) * rs + W) * 4u, ss[q]);
-      }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
-    cluster_sync();  // B: every partial has landed in its owner's inbox
     const int mcount = (m_end - m0) < BN ? (m_end - m0) : BN;
+    // epilogue inputs (residual, bias, scale) of this thread's output quads, loaded before the
+    // exchange so that their latency overlaps it: at most BN / 16 quads per thread (tiles of up
+    // to 64 rows; 128-row tiles load them in the loop, keeping two CTAs' registers per SM)
+    constexpr int kQuads = BN <= 64 ? BN / 16 : 1;
+    constexpr bool kPreload = BN <= 64;
+    Inputs4 pre[kQuads];
+    if constexpr (EPI != Q3T_EPI_SWIGLU_PAIRED && kPreload) {
+      const int nq = W / 4, units = mcount * nq;
+#pragma unroll
+      for (int i = 0; i < kQuads; ++i) {
+        const int u = threadIdx.x + i * kThreads;
+        if (u < units) pre[i] = load_inputs4<EPI>(a, m0 + u / nq, n0 + rank * W + (u % nq) * 4);
+      }
+    }
+    const float* inbox = reinterpret_cast<const float*>(smem);
+    int slice = 0, rs = W + 4;  // bulk: floats per slice; store form: inbox row stride
+    bool got = true;
+    if constexpr (C::kBulkExchange) {
+      slice = BN * W + BN + 16;  // [BN][W] partials, [BN] partial row sums, padding (bank spread)
+      float* staging = reinterpret_cast<float*>(smem);  // [cs][slice], by owner
+      inbox = staging + cs * slice;                     // [cs][slice], by source rank
+#pragma unroll 1
+      for (int c0 = 16 * half; c0 < BN; c0 += 32) {
+        float v[16];
+        tmem_ld16(taddr + c0, v);
+        float* dst = staging + owner * slice + c0 * W + fl;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) dst[j * W] = ok ? v[j] : 0.f;
+      }
+      if (a.row_norm && threadIdx.x < BN)  // this CTA's partial row sums go to every owner
+        for (int o = 0; o < cs; ++o) staging[o * slice + BN * W + threadIdx.x] = rnorm[threadIdx.x];
+      if (threadIdx.x == 0) mbar_expect_tx(inbox_bar, uint32_t((cs - 1) * slice * 4));
+      fence_async_shared();  // generic-proxy staging writes, before the bulk copies read them
+      tc_fence_before();
+      __syncthreads();
+      if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
+      cluster_sync();  // every ring of the cluster is idle and every inbox barrier armed
+      if (threadIdx.x == 0)
+        for (int o = 0; o < cs; ++o)
+          if (o != rank)
+            bulk_copy_peer(map_peer(smem_u32(inbox + rank * slice), uint32_t(o)), staging + o * slice,
+                           uint32_t(slice * 4), map_peer(smem_u32(inbox_bar), uint32_t(o)));
+      got = mbar_wait(inbox_bar, 0, a.status, kStatusTmaTimeout);
+      cluster_arrive();  // this CTA's inbox is complete; it leaves only once every inbox is
+    } else {
+      cluster_sync();  // A
+      const uint32_t inbox_u32 = smem_u32(inbox);
+      const uint32_t dst = map_peer(inbox_u32, uint32_t(owner)) + uint32_t(rank * BN * rs + fl) * 4u;
+#pragma unroll 1
+      for (int c0 = 16 * half; c0 < BN; c0 += 32) {
+        float v[16];
+        tmem_ld16(taddr + c0, v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) st_peer1(dst + uint32_t((c0 + j) * rs) * 4u, ok ? v[j] : 0.f);
+      }
+      if (a.row_norm && threadIdx.x < BN)  // this CTA's partial row sums go to every owner
+        for (int o = 0; o < cs; ++o)
+          st_peer1(map_peer(inbox_u32, uint32_t(o)) + uint32_t((rank * BN + threadIdx.x) * rs + W) * 4u,
+                   rnorm[threadIdx.x]);
+      tc_fence_before();
+      __syncthreads();
+      if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
+      cluster_sync();  // B: every partial has landed in its owner's inbox
+    }
+    // partials of source rank j for activation row c (W features) and its partial row sum
+    auto part = [&](int j, int c) -> const float* {
+      if constexpr (C::kBulkExchange)
+        return (j == rank ? reinterpret_cast<const float*>(smem) + rank * slice : inbox + j * slice) + c * W;
+      else
+        return inbox + (j * BN + c) * rs;
+    };
+    auto part_sum = [&](int j, int c) -> float {
+      if constexpr (C::kBulkExchange)
+        return (j == rank ? reinterpret_cast<const float*>(smem) + rank * slice : inbox + j * slice)[BN * W + c];
+      else
+        return inbox[(j * BN + c) * rs + W];
+    };
     auto row_scale = [&](int c) -> float {
       float total = 0.f;
-      for (int j = 0; j < cs; ++j) total += inbox[(j * BN + c) * rs + W];
+      for (int j = 0; j < cs; ++j) total += part_sum(j, c);
       return 1.0f / sqrtf(total / float(a.in_features) + a.norm_eps);
     };
-    if constexpr (EPI == Q3T_EPI_SWIGLU_PAIRED) {
+    if (!got) {
+      // the inbox never completed (status raised): no output
+    } else if constexpr (EPI == Q3T_EPI_SWIGLU_PAIRED) {
       const int hw = W / 2, nq = hw / 4;
       const int units = mcount * nq;
       for (int u = threadIdx.x; u < units; u += blockDim.x) {
@@ -536,7 +620,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int f = (u % nq) * 4;  // local gate feature; its up partner sits at hw + f
         float4 g = make_float4(0.f, 0.f, 0.f, 0.f), up = g;
         for (int j = 0; j < cs; ++j) {
-          const float* row = inbox + (j * BN + c) * rs;
+          const float* row = part(j, c);
           const float4 gv = *reinterpret_cast<const float4*>(row + f);
           const float4 uv = *reinterpret_cast<const float4*>(row + hw + f);
           g.x += gv.x; g.y += gv.y; g.z += gv.z; g.w += gv.w;
@@ -557,14 +641,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
       const int nq = W / 4;
       const int units = mcount * nq;
-      for (int u = threadIdx.x; u < units; u += blockDim.x) {
+#pragma unroll
+      for (int i = 0; i < (kPreload ? kQuads : BN / 16); ++i) {
+        const int u = threadIdx.x + i * kThreads;
+        if (u >= units) break;
         const int c = u / nq;
         const int f = (u % nq) * 4;
         const int n = n0 + rank * W + f;
-        const Inputs4 in = load_inputs4<EPI>(a, m0 + c, n);
+        const Inputs4 in = kPreload ? pre[kPreload ? i : 0] : load_inputs4<EPI>(a, m0 + c, n);
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int j = 0; j < cs; ++j) {
-          const float4 v = *reinterpret_cast<const float4*>(inbox + (j * BN + c) * rs + f);
+          const float4 v = *reinterpret_cast<const float4*>(part(j, c) + f);
           acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
         }
         float vals[4] = {acc.x, acc.y, acc.z, acc.w};
@@ -576,6 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         store_features4<EPI>(a, m0 + c, n, vals, in);
       }
     }
+    if constexpr (C::kBulkExchange) cluster_wait();
   } else if constexpr (EPI == Q3T_EPI_SWIGLU_PAIRED) {
     // ---------------- one CTA per tile, paired SwiGLU: the tile goes through shared memory so
     // that each thread finalises whole gate/up quad pairs
@@ -589,12 +677,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int j = 0; j < 16; ++j) red[(c0 + j) * C::kRedStride + r] = ok ? v[j] : 0.f;
     }
-    if (a.row_norm && (warp == 2 || warp == 3))
-#pragma unroll
-      for (int q = 0; q < RPT; ++q) {
-        const int m = threadIdx.x - 64 + 64 * q;
-        if (m < BN) rnorm[m] = 1.0f / sqrtf(ss[q] / float(a.in_features) + a.norm_eps);
-      }
+    if (a.row_norm && threadIdx.x < BN)
+      rnorm[threadIdx.x] = 1.0f / sqrtf(rnorm[threadIdx.x] / float(a.in_features) + a.norm_eps);
     tc_fence_before();
     __syncthreads();
     if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);

@@ -58,6 +58,8 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "q3t_attention_plan": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _p, _sz, _p]),
     "q3t_decode_attention_qkv": (_i32, [_p, _i64, _p, _p, _f32, _p, _p, _i64, _p, _p, _p, _p, _p, _i64, _i64, _i64,
                                         _i64, _i64, _i64, _i64, _f32, _p, _sz, _p, _p]),
+    "q3t_decode_attention_qkv_ex": (_i32, [_p, _i64, _p, _p, _f32, _p, _p, _i64, _p, _p, _p, _p, _p, _i64, _i64,
+                                           _i64, _i64, _i64, _i64, _i64, _f32, _p, _sz, _p, _sz, _p, _sz, _p, _p]),
     "q3t_linear_rownorm": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _p, _p, _i64, _i32, _i32, _p, _i64, _p, _f32, _p,
                                   _p, _p]),
     "q3t_linear": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _p, _p, _i64, _i32, _i32, _p, _i64, _p, _p, _p, _sz,

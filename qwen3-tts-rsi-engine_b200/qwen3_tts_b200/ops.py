@@ -472,12 +472,26 @@ def attention_plan(positions, workspace, *, q_heads, kv_heads, head_dim, context
          workspace.data_ptr(), workspace.numel() * workspace.element_size(), _stream())
 
 
+def _prefetch_range(weight):
+    """(pointer, bytes) of a weight tensor or TiledWeight for an L2 prefetch hint, or (None, 0)."""
+    if weight is None:
+        return None, 0
+    t = weight.tiles if isinstance(weight, TiledWeight) else weight
+    _need_cuda(t)
+    return t.data_ptr(), (t.numel() * t.element_size()) // 16 * 16
+
+
 def decode_attention_qkv(qkv, q_norm_weight, k_norm_weight, eps, cos_table, sin_table, rotary_positions, keys,
                          values, positions, *, q_heads, kv_heads, head_dim, context=None, scale=None, out=None,
-                         workspace: Optional[torch.Tensor] = None, tag: str = "attention"):
+                         workspace: Optional[torch.Tensor] = None, prefetch=(), tag: str = "attention"):
     """Decode attention straight from the QKV projection rows: per-head q/k RMSNorm, RoPE and the
-    K/V write of each row's position fused into the attention kernel (one query row per slot)."""
+    K/V write of each row's position fused into the attention kernel (one query row per slot).
+    `prefetch`: up to two weights (tensors or TiledWeights, normally the projections that follow)
+    that the kernel pulls into L2 while the keys stream (q3t_decode_attention_qkv_ex)."""
     _need_cuda(qkv, cos_table, sin_table, rotary_positions, keys, values, positions)
+    prefetch = [w for w in prefetch if w is not None]
+    if len(prefetch) > 2:
+        raise ValueError("decode_attention_qkv: at most two prefetch ranges")
     rows = qkv.shape[0]
     n_slots, kvh, capacity, width = keys.shape
     if (qkv.ndim != 2 or qkv.stride(1) != 1 or qkv.dtype != BF16 or width != head_dim or kvh != kv_heads
@@ -489,6 +503,14 @@ def decode_attention_qkv(qkv, q_norm_weight, k_norm_weight, eps, cos_table, sin_
     out = torch.empty(rows, q_heads, head_dim, dtype=BF16, device=qkv.device) if out is None else out
     need = decode_attention_workspace_bytes(rows, q_heads, head_dim, context)
     ws = workspace if workspace is not None else SCRATCH.workspace(need, qkv.device, tag)
+    if prefetch:
+        (p0, n0), (p1, n1) = (list(map(_prefetch_range, prefetch)) + [(None, 0)])[:2]
+        call("q3t_decode_attention_qkv_ex", qkv.data_ptr(), qkv.stride(0), _ptr(q_norm_weight), _ptr(k_norm_weight),
+             float(eps), cos_table.data_ptr(), sin_table.data_ptr(), cos_table.shape[0], rotary_positions.data_ptr(),
+             keys.data_ptr(), values.data_ptr(), positions.data_ptr(), out.data_ptr(), rows, q_heads, kv_heads,
+             head_dim, n_slots, capacity, context, float(scale), ws.data_ptr(), ws.numel(), p0, n0, p1, n1,
+             status_word(qkv.device).data_ptr(), _stream())
+        return out
     call("q3t_decode_attention_qkv", qkv.data_ptr(), qkv.stride(0), _ptr(q_norm_weight), _ptr(k_norm_weight),
          float(eps), cos_table.data_ptr(), sin_table.data_ptr(), cos_table.shape[0], rotary_positions.data_ptr(),
          keys.data_ptr(), values.data_ptr(), positions.data_ptr(), out.data_ptr(), rows, q_heads, kv_heads, head_dim,

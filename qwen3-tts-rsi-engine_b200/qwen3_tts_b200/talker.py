@@ -25,6 +25,12 @@ from .weights import pack_decoder
 BF16 = torch.bfloat16
 # Run each layer's projections as one persistent q3t_linear_chain launch where the shape allows.
 CHAIN_PROJECTIONS = False
+# Which kernels pull later projections' weights into L2 in the decode step: "none", "gemm" (each
+# GEMM the next GEMM's) or "attention" (the attention kernel O and gate/up, O down, gate/up the
+# next QKV). Measured on the 28-layer step (64 / 32 slots): none 2.96 / 1.94 ms, gemm 2.98 /
+# 1.94 ms, attention 3.16 / 2.08 ms - the weight streams already run near the HBM rate and the
+# prefetch only adds traffic.
+PREFETCH_PLAN = "none"
 
 
 def rope_tables(positions: int, dim: int, theta: float, device) -> tuple[torch.Tensor, torch.Tensor]:
@@ -102,7 +108,8 @@ class TalkerStep:
         self.cos, self.sin = cos, sin
         self.norm_mode = norm_mode
         self.fused_attention = fused_attention   # q/k norm, RoPE and KV write inside the attention kernel
-        self.prefetch_weights = True             # GEMMs pull the next GEMM's weights into L2
+        self.prefetch_plan = PREFETCH_PLAN       # see PREFETCH_PLAN
+        self.prefetch_weights = PREFETCH_PLAN != "none"
         dev = arena.device
         B, H = batch, cfg.hidden
         self.inputs = torch.zeros(B, H, dtype=BF16, device=dev)
@@ -142,20 +149,23 @@ class TalkerStep:
         # split-KV chunks sized once per step for this batch's contexts (all layers share them)
         ops.attention_plan(self.positions, self.ws_attn, q_heads=cfg.q_heads, kv_heads=cfg.kv_heads,
                            head_dim=cfg.head_dim, context=self.context)
-        # each GEMM pulls the next GEMM's weights into L2 while it runs
+        # weights of later GEMMs are pulled into L2 ahead of use
         pf = (lambda t: t) if self.prefetch_weights else (lambda t: None)
+        by_attention = self.prefetch_plan == "attention" and self.fused_attention
         for i, layer in enumerate(layers):
             following = layers[i + 1].qkv if i + 1 < len(layers) else w["head"]
+            after_qkv = None if by_attention else pf(layer.o)
             if layer.folded:
-                lw(res_in, layer.qkv, out=self.qkv, row_norm_eps=cfg.eps, prefetch=pf(layer.o))
+                lw(res_in, layer.qkv, out=self.qkv, row_norm_eps=cfg.eps, prefetch=after_qkv)
             else:
                 ops.rms_norm(res_in, layer.input_norm, cfg.eps, self.norm_mode, out=self.xn)
-                lw(self.xn, layer.qkv, out=self.qkv, workspace=self.ws_linear, prefetch=pf(layer.o))
+                lw(self.xn, layer.qkv, out=self.qkv, workspace=self.ws_linear, prefetch=after_qkv)
             if self.fused_attention:
                 ops.decode_attention_qkv(self.qkv, layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin,
                                          self.rotary, self.arena.keys[i], self.arena.values[i], self.positions,
                                          q_heads=cfg.q_heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
-                                         context=self.context, out=self.attn, workspace=self.ws_attn)
+                                         context=self.context, out=self.attn, workspace=self.ws_attn,
+                                         prefetch=(pf(layer.o), pf(layer.gate_up)) if by_attention else ())
             else:
                 ops.qk_norm_rope_kv(self.qkv, layer.q_norm, layer.k_norm, cfg.eps, self.cos, self.sin, self.rotary,
                                     self.positions, self.arena.keys[i], self.arena.values[i], q_heads=cfg.q_heads,
@@ -163,16 +173,17 @@ class TalkerStep:
                 ops.decode_attention(self.q, self.arena.keys[i], self.arena.values[i], self.positions,
                                      context=self.context, out=self.attn, workspace=self.ws_attn)
             lw(self.attn.view(B, cfg.q_width), layer.o, out=self.h, epilogue=_lib.EPI_RESIDUAL, residual=res_in,
-               workspace=self.ws_linear, prefetch=pf(layer.gate_up))
+               workspace=self.ws_linear, prefetch=pf(layer.down if by_attention else layer.gate_up))
+            after_gate_up = pf(following if by_attention else layer.down)
             if layer.folded:
                 lw(self.h, layer.gate_up, out=self.act, epilogue=_lib.EPI_SWIGLU_PAIRED, row_norm_eps=cfg.eps,
-                   prefetch=pf(layer.down))
+                   prefetch=after_gate_up)
             else:
                 ops.rms_norm(self.h, layer.post_norm, cfg.eps, self.norm_mode, out=self.xn)
                 lw(self.xn, layer.gate_up, out=self.act, epilogue=_lib.EPI_SWIGLU_PAIRED, workspace=self.ws_linear,
-                   prefetch=pf(layer.down))
+                   prefetch=after_gate_up)
             lw(self.act, layer.down, out=self.h, epilogue=_lib.EPI_RESIDUAL, residual=self.h,
-               workspace=self.ws_linear, prefetch=pf(following))
+               workspace=self.ws_linear, prefetch=None if by_attention else pf(following))
             res_in = self.h
         ops.rms_norm(res_in, w["norm"], cfg.eps, self.norm_mode, out=self.hidden)
         lw(self.hidden, w["head"], out=self.logits, workspace=self.ws_linear)

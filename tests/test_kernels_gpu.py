@@ -500,6 +500,20 @@ def test_fused_qkv_attention_equals_separate_kernels(ops, cuda, rows, q_heads, k
     torch.cuda.synchronize()
     assert torch.equal(k2, k1) and torch.equal(v2, v1)
     assert torch.equal(got, ref)
+    # the L2 prefetch hint of q3t_decode_attention_qkv_ex (two weight ranges, one of them
+    # tiled) changes nothing that the kernel computes or writes
+    pf_a = torch.randn(3000, 64, generator=gen).to(BF16).to(cuda)
+    pf_b = ops.pack_tiles(torch.randn(256, 128, generator=gen).to(BF16).to(cuda))
+    k3, v3 = keys.clone(), values.clone()
+    hinted = ops.decode_attention_qkv(qkv, qn, kn, 1e-6, cos, sin, rotary, k3, v3, positions, q_heads=q_heads,
+                                      kv_heads=kv_heads, head_dim=head_dim, context=capacity, prefetch=(pf_a, pf_b))
+    torch.cuda.synchronize()
+    assert torch.equal(k3, k1) and torch.equal(v3, v1)
+    assert torch.equal(hinted, ref)
+    with pytest.raises(ValueError):
+        ops.decode_attention_qkv(qkv, qn, kn, 1e-6, cos, sin, rotary, k3, v3, positions, q_heads=q_heads,
+                                 kv_heads=kv_heads, head_dim=head_dim, context=capacity,
+                                 prefetch=(pf_a, pf_a, pf_a))
     assert_status_clean(ops, cuda)
 
 
