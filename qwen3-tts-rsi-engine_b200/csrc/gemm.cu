@@ -38,9 +38,9 @@ constexpr int kABytes = kTileN * kTileK * 2;
 
 template <int BN>
 struct Cfg {
-  // (Measured: three stages at BN <= 32, which would let a CTA of the next kernel
-  // become resident beside two of this one, ran the talker GEMMs ~10% slower.)
-  static constexpr int kStages = BN <= 16 ? 6 : BN <= 32 ? 5 : BN <= 64 ? 4 : BN <= 128 ? 3 : 2;
+  // Tiles of <= 64 rows keep a split-K inbox beside the ring, so they have one stage fewer than
+  // before the inbox existed (two CTAs still fit on an SM).
+  static constexpr int kStages = BN <= 16 ? 5 : BN <= 32 ? 4 : BN <= 128 ? 3 : 2;
   static constexpr int kBBytes = BN * kTileK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
@@ -49,16 +49,18 @@ struct Cfg {
   static constexpr int kRedStride = kTileN + 4;
   static constexpr int kRedBytes = BN * kRedStride * 4;
   static constexpr int kMain = kRing > kRedBytes ? kRing : kRedBytes;
-  // Split-K exchange by bulk copies: a CTA's partials grouped by owner (staging) and the peers'
-  // partials of its own features (inbox), cs slices each of [BN][W] partials + [BN] row sums +
-  // 16 floats of padding, inside the idle ring; larger tiles keep the store-based exchange.
   static constexpr int kNormRows = (BN + 5) / 6;          // activation rows per norm warp (warps 2-7)
   static constexpr int kNormGroups = (kNormRows + 3) / 4;  // four rows per warp load
-  static constexpr int kExchangeFloats = 2 * (BN * kTileN + 8 * (BN + 16));
-  static constexpr bool kBulkExchange = kExchangeFloats * 4 <= kRing;
-  // main area + barriers (2 per stage + done) + tmem slot + flags, row scales [BN] of the
+  // Split-K exchange (tiles of <= 64 rows): the owner of a feature receives every cluster peer's
+  // fp32 partials of it in a dedicated inbox, [source rank][W + 1][BN + 4] floats (feature-major,
+  // rows contiguous; row W of a source holds its partial row sums), at most (128 + 8)(BN + 4)
+  // floats for any split count. Larger tiles exchange through the idle ring.
+  static constexpr bool kAsyncExchange = BN <= 64;
+  static constexpr int kInboxRow = BN + 4;
+  static constexpr int kInboxBytes = kAsyncExchange ? (kTileN + 8) * kInboxRow * 4 : 0;
+  // main area, inbox, barriers (2 per stage + done + 2) + tmem slot + flags, row scales [BN] of the
   // folded RMSNorm, plus 1 KB alignment slack
-  static constexpr int kSmem = kMain + 256 + 1024 + 1024;
+  static constexpr int kSmem = kMain + kInboxBytes + 256 + 1024 + 1024;
 };
 
 struct GemmArgs {
@@ -227,16 +229,15 @@ Q3T_DEV uint32_t map_peer(uint32_t local_smem, uint32_t rank) {
 Q3T_DEV void st_peer1(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
-// Bulk copy of `bytes` from this CTA's shared memory to a cluster peer's (dst and the peer's
-// mbarrier are shared::cluster addresses from map_peer); completion is counted on that
-// mbarrier (complete_tx). Both addresses 16-byte aligned, bytes a multiple of 16.
-Q3T_DEV void bulk_copy_peer(uint32_t dst, const void* src, uint32_t bytes, uint32_t peer_bar) {
-  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+Q3T_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory"); }
+// 16 bytes from registers into a cluster peer's shared memory, counted on the peer's mbarrier
+// (complete_tx); both are shared::cluster addresses from map_peer, dst 16-byte aligned.
+Q3T_DEV void st_async4(uint32_t dst, float a0, float a1, float a2, float a3, uint32_t peer_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
                    dst),
-               "r"(smem_u32(src)), "r"(bytes), "r"(peer_bar)
+               "f"(a0), "f"(a1), "f"(a2), "f"(a3), "r"(peer_bar)
                : "memory");
 }
-Q3T_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory"); }
 Q3T_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
 
 // One CTA = 128 weight rows x BN activation rows x one K slice. The CTAs of
@@ -254,7 +255,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int S = C::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kMain);
+  float* inbox_area = reinterpret_cast<float*>(smem + C::kMain);  // split-K inbox (kAsyncExchange)
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kMain + C::kInboxBytes);
   uint64_t* empty = full + S;
   uint64_t* done = empty + S;
   uint64_t* epi_bar = done + 1;  // residual tile of the staged epilogue
@@ -265,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* red = reinterpret_cast<float*>(smem);
   // folded RMSNorm: per activation row its sum of squares over this CTA's K slice, later turned
   // into the row scale in place
-  float* rnorm = reinterpret_cast<float*>(smem + C::kMain + 256);
+  float* rnorm = reinterpret_cast<float*>(smem + C::kMain + C::kInboxBytes + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kTileN;
@@ -291,6 +293,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(done, 1);
     mbar_init(epi_bar, 1);
     mbar_init(inbox_bar, 1);
+    if (C::kAsyncExchange && clustered) {
+      // every cluster peer sends W features x BN rows of partials (+ BN row sums with row_norm)
+      const int W = kTileN / a.splits;
+      mbar_expect_tx(inbox_bar, uint32_t((a.splits - 1) * (W + (a.row_norm ? 1 : 0)) * BN * 4));
+    }
     *abort_flag = 0;
     *consumed = 0;
     fence_mbar_init();
@@ -308,6 +315,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // peers send into this CTA's inbox only after its barrier is initialised and armed: this arrive
+  // pairs with the cluster wait before the sends
+  if (C::kAsyncExchange && clustered) cluster_arrive();
   const uint32_t tmem = *tmem_slot;
   int issued = 0;  // producer only
   if (a.prefetch != nullptr && threadIdx.x == 64) {
@@ -504,14 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (clustered) {
     // ---------------- split-K reduction across the cluster. The CTA that finalises a feature
     // (its owner) receives every peer's fp32 partials of it and sums them in rank order
-    // (deterministic). Bulk form (tiles of <= 64 rows): each CTA writes its partials, grouped by
-    // owner, into its own idle ring; after one cluster barrier (every CTA past its MMAs, so every
-    // ring is free and every inbox barrier armed) one thread copies each owner's slice into that
-    // owner's inbox with a bulk shared::cluster copy counted on the owner's inbox barrier; the
-    // owner reduces as soon as its inbox is complete. A split arrive/wait cluster barrier keeps
-    // every CTA resident until all copies of the cluster have landed. Store form (larger tiles):
-    // each thread stores its partials into the owner's shared memory, then a second cluster
-    // barrier.
+    // (deterministic).
     if (threadIdx.x == 0 && *abort_flag)  // outstanding ring loads land before the ring is reused
       for (int j = *consumed; j < issued; ++j) mbar_wait(&full[j % S], (j / S) & 1, a.status, kStatusTmaTimeout);
     __syncthreads();
@@ -528,52 +531,161 @@ __global__ void __launch_bounds__(kThreads, 1)
       fl = r - owner * W;
     }
     const int mcount = (m_end - m0) < BN ? (m_end - m0) : BN;
-    // epilogue inputs (residual, bias, scale) of this thread's output quads, loaded before the
-    // exchange so that their latency overlaps it: at most BN / 16 quads per thread (tiles of up
-    // to 64 rows; 128-row tiles load them in the loop, keeping two CTAs' registers per SM)
-    constexpr int kQuads = BN <= 64 ? BN / 16 : 1;
-    constexpr bool kPreload = BN <= 64;
-    Inputs4 pre[kQuads];
-    if constexpr (EPI != Q3T_EPI_SWIGLU_PAIRED && kPreload) {
-      const int nq = W / 4, units = mcount * nq;
+    if constexpr (C::kAsyncExchange) {
+      // Register form (tiles of <= 64 rows): every thread sends its half of its feature's rows
+      // straight from the accumulator registers into the owner's inbox - st.async into a peer,
+      // counted on the peer's inbox barrier (armed with the bytes expected at kernel start), or
+      // plain stores into its own. No cluster barrier follows the MMAs: the inbox is not shared
+      // with the ring, and the only cluster barrier (arrive at start, wait before the first send)
+      // orders the sends after every peer armed its inbox. The owner reduces once its inbox is
+      // complete; a sender can leave as soon as it is done (its sends read registers only).
+      constexpr int R4 = C::kInboxRow;
+      const int slot_floats = (W + 1) * R4;  // one source's slot: W feature rows + the row sums
+      // output quads of this thread: feature f (lane-adjacent) x rows 4q..4q+3, loaded early
+      const int nf = EPI == Q3T_EPI_SWIGLU_PAIRED ? W / 2 : W;
+      const int units = nf * (BN / 4);
+      // at most 64 features per owner (two or more splits): nf divides the block, so a thread's
+      // quads all belong to one feature
+      constexpr int kU = (64 * BN / 4) / kThreads;
+      const int fq = threadIdx.x % nf, nq = n0 + rank * W + fq;
+      const bool nlive = nq < a.out_features;
+      float pre_r[kU][4];
+      float pre_b = 0.f, pre_g = 0.f;
+      if constexpr (EPI != Q3T_EPI_SWIGLU_PAIRED) {
+        pre_b = (nlive && a.bias != nullptr) ? __bfloat162float(a.bias[nq]) : 0.f;
+        pre_g = !nlive                          ? 0.f
+                : EPI == Q3T_EPI_RESIDUAL_SCALED ? __bfloat162float(a.scale[nq])
+                : EPI == Q3T_EPI_SNAKE           ? a.snake_inv[nq]
+                                                 : 0.f;
 #pragma unroll
-      for (int i = 0; i < kQuads; ++i) {
-        const int u = threadIdx.x + i * kThreads;
-        if (u < units) pre[i] = load_inputs4<EPI>(a, m0 + u / nq, n0 + rank * W + (u % nq) * 4);
-      }
-    }
-    const float* inbox = reinterpret_cast<const float*>(smem);
-    int slice = 0, rs = W + 4;  // bulk: floats per slice; store form: inbox row stride
-    bool got = true;
-    if constexpr (C::kBulkExchange) {
-      slice = BN * W + BN + 16;  // [BN][W] partials, [BN] partial row sums, padding (bank spread)
-      float* staging = reinterpret_cast<float*>(smem);  // [cs][slice], by owner
-      inbox = staging + cs * slice;                     // [cs][slice], by source rank
-#pragma unroll 1
-      for (int c0 = 16 * half; c0 < BN; c0 += 32) {
-        float v[16];
-        tmem_ld16(taddr + c0, v);
-        float* dst = staging + owner * slice + c0 * W + fl;
+        for (int i = 0; i < kU; ++i) {
+          const int u = threadIdx.x + i * kThreads, q = u / nf;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) dst[j * W] = ok ? v[j] : 0.f;
+          for (int e = 0; e < 4; ++e) {
+            const int m = m0 + 4 * q + e;
+            pre_r[i][e] = (has_residual(EPI) && nlive && u < units && m < m_end)
+                              ? __bfloat162float(a.residual[int64_t(m) * a.res_stride + nq])
+                              : (EPI == Q3T_EPI_SNAKE && nlive ? a.snake_alpha[nq] : 0.f);
+          }
+        }
       }
-      if (a.row_norm && threadIdx.x < BN)  // this CTA's partial row sums go to every owner
-        for (int o = 0; o < cs; ++o) staging[o * slice + BN * W + threadIdx.x] = rnorm[threadIdx.x];
-      if (threadIdx.x == 0) mbar_expect_tx(inbox_bar, uint32_t((cs - 1) * slice * 4));
-      fence_async_shared();  // generic-proxy staging writes, before the bulk copies read them
+      cluster_wait();  // every peer's inbox barrier is initialised and armed
+      {
+        // this thread's BN / 2 rows of feature r (half 0: the first half of the rows), one TMEM load
+        constexpr int NC = BN / 2;
+        float v[NC];
+        const int c0 = half * NC;
+        tmem_ld<NC>(taddr + c0, v);
+        if (!ok) {
+#pragma unroll
+          for (int j = 0; j < NC; ++j) v[j] = 0.f;
+        }
+        const int at = rank * slot_floats + fl * R4 + c0;  // source slot `rank`, feature row fl
+        if (owner == rank) {
+#pragma unroll
+          for (int j = 0; j < NC; j += 4)
+            *reinterpret_cast<float4*>(inbox_area + at + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+          const uint32_t dst = map_peer(smem_u32(inbox_area), uint32_t(owner)) + uint32_t(at) * 4u;
+          const uint32_t bar = map_peer(smem_u32(inbox_bar), uint32_t(owner));
+#pragma unroll
+          for (int j = 0; j < NC; j += 4) st_async4(dst + uint32_t(j) * 4u, v[j], v[j + 1], v[j + 2], v[j + 3], bar);
+        }
+      }
+      if (a.row_norm && threadIdx.x < BN / 4) {  // this CTA's partial row sums go to every owner
+        const float4 sums = *reinterpret_cast<const float4*>(rnorm + 4 * threadIdx.x);
+        const int at = rank * slot_floats + W * R4 + 4 * threadIdx.x;
+        for (int o = 0; o < cs; ++o) {
+          if (o == rank) {
+            *reinterpret_cast<float4*>(inbox_area + at) = sums;
+          } else {
+            st_async4(map_peer(smem_u32(inbox_area), uint32_t(o)) + uint32_t(at) * 4u, sums.x, sums.y, sums.z,
+                      sums.w, map_peer(smem_u32(inbox_bar), uint32_t(o)));
+          }
+        }
+      }
       tc_fence_before();
-      __syncthreads();
+      __syncthreads();  // this CTA's own slot is written and every TMEM read is done
       if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
-      cluster_sync();  // every ring of the cluster is idle and every inbox barrier armed
-      if (threadIdx.x == 0)
-        for (int o = 0; o < cs; ++o)
-          if (o != rank)
-            bulk_copy_peer(map_peer(smem_u32(inbox + rank * slice), uint32_t(o)), staging + o * slice,
-                           uint32_t(slice * 4), map_peer(smem_u32(inbox_bar), uint32_t(o)));
-      got = mbar_wait(inbox_bar, 0, a.status, kStatusTmaTimeout);
-      cluster_arrive();  // this CTA's inbox is complete; it leaves only once every inbox is
+      if (!mbar_wait(inbox_bar, 0, a.status, kStatusTmaTimeout)) return;  // peers' partials
+      // folded RMSNorm: one scale per row (sum of every source's partial row sums in rank order),
+      // into the idle ring
+      float* rscale = reinterpret_cast<float*>(smem);
+      if (a.row_norm) {
+        if (threadIdx.x < BN) {
+          float t = 0.f;
+          for (int j = 0; j < cs; ++j) t += inbox_area[j * slot_floats + W * R4 + threadIdx.x];
+          rscale[threadIdx.x] = 1.0f / sqrtf(t / float(a.in_features) + a.norm_eps);
+        }
+        __syncthreads();
+      }
+      // the sums of this thread's quads, every quad's partials loaded before any is used
+      const int lg = __ffs(nf) - 1;
+      float4 acc[kU], upv[kU];
+      int qs[kU];
+      bool live[kU];
+#pragma unroll
+      for (int i = 0; i < kU; ++i) {
+        const int u = threadIdx.x + i * kThreads;
+        const int q = u >> lg;
+        live[i] = u < units && 4 * q < mcount;
+        qs[i] = live[i] ? q : 0;
+        acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        upv[i] = acc[i];
+      }
+      for (int j = 0; j < cs; ++j) {
+        const float* src = inbox_area + j * slot_floats + fq * R4;
+#pragma unroll
+        for (int i = 0; i < kU; ++i) {
+          const float4 p = *reinterpret_cast<const float4*>(src + 4 * qs[i]);
+          acc[i].x += p.x; acc[i].y += p.y; acc[i].z += p.z; acc[i].w += p.w;
+          if constexpr (EPI == Q3T_EPI_SWIGLU_PAIRED) {
+            const float4 w = *reinterpret_cast<const float4*>(src + nf * R4 + 4 * qs[i]);
+            upv[i].x += w.x; upv[i].y += w.y; upv[i].z += w.z; upv[i].w += w.w;
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kU; ++i) {
+        if (!live[i]) continue;
+        const int q = qs[i];
+        float av[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
+        float uv[4] = {upv[i].x, upv[i].y, upv[i].z, upv[i].w};
+        if (a.row_norm) {
+          const float4 rn = *reinterpret_cast<const float4*>(rscale + 4 * q);
+          const float rv[4] = {rn.x, rn.y, rn.z, rn.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            av[e] *= rv[e];
+            uv[e] *= rv[e];
+          }
+        }
+        if constexpr (EPI == Q3T_EPI_SWIGLU_PAIRED) {
+          const int ft = rank * nf + fq;  // gate feature within the tile
+          if (n0 + 64 + ft < a.out_features) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int m = m0 + 4 * q + e;
+              if (m < m_end)
+                static_cast<__nv_bfloat16*>(a.out)[int64_t(m) * a.out_stride + (n0 / 2 + ft)] =
+                    __float2bfloat16_rn(silu_gate(bf16r(av[e]), bf16r(uv[e])));
+            }
+          }
+        } else if (nlive) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int m = m0 + 4 * q + e;
+            if (m < m_end) store_value<EPI>(a, m, nq, epilogue_value<EPI>(av[e] + pre_b, pre_r[i][e], pre_g));
+          }
+        }
+      }
     } else {
-      cluster_sync();  // A
+      // Ring form (128-row tiles): after one cluster barrier (every ring idle) each thread stores
+      // its partials into the owner's shared memory, then a second cluster barrier; the owner
+      // reduces its inbox in rank order.
+      const int rs = W + 4;  // inbox row stride in floats; column W holds the partial row sums
+      float* inbox = reinterpret_cast<float*>(smem);  // [cs][BN][rs]
+      cluster_sync();
       const uint32_t inbox_u32 = smem_u32(inbox);
       const uint32_t dst = map_peer(inbox_u32, uint32_t(owner)) + uint32_t(rank * BN * rs + fl) * 4u;
 #pragma unroll 1
@@ -590,80 +702,61 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncthreads();
       if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
-      cluster_sync();  // B: every partial has landed in its owner's inbox
-    }
-    // partials of source rank j for activation row c (W features) and its partial row sum
-    auto part = [&](int j, int c) -> const float* {
-      if constexpr (C::kBulkExchange)
-        return (j == rank ? reinterpret_cast<const float*>(smem) + rank * slice : inbox + j * slice) + c * W;
-      else
-        return inbox + (j * BN + c) * rs;
-    };
-    auto part_sum = [&](int j, int c) -> float {
-      if constexpr (C::kBulkExchange)
-        return (j == rank ? reinterpret_cast<const float*>(smem) + rank * slice : inbox + j * slice)[BN * W + c];
-      else
-        return inbox[(j * BN + c) * rs + W];
-    };
-    auto row_scale = [&](int c) -> float {
-      float total = 0.f;
-      for (int j = 0; j < cs; ++j) total += part_sum(j, c);
-      return 1.0f / sqrtf(total / float(a.in_features) + a.norm_eps);
-    };
-    if (!got) {
-      // the inbox never completed (status raised): no output
-    } else if constexpr (EPI == Q3T_EPI_SWIGLU_PAIRED) {
-      const int hw = W / 2, nq = hw / 4;
-      const int units = mcount * nq;
-      for (int u = threadIdx.x; u < units; u += blockDim.x) {
-        const int c = u / nq;
-        const int f = (u % nq) * 4;  // local gate feature; its up partner sits at hw + f
-        float4 g = make_float4(0.f, 0.f, 0.f, 0.f), up = g;
-        for (int j = 0; j < cs; ++j) {
-          const float* row = part(j, c);
-          const float4 gv = *reinterpret_cast<const float4*>(row + f);
-          const float4 uv = *reinterpret_cast<const float4*>(row + hw + f);
-          g.x += gv.x; g.y += gv.y; g.z += gv.z; g.w += gv.w;
-          up.x += uv.x; up.y += uv.y; up.z += uv.z; up.w += uv.w;
-        }
-        if (a.row_norm) {
-          const float rn = row_scale(c);
-          g.x *= rn; g.y *= rn; g.z *= rn; g.w *= rn;
-          up.x *= rn; up.y *= rn; up.z *= rn; up.w *= rn;
-        }
-        const int ft = rank * hw + f;  // gate feature within the tile
-        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + int64_t(m0 + c) * a.out_stride + (n0 / 2 + ft);
-        const float gs[4] = {g.x, g.y, g.z, g.w}, us[4] = {up.x, up.y, up.z, up.w};
+      cluster_sync();  // every partial has landed in its owner's inbox
+      auto row_scale = [&](int c) -> float {
+        float total = 0.f;
+        for (int j = 0; j < cs; ++j) total += inbox[(j * BN + c) * rs + W];
+        return 1.0f / sqrtf(total / float(a.in_features) + a.norm_eps);
+      };
+      if constexpr (EPI == Q3T_EPI_SWIGLU_PAIRED) {
+        const int hw = W / 2, nq = hw / 4;
+        const int units = mcount * nq;
+        for (int u = threadIdx.x; u < units; u += blockDim.x) {
+          const int c = u / nq;
+          const int f = (u % nq) * 4;  // local gate feature; its up partner sits at hw + f
+          float4 g = make_float4(0.f, 0.f, 0.f, 0.f), up = g;
+          for (int j = 0; j < cs; ++j) {
+            const float* row = inbox + (j * BN + c) * rs;
+            const float4 gv = *reinterpret_cast<const float4*>(row + f);
+            const float4 uv = *reinterpret_cast<const float4*>(row + hw + f);
+            g.x += gv.x; g.y += gv.y; g.z += gv.z; g.w += gv.w;
+            up.x += uv.x; up.y += uv.y; up.z += uv.z; up.w += uv.w;
+          }
+          if (a.row_norm) {
+            const float rn = row_scale(c);
+            g.x *= rn; g.y *= rn; g.z *= rn; g.w *= rn;
+            up.x *= rn; up.y *= rn; up.z *= rn; up.w *= rn;
+          }
+          const int ft = rank * hw + f;  // gate feature within the tile
+          __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + int64_t(m0 + c) * a.out_stride + (n0 / 2 + ft);
+          const float gs[4] = {g.x, g.y, g.z, g.w}, us[4] = {up.x, up.y, up.z, up.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (n0 + 64 + ft + j < a.out_features) o[j] = __float2bfloat16_rn(silu_gate(bf16r(gs[j]), bf16r(us[j])));
-      }
-    } else {
-      const int nq = W / 4;
-      const int units = mcount * nq;
-#pragma unroll
-      for (int i = 0; i < (kPreload ? kQuads : BN / 16); ++i) {
-        const int u = threadIdx.x + i * kThreads;
-        if (u >= units) break;
-        const int c = u / nq;
-        const int f = (u % nq) * 4;
-        const int n = n0 + rank * W + f;
-        const Inputs4 in = kPreload ? pre[kPreload ? i : 0] : load_inputs4<EPI>(a, m0 + c, n);
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int j = 0; j < cs; ++j) {
-          const float4 v = *reinterpret_cast<const float4*>(part(j, c) + f);
-          acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+          for (int j = 0; j < 4; ++j)
+            if (n0 + 64 + ft + j < a.out_features) o[j] = __float2bfloat16_rn(silu_gate(bf16r(gs[j]), bf16r(us[j])));
         }
-        float vals[4] = {acc.x, acc.y, acc.z, acc.w};
-        if (a.row_norm) {
-          const float rn = row_scale(c);
+      } else {
+        const int nq = W / 4;
+        const int units = mcount * nq;
+        for (int u = threadIdx.x; u < units; u += blockDim.x) {
+          const int c = u / nq;
+          const int f = (u % nq) * 4;
+          const int n = n0 + rank * W + f;
+          const Inputs4 in = load_inputs4<EPI>(a, m0 + c, n);
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int j = 0; j < cs; ++j) {
+            const float4 v = *reinterpret_cast<const float4*>(inbox + (j * BN + c) * rs + f);
+            acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+          }
+          float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+          if (a.row_norm) {
+            const float rn = row_scale(c);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) vals[j] *= rn;
+            for (int j = 0; j < 4; ++j) vals[j] *= rn;
+          }
+          store_features4<EPI>(a, m0 + c, n, vals, in);
         }
-        store_features4<EPI>(a, m0 + c, n, vals, in);
       }
     }
-    if constexpr (C::kBulkExchange) cluster_wait();
   } else if constexpr (EPI == Q3T_EPI_SWIGLU_PAIRED) {
     // ---------------- one CTA per tile, paired SwiGLU: the tile goes through shared memory so
     // that each thread finalises whole gate/up quad pairs
