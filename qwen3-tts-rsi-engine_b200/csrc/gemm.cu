@@ -230,12 +230,13 @@ Q3T_DEV void st_peer1(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 Q3T_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory"); }
-// 16 bytes from registers into a cluster peer's shared memory, counted on the peer's mbarrier
-// (complete_tx); both are shared::cluster addresses from map_peer, dst 16-byte aligned.
-Q3T_DEV void st_async4(uint32_t dst, float a0, float a1, float a2, float a3, uint32_t peer_bar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+// Bulk copy of `bytes` from this CTA's shared memory to a cluster peer's (dst and the peer's
+// mbarrier are shared::cluster addresses from map_peer); completion is counted on that
+// mbarrier (complete_tx). Both addresses 16-byte aligned, bytes a multiple of 16.
+Q3T_DEV void bulk_copy_peer(uint32_t dst, const void* src, uint32_t bytes, uint32_t peer_bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                    dst),
-               "f"(a0), "f"(a1), "f"(a2), "f"(a3), "r"(peer_bar)
+               "r"(smem_u32(src)), "r"(bytes), "r"(peer_bar)
                : "memory");
 }
 Q3T_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
@@ -294,9 +295,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(epi_bar, 1);
     mbar_init(inbox_bar, 1);
     if (C::kAsyncExchange && clustered) {
-      // every cluster peer sends W features x BN rows of partials (+ BN row sums with row_norm)
+      // every cluster peer copies W feature rows of partials (+ its row sums with row_norm)
       const int W = kTileN / a.splits;
-      mbar_expect_tx(inbox_bar, uint32_t((a.splits - 1) * (W + (a.row_norm ? 1 : 0)) * BN * 4));
+      mbar_expect_tx(inbox_bar, uint32_t((a.splits - 1) * (W + (a.row_norm ? 1 : 0)) * C::kInboxRow * 4));
     }
     *abort_flag = 0;
     *consumed = 0;
@@ -532,13 +533,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const int mcount = (m_end - m0) < BN ? (m_end - m0) : BN;
     if constexpr (C::kAsyncExchange) {
-      // Register form (tiles of <= 64 rows): every thread sends its half of its feature's rows
-      // straight from the accumulator registers into the owner's inbox - st.async into a peer,
-      // counted on the peer's inbox barrier (armed with the bytes expected at kernel start), or
-      // plain stores into its own. No cluster barrier follows the MMAs: the inbox is not shared
-      // with the ring, and the only cluster barrier (arrive at start, wait before the first send)
-      // orders the sends after every peer armed its inbox. The owner reduces once its inbox is
-      // complete; a sender can leave as soon as it is done (its sends read registers only).
+      // Inbox form (tiles of <= 64 rows): every thread writes its half of its feature's rows from
+      // the accumulator registers into this CTA's idle ring, grouped by owner in the owner's inbox
+      // slot layout (its own features straight into its own inbox), and one thread copies each
+      // owner's slot into that owner's dedicated inbox with a bulk shared::cluster copy counted on
+      // the owner's inbox barrier (armed with the expected bytes at kernel start). No cluster
+      // barrier follows the MMAs: the inbox is not shared with the ring, and the cluster barrier
+      // begun at kernel start (waited before the first copy) only orders the copies after every
+      // peer armed its barrier. The owner reduces once its inbox is complete; a second split
+      // cluster barrier (arrive then, wait before exit) keeps every CTA resident until all copies
+      // out of its staging have landed.
       constexpr int R4 = C::kInboxRow;
       const int slot_floats = (W + 1) * R4;  // one source's slot: W feature rows + the row sums
       // output quads of this thread: feature f (lane-adjacent) x rows 4q..4q+3, loaded early
@@ -570,6 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       cluster_wait();  // every peer's inbox barrier is initialised and armed
+      float* staging = reinterpret_cast<float*>(smem);  // the idle ring: [cs][slot_floats], by owner
       {
         // this thread's BN / 2 rows of feature r (half 0: the first half of the rows), one TMEM load
         constexpr int NC = BN / 2;
@@ -580,37 +585,39 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < NC; ++j) v[j] = 0.f;
         }
-        const int at = rank * slot_floats + fl * R4 + c0;  // source slot `rank`, feature row fl
-        if (owner == rank) {
+        // owner `rank`: straight into this CTA's inbox; other owners: this CTA's idle ring
+        // (staging, one slot per owner in the inbox slot layout), copied out below
+        float* dst = (owner == rank ? inbox_area + rank * slot_floats : staging + owner * slot_floats) + fl * R4 + c0;
 #pragma unroll
-          for (int j = 0; j < NC; j += 4)
-            *reinterpret_cast<float4*>(inbox_area + at + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-        } else {
-          const uint32_t dst = map_peer(smem_u32(inbox_area), uint32_t(owner)) + uint32_t(at) * 4u;
-          const uint32_t bar = map_peer(smem_u32(inbox_bar), uint32_t(owner));
-#pragma unroll
-          for (int j = 0; j < NC; j += 4) st_async4(dst + uint32_t(j) * 4u, v[j], v[j + 1], v[j + 2], v[j + 3], bar);
-        }
+        for (int j = 0; j < NC; j += 4)
+          *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
       }
-      if (a.row_norm && threadIdx.x < BN / 4) {  // this CTA's partial row sums go to every owner
-        const float4 sums = *reinterpret_cast<const float4*>(rnorm + 4 * threadIdx.x);
-        const int at = rank * slot_floats + W * R4 + 4 * threadIdx.x;
-        for (int o = 0; o < cs; ++o) {
-          if (o == rank) {
-            *reinterpret_cast<float4*>(inbox_area + at) = sums;
-          } else {
-            st_async4(map_peer(smem_u32(inbox_area), uint32_t(o)) + uint32_t(at) * 4u, sums.x, sums.y, sums.z,
-                      sums.w, map_peer(smem_u32(inbox_bar), uint32_t(o)));
-          }
-        }
+      if (a.row_norm && threadIdx.x < cs * (BN / 4)) {  // this CTA's partial row sums go to every owner
+        const int o = threadIdx.x / (BN / 4), k = threadIdx.x % (BN / 4);  // owner o, rows 4k..4k+3
+        float* dst = (o == rank ? inbox_area + rank * slot_floats : staging + o * slot_floats) + W * R4 + 4 * k;
+        *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(rnorm + 4 * k);
       }
+      fence_async_shared();  // the staging writes, before the bulk copies read them
       tc_fence_before();
-      __syncthreads();  // this CTA's own slot is written and every TMEM read is done
+      __syncthreads();  // staging and this CTA's own slot are written, every TMEM read is done
       if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
-      if (!mbar_wait(inbox_bar, 0, a.status, kStatusTmaTimeout)) return;  // peers' partials
+      if (threadIdx.x == 0) {
+        const uint32_t bytes = uint32_t((W + (a.row_norm ? 1 : 0)) * R4 * 4);
+        for (int o = 0; o < cs; ++o)
+          if (o != rank)
+            bulk_copy_peer(map_peer(smem_u32(inbox_area + rank * slot_floats), uint32_t(o)), staging + o * slot_floats,
+                           bytes, map_peer(smem_u32(inbox_bar), uint32_t(o)));
+      }
+      const bool got = mbar_wait(inbox_bar, 0, a.status, kStatusTmaTimeout);  // peers' partials
+      cluster_arrive();  // this CTA's inbox is complete; it leaves once every inbox is (its staging is read)
+      if (!got) {
+        cluster_wait();
+        return;
+      }
       // folded RMSNorm: one scale per row (sum of every source's partial row sums in rank order),
-      // into the idle ring
-      float* rscale = reinterpret_cast<float*>(smem);
+      // over this CTA's own row sums (already copied into its inbox and staging; the ring may
+      // still be read by copies in flight)
+      float* rscale = rnorm;
       if (a.row_norm) {
         if (threadIdx.x < BN) {
           float t = 0.f;
@@ -679,6 +686,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      cluster_wait();  // every inbox of the cluster is complete: no copy still reads this CTA's staging
     } else {
       // Ring form (128-row tiles): after one cluster barrier (every ring idle) each thread stores
       // its partials into the owner's shared memory, then a second cluster barrier; the owner
