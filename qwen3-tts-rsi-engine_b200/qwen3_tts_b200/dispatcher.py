@@ -9,9 +9,12 @@ independent ``ContinuousModel`` replicas with no collective on the data path.
 * each new request goes to the live engine with the fewest requests in flight
   (ties: lowest rank), never above ``per_engine``;
 * each engine process (``engine_main``) runs its own tick loop on its GPU and
-  streams ``delta`` / ``done`` events back over one shared queue; a request's PCM
-  crosses the process boundary once, as its deltas (``done`` carries the record
-  without the audio, which the dispatcher reassembles from the deltas it relayed);
+  sends ONE message per tick over its own result pipe (the tick's audio deltas
+  and finished records; a sender thread writes the pipe, so the GPU loop never
+  blocks on the host side); the dispatcher waits on all pipes at once. A
+  request's PCM crosses the process boundary once, as its deltas (the finished
+  record carries no audio; the dispatcher reassembles it from the deltas it
+  relayed);
 * cancellations go to the engine that owns the request;
 * failure detection is on the host: an engine that raises or whose process
   exits is marked dead, its in-flight requests complete with
@@ -26,7 +29,9 @@ import importlib
 import logging
 import multiprocessing as mp
 import queue as queue_mod
+import threading
 import time
+from multiprocessing import connection as mp_connection
 from dataclasses import dataclass, field
 
 LOGGER = logging.getLogger(__name__)
@@ -38,8 +43,40 @@ def _load(spec: str):
     return getattr(importlib.import_module(module), attr)
 
 
-def engine_main(rank: int, device: str, kwargs: dict, inbox, outbox, factory: str | None) -> None:
-    """Engine process: build the model, then tick while requests are in flight."""
+class _PipeSender:
+    """Engine side of a result pipe: messages are queued locally and written by a thread, so the
+    engine's tick loop never waits for the dispatcher to read."""
+
+    def __init__(self, conn):
+        self.conn = conn
+        self.queue: queue_mod.SimpleQueue = queue_mod.SimpleQueue()
+        self.thread = threading.Thread(target=self._run, name="q3t-result-pipe", daemon=True)
+        self.thread.start()
+
+    def _run(self) -> None:
+        while True:
+            message = self.queue.get()
+            if message is None:
+                return
+            try:
+                self.conn.send(message)
+            except (OSError, EOFError, BrokenPipeError):  # the dispatcher is gone
+                return
+
+    def put(self, message) -> None:
+        self.queue.put(message)
+
+    def close(self) -> None:
+        """Flush every queued message, then close the pipe."""
+        self.queue.put(None)
+        self.thread.join(timeout=30)
+        self.conn.close()
+
+
+def engine_main(rank: int, device: str, kwargs: dict, inbox, result_conn, factory: str | None) -> None:
+    """Engine process: build the model, then tick while requests are in flight. Each tick's
+    events go to the dispatcher as one ("tick", rank, deltas, records) message."""
+    outbox = _PipeSender(result_conn)
     try:
         if factory is None:
             from qwen3_tts_b200.continuous import ContinuousModel
@@ -49,6 +86,7 @@ def engine_main(rank: int, device: str, kwargs: dict, inbox, outbox, factory: st
         outbox.put(("hello", rank, list(model.speakers), list(model.languages)))
     except Exception as error:  # the dispatcher sees the engine as dead
         outbox.put(("failed", rank, f"engine start failed: {error!r}"))
+        outbox.close()
         return
     active: set = set()
     try:
@@ -73,20 +111,22 @@ def engine_main(rank: int, device: str, kwargs: dict, inbox, outbox, factory: st
                 break
             if not submissions and not cancelled and not active:
                 continue
-
-            def emit(identifier, pcm, rate):
-                outbox.put(("delta", rank, identifier, pcm, rate))
-
+            deltas, records = [], []
+            emit = lambda identifier, pcm, rate: deltas.append((identifier, pcm, rate))
             for identifier, output in model.tick(submissions, emit, cancelled):
                 active.discard(identifier)
                 # the audio already crossed as deltas: the record travels without its PCM
-                outbox.put(("done", rank, identifier, {k: v for k, v in output.items() if k != "pcm"}))
+                records.append((identifier, {k: v for k, v in output.items() if k != "pcm"}))
+            if deltas or records:
+                outbox.put(("tick", rank, deltas, records))
     except Exception as error:
         LOGGER.exception("engine %d failed", rank)
         outbox.put(("failed", rank, repr(error)))
+        outbox.close()
         return
     model.close()
     outbox.put(("closed", rank))
+    outbox.close()
 
 
 @dataclass
@@ -95,6 +135,7 @@ class Engine:
     device: str
     process: object = None
     inbox: object = None
+    results: object = None                         # dispatcher end of the engine's result pipe
     alive: bool = False
     requests: dict = field(default_factory=dict)   # identifier -> [frames delivered (bytes)]
     last_event: float = 0.0
@@ -106,7 +147,6 @@ class Dispatcher:
         self.ctx = mp.get_context("spawn")
         self.kwargs, self.per_engine, self.factory, self.restart = engine_kwargs, per_engine, factory, restart
         self.stall_timeout = stall_timeout
-        self.outbox = self.ctx.Queue()
         devices = devices or [f"cuda:{i}" for i in range(gpus)]
         self.engines = [Engine(rank, device) for rank, device in enumerate(devices)]
         self.speakers: list = []
@@ -123,12 +163,37 @@ class Dispatcher:
 
     # ------------------------------------------------------------------ processes
     def _spawn(self, engine: Engine) -> None:
+        if engine.results is not None:
+            engine.results.close()
         engine.inbox = self.ctx.Queue()
+        reader, writer = self.ctx.Pipe(duplex=False)
+        engine.results = reader
         engine.process = self.ctx.Process(target=engine_main, name=f"q3t-engine-{engine.rank}", daemon=True,
-                                          args=(engine.rank, engine.device, self.kwargs, engine.inbox, self.outbox,
+                                          args=(engine.rank, engine.device, self.kwargs, engine.inbox, writer,
                                                 self.factory))
         engine.process.start()
+        writer.close()  # the engine process holds the writing end
         engine.alive = False
+
+    def _poll(self, timeout: float) -> list:
+        """Events from every engine's result pipe, waiting up to `timeout` for the first. A pipe
+        whose engine is gone yields a ("failed", rank, reason) event."""
+        pipes = {e.results: e for e in self.engines if e.results is not None}
+        events: list = []
+        for conn in mp_connection.wait(list(pipes), timeout=timeout):
+            engine = pipes[conn]
+            ended = False  # the engine said goodbye ("failed" / "closed") before its pipe closed
+            try:
+                while conn.poll():
+                    event = conn.recv()
+                    ended = ended or event[0] in ("failed", "closed")
+                    events.append(event)
+            except (EOFError, OSError):
+                conn.close()
+                engine.results = None
+                if engine.alive and not ended:
+                    events.append(("failed", engine.rank, "result pipe closed"))
+        return events
 
     def _wait_ready(self, timeout: float) -> None:
         deadline = time.monotonic() + timeout
@@ -136,21 +201,21 @@ class Dispatcher:
             remaining = deadline - time.monotonic()
             if remaining <= 0:
                 raise RuntimeError("Engines did not start in time")
-            try:
-                event = self.outbox.get(timeout=min(remaining, 1.0))
-            except queue_mod.Empty:
+            events = self._poll(min(remaining, 1.0))
+            if not events:
                 for engine in self.engines:
                     if not engine.alive and not engine.process.is_alive():
                         raise RuntimeError(f"Engine {engine.rank} exited during start")
                 continue
-            if event[0] == "hello":
-                engine = self.engines[event[1]]
-                engine.alive = True
-                self.speakers, self.languages = event[2], event[3]
-            elif event[0] == "failed":
-                raise RuntimeError(event[2])
-            else:
-                self.pending_events.append(event)
+            for event in events:
+                if event[0] == "hello":
+                    engine = self.engines[event[1]]
+                    engine.alive = True
+                    self.speakers, self.languages = event[2], event[3]
+                elif event[0] == "failed":
+                    raise RuntimeError(event[2])
+                else:
+                    self.pending_events.append(event)
 
     # ------------------------------------------------------------------ routing
     def load(self) -> list:
@@ -196,30 +261,23 @@ class Dispatcher:
         in_flight = any(e.requests for e in self.engines)
         events = self.pending_events
         self.pending_events = []
-        try:
-            if not events:
-                events.append(self.outbox.get(timeout=0.05 if in_flight else 0.0005))
-            while True:
-                events.append(self.outbox.get_nowait())
-        except queue_mod.Empty:
-            pass
+        events += self._poll(0.0 if events else (0.05 if in_flight else 0.0005))
         now = time.monotonic()
         for event in events:
             kind, rank = event[0], event[1]
             engine = self.engines[rank]
             engine.last_event = now
-            if kind == "delta":
-                identifier = event[2]
-                if identifier in engine.requests:
-                    engine.requests[identifier].append(event[3])
-                    if emit is not None:
-                        emit(identifier, event[3], event[4])
-            elif kind == "done":
-                identifier = event[2]
-                delivered = engine.requests.pop(identifier, None)
-                if delivered is not None:
-                    self.owner.pop(identifier, None)
-                    outputs.append((identifier, dict(event[3], pcm=b"".join(delivered))))
+            if kind == "tick":
+                for identifier, pcm, rate in event[2]:
+                    if identifier in engine.requests:
+                        engine.requests[identifier].append(pcm)
+                        if emit is not None:
+                            emit(identifier, pcm, rate)
+                for identifier, record in event[3]:
+                    delivered = engine.requests.pop(identifier, None)
+                    if delivered is not None:
+                        self.owner.pop(identifier, None)
+                        outputs.append((identifier, dict(record, pcm=b"".join(delivered))))
             elif kind == "failed":
                 self._fail_engine(engine, event[2], outputs)
             elif kind == "hello":
@@ -235,9 +293,15 @@ class Dispatcher:
         for engine in self.engines:
             if engine.process is not None and engine.process.is_alive():
                 engine.inbox.put(("stop",))
+        deadline = time.monotonic() + 30
+        while any(e.process is not None and e.process.is_alive() for e in self.engines) and time.monotonic() < deadline:
+            self._poll(0.1)  # drain the pipes so that every engine can flush and exit
         for engine in self.engines:
             if engine.process is not None:
-                engine.process.join(timeout=30)
+                engine.process.join(timeout=5)
                 if engine.process.is_alive():
                     engine.process.kill()
                     engine.process.join(timeout=5)
+            if engine.results is not None:
+                engine.results.close()
+                engine.results = None

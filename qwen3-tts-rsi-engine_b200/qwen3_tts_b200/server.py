@@ -38,31 +38,45 @@ MAX_INPUT_CHARS = 10000
 class AudioChannel:
     """Bounded per-request audio queue fed from the model-owner thread.
 
-    ``emit`` blocks the owner thread for at most 30 s when the client falls
-    behind (16 queued chunks); a timeout or a closed loop marks the channel
-    failed and later chunks are dropped."""
+    ``emit`` hands a chunk to the event loop without waiting for it (one
+    ``call_soon_threadsafe``, no round trip), with the chunk already base64
+    encoded on the emitting thread, so the loop only frames and writes events.
+    At most ``depth`` chunks are queued: when the client falls behind, ``emit``
+    blocks the owner thread for at most ``timeout`` (30 s) for a free place; a
+    timeout or a closed loop marks the channel failed and later chunks are
+    dropped."""
 
-    def __init__(self, loop, depth: int = 16):
+    def __init__(self, loop, depth: int = 16, timeout: float = 30.0):
         self.loop = loop
-        self.queue = asyncio.Queue(maxsize=depth)
+        self.queue: asyncio.Queue = asyncio.Queue()
+        self.places = threading.Semaphore(depth)
+        self.timeout = timeout
         self.closed = threading.Event()
         self.error = None
 
     def emit(self, pcm: bytes, sample_rate: int) -> None:
         if self.closed.is_set():
             return
-        future = asyncio.run_coroutine_threadsafe(self.queue.put((pcm, sample_rate)), self.loop)
+        if not self.places.acquire(timeout=self.timeout):
+            self.error = TimeoutError("client stopped reading audio")
+            self.closed.set()
+            return
+        chunk = (len(pcm), base64.b64encode(pcm).decode(), sample_rate)
         try:
-            future.result(timeout=30)
-        except Exception as error:  # the client stopped reading or the loop is gone
-            future.cancel()
+            self.loop.call_soon_threadsafe(self.queue.put_nowait, chunk)
+        except RuntimeError as error:  # the loop is gone
             self.error = error
             self.closed.set()
+
+    def taken(self) -> None:
+        """The consumer took one chunk off the queue: one more may be queued."""
+        self.places.release()
 
     def close(self) -> None:
         self.closed.set()
         while not self.queue.empty():
             self.queue.get_nowait()
+            self.places.release()
 
 
 def normalize(payload, speakers, languages) -> dict:
@@ -100,9 +114,9 @@ def sse(event: dict) -> bytes:
     return ("data: " + json.dumps(event) + "\n\n").encode()
 
 
-def delta(pcm: bytes, sample_rate: int) -> dict:
-    return {"type": "speech.audio.delta", "audio": base64.b64encode(pcm).decode(), "sample_rate": sample_rate,
-            "channels": 1}
+def delta(pcm: bytes, sample_rate: int, encoded: str | None = None) -> dict:
+    audio = encoded if encoded is not None else base64.b64encode(pcm).decode()
+    return {"type": "speech.audio.delta", "audio": audio, "sample_rate": sample_rate, "channels": 1}
 
 
 def settle(future, channel, output) -> None:
@@ -322,9 +336,10 @@ class SpeechService:
                     chunk.cancel()
                     await asyncio.gather(chunk, return_exceptions=True)
             if chunk.done() and not chunk.cancelled():
-                pcm, rate = chunk.result()
-                sent += len(pcm)
-                yield delta(pcm, rate)
+                size, encoded, rate = chunk.result()
+                channel.taken()
+                sent += size
+                yield delta(b"", rate, encoded)
         output = await future
         if sent > len(output["pcm"]):
             raise RuntimeError("Streaming output exceeded final waveform length")

@@ -209,3 +209,33 @@ def test_normalize_keeps_token_ids_and_defaults():
     assert request["input_ids"] == [1, 2, 3] and request["seed"] == 42 and request["max_new_tokens"] == 2048
     with pytest.raises(ValueError):
         normalize({"input": "hi", "input_ids": [-1]}, ["ryan"], ["english"])
+
+
+def test_audio_channel_hands_chunks_to_the_loop_without_a_round_trip():
+    """emit() queues a base64-encoded chunk on the event loop without waiting for the loop (the
+    owner thread never blocks on it while places are free); with `depth` chunks unread it waits
+    for a place, and after its timeout marks the channel failed and drops later chunks."""
+    import asyncio
+    import base64
+    import time
+    loop = asyncio.new_event_loop()
+    try:
+        channel = AudioChannel(loop, depth=2, timeout=0.2)
+        start = time.monotonic()
+        channel.emit(b"ab", 24000)
+        channel.emit(b"cde", 24000)   # the loop is not even running: no round trip
+        assert time.monotonic() - start < 0.1
+        channel.emit(b"fg", 24000)    # no free place: waits 0.2 s, then fails the channel
+        assert channel.closed.is_set() and isinstance(channel.error, TimeoutError)
+        channel.emit(b"hi", 24000)    # dropped
+
+        async def drain():
+            got = []
+            while not channel.queue.empty():
+                got.append(await channel.queue.get())
+                channel.taken()
+            return got
+        got = loop.run_until_complete(drain())
+        assert got == [(2, base64.b64encode(b"ab").decode(), 24000), (3, base64.b64encode(b"cde").decode(), 24000)]
+    finally:
+        loop.close()
