@@ -437,6 +437,41 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   grid_dependency_wait();
 
+  // ---------------- split-K epilogue inputs (inbox form), loaded while the MMAs still run: the
+  // output quads of this thread are feature fq x rows 4q..4q+3, q = (thread + i * 256) / nf
+  const int xr_cs = a.splits;
+  const int xr_rank = clustered ? int(cluster_rank()) : 0;
+  const int xr_W = kTileN / xr_cs;
+  const int nf = EPI == Q3T_EPI_SWIGLU_PAIRED ? xr_W / 2 : xr_W;
+  const int units = nf * (BN / 4);
+  // at most 64 features per owner (two or more splits): nf divides the block, so a thread's quads
+  // all belong to one feature
+  constexpr int kU = BN / 16 > 0 ? BN / 16 : 1;
+  const int fq = int(threadIdx.x) % nf, nq = n0 + xr_rank * xr_W + fq;
+  const bool nlive = nq < a.out_features;
+  float pre_r[kU][4];
+  float pre_b = 0.f, pre_g = 0.f;
+  if constexpr (C::kAsyncExchange && EPI != Q3T_EPI_SWIGLU_PAIRED) {
+    if (clustered) {
+      pre_b = (nlive && a.bias != nullptr) ? __bfloat162float(a.bias[nq]) : 0.f;
+      pre_g = !nlive                          ? 0.f
+              : EPI == Q3T_EPI_RESIDUAL_SCALED ? __bfloat162float(a.scale[nq])
+              : EPI == Q3T_EPI_SNAKE           ? a.snake_inv[nq]
+                                               : 0.f;
+#pragma unroll
+      for (int i = 0; i < kU; ++i) {
+        const int u = threadIdx.x + i * kThreads, q = u / nf;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int m = m0 + 4 * q + e;
+          pre_r[i][e] = (has_residual(EPI) && nlive && u < units && m < m_end)
+                            ? __bfloat162float(a.residual[int64_t(m) * a.res_stride + nq])
+                            : (EPI == Q3T_EPI_SNAKE && nlive ? a.snake_alpha[nq] : 0.f);
+        }
+      }
+    }
+  }
+
   // ---------------- TMEM -> registers
   const bool ok = mbar_wait(done, 0, a.status, kStatusMmaTimeout);
   tc_fence_after();
@@ -545,34 +580,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       // out of its staging have landed.
       constexpr int R4 = C::kInboxRow;
       const int slot_floats = (W + 1) * R4;  // one source's slot: W feature rows + the row sums
-      // output quads of this thread: feature f (lane-adjacent) x rows 4q..4q+3, loaded early
-      const int nf = EPI == Q3T_EPI_SWIGLU_PAIRED ? W / 2 : W;
-      const int units = nf * (BN / 4);
-      // at most 64 features per owner (two or more splits): nf divides the block, so a thread's
-      // quads all belong to one feature
-      constexpr int kU = (64 * BN / 4) / kThreads;
-      const int fq = threadIdx.x % nf, nq = n0 + rank * W + fq;
-      const bool nlive = nq < a.out_features;
-      float pre_r[kU][4];
-      float pre_b = 0.f, pre_g = 0.f;
-      if constexpr (EPI != Q3T_EPI_SWIGLU_PAIRED) {
-        pre_b = (nlive && a.bias != nullptr) ? __bfloat162float(a.bias[nq]) : 0.f;
-        pre_g = !nlive                          ? 0.f
-                : EPI == Q3T_EPI_RESIDUAL_SCALED ? __bfloat162float(a.scale[nq])
-                : EPI == Q3T_EPI_SNAKE           ? a.snake_inv[nq]
-                                                 : 0.f;
-#pragma unroll
-        for (int i = 0; i < kU; ++i) {
-          const int u = threadIdx.x + i * kThreads, q = u / nf;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int m = m0 + 4 * q + e;
-            pre_r[i][e] = (has_residual(EPI) && nlive && u < units && m < m_end)
-                              ? __bfloat162float(a.residual[int64_t(m) * a.res_stride + nq])
-                              : (EPI == Q3T_EPI_SNAKE && nlive ? a.snake_alpha[nq] : 0.f);
-          }
-        }
-      }
       cluster_wait();  // every peer's inbox barrier is initialised and armed
       float* staging = reinterpret_cast<float*>(smem);  // the idle ring: [cs][slot_floats], by owner
       {
