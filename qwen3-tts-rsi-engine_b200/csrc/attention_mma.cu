@@ -24,13 +24,15 @@ namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
-template <int D, int G>
+template <int D, int G, int STAGES = 2>
 struct MmaCfg {
   static constexpr int kTile = 64;                    // keys per tile, 16 per warp
   static constexpr int kBoxes = D / 64;               // 128-byte TMA boxes per key row
   static constexpr int kBoxBytes = kTile * 128;       // 8 KB
   static constexpr int kStageBytes = 2 * kBoxes * kBoxBytes;
-  static constexpr int kStages = 2;                   // 2 x 32 KB ring: three CTAs fit on an SM
+  // 2 x 32 KB ring: three CTAs fit on an SM. One stage for contexts of one tile (the code
+  // predictor's 17 positions): four CTAs per SM, so 512 (row, kv head) CTAs run as one wave.
+  static constexpr int kStages = STAGES;
   static constexpr int kSmem = kStages * kStageBytes + 1024;
   static constexpr int kPart = G * (D + 2);
   static constexpr int kQBytes = G * D * 2;           // the G query rows of one (row, kv head)
@@ -119,8 +121,8 @@ Q3T_DEV void norm_rope(float (&x)[D / 32], const __nv_bfloat16* w, float eps, co
   }
 }
 
-template <int D, int G, bool FUSED>
-__global__ void __launch_bounds__(128, 3)
+template <int D, int G, bool FUSED, int STAGES>
+__global__ void __launch_bounds__(128, STAGES == 1 ? 4 : 3)
     decode_attention_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                                 const __nv_bfloat16* __restrict__ query, const int64_t* __restrict__ positions,
                                 __nv_bfloat16* __restrict__ out, int kv_heads, int64_t capacity, int64_t context,
@@ -128,7 +130,7 @@ __global__ void __launch_bounds__(128, 3)
                                 const unsigned* __restrict__ plan, float qscale, float* __restrict__ partials,
                                 unsigned* __restrict__ counters,
                                 int max_chunks, unsigned* status, const FusedQKV f) {
-  using C = MmaCfg<D, G>;
+  using C = MmaCfg<D, G, STAGES>;
   constexpr int S = C::kStages;
   constexpr int KS = D / 16;  // k-steps of S = Q K^T
   constexpr int NT = D / 8;   // n-tiles of O = P V
@@ -442,11 +444,11 @@ __global__ void __launch_bounds__(128, 3)
   if (threadIdx.x == 0) *counter = 0u;
 }
 
-template <int D, int G, bool FUSED>
-int launch_mma(const AttentionCall& a, const FusedQKV& f) {
-  using C = MmaCfg<D, G>;
+template <int D, int G, bool FUSED, int STAGES>
+int launch_mma_stages(const AttentionCall& a, const FusedQKV& f) {
+  using C = MmaCfg<D, G, STAGES>;
   static PerDevice smem_once;
-  if (const int rc = smem_limit(smem_once, decode_attention_mma_kernel<D, G, FUSED>, C::kSmem, "attention: set smem"))
+  if (const int rc = smem_limit(smem_once, decode_attention_mma_kernel<D, G, FUSED, STAGES>, C::kSmem, "attention: set smem"))
     return rc;
   const int64_t arena_rows = a.arena_slots * a.kv_heads * a.capacity;
   CUtensorMap tmk, tmv;
@@ -454,11 +456,18 @@ int launch_mma(const AttentionCall& a, const FusedQKV& f) {
   if (rc) return rc;
   rc = make_map_bf16(&tmv, a.values, arena_rows, D, D, 64, C::kTile);
   if (rc) return rc;
-  return launch(decode_attention_mma_kernel<D, G, FUSED>, dim3(a.max_chunks, unsigned(a.kv_heads), unsigned(a.rows)),
+  return launch(decode_attention_mma_kernel<D, G, FUSED, STAGES>, dim3(a.max_chunks, unsigned(a.kv_heads), unsigned(a.rows)),
                 dim3(128), size_t(C::kSmem), a.stream, true, "decode_attention_mma", tmk, tmv,
                 static_cast<const __nv_bfloat16*>(a.query), a.positions, static_cast<__nv_bfloat16*>(a.out),
                 int(a.kv_heads), a.capacity, a.context, int(a.window), int(a.rows_per_slot), a.slots, a.chunk,
                 a.plan, a.scale * kLog2e, a.partials, a.counters, a.max_chunks, a.status, f);
+}
+
+// Contexts of one key tile (every chunk is one tile) take the one-stage kernel.
+template <int D, int G, bool FUSED>
+int launch_mma(const AttentionCall& a, const FusedQKV& f) {
+  if (a.context <= MmaCfg<D, G>::kTile) return launch_mma_stages<D, G, FUSED, 1>(a, f);
+  return launch_mma_stages<D, G, FUSED, 2>(a, f);
 }
 
 }  // namespace
@@ -472,11 +481,11 @@ int wave_of() {
   const int rc = once.run(
       [&](int dev) {
         using C = MmaCfg<D, G>;
-        if (cudaFuncSetAttribute(decode_attention_mma_kernel<D, G, FUSED>,
+        if (cudaFuncSetAttribute(decode_attention_mma_kernel<D, G, FUSED, 2>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
           return check_cuda("attention: set smem");
         int per_sm = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_attention_mma_kernel<D, G, FUSED>, 128,
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_attention_mma_kernel<D, G, FUSED, 2>, 128,
                                                           size_t(C::kSmem)) != cudaSuccess || per_sm < 1)
           per_sm = 1;
         resident[dev].store(per_sm * sm_count(), std::memory_order_relaxed);

@@ -472,7 +472,8 @@ def test_linear_rownorm_equals_rmsnorm_then_linear(ops, cuda, rows, k, n):
 
 
 @pytest.mark.parametrize("rows,q_heads,kv_heads,head_dim,capacity,norms", [
-    (32, 16, 8, 128, 2304, True), (5, 16, 8, 128, 128, True), (7, 8, 8, 128, 640, False), (4, 4, 2, 64, 300, True)])
+    (32, 16, 8, 128, 2304, True), (5, 16, 8, 128, 128, True), (7, 8, 8, 128, 640, False), (4, 4, 2, 64, 300, True),
+    (64, 16, 8, 128, 17, True)])
 def test_fused_qkv_attention_equals_separate_kernels(ops, cuda, rows, q_heads, kv_heads, head_dim, capacity, norms):
     """q3t_decode_attention_qkv (q/k norm + RoPE + KV write inside the attention kernel)
     against q3t_qk_norm_rope_kv followed by q3t_decode_attention: the same per-op bf16
@@ -605,8 +606,11 @@ def test_decode_attention_config1(ops, cuda):
 
 
 @pytest.mark.parametrize("B,Hq,Hkv,D,cap", [(32, 16, 8, 128, 2304), (64, 16, 8, 128, 1024), (3, 8, 8, 64, 143),
-                                            (5, 16, 8, 128, 16), (2, 16, 8, 64, 300)])
+                                            (5, 16, 8, 128, 16), (2, 16, 8, 64, 300), (64, 16, 8, 128, 17),
+                                            (7, 8, 8, 64, 64)])
 def test_decode_attention_ragged(ops, cuda, B, Hq, Hkv, D, cap):
+    """Ragged positions against the fp32 oracle; contexts of one 64-key tile (16, 17 - the code
+    predictor's - and 64) take the one-stage kernel (four CTAs per SM), longer ones the two-stage."""
     pos = (uniform(80 + B, (B,)) * cap).astype(np.int64).clip(0, cap - 1)
     pos[0] = 0
     pos[-1] = cap - 1
