@@ -73,9 +73,8 @@ def parse_args():
     p.add_argument("--concurrency", type=int, default=SERVING_SLOTS, help="serving/dispatch: requests in flight")
     p.add_argument("--requests", type=int, default=128, help="serving/dispatch: synthetic requests per GPU")
     p.add_argument("--batch", type=int, default=64, help="predictor / codec: rows or streams (BASELINE configs 3, 4)")
-    p.add_argument("--codec-streams", type=int, default=1, choices=[1, 2],
-                   help="serving/dispatch: codec decode lanes (ContinuousModel codec_streams; one lane is the "
-                        "engine's default and measured faster in the steady state)")
+    p.add_argument("--codec-streams", type=int, default=2, choices=[1, 2],
+                   help="serving/dispatch: codec decode lanes (ContinuousModel codec_streams)")
     p.add_argument("--frames", type=int, default=200, help="predictor: timed frames (BASELINE config 3)")
     p.add_argument("--no-pipeline", action="store_true",
                    help="serving: decode each tick's audio before the next tick (pipeline_audio off)")

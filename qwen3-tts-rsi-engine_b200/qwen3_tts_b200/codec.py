@@ -371,7 +371,11 @@ class CodecStep:
 
     @torch.inference_mode()
     def run(self, indices, codes, clone: bool = True):
-        self.indices.copy_(indices if isinstance(indices, torch.Tensor) else torch.tensor(indices))
+        # slot indices from pinned host memory, asynchronously: a pageable or blocking copy would
+        # make the host wait for everything queued on this stream (the tick the decode follows)
+        if not isinstance(indices, torch.Tensor):
+            indices = torch.tensor(indices, dtype=torch.long, pin_memory=True)
+        self.indices.copy_(indices, non_blocking=True)
         self.codes.copy_(codes)
         if self.graph is None:
             self.compute()
@@ -439,7 +443,9 @@ class CodecSlots:
         """Decode new codes of the given slots -> (wave fp32 [b, len*1920], pcm16 [b, len*1920])."""
         indices = list(indices)
         self._validate(indices, codes)
-        return self._graph(len(indices), codes.shape[-1], lane).run(torch.tensor(indices, device=self.device), codes)
+        # the slot list as a pinned host tensor: the graph uploads it without waiting on the stream
+        slots = torch.tensor(indices, dtype=torch.long, pin_memory=torch.cuda.is_available())
+        return self._graph(len(indices), codes.shape[-1], lane).run(slots, codes)
 
     def decode_groups(self, groups, on_output=None):
         """Decode several (indices, codes) groups (codec_slots.py:241-305 surface); the groups'
