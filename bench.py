@@ -30,6 +30,7 @@ serving through the host dispatcher over several GPUs from one process).
 from __future__ import annotations
 
 import argparse
+import collections
 import json
 import math
 import os
@@ -607,7 +608,10 @@ def steady_state(model, requests, steps: int, warmup: int, seed: int, dist) -> d
         for state in states:
             state.frames += 1
 
-    flights = []   # pipelined audio in flight (kept alive until the region ends)
+    # pipelined audio in flight: the last few steps' buffers stay referenced (a server releases a
+    # tick's audio once delivered); older ones return to the pinned-memory cache once their copies
+    # complete, so steps reuse host buffers instead of allocating new pinned memory each step
+    flights = collections.deque(maxlen=4)
 
     def step(i):
         tick_only()
