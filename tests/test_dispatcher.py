@@ -90,3 +90,30 @@ def test_a_stalled_engine_is_detected_by_the_watchdog():
         assert d.load() == [None]
     finally:
         d.close()
+
+
+def test_result_pipe_yields_one_failure_per_engine_end():
+    """An engine that reports its own failure and then closes its result pipe produces exactly
+    one failure event (a second one would kill the replacement process); a pipe that closes
+    without a goodbye produces one too, and only for an engine still marked alive."""
+    import multiprocessing as mp
+    from types import SimpleNamespace
+    from qwen3_tts_b200.dispatcher import Dispatcher as D, Engine
+
+    ctx = mp.get_context("spawn")
+
+    def engine_with(messages, alive=True):
+        reader, writer = ctx.Pipe(duplex=False)
+        for message in messages:
+            writer.send(message)
+        writer.close()
+        return Engine(rank=0, device="cpu:0", results=reader, alive=alive)
+
+    holder = SimpleNamespace(engines=[engine_with([("tick", 0, [], []), ("failed", 0, "boom")])])
+    events = D._poll(holder, 1.0)
+    assert [e[0] for e in events] == ["tick", "failed"]
+    assert holder.engines[0].results is None              # the closed pipe is dropped
+    holder = SimpleNamespace(engines=[engine_with([])])   # exited without a word
+    assert D._poll(holder, 1.0) == [("failed", 0, "result pipe closed")]
+    holder = SimpleNamespace(engines=[engine_with([], alive=False)])
+    assert D._poll(holder, 1.0) == []                     # already failed: no second failure
