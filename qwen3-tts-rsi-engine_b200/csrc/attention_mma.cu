@@ -9,7 +9,8 @@
 //   O += P V  : (D/8) n-tiles x 1 k-step, V from ldmatrix.trans,
 // i.e. ~100 instructions per 16 keys. K/V tiles (64 keys) arrive by 2-D TMA
 // with 128-byte swizzle (conflict-free ldmatrix) into a 2-stage ring (three
-// CTAs per SM keep six tiles in flight), the query rows by one bulk copy on
+// CTAs per SM keep six tiles in flight; contexts of one tile use a one-stage
+// instance, four CTAs per SM), the query rows by one bulk copy on
 // the first tile's barrier; each of
 // the 4 warps owns 16 keys of a tile and keeps its own online softmax, and
 // the warps, then the chunk CTAs of a slot (fp32 partials + ticket, chunk

@@ -7,20 +7,19 @@
 // rows, streams its 128 x K weight slab through a TMA/mbarrier ring into
 // 128-byte-swizzled shared memory and accumulates in TMEM. K is split across
 // the CTAs of a thread-block cluster (1..8 splits) so that ~2 CTAs per SM
-// stream weights; once every CTA of the cluster is past its MMAs, each pushes
-// its fp32 partials into the shared memory of the CTA that finalises those
-// features (distributed shared memory stores), and every CTA reduces its inbox
-// in fixed rank order (deterministic, no global scratch) and applies the fused
-// epilogue.
+// stream weights. Each CTA finalises 128 / splits of the tile's features: the
+// other CTAs' fp32 partials of them reach it through distributed shared memory
+// (tiles of <= 64 rows: a dedicated inbox filled by one bulk copy per source;
+// 128-row tiles: stores into its idle ring), and it reduces them in fixed rank
+// order (deterministic, no global scratch) and applies the fused epilogue.
 //
 // Roles (256 threads): warp0.lane0 = TMA producer, warp1 = TMEM owner and
-// lane0 = MMA issuer, warps 2-3 = row sums of the folded RMSNorm, all eight
-// warps = epilogue (warp w reads TMEM lanes 32(w%4)..+31, i.e. output features,
-// and every other 16-column chunk of activation rows, starting at 16(w/4)).
+// lane0 = MMA issuer, warps 2-7 = row sums of the folded RMSNorm, all eight
+// warps = epilogue (warp w reads TMEM lanes 32(w%4)..+31, i.e. output features).
 // Eight epilogue warps keep enough work in flight for the latency-bound
-// epilogues (SnakeBeta, split-K partial loads). Weight tiles of the first ring slots are requested before
-// griddepcontrol.wait, so with programmatic dependent launch the weight stream
-// starts while the previous kernel is still finishing.
+// epilogues (SnakeBeta, split-K partial loads). Weight tiles of the first ring
+// slots are requested before griddepcontrol.wait, so with programmatic dependent
+// launch the weight stream starts while the previous kernel is still finishing.
 #include "common.cuh"
 #include "host.cuh"
 
@@ -38,8 +37,8 @@ constexpr int kABytes = kTileN * kTileK * 2;
 
 template <int BN>
 struct Cfg {
-  // Tiles of <= 64 rows keep a split-K inbox beside the ring, so they have one stage fewer than
-  // before the inbox existed (two CTAs still fit on an SM).
+  // Ring depth: as deep as two CTAs per SM allow; tiles of <= 64 rows also hold a split-K inbox
+  // beside the ring.
   static constexpr int kStages = BN <= 16 ? 5 : BN <= 32 ? 4 : BN <= 128 ? 3 : 2;
   static constexpr int kBBytes = BN * kTileK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
