@@ -20,6 +20,8 @@ independent ``ContinuousModel`` replicas with no collective on the data path.
   exits is marked dead, its in-flight requests complete with
   ``finish_reason "error"`` (the audio already streamed stays delivered), and
   a fresh process is started for that GPU; the other engines are unaffected.
+  A replacement that fails or exits while starting is not started again: its
+  GPU takes no more requests (logged).
 
 Processes use the ``spawn`` start method (CUDA state is never forked).
 """
@@ -137,6 +139,7 @@ class Engine:
     inbox: object = None
     results: object = None                         # dispatcher end of the engine's result pipe
     alive: bool = False
+    starting: bool = False                         # spawned, no "hello" yet
     requests: dict = field(default_factory=dict)   # identifier -> [frames delivered (bytes)]
     last_event: float = 0.0
 
@@ -174,6 +177,7 @@ class Dispatcher:
         engine.process.start()
         writer.close()  # the engine process holds the writing end
         engine.alive = False
+        engine.starting = True
 
     def _poll(self, timeout: float) -> list:
         """Events from every engine's result pipe, waiting up to `timeout` for the first. A pipe
@@ -210,7 +214,7 @@ class Dispatcher:
             for event in events:
                 if event[0] == "hello":
                     engine = self.engines[event[1]]
-                    engine.alive = True
+                    engine.alive, engine.starting = True, False
                     self.speakers, self.languages = event[2], event[3]
                 elif event[0] == "failed":
                     raise RuntimeError(event[2])
@@ -248,6 +252,17 @@ class Dispatcher:
         if self.restart:
             self._spawn(engine)
 
+    def _retire(self, engine: Engine, reason: str) -> None:
+        """A replacement engine that failed while starting is not started again (a start that fails
+        once, e.g. out of device memory, would fail in a loop): its device leaves the rotation."""
+        LOGGER.error("engine %d could not start again (%s); its device takes no more requests", engine.rank, reason)
+        engine.starting = False
+        if engine.process is not None:
+            engine.process.join(timeout=5)
+            if engine.process.is_alive():
+                engine.process.kill()
+                engine.process.join(timeout=5)
+
     # ------------------------------------------------------------------ the continuous-model interface
     def tick(self, submissions=(), emit=None, cancelled=()):
         outputs: list = []
@@ -279,14 +294,19 @@ class Dispatcher:
                         self.owner.pop(identifier, None)
                         outputs.append((identifier, dict(record, pcm=b"".join(delivered))))
             elif kind == "failed":
-                self._fail_engine(engine, event[2], outputs)
+                if engine.alive:
+                    self._fail_engine(engine, event[2], outputs)
+                elif engine.starting:
+                    self._retire(engine, event[2])
             elif kind == "hello":
-                engine.alive = True
+                engine.alive, engine.starting = True, False
         for engine in self.engines:
             if engine.alive and engine.process is not None and not engine.process.is_alive():
                 self._fail_engine(engine, f"process exited with code {engine.process.exitcode}", outputs)
             elif engine.alive and engine.requests and now - engine.last_event > self.stall_timeout:
                 self._fail_engine(engine, f"no progress for {self.stall_timeout:.0f} s", outputs)
+            elif engine.starting and engine.process is not None and not engine.process.is_alive():
+                self._retire(engine, f"process exited with code {engine.process.exitcode}")
         return outputs
 
     def close(self) -> None:

@@ -3,7 +3,8 @@
 Every request emits one 1920-sample PCM16 chunk per tick whose samples encode
 (identifier, frame) and finishes after ``max_new_tokens - 1`` frames with
 "length". Inputs steer failures: "crash" raises inside tick, "exit" ends the
-process, "hang" stops the engine from making progress.
+process, "hang" stops the engine from making progress; ``start_marker`` makes
+every start after the first fail.
 """
 import os
 import time
@@ -16,7 +17,12 @@ def chunk(identifier: int, frame: int) -> bytes:
 
 
 class FakeEngine:
-    def __init__(self, device="cpu", **kwargs):
+    def __init__(self, device="cpu", start_marker=None, **kwargs):
+        # start_marker: a file path; every start after the first one that created it fails
+        if start_marker is not None:
+            if os.path.exists(start_marker):
+                raise RuntimeError("scripted start failure")
+            open(start_marker, "w").close()
         self.device = device
         self.speakers, self.languages = ["ryan", "voice_a"], ["auto", "english"]
         self.active = {}

@@ -92,6 +92,28 @@ def test_a_stalled_engine_is_detected_by_the_watchdog():
         d.close()
 
 
+def test_a_replacement_that_fails_to_start_is_not_started_again(tmp_path):
+    d = Dispatcher(1, {"start_marker": str(tmp_path / "started")}, per_engine=2, factory=FACTORY,
+                   devices=["cpu:0"], start_timeout=120)
+    try:
+        results, _ = drive(d, [(0, {"input": "crash", "max_new_tokens": 5})], until=lambda r: 0 in r, limit=30)
+        assert results[0]["finish_reason"] == "error"
+        first_replacement = d.engines[0].process
+        deadline = time.monotonic() + 60
+        while d.engines[0].starting and time.monotonic() < deadline:
+            d.tick([], None, [])
+        engine = d.engines[0]
+        assert not engine.starting and not engine.alive and d.load() == [None]
+        assert engine.process is first_replacement and not engine.process.is_alive()   # no second respawn
+        for _ in range(20):
+            d.tick([], None, [])
+        assert d.engines[0].process is first_replacement
+        with pytest.raises(RuntimeError, match="No engine has a free slot"):
+            d.tick([(1, {"input": "x", "max_new_tokens": 3})], None, [])
+    finally:
+        d.close()
+
+
 def test_result_pipe_yields_one_failure_per_engine_end():
     """An engine that reports its own failure and then closes its result pipe produces exactly
     one failure event (a second one would kill the replacement process); a pipe that closes
