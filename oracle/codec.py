@@ -1,5 +1,7 @@
 """12.5 Hz codec decoder restated on the CPU: module stack and incremental state.
 
+TEST INFRASTRUCTURE ONLY (see the package docstring).
+
 Two parts:
 
 1. Stand-in modules for the qwen-tts tokenizer-v2 decoder (absent here),

@@ -1,5 +1,7 @@
 """Qwen3-style decoder (talker and code predictor) restated on the CPU.
 
+TEST INFRASTRUCTURE ONLY (see the package docstring).
+
 The layer is the one the reference drives through HF modules and replaces
 piecewise: RMSNorm (operators.py:16-23), packed QKV projection, per-head
 q_norm/k_norm, rotate-half RoPE, cache update and GQA attention

@@ -1,5 +1,8 @@
 """Elementwise and normalisation ops restated on the CPU, including the
-reference's explicit bf16-rounding variants."""
+reference's explicit bf16-rounding variants.
+
+TEST INFRASTRUCTURE ONLY (see the package docstring).
+"""
 from __future__ import annotations
 
 import torch

@@ -1,4 +1,7 @@
-"""Slot-table KV arena and decode attention restated on the CPU."""
+"""Slot-table KV arena and decode attention restated on the CPU.
+
+TEST INFRASTRUCTURE ONLY (see the package docstring).
+"""
 from __future__ import annotations
 
 import torch

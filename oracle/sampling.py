@@ -1,4 +1,7 @@
-"""Sampling restated on the CPU (torch fp32 ops, as the reference calls them)."""
+"""Sampling restated on the CPU (torch fp32 ops, as the reference calls them).
+
+TEST INFRASTRUCTURE ONLY (see the package docstring).
+"""
 from __future__ import annotations
 
 import numpy as np

@@ -1,4 +1,7 @@
-"""Host-side scheduling rules of the reference (pure Python, exact)."""
+"""Host-side scheduling rules of the reference (pure Python, exact).
+
+TEST INFRASTRUCTURE ONLY (see the package docstring).
+"""
 from __future__ import annotations
 
 
