@@ -1060,16 +1060,19 @@ class CpuTick:
         return (t1 - t0) * 28 + (t2 - t1) + (t3 - t2) + (t4 - t3) * self.streams
 
 
-def cpu_serving_sample(args, steps: int):
-    """Seconds per CPU tick (median of `steps`) and the thread count, on the serving workload's
-    steady state (same requests and contexts as the GPU arm's)."""
+def cpu_serving_sample(args, steps: int, threads=None):
+    """Seconds per CPU tick (median of `steps`) and the thread count used (`threads`, default every
+    host core), on the serving workload's steady state (same requests and contexts as the GPU
+    arm's)."""
     requests = serving_requests(args.seed + 104729, SERVING_SLOTS)
     advance = steady_advance(requests, args.seed)
     positions = [len(r["input_ids"]) + PROMPT_PREFIX + a for r, a in zip(requests, advance)]
-    torch.set_num_threads(os.cpu_count() or 1)
+    torch.set_num_threads(threads or os.cpu_count() or 1)
     tick = CpuTick(SERVING_SLOTS, positions, args.seed, steps)
     times = [tick.step() for _ in range(steps)]
-    return float(np.median(times)), torch.get_num_threads()
+    used = torch.get_num_threads()
+    torch.set_num_threads(os.cpu_count() or 1)
+    return float(np.median(times)), used
 
 
 CPU_SERVING_SAMPLE = ("oracle fp32 serving tick at 64 slots (steady state, same requests and contexts): talker 1 of "
@@ -1206,8 +1209,11 @@ def serving_line(args, dist) -> dict:
     }
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         per_tick, threads = cpu_serving_sample(args, 3)
+        per_tick4, _ = cpu_serving_sample(args, 1, threads=4)
         line["cpu_baseline"] = {"value": SERVING_SLOTS / per_tick, "unit": UNIT, "cores": threads, "kind": "port",
-                                "sample": CPU_SERVING_SAMPLE + " of 3 ticks"}
+                                "value_4_threads": SERVING_SLOTS / per_tick4,
+                                "sample": CPU_SERVING_SAMPLE + " of 3 ticks; value_4_threads = one tick of the same "
+                                          "at 4 threads (the reference's default torch thread count)"}
     return line
 
 
